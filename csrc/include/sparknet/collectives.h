@@ -1,0 +1,34 @@
+// Host-side declarations of the collective launchers (collectives.cu, fused.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "proto.h"
+
+namespace sn {
+
+enum GatherAlgo : int { kGatherLL = 0, kGatherPush = 1, kGatherNvls = 2 };
+
+// Per-rank pointers for an emulated launch (all ranks inside one cooperative grid).
+struct EmuViews {
+  View v[kMaxRanks];
+  const char* in[kMaxRanks];
+  char* out[kMaxRanks];
+  const char* residual[kMaxRanks];
+  char* residual_out[kMaxRanks];
+};
+
+struct LaunchGeom {
+  int blocks;
+  int threads;
+  int ranks;      // grid.y for emulated launches
+  bool emulate;
+  int cluster;    // thread-block cluster size (fused kernels), 1 = none
+};
+
+void launch_allreduce(const Job& j, const EmuViews* e, int dtype, int algo, const LaunchGeom& g, cudaStream_t s);
+void launch_reducescatter(const Job& j, const EmuViews* e, int dtype, const LaunchGeom& g, cudaStream_t s);
+void launch_gather(const Job& j, const EmuViews* e, int algo, int op, const LaunchGeom& g, cudaStream_t s);
+void launch_fused_norm(const Job& j, const EmuViews* e, int dtype, int algo, const LaunchGeom& g, cudaStream_t s);
+
+}  // namespace sn

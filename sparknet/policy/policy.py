@@ -1,0 +1,224 @@
+"""One collective policy, fixed before any graph capture.
+
+Which transport carries each collective is decided from the operation, dtype,
+contiguity, byte size and world size only: values every tensor-parallel rank
+shares, never pointer values or timing, so every rank routes the same call the same
+way.  A transport failure is a coordinated failure, never a local switch to another
+backend (fail-stop).
+
+The reference (``sparknet/policy/policy.py:34-114``) has two backends: its one-shot
+RDMA collectives or NCCL.  On an NVSwitch box there are four:
+
+- ``oneshot``: every rank pushes its whole input into every peer (latency-optimal,
+  W-1 times the message crosses each rank's NVLink);
+- ``twoshot``: reduce-scatter then all-gather over pushes (2(W-1)/W of the message
+  per rank; bandwidth-optimal for mid-size messages);
+- ``nvls``: NVLink SHARP in-switch reduction with ``multimem`` (opt-in: the switch's
+  summation order is not the rank order, so results are rank-identical but not
+  equal to the sequential fp32 reference);
+- ``nccl``: everything above the registered capacity, and every ineligible tensor.
+
+Three limits stay distinct, as in the reference:
+
+- the all-reduce **dispatch** ceiling: the largest message sent to the custom kernels;
+- the all-reduce **capacity**: the registered slot size (may exceed dispatch; vLLM's
+  sequence-parallel threshold reads it);
+- the all-gather limit on the **input shard**.
+
+The one-shot/two-shot crossover is a per-world-size table measured on B200
+(``sparknet probe collectives --benchmark`` writes one; ``crossover_from_timings``
+turns its timings into a table).
+"""
+
+from __future__ import annotations
+
+import json
+from dataclasses import dataclass, field
+from typing import Mapping
+
+PACK_BYTES = 16
+SUPPORTED_DTYPES = ("float16", "bfloat16", "float32")
+_GATHER_REJECTED_DTYPES = ("bool", "complex64", "complex128")
+BACKENDS = ("oneshot", "twoshot", "nvls", "nccl")
+GATHER_ALGORITHMS = ("ll", "push", "nvls")
+
+ENV_CAPACITY = "SPARKNET_ALLREDUCE_CAPACITY_BYTES"
+ENV_DISPATCH = "SPARKNET_ALLREDUCE_DISPATCH_MAX_BYTES"
+ENV_GATHER = "SPARKNET_ALLGATHER_MAX_BYTES"
+ENV_CROSSOVER = "SPARKNET_ONESHOT_MAX_BYTES"
+ENV_ALGO = "SPARKNET_ALGO"
+ENV_NVLS = "SPARKNET_NVLS"
+
+# Largest all-reduce (bytes per rank) that one-shot carries, by world size.  Above
+# it two-shot moves less data per link.  Measured on 8x B200 (NVLink 5, NVSwitch);
+# the values are rank-invariant constants, not runtime measurements.
+DEFAULT_ONESHOT_MAX = {1: 1 << 62, 2: 1 << 20, 4: 512 << 10, 8: 256 << 10}
+# Largest all-gather shard that travels in LL8 form (payload + flag per 8 bytes);
+# larger shards use bulk pushes with per-block flags (or NVLS broadcast when enabled).
+DEFAULT_LL_MAX = 64 << 10
+# Messages at or above this use NVLS when it is enabled and available.
+DEFAULT_NVLS_MIN = 256 << 10
+
+
+@dataclass(frozen=True)
+class CollectivePolicy:
+    all_reduce_dispatch_bytes: int
+    all_reduce_capacity_bytes: int
+    all_gather_shard_bytes: int
+    oneshot_max_bytes: Mapping[int, int] = field(default_factory=lambda: dict(DEFAULT_ONESHOT_MAX))
+    ll_max_bytes: int = DEFAULT_LL_MAX
+    allow_nvls: bool = False
+    nvls_min_bytes: int = DEFAULT_NVLS_MIN
+    force: str | None = None
+
+    def problems(self) -> list[str]:
+        errors = []
+        for label, value in (("all_reduce_dispatch_bytes", self.all_reduce_dispatch_bytes),
+                             ("all_reduce_capacity_bytes", self.all_reduce_capacity_bytes),
+                             ("all_gather_shard_bytes", self.all_gather_shard_bytes)):
+            if value < PACK_BYTES or value % PACK_BYTES:
+                errors.append(f"{label} must be a multiple of {PACK_BYTES} bytes, at least {PACK_BYTES}")
+        if self.all_reduce_dispatch_bytes > self.all_reduce_capacity_bytes:
+            errors.append("all-reduce dispatch must not exceed registered capacity")
+        if self.force is not None and self.force not in BACKENDS:
+            errors.append(f"{ENV_ALGO} must be one of {BACKENDS}, got {self.force!r}")
+        if self.force == "nvls" and not self.allow_nvls:
+            errors.append(f"{ENV_ALGO}=nvls needs {ENV_NVLS}=1 (NVLS sums are not in rank order)")
+        for world, limit in self.oneshot_max_bytes.items():
+            if int(world) < 1 or int(limit) < 0:
+                errors.append(f"one-shot crossover for world {world} must be a non-negative byte count")
+        return errors
+
+    # -- all-reduce --------------------------------------------------------------
+    def all_reduce_eligible(self, nbytes: int, dtype: str, *, contiguous: bool = True) -> bool:
+        return (contiguous and dtype in SUPPORTED_DTYPES and 0 < nbytes <= self.all_reduce_dispatch_bytes
+                and nbytes % PACK_BYTES == 0)
+
+    def all_reduce_backend(self, nbytes: int, dtype: str, *, contiguous: bool = True, world: int = 8) -> str:
+        """``oneshot``, ``twoshot`` or ``nvls`` for an eligible input, else ``nccl``."""
+        if not self.all_reduce_eligible(nbytes, dtype, contiguous=contiguous):
+            return "nccl"
+        if self.force is not None:
+            return self.force
+        if world <= 1:
+            return "oneshot"
+        if self.allow_nvls and nbytes >= self.nvls_min_bytes:
+            return "nvls"
+        return "oneshot" if nbytes <= self.oneshot_limit(world) else "twoshot"
+
+    def oneshot_limit(self, world: int) -> int:
+        if world in self.oneshot_max_bytes:
+            return int(self.oneshot_max_bytes[world])
+        # between measured sizes: the nearest smaller world's limit
+        smaller = [w for w in self.oneshot_max_bytes if w <= world]
+        return int(self.oneshot_max_bytes[max(smaller)]) if smaller else 0
+
+    # -- all-gather --------------------------------------------------------------
+    def all_gather_backend(self, shard_bytes: int, dtype: str, *, dim: int, ndim: int,
+                           contiguous: bool = True) -> str:
+        """``oneshot`` (a custom kernel) for a contiguous shard concatenated along dim 0
+        or the last dim within the limit, else ``nccl``."""
+        if dim < 0:
+            dim += ndim
+        if (contiguous and ndim > 0 and dtype not in _GATHER_REJECTED_DTYPES and dim in (0, ndim - 1)
+                and 0 < shard_bytes <= self.all_gather_shard_bytes):
+            return "oneshot"
+        return "nccl"
+
+    def all_gather_algorithm(self, shard_bytes: int, *, row_bytes: int, nvls_available: bool) -> str:
+        """Which custom all-gather kernel: ``ll``, ``push`` or ``nvls`` (all rank-invariant)."""
+        if shard_bytes <= self.ll_max_bytes and shard_bytes % 8 == 0 and row_bytes % 8 == 0:
+            return "ll"
+        if self.allow_nvls and nvls_available and shard_bytes >= self.nvls_min_bytes:
+            return "nvls"
+        return "push"
+
+    @staticmethod
+    def reduce_scatter_backend(nbytes: int = 0, capacity: int | None = None) -> str:
+        """Reduce-scatter uses the custom kernel within capacity, NCCL above it."""
+        if capacity is not None and 0 < nbytes <= capacity:
+            return "oneshot"
+        return "nccl"
+
+    # -- environment round trip ----------------------------------------------------
+    def environment(self) -> dict[str, str]:
+        env = {
+            ENV_CAPACITY: str(self.all_reduce_capacity_bytes),
+            ENV_DISPATCH: str(self.all_reduce_dispatch_bytes),
+            ENV_GATHER: str(self.all_gather_shard_bytes),
+            ENV_CROSSOVER: json.dumps({str(k): int(v) for k, v in sorted(self.oneshot_max_bytes.items())
+                                       if v < (1 << 62)}),
+        }
+        if self.allow_nvls:
+            env[ENV_NVLS] = "1"
+        if self.force:
+            env[ENV_ALGO] = self.force
+        return env
+
+    @classmethod
+    def from_environment(cls, env: Mapping[str, str]) -> "CollectivePolicy":
+        """Read the limits, in bytes, as a recipe sets them."""
+        capacity = env.get(ENV_CAPACITY)
+        gather = env.get(ENV_GATHER)
+        if not capacity or not gather:
+            raise ValueError("the environment names no all-reduce capacity or all-gather limit")
+        dispatch = env.get(ENV_DISPATCH) or capacity
+        crossovers = dict(DEFAULT_ONESHOT_MAX)
+        if env.get(ENV_CROSSOVER):
+            crossovers.update({int(k): int(v) for k, v in json.loads(env[ENV_CROSSOVER]).items()})
+        policy = cls(int(dispatch), int(capacity), int(gather), oneshot_max_bytes=crossovers,
+                     allow_nvls=env.get(ENV_NVLS, "0") not in ("", "0", "false", "False"),
+                     force=env.get(ENV_ALGO) or None)
+        errors = policy.problems()
+        if errors:
+            raise ValueError("; ".join(errors))
+        return policy
+
+
+def crossover_from_timings(rows: list[dict]) -> dict[int, int]:
+    """The largest size at which one-shot beat two-shot, per world size.
+
+    ``rows`` are probe timing rows with ``world_size``, ``nbytes``, ``algorithm`` and
+    ``p50_us`` keys.  Sizes are compared pairwise; the crossover is the largest size
+    below the first size where two-shot wins.
+    """
+    table: dict[int, int] = {}
+    by_world: dict[int, dict[int, dict[str, float]]] = {}
+    for row in rows:
+        by_world.setdefault(int(row["world_size"]), {}).setdefault(int(row["nbytes"]), {})[row["algorithm"]] = \
+            float(row["p50_us"])
+    for world, sizes in by_world.items():
+        limit = 0
+        for nbytes in sorted(sizes):
+            arms = sizes[nbytes]
+            if "oneshot" not in arms or "twoshot" not in arms:
+                continue
+            if arms["oneshot"] <= arms["twoshot"]:
+                limit = nbytes
+            else:
+                break
+        table[world] = limit
+    return table
+
+
+# Profiles for one B200 box: the product (NVLink kernels below 2 MiB dispatch,
+# 8 MiB registered capacity, 16 MiB gather shards).
+NVLINK_POLICY = CollectivePolicy(2 * 1024 * 1024, 8 * 1024 * 1024, 16 * 1024 * 1024)
+
+
+def policy_for_profile(name: str) -> CollectivePolicy | None:
+    """The policy a named profile sets; None for an NCCL-only profile."""
+    from sparknet.nccl.profiles import profile
+
+    limits = profile(name)["limits"]
+    if limits["ALLREDUCE_CAPACITY_BYTES"] is None:
+        return None
+    capacity = int(limits["ALLREDUCE_CAPACITY_BYTES"])
+    dispatch = int(limits["ALLREDUCE_DISPATCH_MAX_BYTES"] or capacity)
+    return CollectivePolicy(dispatch, capacity, int(limits["ALLGATHER_MAX_BYTES"]))
+
+
+__all__ = [
+    "BACKENDS", "GATHER_ALGORITHMS", "PACK_BYTES", "SUPPORTED_DTYPES", "CollectivePolicy", "NVLINK_POLICY",
+    "crossover_from_timings", "policy_for_profile",
+]

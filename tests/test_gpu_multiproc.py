@@ -1,0 +1,46 @@
+"""Multi-process NVLink tests: one rank per GPU via torch.distributed.run (skipped on
+boxes with fewer than two GPUs).  Mirrors the reference's GPU suite
+(reference tests/gpu/test_oneshot_gpu.py) on the real peer-to-peer path."""
+
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _world():
+    return min(torch.cuda.device_count(), 8) if torch.cuda.is_available() else 0
+
+
+def run_workers(world, extra_env=None, timeout=600):
+    env = dict(os.environ)
+    env.update(extra_env or {})
+    env.setdefault("NCCL_NVLS_ENABLE", "0")
+    cmd = ["timeout", "-k", "30", str(timeout), sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={world}", "--master-addr", "127.0.0.1", "--master-port", str(29500 + os.getpid() % 1000),
+           str(ROOT / "tests" / "workers" / "mp_worker.py")]
+    proc = subprocess.run(cmd, env=env, cwd=ROOT, capture_output=True, text=True, timeout=timeout + 60)
+    lines = [json.loads(l) for l in proc.stdout.splitlines() if l.startswith("{")]
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-5000:]
+    return lines
+
+
+@pytest.mark.skipif(_world() < 2, reason="needs two or more GPUs")
+def test_multiprocess_collectives():
+    lines = run_workers(_world())
+    assert len(lines) == _world() and all(l["checks"] > 10 and not l["failures"] for l in lines), lines
+
+
+@pytest.mark.skipif(_world() < 2 or os.environ.get("SPARKNET_TEST_NVLS") != "1",
+                    reason="needs two or more GPUs and SPARKNET_TEST_NVLS=1")
+def test_multiprocess_collectives_nvls():
+    lines = run_workers(_world(), {"SPARKNET_NVLS": "1"})
+    assert len(lines) == _world() and all(not l["failures"] for l in lines), lines

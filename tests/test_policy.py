@@ -1,0 +1,88 @@
+"""Policy boundaries (CPU only), after the reference's tests/test_policy.py."""
+
+import pytest
+
+from sparknet.policy import CollectivePolicy, crossover_from_timings
+from sparknet.policy.policy import DEFAULT_ONESHOT_MAX
+
+
+def make(**kw):
+    base = dict(all_reduce_dispatch_bytes=2 << 20, all_reduce_capacity_bytes=8 << 20, all_gather_shard_bytes=16 << 20)
+    base.update(kw)
+    return CollectivePolicy(**base)
+
+
+def test_limits_are_distinct_and_validated():
+    assert make().problems() == []
+    assert "dispatch" in " ".join(make(all_reduce_dispatch_bytes=16 << 20).problems())
+    assert make(all_gather_shard_bytes=17).problems()
+    assert make(force="bogus").problems()
+    assert make(force="nvls").problems()  # NVLS is opt-in
+    assert make(force="nvls", allow_nvls=True).problems() == []
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_all_reduce_backend_boundaries(world):
+    p = make()
+    limit = DEFAULT_ONESHOT_MAX[world]
+    assert p.all_reduce_backend(16, "bfloat16", world=world) == "oneshot"
+    assert p.all_reduce_backend(limit, "bfloat16", world=world) == "oneshot"
+    assert p.all_reduce_backend(limit + 16, "bfloat16", world=world) == "twoshot"
+    assert p.all_reduce_backend(2 << 20, "bfloat16", world=world) in ("oneshot", "twoshot")
+    assert p.all_reduce_backend((2 << 20) + 16, "bfloat16", world=world) == "nccl"
+    assert p.all_reduce_backend(1024 + 8, "bfloat16", world=world) == "nccl"   # not a 16-byte multiple
+    assert p.all_reduce_backend(1024, "int32", world=world) == "nccl"
+    assert p.all_reduce_backend(1024, "bfloat16", contiguous=False, world=world) == "nccl"
+    assert p.all_reduce_backend(0, "bfloat16", world=world) == "nccl"
+
+
+def test_world_one_and_unlisted_worlds():
+    p = make()
+    assert p.all_reduce_backend(1 << 20, "float32", world=1) == "oneshot"
+    assert p.oneshot_limit(6) == DEFAULT_ONESHOT_MAX[4]
+    assert p.oneshot_limit(3) == DEFAULT_ONESHOT_MAX[2]
+
+
+def test_nvls_only_when_allowed():
+    assert make().all_reduce_backend(1 << 20, "bfloat16", world=8) == "twoshot"
+    assert make(allow_nvls=True).all_reduce_backend(1 << 20, "bfloat16", world=8) == "nvls"
+    assert make(allow_nvls=True).all_reduce_backend(4096, "bfloat16", world=8) == "oneshot"
+
+
+def test_all_gather_backend_and_algorithm():
+    p = make()
+    assert p.all_gather_backend(1024, "bfloat16", dim=0, ndim=2) == "oneshot"
+    assert p.all_gather_backend(1024, "bfloat16", dim=-1, ndim=3) == "oneshot"
+    assert p.all_gather_backend(1024, "bfloat16", dim=1, ndim=3) == "nccl"
+    assert p.all_gather_backend(1024, "bool", dim=0, ndim=1) == "nccl"
+    assert p.all_gather_backend((16 << 20) + 16, "bfloat16", dim=0, ndim=1) == "nccl"
+    assert p.all_gather_algorithm(1024, row_bytes=1024, nvls_available=False) == "ll"
+    assert p.all_gather_algorithm(1 << 20, row_bytes=4096, nvls_available=True) == "push"
+    assert make(allow_nvls=True).all_gather_algorithm(1 << 20, row_bytes=4096, nvls_available=True) == "nvls"
+    assert p.all_gather_algorithm(1020, row_bytes=12, nvls_available=False) == "push"
+
+
+def test_rank_invariance_ignores_everything_but_shape():
+    """Same inputs, same answer, whatever else differs (nothing else is an argument)."""
+    p = make()
+    answers = {p.all_reduce_backend(n, "bfloat16", world=8) for _ in range(3) for n in [65536]}
+    assert len(answers) == 1
+
+
+def test_environment_round_trip():
+    p = make(allow_nvls=True, oneshot_max_bytes={2: 1 << 20, 8: 128 << 10})
+    q = CollectivePolicy.from_environment(p.environment())
+    assert q.all_reduce_capacity_bytes == p.all_reduce_capacity_bytes
+    assert q.allow_nvls and q.oneshot_limit(8) == 128 << 10
+    with pytest.raises(ValueError):
+        CollectivePolicy.from_environment({})
+
+
+def test_crossover_from_timings():
+    rows = [
+        {"world_size": 8, "nbytes": 1 << 16, "algorithm": "oneshot", "p50_us": 5.0},
+        {"world_size": 8, "nbytes": 1 << 16, "algorithm": "twoshot", "p50_us": 7.0},
+        {"world_size": 8, "nbytes": 1 << 18, "algorithm": "oneshot", "p50_us": 9.0},
+        {"world_size": 8, "nbytes": 1 << 18, "algorithm": "twoshot", "p50_us": 8.0},
+    ]
+    assert crossover_from_timings(rows) == {8: 1 << 16}
