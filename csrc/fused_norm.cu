@@ -85,8 +85,10 @@ SN_DEV void fused_body(const Job& j, int algo) {
 
   Ctrl* ctrl = ctrl_of(j);
   if (int32_t(j.rank) == j.skip_rank) return;
-  if (m.ld_volatile_u32(&ctrl->poison)) return;
-  uint32_t seq = m.ld_volatile_u32(&ctrl->epoch) + 1u;
+  uint32_t epoch, poison;
+  m.ld_volatile_pair(&ctrl->epoch, epoch, poison);
+  if (poison) return;
+  uint32_t seq = epoch + 1u;
   if (!seq) seq = 1u;
   OpCtx c{ctrl, j.v.status, seq, j.rank, blockIdx.x, kOpFusedNorm};
 

@@ -67,6 +67,10 @@ struct DevMem {
     asm volatile("ld.volatile.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
   }
+  // epoch and poison words of Ctrl in one access
+  SN_DEV void ld_volatile_pair(const uint32_t* p, uint32_t& a, uint32_t& b) const {
+    asm volatile("ld.volatile.global.v2.u32 {%0,%1}, [%2];" : "=r"(a), "=r"(b) : "l"(p) : "memory");
+  }
   SN_DEV void st_release_u32(uint32_t* p, uint32_t v) const {
     asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
   }

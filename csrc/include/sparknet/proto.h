@@ -53,9 +53,10 @@ struct Pack16 {
 // the owning rank's kernels touch them, so they need no peer-scope ordering.
 // ---------------------------------------------------------------------------
 struct Ctrl {
+  // epoch and poison are adjacent so one 8-byte load at kernel entry reads both
   uint32_t epoch;                  // sequence of the last completed collective
-  uint32_t done;                   // blocks of the current collective that finished
   uint32_t poison;                 // nonzero after a failed wait: every kernel exits at entry
+  uint32_t done;                   // blocks of the current collective that finished
   uint32_t ops;                    // collectives completed (stats)
   uint32_t bar_count[kMaxBlocks];  // per-block barrier generation (push/flag protocols)
   uint32_t mc_count[kMaxBlocks];   // per-block multicast barrier target
@@ -710,16 +711,16 @@ SN_HD void push_receive(M& m, const Job& j, const OpCtx& c, bool exchange, uint6
 }
 
 // Completion: the last block to finish publishes the sequence as the new epoch.
-// Every block read the epoch at entry, so none can read the new value early; the
-// next collective on this rank starts after this kernel completes.
+// Every block consumed its entry read of the epoch (it computed `seq` from it)
+// before its increment of `done`, so no block can read the new value early, and the
+// next collective on this rank starts only after this kernel completes.  No fence is
+// needed: the kernel boundary publishes the new epoch to the next launch.
 template <class M>
 SN_HD void finish_op(M& m, Ctrl* ctrl, uint32_t seq, uint32_t nblocks) {
-  m.fence_device();
   uint32_t old = m.atomic_add_u32(&ctrl->done, 1u);
   if (old == nblocks - 1u) {
     ctrl->done = 0u;
     ctrl->ops = ctrl->ops + 1u;
-    m.fence_device();
     m.st_volatile_u32(&ctrl->epoch, seq);
   }
 }
