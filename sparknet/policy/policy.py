@@ -50,9 +50,11 @@ ENV_ALGO = "SPARKNET_ALGO"
 ENV_NVLS = "SPARKNET_NVLS"
 
 # Largest all-reduce (bytes per rank) that one-shot carries, by world size.  Above
-# it two-shot moves less data per link.  Measured on 8x B200 (NVLink 5, NVSwitch);
-# the values are rank-invariant constants, not runtime measurements.
-DEFAULT_ONESHOT_MAX = {1: 1 << 62, 2: 1 << 20, 4: 512 << 10, 8: 256 << 10}
+# it two-shot moves less data per link.  Measured on 8x B200 (NVLink 5, NVSwitch) with
+# ``sparknet probe collectives --benchmark --sweep`` (8 GPUs: one-shot 11.9 us vs
+# two-shot 14.5 us at 480 KiB, 17.5 vs 15.1 us at 1 MiB); the values are
+# rank-invariant constants, not runtime measurements.
+DEFAULT_ONESHOT_MAX = {1: 1 << 62, 2: 1 << 20, 4: 512 << 10, 8: 512 << 10}
 # Largest all-gather shard that travels in LL8 form (payload + flag per 8 bytes);
 # larger shards use bulk pushes with per-block flags (or NVLS broadcast when enabled).
 DEFAULT_LL_MAX = 64 << 10

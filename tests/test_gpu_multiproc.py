@@ -21,14 +21,18 @@ def _world():
 
 
 def run_workers(world, extra_env=None, timeout=600):
+    import tempfile
+
+    out_dir = tempfile.mkdtemp(prefix="sparknet-mp-")
     env = dict(os.environ)
     env.update(extra_env or {})
+    env["SPARKNET_TEST_OUT"] = out_dir
     env.setdefault("NCCL_NVLS_ENABLE", "0")
     cmd = ["timeout", "-k", "30", str(timeout), sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={world}", "--master-addr", "127.0.0.1", "--master-port", str(29500 + os.getpid() % 1000),
            str(ROOT / "tests" / "workers" / "mp_worker.py")]
     proc = subprocess.run(cmd, env=env, cwd=ROOT, capture_output=True, text=True, timeout=timeout + 60)
-    lines = [json.loads(l) for l in proc.stdout.splitlines() if l.startswith("{")]
+    lines = [json.loads(p.read_text()) for p in sorted(Path(out_dir).glob("rank*.json"))]
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-5000:]
     return lines
 

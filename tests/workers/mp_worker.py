@@ -166,7 +166,11 @@ def main():
     dist.barrier(group=cpu)
     rt.close()
     dist.barrier(group=cpu)
-    print(json.dumps(results), flush=True)
+    out_dir = os.environ.get("SPARKNET_TEST_OUT")
+    if out_dir:  # one file per rank: ranks printing at once interleave their lines
+        Path(out_dir, f"rank{rank}.json").write_text(json.dumps(results))
+    else:
+        print(json.dumps(results), flush=True)
     dist.destroy_process_group()
     return 1 if FAILURES else 0
 
