@@ -415,6 +415,7 @@ uint64_t layout_total(int world, uint64_t lam_cap, uint64_t ll_cap, uint64_t pus
 
 void register_trace(py::module_& m);
 void register_gemm(py::module_& m);
+void register_decode(py::module_& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   using namespace sn;
@@ -484,4 +485,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
 
   register_trace(m);
   register_gemm(m);
+  register_decode(m);
 }

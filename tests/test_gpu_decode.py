@@ -1,0 +1,124 @@
+"""Decode-step kernels against plain PyTorch fp32 references (GPU)."""
+
+import math
+
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+
+def rope_ref(x, cos, sin, pos):
+    x = x.float()
+    x1, x2 = x[..., :64], x[..., 64:]
+    c, s = cos[pos][:, None, :], sin[pos][:, None, :]
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
+
+
+def test_rope_qkv_cache(device, native):
+    B, Hq, Hkv, L = 3, 8, 2, 40
+    qkv = torch.randn(B, (Hq + 2 * Hkv) * 128, device=device).to(torch.bfloat16)
+    ang = torch.arange(L, dtype=torch.float64)[:, None] / (5e5 ** (torch.arange(64, dtype=torch.float64) * 2 / 128))
+    cos, sin = ang.cos().float().to(device), ang.sin().float().to(device)
+    pos = torch.tensor([0, 7, 39], dtype=torch.int32, device=device)
+    q = torch.empty(B, Hq, 128, dtype=torch.bfloat16, device=device)
+    kc = torch.zeros(B, L, Hkv, 128, dtype=torch.bfloat16, device=device)
+    vc = torch.zeros_like(kc)
+    native.rope_qkv_cache(qkv, cos, sin, pos, q, kc, vc, Hq, Hkv)
+    torch.cuda.synchronize()
+    parts = qkv.view(B, Hq + 2 * Hkv, 128)
+    p = pos.long()
+    torch.testing.assert_close(q.float(), rope_ref(parts[:, :Hq], cos, sin, p), rtol=1e-2, atol=1e-2)
+    for b in range(B):
+        torch.testing.assert_close(kc[b, p[b]].float(), rope_ref(parts[b:b + 1, Hq:Hq + Hkv], cos, sin, p[b:b + 1])[0],
+                                   rtol=1e-2, atol=1e-2)
+        assert torch.equal(vc[b, p[b]], parts[b, Hq + Hkv:])
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,L", [(1, 8, 1, 1025), (4, 8, 1, 300), (2, 64, 8, 129), (64, 8, 1, 1280), (3, 4, 4, 33)])
+def test_decode_attention(device, native, B, Hq, Hkv, L):
+    Lmax = L + 7
+    q = torch.randn(B, Hq, 128, device=device).to(torch.bfloat16)
+    kc = torch.randn(B, Lmax, Hkv, 128, device=device).to(torch.bfloat16)
+    vc = torch.randn(B, Lmax, Hkv, 128, device=device).to(torch.bfloat16)
+    lengths = torch.randint(1, L + 1, (B,), dtype=torch.int32, device=device)
+    lengths[0] = L
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    ws = torch.empty(native.attention_workspace_floats(B, Hq, Hkv, L, sms), dtype=torch.float32, device=device)
+    out = torch.empty(B, Hq, 128, dtype=torch.bfloat16, device=device)
+    native.decode_attention(q, kc, vc, lengths, out, ws, L, 1 / math.sqrt(128))
+    torch.cuda.synchronize()
+    G = Hq // Hkv
+    for b in range(B):
+        n = int(lengths[b])
+        k = kc[b, :n].float().repeat_interleave(G, dim=1)          # [n, Hq, 128]
+        v = vc[b, :n].float().repeat_interleave(G, dim=1)
+        s = torch.einsum("hd,nhd->hn", q[b].float(), k) / math.sqrt(128)
+        ref = torch.einsum("hn,nhd->hd", s.softmax(-1), v)
+        torch.testing.assert_close(out[b].float(), ref, rtol=2e-2, atol=2e-2)
+
+
+def test_add_rmsnorm_silu_argmax(device, native):
+    x = torch.randn(5, 8192, device=device).to(torch.bfloat16)
+    r = torch.randn(5, 8192, device=device).to(torch.bfloat16)
+    g = (1 + 0.02 * torch.randn(8192, device=device)).to(torch.bfloat16)
+    out, rout = torch.empty_like(x), torch.empty_like(x)
+    native.add_rmsnorm(x, r, rout, g, out, 1e-5)
+    torch.cuda.synchronize()
+    want_r = (x.float() + r.float()).to(torch.bfloat16)
+    assert torch.equal(rout, want_r)
+    want = (want_r.float() * torch.rsqrt(want_r.float().pow(2).mean(-1, keepdim=True) + 1e-5) * g.float())
+    torch.testing.assert_close(out.float(), want, rtol=1e-2, atol=1e-2)
+    gu = torch.randn(3, 2 * 1000, device=device).to(torch.bfloat16)
+    act = torch.empty(3, 1000, dtype=torch.bfloat16, device=device)
+    native.silu_mul(gu, act)
+    torch.cuda.synchronize()
+    g_, u_ = gu.float()[:, :1000], gu.float()[:, 1000:]
+    torch.testing.assert_close(act.float(), torch.nn.functional.silu(g_) * u_, rtol=1e-2, atol=1e-2)
+    logits = torch.randn(4, 16032, device=device).to(torch.bfloat16)
+    best = torch.empty(4, 2, dtype=torch.float32, device=device)
+    native.row_argmax(logits, 1000, best)
+    torch.cuda.synchronize()
+    vals, idx = logits.float().max(-1)
+    assert torch.equal(best[:, 0], vals) and torch.equal(best[:, 1].long(), idx + 1000)
+
+
+def test_tiny_model_step_matches_torch(device, native):
+    from sparknet.models.llama import LlamaConfig, TPLlama
+
+    cfg = LlamaConfig.tiny(layers=2)
+    m = TPLlama(cfg, rank=0, world=1, device=device, batch=2, max_len=32)
+    m.fill_prompt_cache(5)
+    m.tokens.copy_(torch.tensor([3, 9], device=device))
+    tokens0, pos0 = m.tokens.clone(), m.positions.clone().long()
+    kcache0 = [L["k"].clone() for L in m.layers]
+    vcache0 = [L["v"].clone() for L in m.layers]
+    m.step_kernels()
+    torch.cuda.synchronize()
+    # fp32 reference of the same step
+    f = lambda t: t.float()  # noqa: E731
+    rms = lambda v, g: v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + cfg.eps) * f(g)  # noqa: E731
+    res = f(m.embed[tokens0])
+    x = rms(res, m.layers[0]["ln1"])
+    for i, L in enumerate(m.layers):
+        qkv = (x @ f(L["wqkv"])).view(2, -1, 128)
+        q, k, v = qkv[:, :m.hq], qkv[:, m.hq:m.hq + m.hkv], qkv[:, m.hq + m.hkv:]
+        q, k = rope_ref(q, m.cos, m.sin, pos0), rope_ref(k, m.cos, m.sin, pos0)
+        outs = []
+        for b in range(2):
+            n = int(pos0[b]) + 1
+            kk = torch.cat([f(kcache0[i][b, :n - 1]), k[b:b + 1]], 0).repeat_interleave(m.hq // m.hkv, 1)
+            vv = torch.cat([f(vcache0[i][b, :n - 1]), v[b:b + 1]], 0).repeat_interleave(m.hq // m.hkv, 1)
+            s = torch.einsum("hd,nhd->hn", q[b], kk) / math.sqrt(128)
+            outs.append(torch.einsum("hn,nhd->hd", s.softmax(-1), vv))
+        attn = torch.stack(outs).view(2, -1)
+        res = res + attn @ f(L["wo"])
+        x = rms(res, L["ln2"])
+        gu = x @ f(L["wgu"])
+        act = torch.nn.functional.silu(gu[:, :m.f]) * gu[:, m.f:]
+        res = res + act @ f(L["wdown"])
+        x = rms(res, m.layers[i + 1]["ln1"] if i + 1 < len(m.layers) else m.norm)
+    logits = x @ f(m.lm_head)
+    torch.testing.assert_close(m.logits.float(), logits, rtol=5e-2, atol=5e-2)
+    assert torch.equal(m.positions.long(), pos0 + 1)

@@ -20,7 +20,7 @@ def _world():
     return min(torch.cuda.device_count(), 8) if torch.cuda.is_available() else 0
 
 
-def run_workers(world, extra_env=None, timeout=600):
+def run_workers(world, extra_env=None, timeout=600, script="mp_worker.py"):
     import tempfile
 
     out_dir = tempfile.mkdtemp(prefix="sparknet-mp-")
@@ -30,7 +30,7 @@ def run_workers(world, extra_env=None, timeout=600):
     env.setdefault("NCCL_NVLS_ENABLE", "0")
     cmd = ["timeout", "-k", "30", str(timeout), sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={world}", "--master-addr", "127.0.0.1", "--master-port", str(29500 + os.getpid() % 1000),
-           str(ROOT / "tests" / "workers" / "mp_worker.py")]
+           str(ROOT / "tests" / "workers" / script)]
     proc = subprocess.run(cmd, env=env, cwd=ROOT, capture_output=True, text=True, timeout=timeout + 60)
     lines = [json.loads(p.read_text()) for p in sorted(Path(out_dir).glob("rank*.json"))]
     assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-5000:]
@@ -48,3 +48,9 @@ def test_multiprocess_collectives():
 def test_multiprocess_collectives_nvls():
     lines = run_workers(_world(), {"SPARKNET_NVLS": "1"})
     assert len(lines) == _world() and all(not l["failures"] for l in lines), lines
+
+
+@pytest.mark.skipif(_world() < 2, reason="needs two or more GPUs")
+def test_multiprocess_tp_decode_arms_agree():
+    lines = run_workers(_world(), script="decode_worker.py")
+    assert len(lines) == _world() and all(not l["failures"] and l["rt_health"] is None for l in lines), lines

@@ -1,0 +1,66 @@
+"""One rank of the multi-GPU decode check: a tiny TP Llama decodes with the fused
+NVLink epilogue and with NCCL; both arms must produce the same tokens on every rank
+and close logits.  Writes one JSON file per rank to $SPARKNET_TEST_OUT."""
+
+import json
+import os
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[2]
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+
+def main():
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist.init_process_group("cpu:gloo,cuda:nccl", timeout=timedelta(seconds=60), device_id=device)
+    rank, world = dist.get_rank(), dist.get_world_size()
+    cpu = dist.new_group(backend="gloo", timeout=timedelta(seconds=60))
+    from sparknet.models.llama import LlamaConfig, TPLlama
+    from sparknet.oneshot import AllReduce
+
+    rt = AllReduce.from_exchange_group(exchange_group=cpu, device=device, max_size=4 << 20, max_gather_bytes=1 << 20)
+    rt.prepare((torch.bfloat16,))
+    cfg = LlamaConfig(hidden=2048, layers=3, heads=16, kv_heads=8, head_dim=128, ffn=4096, vocab=8192)
+    results = {"rank": rank, "failures": []}
+    outs = {}
+    for comm in ("sparknet", "nccl"):
+        m = TPLlama(cfg, rank=rank, world=world, device=device, batch=4, max_len=64, comm=comm, runtime=rt, seed=3)
+        m.fill_prompt_cache(10)
+        m.tokens.copy_(torch.tensor([1, 2, 3, 4], device=device))
+        m.capture()
+        toks = []
+        for _ in range(4):
+            m.replay()
+            toks.append(m.tokens.clone())
+        torch.cuda.synchronize()
+        outs[comm] = (torch.stack(toks).cpu(), m.logits.float().cpu(), m.x.float().cpu())
+        m.release()
+        del m
+    t_s, l_s, x_s = outs["sparknet"]
+    t_n, l_n, x_n = outs["nccl"]
+    gathered = [None] * world
+    dist.all_gather_object(gathered, t_s.tolist(), group=cpu)
+    if any(g != gathered[0] for g in gathered):
+        results["failures"].append("ranks sampled different tokens")
+    if not torch.allclose(x_s, x_n, rtol=5e-2, atol=5e-2):
+        results["failures"].append(f"hidden states differ between arms: {(x_s - x_n).abs().max().item()}")
+    results["tokens_equal_between_arms"] = bool(torch.equal(t_s, t_n))
+    results["rt_health"] = rt.failure()
+    torch.cuda.synchronize()
+    dist.barrier(group=cpu)
+    rt.close()
+    dist.barrier(group=cpu)
+    Path(os.environ["SPARKNET_TEST_OUT"], f"rank{rank}.json").write_text(json.dumps(results))
+    dist.destroy_process_group()
+    return 1 if results["failures"] else 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
