@@ -1,0 +1,56 @@
+"""``C = A @ B.T`` on 5th-generation tensor cores (tcgen05, TMEM accumulators, TMA).
+
+Both operands are K-major (row-major ``A[M, K]`` and ``B[N, K]``), bf16 in, fp32
+accumulation, bf16 out.  K must be a multiple of 64 and N of 32.  The kernel is a
+persistent, warp-specialised loop (TMA warp, MMA warp, four epilogue warps) with a
+4-stage shared-memory ring and a double-buffered accumulator in TMEM.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _native
+
+_ERRORS = {1: "an mbarrier wait timed out", 2: "a peer flag wait timed out"}
+
+
+class GemmError(RuntimeError):
+    pass
+
+
+def _err_word(device) -> torch.Tensor:
+    key = (device.type, device.index)
+    buf = _err_word.cache.get(key)
+    if buf is None:
+        buf = torch.zeros(1, dtype=torch.int32, device=device)
+        _err_word.cache[key] = buf
+    return buf
+
+
+_err_word.cache = {}
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, *, block_n: int = 256,
+         max_ctas: int = 0, check: bool = False) -> torch.Tensor:
+    """``a @ b.T`` for bf16 ``a [M, K]`` and ``b [N, K]``."""
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise ValueError("gemm takes bfloat16 operands")
+    M, K = a.shape
+    N = b.shape[0]
+    if b.shape[1] != K:
+        raise ValueError("a and b must share K")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=a.device)
+    err = _err_word(a.device)
+    _native.load().gemm(a, b, out, err, block_n, max_ctas)
+    if check:
+        torch.cuda.synchronize(a.device)
+        code = int(err.item())
+        if code:
+            err.zero_()
+            raise GemmError(f"tcgen05 GEMM failed: {_ERRORS.get(code, code)}")
+    return out
+
+
+__all__ = ["GemmError", "gemm"]

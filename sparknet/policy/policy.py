@@ -54,10 +54,12 @@ ENV_NVLS = "SPARKNET_NVLS"
 # ``sparknet probe collectives --benchmark --sweep`` (8 GPUs: one-shot 11.9 us vs
 # two-shot 14.5 us at 480 KiB, 17.5 vs 15.1 us at 1 MiB); the values are
 # rank-invariant constants, not runtime measurements.
-DEFAULT_ONESHOT_MAX = {1: 1 << 62, 2: 1 << 20, 4: 512 << 10, 8: 512 << 10}
+DEFAULT_ONESHOT_MAX = {1: 1 << 62, 2: 4 << 20, 4: 512 << 10, 8: 512 << 10}
 # Largest all-gather shard that travels in LL8 form (payload + flag per 8 bytes);
 # larger shards use bulk pushes with per-block flags (or NVLS broadcast when enabled).
-DEFAULT_LL_MAX = 64 << 10
+# LL doubles the bytes but needs no fence or flag round trip: on 2 GPUs a 256 KiB
+# shard took 19 us as a flagged bulk push, where LL moves it in a few microseconds.
+DEFAULT_LL_MAX = 1 << 20
 # Messages at or above this use NVLS when it is enabled and available.
 DEFAULT_NVLS_MIN = 256 << 10
 

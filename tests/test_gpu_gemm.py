@@ -1,0 +1,49 @@
+"""tcgen05 GEMM numerics against a plain PyTorch fp32 reference (GPU)."""
+
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 128), (1000, 1280, 1024), (384, 4096, 8192),
+                                   (4096, 1280, 8192), (130, 96, 192)])
+@pytest.mark.parametrize("block_n", [256, 128])
+def test_gemm_matches_fp32(device, native, M, N, K, block_n):
+    from sparknet.ops.gemm import gemm
+
+    g = torch.Generator(device=device).manual_seed(M + N + K)
+    a = torch.randn(M, K, generator=g, device=device).to(torch.bfloat16)
+    b = torch.randn(N, K, generator=g, device=device).to(torch.bfloat16)
+    c = gemm(a, b, block_n=block_n, check=True)
+    ref = a.float() @ b.float().T
+    err = (c.float() - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    assert err <= 1e-2 * scale, (err, scale)
+
+
+def test_gemm_throughput(device, native):
+    """Not a threshold test: records TFLOP/s of a prefill-shaped GEMM next to cuBLAS."""
+    from sparknet.ops.gemm import gemm
+
+    M, N, K = 8192, 7168, 8192
+    a = torch.randn(M, K, device=device).to(torch.bfloat16)
+    b = torch.randn(N, K, device=device).to(torch.bfloat16)
+    c = torch.empty(M, N, dtype=torch.bfloat16, device=device)
+    for _ in range(3):
+        gemm(a, b, c)
+        torch.mm(a, b.T)
+    torch.cuda.synchronize()
+    res = {}
+    for name, fn in (("tcgen05", lambda: gemm(a, b, c)), ("cublas", lambda: torch.mm(a, b.T))):
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record()
+        for _ in range(10):
+            fn()
+        en.record()
+        en.synchronize()
+        res[name] = 2 * M * N * K * 10 / (st.elapsed_time(en) / 1000) / 1e12
+    print(f"\nGEMM {M}x{N}x{K} TFLOP/s: {res}")
+    gemm(a, b, c, check=True)
+    assert res["tcgen05"] > 100

@@ -33,7 +33,8 @@ def run_workers(world, extra_env=None, timeout=600, script="mp_worker.py"):
            str(ROOT / "tests" / "workers" / script)]
     proc = subprocess.run(cmd, env=env, cwd=ROOT, capture_output=True, text=True, timeout=timeout + 60)
     lines = [json.loads(p.read_text()) for p in sorted(Path(out_dir).glob("rank*.json"))]
-    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-5000:]
+    failures = [l.get("failures") for l in lines]
+    assert proc.returncode == 0, f"failures={failures}\n" + proc.stdout[-3000:] + proc.stderr[-5000:]
     return lines
 
 

@@ -24,7 +24,7 @@ def test_limits_are_distinct_and_validated():
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_all_reduce_backend_boundaries(world):
     p = make()
-    limit = DEFAULT_ONESHOT_MAX[world]
+    limit = min(DEFAULT_ONESHOT_MAX[world], p.all_reduce_dispatch_bytes)
     assert p.all_reduce_backend(16, "bfloat16", world=world) == "oneshot"
     assert p.all_reduce_backend(limit, "bfloat16", world=world) == "oneshot"
     assert p.all_reduce_backend(limit + 16, "bfloat16", world=world) in ("twoshot", "nccl")
@@ -57,8 +57,9 @@ def test_all_gather_backend_and_algorithm():
     assert p.all_gather_backend(1024, "bool", dim=0, ndim=1) == "nccl"
     assert p.all_gather_backend((16 << 20) + 16, "bfloat16", dim=0, ndim=1) == "nccl"
     assert p.all_gather_algorithm(1024, row_bytes=1024, nvls_available=False) == "ll"
-    assert p.all_gather_algorithm(1 << 20, row_bytes=4096, nvls_available=True) == "push"
-    assert make(allow_nvls=True).all_gather_algorithm(1 << 20, row_bytes=4096, nvls_available=True) == "nvls"
+    assert p.all_gather_algorithm(1 << 20, row_bytes=4096, nvls_available=True) == "ll"
+    assert p.all_gather_algorithm(2 << 20, row_bytes=4096, nvls_available=True) == "push"
+    assert make(allow_nvls=True).all_gather_algorithm(2 << 20, row_bytes=4096, nvls_available=True) == "nvls"
     assert p.all_gather_algorithm(1020, row_bytes=12, nvls_available=False) == "push"
 
 

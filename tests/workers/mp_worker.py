@@ -64,6 +64,8 @@ def main():
     rt.set_timeout_ms(5000)
     rt.prepare((torch.bfloat16, torch.float16, torch.float32), padded_gather=True)
     results = {"rank": rank, "world": world, "multicast": rt.has_multicast, "checks": 0}
+    if nvls:
+        print(f"rank {rank}: multicast available: {rt.has_multicast}", flush=True)
     algos = ["oneshot", "twoshot"] + (["nvls"] if rt.has_multicast else [])
 
     def check_same_everywhere(t, what):
@@ -156,7 +158,11 @@ def main():
         graph.replay()
         torch.cuda.synchronize()
         for x, o in zip(xs, outs):
-            expect(torch.equal(o, rank_order_sum(gather_all(x, world))), f"graph replay {step}")
+            want = rank_order_sum(gather_all(x, world))
+            if rt.algorithm_for(x.numel() * 2, x.dtype) == "nvls":  # switch order, not rank order
+                expect(torch.allclose(o.float(), want.float(), rtol=2e-2, atol=2e-2), f"graph replay {step} (nvls)")
+            else:
+                expect(torch.equal(o, want), f"graph replay {step}")
     expect(rt.failure() is None, f"health: {rt.failure()}")
     results["checks"] += 1
     results["stats"] = {k: v for k, v in rt.stats().items() if k in ("calls", "epoch", "transport")}
