@@ -109,6 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   __shared__ uint32_t err_local;
+  __shared__ uint32_t tile_done[2];  // epilogue warps done with the tile in accumulator 0/1
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile uint32_t* err = &err_local;
@@ -163,6 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     err_local = 0;
+    tile_done[0] = tile_done[1] = 0;
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -320,13 +322,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
-      if (p.mode == 2) {
-        // publish the tile to its owner once all four epilogue warps stored their rows
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (warp == 2 && lane == 0) {
+      if (p.mode == 2 && lane == 0) {
+        // Publish the tile to its owner once all four epilogue warps stored their rows.
+        // No CTA barrier (a warp that gave up on a wait must not strand the others):
+        // each warp fences its own stores at system scope, then counts in; the fourth
+        // warp to count in raises the owner's flag.
+        m.fence_sys();
+        uint32_t prev;
+        asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
+                     : "=r"(prev) : "r"(smem_u32(&tile_done[acc])) : "memory");
+        if (prev % kEpiWarps == kEpiWarps - 1) {
           const int owner = m0 / p.rs.shard_rows;
           const int tile_in = ((m0 % p.rs.shard_rows) / kBM) * p.rs.tiles_n + n0 / BN;
-          m.fence_sys();
           uint32_t* f = reinterpret_cast<uint32_t*>(p.rs.peer_base[owner] + p.rs.gflag_off) +
                         p.rs.rank * p.rs.tiles_per_shard + tile_in;
           m.st_release_u32(f, p.rs.seq);
