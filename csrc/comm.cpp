@@ -21,6 +21,7 @@
 #include <vector>
 
 #include "sparknet/collectives.h"
+#include "sparknet/gemm_fused.h"
 #include "sparknet/symm_mem.h"
 
 namespace py = pybind11;
@@ -334,6 +335,31 @@ class Comm {
     }
   }
 
+  // -- fused prefill GEMMs (tcgen05) ----------------------------------------------
+  RegionDesc region() const {
+    if (emulate_) throw std::invalid_argument("the fused GEMMs run on real ranks (one GPU each)");
+    RegionDesc r;
+    memset(&r, 0, sizeof(r));
+    for (int q = 0; q < world_; ++q) r.base[q] = view_.base[q];
+    r.world = world_;
+    r.rank = rank_;
+    r.ctrl_off = L_.ctrl_off;
+    r.gflag_off = L_.gflag_off;
+    r.push_off = L_.push_off;
+    r.push_cap = L_.push_cap;
+    r.status = status_d_;
+    return r;
+  }
+
+  void ag_gemm(const at::Tensor& x_shard, const at::Tensor& w, at::Tensor& out, at::Tensor& err, int copy_ctas,
+               int max_ctas) {
+    tc::ag_gemm(region(), x_shard, w, out, err, copy_ctas, max_ctas);
+  }
+
+  void gemm_rs(const at::Tensor& a, const at::Tensor& w, at::Tensor& out, at::Tensor& err, int max_ctas) {
+    tc::gemm_rs(region(), a, w, out, err, max_ctas);
+  }
+
   // -- health ---------------------------------------------------------------------
   py::dict status(int which) const {
     const Status& s = status_h_[which];
@@ -467,6 +493,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            py::arg("src_peer_stride"), py::arg("dst_peer_stride"), py::arg("total_src_bytes"),
            py::arg("valid_out_bytes"), py::arg("copy_self"), py::arg("threads") = 0, py::arg("max_blocks") = 0)
       .def("barrier", &Comm::barrier, py::arg("blocks") = 1)
+      .def("ag_gemm", &Comm::ag_gemm, py::arg("x_shard"), py::arg("w"), py::arg("out"), py::arg("err"),
+           py::arg("copy_ctas") = 16, py::arg("max_ctas") = 0)
+      .def("gemm_rs", &Comm::gemm_rs, py::arg("a"), py::arg("w"), py::arg("out"), py::arg("err"),
+           py::arg("max_ctas") = 0)
       .def("fused_norm", &Comm::fused_norm, py::arg("ins"), py::arg("residuals"), py::arg("gamma"), py::arg("eps"),
            py::arg("outs"), py::arg("residual_outs"), py::arg("algo"), py::arg("cluster") = 8,
            py::arg("max_clusters") = 0)

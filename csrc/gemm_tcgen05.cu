@@ -1,15 +1,23 @@
 // tcgen05 GEMMs for sm_100a: a plain persistent GEMM and the tensor-parallel prefill
-// kernels that fuse a collective into it:
+// kernels that fuse a collective into it (one launch each):
 //
-//   gemm            C = A B^T
-//   ag_gemm         C = allgather_rows(A_shard) B^T : copy CTAs push this rank's rows
-//                   of A into every peer's symmetric slot and raise a flag per 128-row
-//                   chunk; GEMM CTAs start on their own rows and load a peer's chunk
-//                   (from local memory) once its flag is up.
-//   gemm_rs         C_shard = reduce_scatter_rows(A B^T) : every output tile is sent,
-//                   in bf16, to the rank that owns its rows (P2P stores from the
-//                   epilogue, a flag per tile); each rank then sums the world's
-//                   partials of its rows in fixed rank order (fp32) as they arrive.
+//   gemm      C = A B^T
+//   ag_gemm   C = allgather_rows(A_shard) B^T.  Copy CTAs push this rank's rows of A,
+//             128-row chunk by chunk, into slot [parity][rank] of every peer's
+//             symmetric region and raise a flag per chunk; GEMM CTAs start on their
+//             own rows (read in place) and TMA-load a peer's chunk from this GPU's
+//             own slot once its flag is up.  Chunk-major tile order: chunk c of every
+//             shard is computed while chunk c+1 is in flight.
+//   gemm_rs   C_shard = reduce_scatter_rows(A B^T).  Output row blocks are computed
+//             in owner-interleaved order; the epilogue stores each bf16 tile straight
+//             into slot [parity][rank] of the owner's region (P2P stores) and raises
+//             the owner's flag for that tile; after its last tile each CTA's
+//             epilogue warps sum, tile by tile as flags arrive, the world's partials
+//             of this rank's rows in fixed rank order (fp32), rounding once.
+//
+// A fused launch is a collective: it reads the device-resident epoch at entry
+// (graph-replayable), its flag waits are bounded and report into the runtime's
+// status record, and its completion advances the epoch.
 //
 // Reference: none (the reference has no GEMM; its prefill collectives go to NCCL).
 #include <ATen/cuda/CUDAContext.h>
@@ -19,10 +27,12 @@
 #include <dlfcn.h>
 #include <torch/extension.h>
 
+#include <algorithm>
 #include <stdexcept>
 #include <string>
 
 #include "sparknet/dev_mem.cuh"
+#include "sparknet/gemm_fused.h"
 #include "sparknet/proto.h"
 #include "sparknet/tc_gemm.cuh"
 
@@ -35,64 +45,45 @@ namespace {
 constexpr int kThreads = 192;   // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int kEpiWarps = 4;
 
-// ---------------------------------------------------------------------------
-// Fusion hooks
-// ---------------------------------------------------------------------------
-struct AgFusion {
-  // Rows of A are grouped in shards of `shard_rows` rows, shard s = rank s's rows.
-  // The own shard is read through `map_local`, the others through `map_gather`
-  // (this rank's symmetric slots), row = s * slot_rows + r.  A chunk of 128 rows of
-  // shard s may be read once gflags[s * chunks_per_shard + chunk] >= seq.
-  int world, rank, shard_rows, slot_rows, chunks_per_shard;
-  const uint32_t* gflags;
-  uint32_t seq;
-};
-
-struct RsFusion {
-  // Output rows are owned in shards of `shard_rows` rows; a tile of owner c is sent
-  // to peers[c] + slot_off(parity, this rank) and flagged at
-  // peer_flags[c] + this_rank * tiles_per_shard + tile_in_shard.
-  int world, rank, shard_rows, tiles_per_shard, tiles_n;
-  char* peer_base[kMaxRanks];   // every rank's region (this rank's mapping)
-  uint64_t slot_off[kMaxRanks]; // offset of slot [parity][src] for src = 0..W-1
-  uint64_t gflag_off;
-  uint32_t seq;
-  int ldp;                       // elements per row of a partial slot (= N)
-};
-
 struct GemmParams {
   int M, N, K;
-  __nv_bfloat16* C;
+  __nv_bfloat16* C;  // plain: output; rs: this rank's reduced rows [shard_rows, N]
   int ldc;
   uint32_t* err;
-  int mode;  // 0 plain, 1 ag, 2 rs
-  AgFusion ag;
-  RsFusion rs;
-  // copy role (ag): this rank's shard, pushed to every peer
+  int mode;          // 0 plain, 1 all-gather -> GEMM, 2 GEMM -> reduce-scatter
+  RegionDesc reg;
+  int shard_rows;    // rows per rank (ag: of A; rs: of C)
+  int slot_rows;     // rows per push slot (ag)
+  // ag copy role
   const char* shard;
-  uint64_t shard_bytes;
-  char* peer_slot[kMaxRanks];       // peers' slot [parity][rank] (this rank's data lands there)
-  uint32_t* peer_gflags[kMaxRanks]; // peers' gflags + rank * chunks_per_shard
   int copy_ctas;
-  // completion bookkeeping of the symmetric region (ag / rs)
-  Ctrl* ctrl;
-  Status* status;
 };
 
+struct Seq {
+  uint32_t seq;
+  uint32_t parity;
+};
 
-// Bounded wait on a flag in this GPU's memory written by a peer.
-__device__ __forceinline__ bool wait_flag(const uint32_t* f, uint32_t want, volatile uint32_t* err) {
+__device__ __forceinline__ Ctrl* ctrl_of(const GemmParams& p) {
+  return reinterpret_cast<Ctrl*>(p.reg.base[p.reg.rank] + p.reg.ctrl_off);
+}
+
+__device__ __forceinline__ uint32_t* gflag(const GemmParams& p, int owner, int src, int idx) {
+  return reinterpret_cast<uint32_t*>(p.reg.base[owner] + p.reg.gflag_off) + size_t(src) * kGFlags + idx;
+}
+
+__device__ __forceinline__ char* slot(const GemmParams& p, int owner, uint32_t parity, int src) {
+  return p.reg.base[owner] + p.reg.push_off + (uint64_t(parity) * p.reg.world + src) * p.reg.push_cap;
+}
+
+// Bounded wait on a flag (in this GPU's memory) until it reaches `want`.
+__device__ __forceinline__ bool wait_flag(const uint32_t* f, uint32_t want, const OpCtx& c, uint32_t peer) {
   DevMem m;
-  for (uint32_t i = 0;; ++i) {
-    if (int32_t(m.ld_acquire_u32(f) - want) >= 0) return true;
-    if ((i & 255u) == 255u) {
-      if (*err) return false;
-      if (i > (1u << 26)) {
-        *err = kTcFlagTimeout;
-        return false;
-      }
-    }
+  WaitState w;
+  while (int32_t(m.ld_acquire_u32(f) - want) < 0) {
+    if (!keep_waiting(m, w, c, peer)) return false;
   }
+  return true;
 }
 
 template <int BN, int STAGES>
@@ -110,36 +101,53 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   __shared__ uint32_t err_local;
   __shared__ uint32_t tile_done[2];  // epilogue warps done with the tile in accumulator 0/1
+  __shared__ Seq sq;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile uint32_t* err = &err_local;
+  const bool fused = p.mode != 0;
+  DevMem m;
+
+  if (threadIdx.x == 0) {
+    err_local = 0;
+    tile_done[0] = tile_done[1] = 0;
+    sq.seq = 0;
+    sq.parity = 0;
+    if (fused) {
+      uint32_t epoch, poison;
+      m.ld_volatile_pair(&ctrl_of(p)->epoch, epoch, poison);
+      sq.seq = poison ? 0u : (epoch + 1u ? epoch + 1u : 1u);
+      sq.parity = sq.seq & 1u;
+    }
+  }
+  __syncthreads();
+  if (fused && sq.seq == 0) return;  // poisoned: every CTA leaves at entry
+  const uint32_t seq = sq.seq, parity = sq.parity;
+  const int W = p.reg.world, rank = p.reg.rank;
+  OpCtx octx{fused ? ctrl_of(p) : nullptr, p.reg.status, seq, uint32_t(rank), blockIdx.x,
+             uint32_t(p.mode == 1 ? kOpAgGemm : kOpGemmRs)};
   const int copy_ctas = p.mode == 1 ? p.copy_ctas : 0;
 
   // ---- copy CTAs (all-gather): push this rank's shard to every peer, flag per chunk
   if (int(blockIdx.x) < copy_ctas) {
-    DevMem m;
-    const uint64_t packs = p.shard_bytes / kPack;
-    const uint64_t chunk_packs = packs / p.ag.chunks_per_shard;
-    const int W = p.ag.world, r = p.ag.rank;
-    for (int c = blockIdx.x; c < p.ag.chunks_per_shard; c += copy_ctas) {
+    const int chunks = p.shard_rows / kBM;
+    const uint64_t chunk_packs = uint64_t(kBM) * p.K * 2 / kPack;
+    for (int c = blockIdx.x; c < chunks; c += copy_ctas) {
       const Pack16* src = reinterpret_cast<const Pack16*>(p.shard) + uint64_t(c) * chunk_packs;
       for (uint64_t i = threadIdx.x; i < chunk_packs; i += blockDim.x) {
         Pack16 v = m.ld_input(src + i);
         for (int k = 1; k < W; ++k) {
-          int q = (r + k) % W;
-          m.st_remote(reinterpret_cast<Pack16*>(p.peer_slot[q]) + uint64_t(c) * chunk_packs + i, v);
+          const int q = (rank + k) % W;
+          m.st_remote(reinterpret_cast<Pack16*>(slot(p, q, parity, rank)) + uint64_t(c) * chunk_packs + i, v);
         }
       }
       __syncthreads();
       if (threadIdx.x == 0) {
-        m.fence_sys();
-        for (int k = 1; k < W; ++k) {
-          int q = (r + k) % W;
-          m.st_release_u32(p.peer_gflags[q] + c, p.ag.seq);
-        }
+        for (int k = 1; k < W; ++k) m.st_release_u32(gflag(p, (rank + k) % W, rank, c), seq);
       }
-      __syncthreads();
     }
+    __syncthreads();
+    if (threadIdx.x == 0) finish_op(m, ctrl_of(p), seq, gridDim.x);
     return;
   }
 
@@ -147,24 +155,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tiles_m = (p.M + kBM - 1) / kBM, tiles_n = (p.N + BN - 1) / BN;
   const int tiles = tiles_m * tiles_n;
   const int kblocks = p.K / kBK;
-  // the row-block order: all-gather starts on this rank's own shard, reduce-scatter
-  // sends to the next owners first and finishes with its own rows
+  const int bps = fused ? p.shard_rows / kBM : 1;  // row blocks per shard
+  // Row-block order.  ag: chunk-major over shards starting at this rank (own rows are
+  // ready first, chunk c of all shards before chunk c+1).  rs: owner-interleaved
+  // starting with the next rank, so every link carries traffic all along and each
+  // owner's tiles arrive progressively.
   auto tile_coord = [&](int t, int& m0, int& n0) {
-    int mb = t / tiles_n, nb = t % tiles_n;
-    if (p.mode == 1) {
-      const int per = p.ag.shard_rows / kBM;
-      mb = (mb + p.ag.rank * per) % tiles_m;
-    } else if (p.mode == 2) {
-      const int per = p.rs.shard_rows / kBM;
-      mb = (mb + (p.rs.rank + 1) * per) % tiles_m;
-    }
+    const int i = t / tiles_n, nb = t % tiles_n;
+    int mb = i;
+    if (p.mode == 1) mb = ((rank + i % W) % W) * bps + i / W;
+    else if (p.mode == 2) mb = ((rank + 1 + i % W) % W) * bps + i / W;
     m0 = mb * kBM;
     n0 = nb * BN;
   };
 
   if (threadIdx.x == 0) {
-    err_local = 0;
-    tile_done[0] = tile_done[1] = 0;
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -199,17 +204,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const CUtensorMap* amap = &map_a;
         int arow = m0;
         if (p.mode == 1) {
-          const int shard = m0 / p.ag.shard_rows, r_in = m0 % p.ag.shard_rows;
-          if (shard == p.ag.rank) {
+          const int shard = m0 / p.shard_rows, r_in = m0 % p.shard_rows;
+          if (shard == rank) {
             arow = r_in;
           } else {
-            if (!wait_flag(p.ag.gflags + shard * p.ag.chunks_per_shard + r_in / kBM, p.ag.seq, err)) {
+            if (!wait_flag(gflag(p, rank, shard, r_in / kBM), seq, octx, uint32_t(shard))) {
+              *err = kTcFlagTimeout;
               ok = false;
               break;
             }
-            asm volatile("fence.proxy.async.global;" ::: "memory");  // peer's stores -> TMA reads
+            asm volatile("fence.proxy.async.global;" ::: "memory");  // peer's stores before TMA reads
             amap = &map_a2;
-            arow = shard * p.ag.slot_rows + r_in;
+            arow = int((parity * W + shard) * p.slot_rows) + r_in;
           }
         }
         for (int kb = 0; kb < kblocks; ++kb) {
@@ -269,17 +275,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           acc_phase ^= 1u;
         }
       }
-      // every MMA this thread issued has completed once `drain` fires
-      mma_commit(drain);
+      mma_commit(drain);  // fires once every MMA this thread issued has completed
       mbar_wait(drain, 0, err);
     }
   } else {
     // ---------------- epilogue (warps 2..5) ----------------
-    const int quad = warp & 3;               // TMEM lanes 32*quad .. +31
+    const int quad = warp & 3;  // TMEM lanes 32*quad .. +31
     const int row = quad * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    DevMem m;
     for (int t = cta; t < tiles; t += ncta) {
       int m0, n0;
       tile_coord(t, m0, n0);
@@ -287,13 +291,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int gm = m0 + row;
       const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN);
-      // destination of this row of the tile
+      int owner = 0;
       __nv_bfloat16* dst_row = nullptr;
       if (p.mode == 2) {
-        const int owner = m0 / p.rs.shard_rows;
-        const int r_in = gm - owner * p.rs.shard_rows;
-        char* base = p.rs.peer_base[owner] + p.rs.slot_off[p.rs.rank];
-        dst_row = reinterpret_cast<__nv_bfloat16*>(base) + size_t(r_in) * p.rs.ldp;
+        owner = m0 / p.shard_rows;
+        dst_row = reinterpret_cast<__nv_bfloat16*>(slot(p, owner, parity, rank)) +
+                  size_t(gm - owner * p.shard_rows) * p.N;
       } else if (gm < p.M) {
         dst_row = p.C + size_t(gm) * p.ldc;
       }
@@ -325,23 +328,48 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (p.mode == 2 && lane == 0) {
         // Publish the tile to its owner once all four epilogue warps stored their rows.
         // No CTA barrier (a warp that gave up on a wait must not strand the others):
-        // each warp fences its own stores at system scope, then counts in; the fourth
-        // warp to count in raises the owner's flag.
+        // each warp fences its stores at system scope and counts in; the fourth warp
+        // to count in raises the owner's flag for this tile.
         m.fence_sys();
         uint32_t prev;
         asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
-                     : "=r"(prev) : "r"(smem_u32(&tile_done[acc])) : "memory");
+                     : "=r"(prev)
+                     : "r"(smem_u32(&tile_done[acc]))
+                     : "memory");
         if (prev % kEpiWarps == kEpiWarps - 1) {
-          const int owner = m0 / p.rs.shard_rows;
-          const int tile_in = ((m0 % p.rs.shard_rows) / kBM) * p.rs.tiles_n + n0 / BN;
-          uint32_t* f = reinterpret_cast<uint32_t*>(p.rs.peer_base[owner] + p.rs.gflag_off) +
-                        p.rs.rank * p.rs.tiles_per_shard + tile_in;
-          m.st_release_u32(f, p.rs.seq);
+          const int tile_in = ((m0 - owner * p.shard_rows) / kBM) * tiles_n + n0 / BN;
+          m.st_release_u32(gflag(p, owner, rank, tile_in), seq);
         }
       }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;
+      }
+    }
+    if (p.mode == 2 && !*err) {
+      // ---- reduce this rank's rows: item = (row block, BN columns); warp takes 32 rows
+      const int items = bps * tiles_n;
+      const char* mine = p.reg.base[rank];
+      for (int it = cta; it < items; it += ncta) {
+        bool ok = true;
+        if (lane < W) ok = wait_flag(gflag(p, rank, lane, it), seq, octx, uint32_t(lane));
+        if (!__all_sync(0xffffffffu, ok)) {
+          *err = kTcFlagTimeout;
+          break;
+        }
+        const int r0 = (it / tiles_n) * kBM + quad * 32, c0 = (it % tiles_n) * BN;
+        for (int e = lane; e < 32 * (BN / 8); e += 32) {
+          const int r = r0 + e / (BN / 8), c = c0 + (e % (BN / 8)) * 8;
+          if (r >= p.shard_rows || c >= p.N) continue;
+          Acc a;
+          acc_zero<kBF16>(a);
+          for (int s = 0; s < W; ++s) {
+            const Pack16* src = reinterpret_cast<const Pack16*>(
+                mine + p.reg.push_off + (uint64_t(parity) * W + s) * p.reg.push_cap) + (size_t(r) * p.N + c) / 8;
+            acc_add<kBF16>(a, m.ld_peer_data(src));
+          }
+          m.st_output(reinterpret_cast<Pack16*>(p.C + size_t(r) * p.ldc + c), acc_round<kBF16>(a));
+        }
       }
     }
   }
@@ -351,47 +379,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * BN);
   }
-  if (threadIdx.x == 0 && err_local) atomicExch(p.err, err_local);
-}
-
-// Reduce-scatter finish: sum the world's bf16 partials of this rank's rows in rank
-// order (fp32), round once.  Work items are 128 x 256 tiles of the owned rows; each
-// waits for the W flags of its tile.
-__global__ void __launch_bounds__(256) k_rs_reduce(GemmParams p, __nv_bfloat16* out, int ldo) {
-  DevMem m;
-  const RsFusion& rs = p.rs;
-  const int tiles_n = rs.tiles_n;
-  const int items = rs.tiles_per_shard;
-  __shared__ uint32_t err_local;
-  if (threadIdx.x == 0) err_local = 0;
-  __syncthreads();
-  volatile uint32_t* err = &err_local;
-  char* mine = rs.peer_base[rs.rank];
-  const uint32_t* flags = reinterpret_cast<const uint32_t*>(mine + rs.gflag_off);
-  for (int it = blockIdx.x; it < items; it += gridDim.x) {
-    if (threadIdx.x < uint32_t(rs.world)) {
-      if (!wait_flag(flags + threadIdx.x * rs.tiles_per_shard + it, rs.seq, err)) {
-      }
-    }
-    __syncthreads();
-    if (*err) break;
-    const int r0 = (it / tiles_n) * kBM, c0 = (it % tiles_n) * 256;
-    // 128 rows x 256 cols = 4096 packs of 8 bf16
-    for (int i = threadIdx.x; i < kBM * 32; i += blockDim.x) {
-      const int r = r0 + i / 32, c = c0 + (i % 32) * 8;
-      if (r >= rs.shard_rows || c >= rs.ldp) continue;
-      Acc a;
-      acc_zero<kBF16>(a);
-      for (int s = 0; s < rs.world; ++s) {
-        const Pack16* src =
-            reinterpret_cast<const Pack16*>(mine + rs.slot_off[s]) + (size_t(r) * rs.ldp + c) / 8;
-        acc_add<kBF16>(a, m.ld_peer_data(src));
-      }
-      m.st_output(reinterpret_cast<Pack16*>(out + size_t(r) * ldo + c), acc_round<kBF16>(a));
-    }
-    __syncthreads();
+  if (threadIdx.x == 0) {
+    if (err_local) atomicExch(p.err, err_local);
+    if (fused) finish_op(m, ctrl_of(p), seq, gridDim.x);
   }
-  if (threadIdx.x == 0 && err_local) atomicExch(p.err, err_local);
 }
 
 // ---------------------------------------------------------------------------
@@ -412,8 +403,8 @@ EncodeFn encode_fn() {
   return fn;
 }
 
-// 2-D bf16 map over `rows` x `cols` (row-major, row pitch `ld` elements), box
-// `box_rows` x 64 with 128-byte swizzle.
+// 2-D bf16 map over `rows` x `cols` (row pitch `ld` elements), box `box_rows` x 64,
+// 128-byte swizzle.
 CUtensorMap make_map(const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
   if (reinterpret_cast<uintptr_t>(base) % 16 || (ld * 2) % 16) throw std::invalid_argument("TMA needs 16-byte alignment");
   CUtensorMap map;
@@ -429,8 +420,8 @@ CUtensorMap make_map(const void* base, uint64_t rows, uint64_t cols, uint64_t ld
 }
 
 template <int BN, int STAGES>
-void launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtensorMap& b, const GemmParams& p, int grid,
-                 cudaStream_t s) {
+void launch(const CUtensorMap& a, const CUtensorMap& a2, const CUtensorMap& b, const GemmParams& p, int grid,
+            cudaStream_t s) {
   using S = Smem<BN, STAGES>;
   auto kern = k_gemm<BN, STAGES>;
   static bool attr = false;
@@ -454,6 +445,20 @@ int sm_count(int device) {
   return n;
 }
 
+GemmParams base_params(int M, int N, int K, at::Tensor& C, at::Tensor& err) {
+  GemmParams p;
+  memset(&p, 0, sizeof(p));
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.C = reinterpret_cast<__nv_bfloat16*>(C.data_ptr());
+  p.ldc = int(C.stride(0));
+  p.err = reinterpret_cast<uint32_t*>(err.data_ptr());
+  return p;
+}
+
+}  // namespace
+
 // C[M,N] = A[M,K] B[N,K]^T
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, at::Tensor& err, int bn, int max_ctas) {
   check_mat(A, "A");
@@ -464,41 +469,79 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, at::Tensor& e
   if (K % kBK) throw std::invalid_argument("K must be a multiple of 64");
   if (N % 32) throw std::invalid_argument("N must be a multiple of 32");
   c10::cuda::CUDAGuard guard(A.device());
-  GemmParams p;
-  memset(&p, 0, sizeof(p));
-  p.M = M;
-  p.N = N;
-  p.K = K;
-  p.C = reinterpret_cast<__nv_bfloat16*>(C.data_ptr());
-  p.ldc = int(C.stride(0));
-  p.err = reinterpret_cast<uint32_t*>(err.data_ptr());
-  p.mode = 0;
+  GemmParams p = base_params(M, N, K, C, err);
   CUtensorMap ma = make_map(A.data_ptr(), M, K, A.stride(0), kBM);
   auto s = at::cuda::getCurrentCUDAStream(A.device().index()).stream();
   int sms = max_ctas > 0 ? max_ctas : sm_count(A.device().index());
   if (bn == 128) {
     CUtensorMap mb = make_map(B.data_ptr(), N, K, B.stride(0), 128);
     int tiles = ((M + 127) / 128) * ((N + 127) / 128);
-    launch_gemm<128, 6>(ma, ma, mb, p, std::min(tiles, sms), s);
+    launch<128, 6>(ma, ma, mb, p, std::min(tiles, sms), s);
   } else {
     CUtensorMap mb = make_map(B.data_ptr(), N, K, B.stride(0), 256);
     int tiles = ((M + 127) / 128) * ((N + 255) / 256);
-    launch_gemm<256, 4>(ma, ma, mb, p, std::min(tiles, sms), s);
+    launch<256, 4>(ma, ma, mb, p, std::min(tiles, sms), s);
   }
 }
 
-}  // namespace
+void ag_gemm(const RegionDesc& reg, const at::Tensor& x_shard, const at::Tensor& B, at::Tensor& C, at::Tensor& err,
+             int copy_ctas, int max_ctas) {
+  check_mat(x_shard, "x_shard");
+  check_mat(B, "B");
+  check_mat(C, "C");
+  const int W = reg.world;
+  const int shard_rows = int(x_shard.size(0)), K = int(x_shard.size(1)), N = int(B.size(0));
+  const int M = shard_rows * W;
+  if (!x_shard.is_contiguous() || B.size(1) != K || C.size(0) != M || C.size(1) != N)
+    throw std::invalid_argument("ag_gemm shapes: x_shard [T/W, K], B [N, K], C [T, N]");
+  if (shard_rows % kBM || K % kBK || N % 32) throw std::invalid_argument("ag_gemm needs T/W % 128, K % 64, N % 32");
+  const uint64_t row_bytes = uint64_t(K) * 2;
+  if (reg.push_cap % row_bytes || reg.push_cap / row_bytes < uint64_t(shard_rows))
+    throw std::invalid_argument("the shard does not fit a push slot (raise max_gather_bytes)");
+  if (shard_rows / kBM > kGFlags) throw std::invalid_argument("too many chunks");
+  c10::cuda::CUDAGuard guard(x_shard.device());
+  GemmParams p = base_params(M, N, K, C, err);
+  p.mode = 1;
+  p.reg = reg;
+  p.shard_rows = shard_rows;
+  p.slot_rows = int(reg.push_cap / row_bytes);
+  p.shard = static_cast<const char*>(x_shard.data_ptr());
+  p.copy_ctas = W > 1 ? std::max(1, copy_ctas) : 0;
+  CUtensorMap ma = make_map(x_shard.data_ptr(), shard_rows, K, K, kBM);
+  // every push slot of this rank's region, both parities, as one [2*W*slot_rows, K] matrix
+  CUtensorMap ma2 = make_map(reg.base[reg.rank] + reg.push_off, uint64_t(2) * W * p.slot_rows, K, K, kBM);
+  CUtensorMap mb = make_map(B.data_ptr(), N, K, B.stride(0), 256);
+  auto s = at::cuda::getCurrentCUDAStream(x_shard.device().index()).stream();
+  int sms = max_ctas > 0 ? max_ctas : sm_count(x_shard.device().index());
+  const int tiles = (M / kBM) * ((N + 255) / 256);
+  launch<256, 4>(ma, ma2, mb, p, std::min(tiles, sms - p.copy_ctas) + p.copy_ctas, s);
+}
 
-// -- fused prefill kernels, called by the communicator (comm.cpp) ----------------
-struct PrefillDesc {
-  // region views
-  char* base[kMaxRanks];
-  int world, rank;
-  uint64_t slot_off[2][kMaxRanks];  // push slots: [parity][src]
-  uint64_t gflag_off;
-  uint64_t slot_bytes;
-  Ctrl* ctrl;
-};
+void gemm_rs(const RegionDesc& reg, const at::Tensor& A, const at::Tensor& B, at::Tensor& C_shard, at::Tensor& err,
+             int max_ctas) {
+  check_mat(A, "A");
+  check_mat(B, "B");
+  check_mat(C_shard, "C_shard");
+  const int W = reg.world;
+  const int M = int(A.size(0)), K = int(A.size(1)), N = int(B.size(0));
+  if (B.size(1) != K || M % W || C_shard.size(0) != M / W || C_shard.size(1) != N)
+    throw std::invalid_argument("gemm_rs shapes: A [T, K], B [N, K], C_shard [T/W, N]");
+  const int shard_rows = M / W;
+  if (shard_rows % kBM || K % kBK || N % 256) throw std::invalid_argument("gemm_rs needs T/W % 128, K % 64, N % 256");
+  if (uint64_t(shard_rows) * N * 2 > reg.push_cap) throw std::invalid_argument("the partial does not fit a push slot");
+  if ((shard_rows / kBM) * (N / 256) > kGFlags) throw std::invalid_argument("too many tiles per shard");
+  c10::cuda::CUDAGuard guard(A.device());
+  GemmParams p = base_params(M, N, K, C_shard, err);
+  p.mode = 2;
+  p.reg = reg;
+  p.shard_rows = shard_rows;
+  CUtensorMap ma = make_map(A.data_ptr(), M, K, A.stride(0), kBM);
+  CUtensorMap mb = make_map(B.data_ptr(), N, K, B.stride(0), 256);
+  auto s = at::cuda::getCurrentCUDAStream(A.device().index()).stream();
+  int sms = max_ctas > 0 ? max_ctas : sm_count(A.device().index());
+  const int tiles = (M / kBM) * (N / 256);
+  launch<256, 4>(ma, ma, mb, p, std::min(tiles, sms), s);
+}
 
 }  // namespace tc
 }  // namespace sn

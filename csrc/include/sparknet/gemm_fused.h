@@ -1,0 +1,25 @@
+// Host-side interface of the fused prefill GEMMs (gemm_tcgen05.cu), used by comm.cpp.
+#pragma once
+
+#include <torch/extension.h>
+
+#include "proto.h"
+
+namespace sn {
+
+// What a fused GEMM needs to know about the communicator's symmetric region.
+struct RegionDesc {
+  char* base[kMaxRanks];   // this rank's mapping of every rank's region
+  int world, rank;
+  uint64_t ctrl_off, gflag_off, push_off, push_cap;
+  Status* status;          // device pointer of the pinned status record
+};
+
+namespace tc {
+void ag_gemm(const RegionDesc& reg, const at::Tensor& x_shard, const at::Tensor& B, at::Tensor& C, at::Tensor& err,
+             int copy_ctas, int max_ctas);
+void gemm_rs(const RegionDesc& reg, const at::Tensor& A, const at::Tensor& B, at::Tensor& C_shard, at::Tensor& err,
+             int max_ctas);
+}  // namespace tc
+
+}  // namespace sn

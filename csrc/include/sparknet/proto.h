@@ -31,10 +31,11 @@ namespace sn {
 // ---------------------------------------------------------------------------
 // Limits and ABI
 // ---------------------------------------------------------------------------
-constexpr int kAbiVersion = 3;       // bumped when Layout/Ctrl/Status change
+constexpr int kAbiVersion = 4;       // bumped when Layout/Ctrl/Status change
 constexpr int kMaxRanks = 8;         // one NVSwitch box
 constexpr int kMaxBlocks = 256;      // per launch (grid.x)
 constexpr int kPack = 16;            // bytes moved per vector access
+constexpr int kGFlags = 4096;        // per-source chunk/tile flags of the fused GEMMs
 constexpr size_t kPage = 4096;
 constexpr uint32_t kSentinel = 0xFFFFFFFFu;  // "not yet written" in Lamport slots
 
@@ -79,13 +80,14 @@ struct Status {
 
 enum OpCode : int {
   kOpAllReduce = 1, kOpAllGather = 2, kOpReduceScatter = 3, kOpExchange = 4,
-  kOpBarrier = 5, kOpFusedNorm = 6
+  kOpBarrier = 5, kOpFusedNorm = 6, kOpAgGemm = 7, kOpGemmRs = 8
 };
 
 // ---------------------------------------------------------------------------
 // Region layout.  Every rank maps every peer's region at the same offsets.
 //   ctrl    : Ctrl (local use)
 //   flags   : u32 [kMaxBlocks][kMaxRanks]   per-block barrier flags written by peers
+//   gflags  : u32 [kMaxRanks][kGFlags]      chunk/tile flags of the fused GEMMs, by source
 //   lamport : 2 parities x W sources x lam_cap     (Lamport slots, all-ones when free)
 //   ll      : 2 parities x W sources x 2*ll_cap    (8-byte data+flag units)
 //   push    : 2 parities x W sources x push_cap    (flagged bulk slots)
@@ -93,7 +95,7 @@ enum OpCode : int {
 struct Layout {
   uint32_t world;
   uint64_t lam_cap, ll_cap, push_cap;
-  uint64_t ctrl_off, flag_off, lam_off, ll_off, push_off, total;
+  uint64_t ctrl_off, flag_off, gflag_off, lam_off, ll_off, push_off, total;
 
   SN_HD static Layout make(uint32_t world, uint64_t lam_cap, uint64_t ll_cap, uint64_t push_cap) {
     Layout l;
@@ -103,7 +105,8 @@ struct Layout {
     l.push_cap = align_up(push_cap, kPage);
     l.ctrl_off = 0;
     l.flag_off = kPage * 3;
-    l.lam_off = align_up(l.flag_off + sizeof(uint32_t) * kMaxBlocks * kMaxRanks, kPage);
+    l.gflag_off = align_up(l.flag_off + sizeof(uint32_t) * kMaxBlocks * kMaxRanks, kPage);
+    l.lam_off = align_up(l.gflag_off + sizeof(uint32_t) * kMaxRanks * kGFlags, kPage);
     l.ll_off = l.lam_off + 2ull * world * l.lam_cap;
     l.push_off = l.ll_off + 2ull * world * 2ull * l.ll_cap;
     l.total = l.push_off + 2ull * world * l.push_cap;

@@ -487,6 +487,56 @@ class NvlinkAllReduce:
             self.check_health()
         return out, residual_out
 
+    # -- fused prefill GEMMs (tcgen05) -------------------------------------------------------
+    def _gemm_err(self) -> torch.Tensor:
+        if getattr(self, "_gemm_err_word", None) is None:
+            self._gemm_err_word = torch.zeros(1, dtype=torch.int32, device=self.device)
+        return self._gemm_err_word
+
+    def ag_gemm(self, x_shard: torch.Tensor, w: torch.Tensor, *, out: Optional[torch.Tensor] = None,
+                copy_ctas: int = 16) -> torch.Tensor:
+        """``all_gather(x_shard, dim=0) @ w.T`` in one kernel (sequence-parallel prefill).
+
+        ``x_shard`` is this rank's ``[T/W, K]`` rows, ``w`` this rank's ``[N, K]``
+        column shard (K-major).  Copy CTAs push the shard to every peer chunk by chunk
+        while tcgen05 tiles consume own rows first and peers' rows as they land.
+        """
+        with self._lock:
+            self.check_health()
+            self._live()
+            capturing = torch.cuda.is_current_stream_capturing()
+            with torch.cuda.device(self.device):
+                if out is None:
+                    out = torch.empty((x_shard.shape[0] * self.world_size, w.shape[0]), dtype=x_shard.dtype,
+                                      device=self.device)
+                self._order_stream(capturing)
+                self._comm.ag_gemm(x_shard, w, out, self._gemm_err(), int(copy_ctas), 0)
+                self._mark_stream(capturing)
+        return out
+
+    def gemm_rs(self, a: torch.Tensor, w: torch.Tensor, *, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """``reduce_scatter(a @ w.T, dim=0)`` in one kernel (row-parallel prefill GEMM).
+
+        ``a`` is ``[T, K/W]`` (this rank's slice of the contraction), ``w`` is
+        ``[N, K/W]``; returns this rank's ``[T/W, N]`` rows summed over ranks in fixed
+        rank order from bf16 partials.
+        """
+        with self._lock:
+            self.check_health()
+            self._live()
+            capturing = torch.cuda.is_current_stream_capturing()
+            with torch.cuda.device(self.device):
+                if out is None:
+                    out = torch.empty((a.shape[0] // self.world_size, w.shape[0]), dtype=a.dtype, device=self.device)
+                self._order_stream(capturing)
+                self._comm.gemm_rs(a, w, out, self._gemm_err(), 0)
+                self._mark_stream(capturing)
+        return out
+
+    def gemm_error(self) -> int:
+        """The fused GEMMs' error word (0 = healthy; synchronises)."""
+        return int(self._gemm_err().item())
+
     # -- health ------------------------------------------------------------------------------
     def set_timeout_ms(self, timeout_ms: int) -> None:
         """How long a wait may see nothing from a peer before the collective gives up.
