@@ -45,6 +45,25 @@ SN_DEV void leave(const Job& j, uint32_t seq) {
   }
 }
 
+// Trace stamps: thread 0 of block 0 owns the collective's record (ring of records,
+// indexed by sequence); emulated launches do not trace.
+SN_DEV void trace_begin(const Job& j, OpCtx& c, uint32_t op) {
+  if (!j.trace || blockIdx.x != 0 || threadIdx.x != 0 || gridDim.y != 1) return;
+  DevMem m;
+  uint64_t* rec = j.trace + uint64_t(c.seq % kTraceRecords) * kTraceWords;
+  rec[0] = uint64_t(c.seq) | (uint64_t(op) << 32);
+  rec[1] = j.nbytes;
+  rec[2] = m.now_ns();
+  rec[4 + j.rank] = rec[2];
+  c.trace = rec;
+}
+
+SN_DEV void trace_end(const OpCtx& c) {
+  if (!c.trace) return;
+  DevMem m;
+  c.trace[3] = m.now_ns();
+}
+
 SN_DEV Job emulated(const Job& j0, const EmuViews& e) {
   Job j = j0;
   j.rank = blockIdx.y;
@@ -125,6 +144,7 @@ SN_DEV void allreduce_body(const Job& j, int algo) {
   if (!seq) return;
   DevMem m;
   OpCtx c{ctrl_of(j), j.v.status, seq, j.rank, blockIdx.x, kOpAllReduce};
+  trace_begin(j, c, kOpAllReduce);
   const uint64_t gtid = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const uint64_t gstride = uint64_t(gridDim.x) * blockDim.x;
   if (j.world == 1) {
@@ -138,6 +158,7 @@ SN_DEV void allreduce_body(const Job& j, int algo) {
   } else {
     nvls_allreduce<D>(j, c, gtid, gstride);
   }
+  trace_end(c);
   leave(j, seq);
 }
 

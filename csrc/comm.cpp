@@ -91,6 +91,7 @@ class Comm {
   }
 
   ~Comm() {
+    if (trace_host_) cudaHostUnregister(trace_host_);
     if (emu_blob_) cudaFree(emu_blob_);
     if (status_h_) cudaFreeHost(status_h_);
   }
@@ -139,6 +140,7 @@ class Comm {
     j.nbytes = nbytes;
     j.valid_out_bytes = -1;
     j.skip_rank = skip_rank_;
+    j.trace = trace_d_;
     return j;
   }
 
@@ -408,6 +410,26 @@ class Comm {
     return d;
   }
 
+  // Trace file: pin the host mapping [addr, addr + bytes) and stamp collectives into
+  // its records (after a header of kTraceHeaderBytes).  addr 0 turns tracing off.
+  void set_trace(uint64_t addr, uint64_t bytes) {
+    if (trace_host_) {
+      cudaHostUnregister(trace_host_);
+      trace_host_ = nullptr;
+      trace_d_ = nullptr;
+    }
+    if (!addr) return;
+    if (bytes < kTraceHeaderBytes + uint64_t(kTraceRecords) * kTraceWords * 8)
+      throw std::invalid_argument("trace mapping too small");
+    c10::cuda::CUDAGuard guard(device_);
+    void* h = reinterpret_cast<void*>(addr);
+    ck_rt(cudaHostRegister(h, bytes, cudaHostRegisterMapped | cudaHostRegisterPortable), "cudaHostRegister(trace)");
+    void* d = nullptr;
+    ck_rt(cudaHostGetDevicePointer(&d, h, 0), "cudaHostGetDevicePointer(trace)");
+    trace_host_ = h;
+    trace_d_ = reinterpret_cast<uint64_t*>(static_cast<char*>(d) + kTraceHeaderBytes);
+  }
+
   // Test hook: in an emulated group, rank `r` skips every following launch (-1: none).
   void set_skip_rank(int r) {
     if (!emulate_ && r >= 0) throw std::invalid_argument("skip_rank is a test hook of emulated groups");
@@ -431,6 +453,8 @@ class Comm {
   Status* status_h_ = nullptr;
   Status* status_d_ = nullptr;
   int skip_rank_ = -1;
+  void* trace_host_ = nullptr;
+  uint64_t* trace_d_ = nullptr;
 };
 
 uint64_t layout_total(int world, uint64_t lam_cap, uint64_t ll_cap, uint64_t push_cap) {
@@ -449,6 +473,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.attr("ABI_VERSION") = kAbiVersion;
   m.attr("MAX_RANKS") = kMaxRanks;
   m.attr("MAX_BLOCKS") = kMaxBlocks;
+  m.attr("TRACE_WORDS") = kTraceWords;
+  m.attr("TRACE_RECORDS") = kTraceRecords;
+  m.attr("TRACE_HEADER_BYTES") = kTraceHeaderBytes;
   m.def("layout_total", &layout_total);
   m.def("fd_listen", &fd_listen);
   m.def("fd_serve", &fd_serve, py::call_guard<py::gil_scoped_release>());
@@ -504,6 +531,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("failed_seq", &Comm::failed_seq, py::arg("which") = 0)
       .def("set_timeout_us", &Comm::set_timeout_us)
       .def("set_skip_rank", &Comm::set_skip_rank)
+      .def("set_trace", &Comm::set_trace)
       .def("status_address", &Comm::status_address)
       .def("ctrl", &Comm::ctrl, py::arg("which") = 0)
       .def("layout", &Comm::layout)

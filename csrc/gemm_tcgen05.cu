@@ -44,6 +44,7 @@ namespace {
 
 constexpr int kThreads = 192;   // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int kEpiWarps = 4;
+constexpr int kGroupM = 16;     // row blocks per rasterisation band
 
 struct GemmParams {
   int M, N, K;
@@ -156,12 +157,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tiles = tiles_m * tiles_n;
   const int kblocks = p.K / kBK;
   const int bps = fused ? p.shard_rows / kBM : 1;  // row blocks per shard
-  // Row-block order.  ag: chunk-major over shards starting at this rank (own rows are
-  // ready first, chunk c of all shards before chunk c+1).  rs: owner-interleaved
-  // starting with the next rank, so every link carries traffic all along and each
-  // owner's tiles arrive progressively.
+  // Tile order.  Tiles go in bands of kGroupM row blocks; inside a band the row block
+  // varies fastest, so the ~148 tiles in flight cover a compact 16 x 9 block whose A
+  // and B tiles stay in L2 (raster along N re-reads all of B for every row block).
+  // Logical row block i maps to a physical one by mode.  ag: chunk-major over shards
+  // starting at this rank (own rows are ready first, chunk c of every shard before
+  // chunk c+1).  rs: owner-interleaved starting with the next rank, so every link
+  // carries traffic all along and each owner's tiles arrive progressively.
   auto tile_coord = [&](int t, int& m0, int& n0) {
-    const int i = t / tiles_n, nb = t % tiles_n;
+    const int band = t / (kGroupM * tiles_n);
+    const int rows_in_band = min(kGroupM, tiles_m - band * kGroupM);
+    const int inner = t - band * kGroupM * tiles_n;
+    const int i = band * kGroupM + inner % rows_in_band, nb = inner / rows_in_band;
     int mb = i;
     if (p.mode == 1) mb = ((rank + i % W) % W) * bps + i / W;
     else if (p.mode == 2) mb = ((rank + 1 + i % W) % W) * bps + i / W;

@@ -327,7 +327,20 @@ struct OpCtx {
   uint32_t rank;
   uint32_t block;
   uint32_t op;
+  uint64_t* trace = nullptr;  // this collective's trace record (thread 0 of block 0 only), or null
 };
+
+// Trace record (u64 words), written by thread 0 of block 0 when tracing is on:
+//   [0] seq | op << 32   [1] bytes   [2] entry ns   [3] exit ns
+//   [4 + s] time pack 0 from source s arrived (this rank's own entry for s == rank)
+constexpr int kTraceWords = 32;
+constexpr int kTraceRecords = 65536;
+constexpr int kTraceHeaderBytes = 4096;
+
+template <class M>
+SN_HD void trace_arrival(M& m, const OpCtx& c, uint64_t gtid, uint64_t i, uint32_t s) {
+  if (c.trace && gtid == 0 && i == 0) c.trace[4 + s] = m.now_ns();
+}
 
 // Records the failure once per rank (first writer wins) and poisons the rank.
 template <class M>
@@ -400,6 +413,8 @@ struct Job {
   // Test hook (emulated groups only): this rank's blocks return at entry, as if
   // the rank never launched the collective.  -1 = none.
   int32_t skip_rank;
+  // Trace ring (device pointer of the pinned trace file's records), or null.
+  uint64_t* trace;
 };
 
 // Index helpers --------------------------------------------------------------
@@ -448,6 +463,7 @@ SN_HD bool oneshot_allreduce(M& m, const Job& j, const OpCtx& c, uint64_t gtid, 
           if (pack_arrived<D>(x)) break;
           if (!keep_waiting(m, w, c, s)) return false;
         }
+        trace_arrival(m, c, gtid, i, s);
         m.st_local(slot, pack_fill(kSentinel));
       }
       acc_add<D>(a, x);

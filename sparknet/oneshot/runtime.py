@@ -44,7 +44,7 @@ import torch.distributed as dist
 from .. import _native
 from ..policy import CollectivePolicy
 from ..policy.policy import DEFAULT_ONESHOT_MAX, ENV_ALGO, ENV_CROSSOVER, ENV_NVLS, PACK_BYTES
-from . import symm
+from . import symm, trace
 from ._freeze import raise_if_kernel_resolution_frozen
 
 logger = logging.getLogger(__name__)
@@ -175,6 +175,7 @@ class NvlinkAllReduce:
         blocks: int = DEFAULT_BLOCKS,
         policy: Optional[CollectivePolicy] = None,
         enable_multicast: Optional[bool] = None,
+        transport=None,
     ) -> None:
         self.device = normalize_device(device)
         self.rank = dist.get_rank(group=exchange_group)
@@ -183,7 +184,9 @@ class NvlinkAllReduce:
         self._closed = False
         self._lock = threading.RLock()
         self._comm = None
-        self._regions = None
+        self._transport = None
+        self._mc = (0, 0, 0)
+        self._trace_map = None
         self._align_buffers: Optional[tuple[torch.Tensor, torch.Tensor]] = None
         self._gather_buffers: Optional[tuple[torch.Tensor, torch.Tensor]] = None
         self._prepared: set[torch.dtype] = set()
@@ -257,12 +260,18 @@ class NvlinkAllReduce:
             if differing:
                 raise RuntimeError("NVLink runtime setup failed: configuration differs from rank 0: "
                                    + "; ".join(differing))
-            self._regions = symm.build_regions(C, group=exchange_group, device_index=self.device.index,
-                                               region_bytes=region_bytes, multicast_bytes=mc_bytes)
+            from ..transport import Geometry, NvlinkP2PTransport, NvlsTransport
+
+            geometry = Geometry(self.world_size, self.rank, self.device.index, region_bytes, mc_bytes)
+            factory = transport or (NvlsTransport if mc_bytes else NvlinkP2PTransport)
+            self._transport = factory(geometry)
+            self._transport.connect(exchange_group)
+            self._transport.start()
+            mc = self._transport.multicast()
+            self._mc = mc or (0, 0, 0)
             try:
                 self._comm = C.Comm(self.rank, self.world_size, self.device.index, *self._caps,
-                                    self._regions.bases, self._regions.mc_ptr, self._regions.mc_uc_ptr,
-                                    self._regions.mc_bytes, False)
+                                    self._transport.bases(), self._mc[0], self._mc[1], self._mc[2], False)
                 self._comm.init_region()
                 self._comm.set_timeout_us(1000 * self.timeout_ms)
             except Exception as exc:  # noqa: BLE001 - reported collectively
@@ -270,6 +279,14 @@ class NvlinkAllReduce:
             symm.collective_check(error, exchange_group, "NVLink runtime setup")
             dist.barrier(group=exchange_group)  # no peer pushes before every region is initialised
         self._status = _StatusView(self._comm.status_address(), 1)
+        self.trace_path = None
+        self._trace_map = None
+        if trace.enabled():
+            samples = C.clock_probe(self.device.index, 200)
+            self.trace_path, self._trace_map, address = trace.open_trace(rank=self.rank, world=self.world_size,
+                                                                         clock_samples=samples)
+            self._comm.set_trace(address, trace.file_bytes())
+            logger.info("collective trace %s", self.trace_path)
         self.has_multicast = bool(self._comm.has_multicast)
         if self.rank == 0:
             logger.info("NVLink collectives ready: world=%d region=%d MiB multicast=%s max_size=%d",
@@ -284,7 +301,7 @@ class NvlinkAllReduce:
         """Build the runtime collectively over ``exchange_group`` (a CPU/gloo group)."""
         if "kernels" in kwargs:
             raise TypeError("the kernels keyword is not supported: the kernels are compiled ahead of time")
-        known = {k: kwargs[k] for k in ("policy", "enable_multicast") if k in kwargs}
+        known = {k: kwargs[k] for k in ("policy", "enable_multicast", "transport") if k in kwargs}
         capacity = max(int(max_size), int(eager_buffer_bytes or 0))
         return cls(exchange_group=exchange_group, device=device, max_size=capacity,
                    max_gather_bytes=max_gather_bytes, threads=threads, blocks=blocks, **known)
@@ -628,7 +645,7 @@ class NvlinkAllReduce:
                                                 nvls_available=self.has_multicast)
         if algo == "ll" and shard_bytes > self._caps[1]:
             algo = "push"
-        if algo == "nvls" and shard_bytes * self.world_size > self._regions.mc_bytes:
+        if algo == "nvls" and shard_bytes * self.world_size > self._mc[2]:
             algo = "push"
         self._comm.all_gather([src], [dst], shard_bytes, row_bytes, dst_row_stride, dst_src_stride,
                               GATHER_CODES[algo], self._threads, self._blocks)
@@ -954,8 +971,17 @@ class NvlinkAllReduce:
             self._closed = True
             with contextlib.suppress(Exception):
                 torch.cuda.synchronize(self.device)
+            if self._comm is not None and self._trace_map is not None:
+                with contextlib.suppress(Exception):
+                    self._comm.set_trace(0, 0)
+                    self._trace_map.flush()
+                # the file stays in /dev/shm for collection; only the mapping goes
+                self._trace_map = None
             self._comm = None
-            self._regions = None
+            if self._transport is not None:
+                self._transport.stop()
+                self._transport.close()
+                self._transport = None
 
     def __del__(self) -> None:  # pragma: no cover - defensive teardown
         with contextlib.suppress(Exception):

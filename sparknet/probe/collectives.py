@@ -376,7 +376,7 @@ def _operation(comm, runtime, name, arm, local, scattered, nbytes):
             return None
         if arm == "oneshot" and nbytes > runtime._caps[0]:
             return None
-        if arm == "nvls" and (not runtime.has_multicast or nbytes > runtime._regions.mc_bytes):
+        if arm == "nvls" and (not runtime.has_multicast or nbytes > runtime._mc[2]):
             return None
         return lambda: runtime.all_reduce(local, algorithm=arm)
     if name == "all_gather":

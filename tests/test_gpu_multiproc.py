@@ -61,3 +61,9 @@ def test_multiprocess_tp_decode_arms_agree():
 def test_multiprocess_fused_prefill_gemms():
     lines = run_workers(_world(), {"SPARKNET_PREFILL_BENCH": "0"}, script="prefill_worker.py")
     assert len(lines) == _world() and all(l["correct"] and not l["failures"] for l in lines), lines
+
+
+@pytest.mark.skipif(_world() < 2, reason="needs two or more GPUs")
+def test_multiprocess_trace_records_peer_arrivals():
+    lines = run_workers(_world(), {"SPARKNET_TRACE": "1"})
+    assert len(lines) == _world() and all(not l["failures"] and l["trace"]["collectives"] > 10 for l in lines), lines

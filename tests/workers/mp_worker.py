@@ -166,6 +166,14 @@ def main():
     expect(rt.failure() is None, f"health: {rt.failure()}")
     results["checks"] += 1
     results["stats"] = {k: v for k, v in rt.stats().items() if k in ("calls", "epoch", "transport")}
+    if rt.trace_path:
+        from sparknet.oneshot import trace
+
+        torch.cuda.synchronize()
+        header, recs = trace.read(rt.trace_path)
+        ph = trace.phases(header, recs)
+        results["trace"] = {"collectives": ph["collectives"], "wait_us": ph.get("wait_us")}
+        expect(ph["collectives"] > 10 and "wait_us" in ph, f"trace recorded {ph}")
     del graph
     results["failures"] = FAILURES
     torch.cuda.synchronize()
