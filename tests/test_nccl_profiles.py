@@ -63,3 +63,14 @@ def test_empty_patch_series(tmp_path):
     assert patchset.series() == [] and patchset.missing() == []
     files = patchset.export(tmp_path)
     assert (tmp_path / "series").read_text() == "" and len(files) == 2
+
+
+def test_recipes_are_current():
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    out = subprocess.run([sys.executable, str(root / "recipes" / "generate.py"), "--check"], capture_output=True,
+                         text=True)
+    assert out.returncode == 0, out.stdout + out.stderr
