@@ -26,15 +26,18 @@
 #include <algorithm>
 #include <stdexcept>
 
+#include "sparknet/attention_kernels.cuh"
+
 namespace py = pybind11;
 
 namespace {
 
-constexpr int kHead = 128;   // head_dim
-constexpr int kTile = 32;    // keys per tile
-constexpr float kLog2e = 1.4426950408889634f;
-
-__device__ __forceinline__ float bf(const __nv_bfloat16 x) { return __bfloat162float(x); }
+using sn::attn::bf;
+using sn::attn::k_decode_attn;
+using sn::attn::k_decode_combine;
+using sn::attn::kHead;
+using sn::attn::kLog2e;
+using sn::attn::kTile;
 
 // ---------------------------------------------------------------------------
 // RoPE + KV cache write.  qkv: [B, (Hq + 2*Hkv) * 128]; cos/sin: [Lmax, 64] fp32;
@@ -67,140 +70,6 @@ __global__ void k_rope_qkv_cache(const __nv_bfloat16* __restrict__ qkv, const fl
   }
   dst[i] = __float2bfloat16_rn(x1);
   dst[i + 64] = __float2bfloat16_rn(x2);
-}
-
-// ---------------------------------------------------------------------------
-// Split-KV decode attention.  grid (B * Hkv, nsplit), block 128 threads.
-// q: [B, Hq, 128] with Hq = G * Hkv; caches [B, Lmax, Hkv, 128]; lengths [B].
-// part_o: [B, Hq, nsplit, 128] fp32 (unnormalised), part_ml: [B, Hq, nsplit, 2] (max, sum),
-// both in log2 units.
-// ---------------------------------------------------------------------------
-template <int G>
-__global__ void __launch_bounds__(128) k_decode_attn(const __nv_bfloat16* __restrict__ q,
-                                                     const __nv_bfloat16* __restrict__ k_cache,
-                                                     const __nv_bfloat16* __restrict__ v_cache,
-                                                     const int* __restrict__ lengths, float* __restrict__ part_o,
-                                                     float* __restrict__ part_ml, int Hkv, int Lmax, int chunk,
-                                                     float scale_log2) {
-  __shared__ float qs[G][kHead];
-  // rows padded by 16 bytes: lane-per-key 16-byte reads hit distinct bank groups
-  __shared__ __align__(16) __nv_bfloat16 tile[kTile][kHead + 8];
-  __shared__ float ps[G][kTile];
-  __shared__ float corr[G];
-  const int b = blockIdx.x / Hkv, h = blockIdx.x % Hkv, s = blockIdx.y, nsplit = gridDim.y;
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const int Hq = G * Hkv;
-  const int len = lengths[b];
-  const int start = s * chunk, end = min(start + chunk, len);
-  for (int i = t; i < G * kHead; i += blockDim.x) {
-    int g = i / kHead, d = i % kHead;
-    qs[g][d] = bf(q[(size_t(b) * Hq + h * G + g) * kHead + d]) * scale_log2;
-  }
-  float m[G], l[G], acc[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m[g] = -INFINITY;
-    l[g] = 0.0f;
-    acc[g] = 0.0f;
-  }
-  const size_t row_stride = size_t(Hkv) * kHead;
-  const __nv_bfloat16* kbase = k_cache + (size_t(b) * Lmax * Hkv + h) * kHead;
-  const __nv_bfloat16* vbase = v_cache + (size_t(b) * Lmax * Hkv + h) * kHead;
-  __syncthreads();
-  for (int k0 = start; k0 < end; k0 += kTile) {
-    const int nk = min(kTile, end - k0);
-    // K tile -> shared (each thread moves 4 x 16 bytes)
-    for (int i = t; i < kTile * (kHead / 8); i += blockDim.x) {
-      int key = i / (kHead / 8), c = i % (kHead / 8);
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (key < nk) v = *reinterpret_cast<const uint4*>(kbase + size_t(k0 + key) * row_stride + c * 8);
-      *reinterpret_cast<uint4*>(&tile[key][c * 8]) = v;
-    }
-    __syncthreads();
-    // scores: thread (warp w, lane = key) computes heads g = w, w + 4, ...
-    for (int g = warp; g < G; g += 4) {
-      float sc = -INFINITY;
-      if (lane < nk) {
-        float dot = 0.0f;
-#pragma unroll
-        for (int c = 0; c < kHead / 8; ++c) {
-          uint4 kv = *reinterpret_cast<const uint4*>(&tile[lane][c * 8]);
-          const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kv);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float2 kf = __bfloat1622float2(k2[e]);
-            dot += qs[g][c * 8 + 2 * e] * kf.x + qs[g][c * 8 + 2 * e + 1] * kf.y;
-          }
-        }
-        sc = dot;
-      }
-      float tmax = sc;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
-      float mnew = fmaxf(m[g], tmax);
-      float p = lane < nk ? exp2f(sc - mnew) : 0.0f;
-      float psum = p;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
-      float c = exp2f(m[g] - mnew);  // m = -inf first: exp2(-inf) = 0
-      l[g] = l[g] * c + psum;
-      m[g] = mnew;
-      ps[g][lane] = p;
-      if (lane == 0) corr[g] = c;
-    }
-    __syncthreads();
-    // V tile -> shared
-    for (int i = t; i < kTile * (kHead / 8); i += blockDim.x) {
-      int key = i / (kHead / 8), c = i % (kHead / 8);
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (key < nk) v = *reinterpret_cast<const uint4*>(vbase + size_t(k0 + key) * row_stride + c * 8);
-      *reinterpret_cast<uint4*>(&tile[key][c * 8]) = v;
-    }
-    __syncthreads();
-    // accumulate: thread t owns dimension d = t for every head of the group
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float a = acc[g] * corr[g];
-      for (int key = 0; key < nk; ++key) a += ps[g][key] * bf(tile[key][t]);
-      acc[g] = a;
-    }
-    __syncthreads();
-  }
-  // m/l live in the warps that own each head; publish them through shared memory
-  __shared__ float mls[G][2];
-  for (int g = warp; g < G; g += 4)
-    if (lane == 0) {
-      mls[g][0] = m[g];
-      mls[g][1] = l[g];
-    }
-  __syncthreads();
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    size_t row = (size_t(b) * Hq + h * G + g) * nsplit + s;
-    part_o[row * kHead + t] = acc[g];
-    if (t == 0) {
-      part_ml[row * 2] = mls[g][0];
-      part_ml[row * 2 + 1] = mls[g][1];
-    }
-  }
-}
-
-// grid B * Hq, block 128: merge the spans of one (sequence, head).
-__global__ void k_decode_combine(const float* __restrict__ part_o, const float* __restrict__ part_ml,
-                                 __nv_bfloat16* __restrict__ out, int nsplit) {
-  const size_t bh = blockIdx.x;
-  const int t = threadIdx.x;
-  float M = -INFINITY;
-  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, part_ml[(bh * nsplit + s) * 2]);
-  float L = 0.0f, o = 0.0f;
-  for (int s = 0; s < nsplit; ++s) {
-    float ms = part_ml[(bh * nsplit + s) * 2], ls = part_ml[(bh * nsplit + s) * 2 + 1];
-    if (ls == 0.0f) continue;
-    float w = exp2f(ms - M);
-    L += ls * w;
-    o += part_o[(bh * nsplit + s) * kHead + t] * w;
-  }
-  out[bh * kHead + t] = __float2bfloat16_rn(L > 0.0f ? o / L : 0.0f);
 }
 
 // ---------------------------------------------------------------------------
@@ -306,11 +175,7 @@ void rope_qkv_cache(const at::Tensor& qkv, const at::Tensor& cos_t, const at::Te
       Hkv, Lmax);
 }
 
-int attn_splits(int B, int Hkv, int max_len, int sms) {
-  int want = std::max(1, (2 * sms + B * Hkv - 1) / (B * Hkv));
-  int max_splits = std::max(1, (max_len + 63) / 64);
-  return std::min(want, max_splits);
-}
+int attn_splits(int B, int Hkv, int max_len, int sms) { return sn::attn::splits(B, Hkv, max_len, sms); }
 
 void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                       const at::Tensor& lengths, at::Tensor& out, at::Tensor& workspace, int max_len, double scale) {
