@@ -94,7 +94,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   using S = Smem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStageBytes);
+  uint8_t* epi_stage = smem + STAGES * S::kStageBytes;  // S::kEpiStageBytes
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + S::kEpiStageBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -298,46 +299,58 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int gm = m0 + row;
       const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * BN);
-      int owner = 0;
-      __nv_bfloat16* dst_row = nullptr;
-      if (p.mode == 2) {
-        owner = m0 / p.shard_rows;
-        dst_row = reinterpret_cast<__nv_bfloat16*>(slot(p, owner, parity, rank)) +
-                  size_t(gm - owner * p.shard_rows) * p.N;
-      } else if (gm < p.M) {
-        dst_row = p.C + size_t(gm) * p.ldc;
-      }
+      const int owner = p.mode == 2 ? m0 / p.shard_rows : 0;
+      (void)gm;
+      // 64 columns at a time: TMEM -> registers (this thread's row) -> staging rows ->
+      // coalesced stores, 8 lanes per 128-byte row segment (4 rows per instruction).
+      uint8_t* wst = epi_stage + (warp - 2) * 32 * S::kStageRowBytes;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        float v[32];
-        tmem_ld32(taddr + uint32_t(c * 32), v);
-        const int gn = n0 + c * 32;
-        if (dst_row != nullptr && gm < p.M && gn < p.N) {
-          uint32_t w[16];
+      for (int c = 0; c < BN / 64; ++c) {
+        float v[64];
+        tmem_ld32(taddr + uint32_t(c * 64), v);
+        tmem_ld32(taddr + uint32_t(c * 64 + 32), v + 32);
+        uint4* my_row = reinterpret_cast<uint4*>(wst + lane * S::kStageRowBytes);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) w[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
-          Pack16* out = reinterpret_cast<Pack16*>(dst_row + gn);
+        for (int q = 0; q < 8; ++q) {
+          uint4 pk;
+          pk.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
+          pk.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
+          pk.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
+          pk.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
+          my_row[q] = pk;
+        }
+        __syncwarp();
+        const int gn = n0 + c * 64 + (lane & 7) * 8;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            Pack16 pk;
-            pk.w[0] = w[4 * q];
-            pk.w[1] = w[4 * q + 1];
-            pk.w[2] = w[4 * q + 2];
-            pk.w[3] = w[4 * q + 3];
-            if (p.mode == 2) m.st_remote(out + q, pk);
-            else m.st_local(out + q, pk);
+        for (int rr = 0; rr < 8; ++rr) {
+          const int r = rr * 4 + (lane >> 3);            // row within this warp's 32
+          const int grow = m0 + quad * 32 + r;
+          const uint4 pk = *reinterpret_cast<const uint4*>(wst + r * S::kStageRowBytes + (lane & 7) * 16);
+          if (grow < p.M && gn < p.N) {
+            Pack16 v16;
+            v16.w[0] = pk.x;
+            v16.w[1] = pk.y;
+            v16.w[2] = pk.z;
+            v16.w[3] = pk.w;
+            if (p.mode == 2) {
+              const int owner_r = grow - owner * p.shard_rows;
+              m.st_remote(reinterpret_cast<Pack16*>(reinterpret_cast<__nv_bfloat16*>(slot(p, owner, parity, rank)) +
+                                                    size_t(owner_r) * p.N + gn), v16);
+            } else {
+              m.st_local(reinterpret_cast<Pack16*>(p.C + size_t(grow) * p.ldc + gn), v16);
+            }
           }
         }
+        __syncwarp();
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      __syncwarp();  // the warp's stores are ordered before lane 0's count below
       if (p.mode == 2 && lane == 0) {
         // Publish the tile to its owner once all four epilogue warps stored their rows.
-        // No CTA barrier (a warp that gave up on a wait must not strand the others):
-        // each warp fences its stores at system scope and counts in; the fourth warp
-        // to count in raises the owner's flag for this tile.
-        m.fence_sys();
+        // Each warp counts in with a CTA-scope release; the fourth raises the owner's
+        // flag with a system-scope release, which is cumulative over the stores the
+        // counts ordered before it.  Counting happens before the accumulator is
+        // released, so no warp can run two tiles ahead and count for the wrong tile.
+        // No CTA barrier: a warp that gave up on a wait cannot strand the others.
         uint32_t prev;
         asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
                      : "=r"(prev)
@@ -348,6 +361,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           m.st_release_u32(gflag(p, owner, rank, tile_in), seq);
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1u;

@@ -657,7 +657,8 @@ SN_HD bool block_barrier_leader(M& m, const Job& j, const OpCtx& c, uint32_t blo
   const uint32_t W = j.world, r = j.rank;
   uint32_t gen = c.ctrl->bar_count[block] + 1u;
   c.ctrl->bar_count[block] = gen;
-  m.fence_sys();
+  // The system-scope release of each flag orders this block's pushes before it (the
+  // caller synchronised the block first; release is cumulative): no separate fence.
   for (uint32_t k = 1; k < W; ++k) {
     uint32_t q = (r + k) % W;
     m.st_release_u32(reinterpret_cast<uint32_t*>(j.v.base[q] + j.L.flag(block, r)), gen);

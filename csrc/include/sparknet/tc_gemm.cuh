@@ -163,7 +163,11 @@ struct Smem {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kBytes = STAGES * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  // epilogue staging: per epilogue warp, 32 rows x 64 bf16 columns, rows padded to
+  // 144 bytes so row-per-thread writes and 16-byte-per-lane reads avoid bank conflicts
+  static constexpr int kStageRowBytes = 144;
+  static constexpr int kEpiStageBytes = 4 * 32 * kStageRowBytes;
+  static constexpr int kBytes = STAGES * kStageBytes + kEpiStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 struct TileCoord {
