@@ -1,0 +1,101 @@
+// Allocation-free decode attention (see sparknet/noalloc.h for who needs it and the
+// contract).  Same kernels as the torch entry point (attention_kernels.cuh); the only
+// difference is where the per-split partials live: a file-scope device array of fixed
+// size instead of a caller- or torch-allocated workspace.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <string>
+
+#include "sparknet/attention_kernels.cuh"
+#include "sparknet/noalloc.h"
+
+namespace {
+
+constexpr size_t kScratchFloats = SPARKNET_NOALLOC_SCRATCH_BYTES / sizeof(float);
+constexpr int kMaxDevices = 64;
+
+// The scratch.  In host code this name is only a host-side stand-in for the symbol:
+// its device address comes from cudaGetSymbolAddress, per device.
+static __device__ __align__(256) float g_attention_scratch[kScratchFloats];
+
+float* g_scratch_ptr[kMaxDevices] = {};
+int g_sms[kMaxDevices] = {};
+thread_local std::string g_error;
+
+int fail(int code, const std::string& what) {
+  g_error = what;
+  return code;
+}
+
+// Once per device, with that device current: the scratch's device address and the SM
+// count used to split sequences.
+int setup(int device, float** scratch, int* sms) {
+  if (device < 0 || device >= kMaxDevices) return fail(1, "device ordinal out of range");
+  if (!g_scratch_ptr[device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_attention_scratch);
+    if (e != cudaSuccess) return fail(3, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    int n = 0;
+    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) return fail(3, std::string("cudaDeviceGetAttribute: ") + cudaGetErrorString(e));
+    g_sms[device] = n;
+    g_scratch_ptr[device] = static_cast<float*>(p);
+  }
+  *scratch = g_scratch_ptr[device];
+  *sms = g_sms[device];
+  return 0;
+}
+
+}  // namespace
+
+extern "C" size_t sparknet_decode_attention_scratch_bytes(int B, int Hq, int Hkv, int max_len) {
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || max_len <= 0 || Hq % Hkv) return 0;
+  // the split count depends on the SM count; 148 SMs on B200 (queried per device at run time)
+  return sn::attn::scratch_floats(B, Hq, Hkv, max_len, 148) * sizeof(float);
+}
+
+extern "C" const char* sparknet_noalloc_last_error(void) { return g_error.c_str(); }
+
+extern "C" int sparknet_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                                 const int32_t* lengths, void* out, int B, int Hq, int Hkv, int Lmax,
+                                                 int max_len, float scale, cudaStream_t stream) {
+  g_error.clear();
+  if (!q || !k_cache || !v_cache || !lengths || !out) return fail(1, "null pointer argument");
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Lmax <= 0 || max_len <= 0 || max_len > Lmax)
+    return fail(1, "sizes must be positive and max_len <= Lmax");
+  if (Hq % Hkv) return fail(1, "query heads must be a multiple of KV heads");
+  const int G = Hq / Hkv;
+  if (G != 1 && G != 2 && G != 4 && G != 8 && G != 16) return fail(1, "unsupported GQA group size");
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return fail(3, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  float* scratch = nullptr;
+  int sms = 0;
+  if (int rc = setup(device, &scratch, &sms)) return rc;
+  const int nsplit = sn::attn::splits(B, Hkv, max_len, sms);
+  const size_t need = size_t(B) * Hq * nsplit * (sn::attn::kHead + 2);
+  if (need > kScratchFloats)
+    return fail(2, "problem needs " + std::to_string(need * sizeof(float)) + " bytes of scratch; the built-in scratch is " +
+                       std::to_string(SPARKNET_NOALLOC_SCRATCH_BYTES) + " bytes (use the allocating entry point)");
+  const int chunk = ((max_len + nsplit - 1) / nsplit + sn::attn::kTile - 1) / sn::attn::kTile * sn::attn::kTile;
+  float* part_o = scratch;
+  float* part_ml = scratch + size_t(B) * Hq * nsplit * sn::attn::kHead;
+  const float scale_log2 = scale * sn::attn::kLog2e;
+  const dim3 grid(B * Hkv, nsplit);
+  const auto* qb = static_cast<const __nv_bfloat16*>(q);
+  const auto* kb = static_cast<const __nv_bfloat16*>(k_cache);
+  const auto* vb = static_cast<const __nv_bfloat16*>(v_cache);
+  switch (G) {
+    case 1: sn::attn::k_decode_attn<1><<<grid, 128, 0, stream>>>(qb, kb, vb, lengths, part_o, part_ml, Hkv, Lmax, chunk, scale_log2); break;
+    case 2: sn::attn::k_decode_attn<2><<<grid, 128, 0, stream>>>(qb, kb, vb, lengths, part_o, part_ml, Hkv, Lmax, chunk, scale_log2); break;
+    case 4: sn::attn::k_decode_attn<4><<<grid, 128, 0, stream>>>(qb, kb, vb, lengths, part_o, part_ml, Hkv, Lmax, chunk, scale_log2); break;
+    case 8: sn::attn::k_decode_attn<8><<<grid, 128, 0, stream>>>(qb, kb, vb, lengths, part_o, part_ml, Hkv, Lmax, chunk, scale_log2); break;
+    default: sn::attn::k_decode_attn<16><<<grid, 128, 0, stream>>>(qb, kb, vb, lengths, part_o, part_ml, Hkv, Lmax, chunk, scale_log2); break;
+  }
+  sn::attn::k_decode_combine<<<B * Hq, sn::attn::kHead, 0, stream>>>(part_o, part_ml,
+                                                                    static_cast<__nv_bfloat16*>(out), nsplit);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(3, std::string("launch: ") + cudaGetErrorString(e));
+  return 0;
+}

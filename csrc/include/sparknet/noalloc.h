@@ -1,0 +1,58 @@
+// Allocation-free C entry point for decode attention.
+//
+// This entry point has no counterpart in the reference (which has no attention or
+// model code at all); it is an addition of this library.
+//
+// Who it is for: callers that cannot allocate device memory at the moment they run
+// attention.  That includes code being recorded into a CUDA graph (cudaMalloc is not
+// allowed while a stream is capturing), inference engines that reserve nearly all of
+// the GPU's memory up front for their own pool (a stray cudaMalloc there can fail or
+// fragment the pool), and plain C/C++ hosts that have no caching allocator and cannot
+// afford cudaMalloc's implicit device synchronisation on a latency-critical path.
+// Such callers pass only their inputs and output; the per-split partial results the
+// kernels need live in a fixed scratch array compiled into the library.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+// Bytes of the library's built-in attention scratch (held by every GPU that loads the
+// library, until the process exits).
+#define SPARKNET_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+// Decode attention, one query token per sequence, head_dim 128, bf16:
+//   q        [B, Hq, 128]            k_cache, v_cache [B, Lmax, Hkv, 128]
+//   lengths  [B] int32 (keys to attend, including the new token)
+//   out      [B, Hq, 128]            (all device pointers)
+//   max_len  upper bound of lengths (decides the split of each sequence)
+//   scale    softmax scale (usually 1/sqrt(128))
+// Returns 0 on success, or a nonzero code with a message from
+// sparknet_noalloc_last_error(): 1 bad argument, 2 problem too large for the built-in
+// scratch, 3 CUDA error.  Launches two kernels on `stream`; allocates nothing.
+//
+// The first call on a device looks up the device address of the scratch array (a
+// CUDA runtime query, done once per device with that device current); make that
+// first call outside any stream capture.  Every call, on every stream, shares the
+// one scratch array, so calls that may overlap on the GPU (different streams, no
+// ordering between them) race and must not be issued.  Each call writes every scratch
+// entry it later reads, so nothing needs clearing between calls.
+__attribute__((visibility("default"))) int sparknet_decode_attention_noalloc(
+    const void* q, const void* k_cache, const void* v_cache, const int32_t* lengths, void* out, int B, int Hq,
+    int Hkv, int Lmax, int max_len, float scale, cudaStream_t stream);
+
+// The message of the last failed call on this host thread ("" after a success).
+__attribute__((visibility("default"))) const char* sparknet_noalloc_last_error(void);
+
+// Bytes of scratch a problem needs (0 if the arguments are invalid); compare with
+// SPARKNET_NOALLOC_SCRATCH_BYTES.
+__attribute__((visibility("default"))) size_t sparknet_decode_attention_scratch_bytes(int B, int Hq, int Hkv,
+                                                                                       int max_len);
+
+#ifdef __cplusplus
+}
+#endif
