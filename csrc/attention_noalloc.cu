@@ -73,29 +73,15 @@ extern "C" int sparknet_decode_attention_noalloc(const void* q, const void* k_ca
   float* scratch = nullptr;
   int sms = 0;
   if (int rc = setup(device, &scratch, &sms)) return rc;
-  const int nsplit = sn::attn::splits(B, Hkv, max_len, sms);
-  const size_t need = size_t(B) * Hq * nsplit * (sn::attn::kHead + 2);
+  if (B * Hkv > sn::attn::kCounterSlots) return fail(1, "too many (sequence, KV head) pairs");
+  const size_t need = sn::attn::scratch_floats(B, Hq, Hkv, max_len, sms);
   if (need > kScratchFloats)
     return fail(2, "problem needs " + std::to_string(need * sizeof(float)) + " bytes of scratch; the built-in scratch is " +
                        std::to_string(SPARKNET_NOALLOC_SCRATCH_BYTES) + " bytes (use the allocating entry point)");
-  const int chunk = ((max_len + nsplit - 1) / nsplit + sn::attn::kTile - 1) / sn::attn::kTile * sn::attn::kTile;
-  float* part_o = scratch;
-  float* part_ml = scratch + size_t(B) * Hq * nsplit * sn::attn::kHead;
-  const float scale_log2 = scale * sn::attn::kLog2e;
-  const dim3 grid(B * Hkv, nsplit);
-  const auto* qb = static_cast<const __nv_bfloat16*>(q);
-  const auto* kb = static_cast<const __nv_bfloat16*>(k_cache);
-  const auto* vb = static_cast<const __nv_bfloat16*>(v_cache);
-  switch (G) {
-    case 1: sn::attn::k_decode_attn<1><<<grid, 128, 0, stream>>>(qb, kb, vb, lengths, part_o, part_ml, Hkv, Lmax, chunk, scale_log2); break;
-    case 2: sn::attn::k_decode_attn<2><<<grid, 128, 0, stream>>>(qb, kb, vb, lengths, part_o, part_ml, Hkv, Lmax, chunk, scale_log2); break;
-    case 4: sn::attn::k_decode_attn<4><<<grid, 128, 0, stream>>>(qb, kb, vb, lengths, part_o, part_ml, Hkv, Lmax, chunk, scale_log2); break;
-    case 8: sn::attn::k_decode_attn<8><<<grid, 128, 0, stream>>>(qb, kb, vb, lengths, part_o, part_ml, Hkv, Lmax, chunk, scale_log2); break;
-    default: sn::attn::k_decode_attn<16><<<grid, 128, 0, stream>>>(qb, kb, vb, lengths, part_o, part_ml, Hkv, Lmax, chunk, scale_log2); break;
-  }
-  sn::attn::k_decode_combine<<<B * Hq, sn::attn::kHead, 0, stream>>>(part_o, part_ml,
-                                                                    static_cast<__nv_bfloat16*>(out), nsplit);
-  e = cudaGetLastError();
+  e = sn::attn::launch_decode_attention(static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k_cache),
+                                        static_cast<const __nv_bfloat16*>(v_cache), lengths,
+                                        static_cast<__nv_bfloat16*>(out), scratch, B, Hq, Hkv, Lmax, max_len, scale, sms,
+                                        stream);
   if (e != cudaSuccess) return fail(3, std::string("launch: ") + cudaGetErrorString(e));
   return 0;
 }

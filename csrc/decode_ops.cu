@@ -33,11 +33,7 @@ namespace py = pybind11;
 namespace {
 
 using sn::attn::bf;
-using sn::attn::k_decode_attn;
-using sn::attn::k_decode_combine;
 using sn::attn::kHead;
-using sn::attn::kLog2e;
-using sn::attn::kTile;
 
 // ---------------------------------------------------------------------------
 // RoPE + KV cache write.  qkv: [B, (Hq + 2*Hkv) * 128]; cos/sin: [Lmax, 64] fp32;
@@ -73,21 +69,41 @@ __global__ void k_rope_qkv_cache(const __nv_bfloat16* __restrict__ qkv, const fl
 }
 
 // ---------------------------------------------------------------------------
-// residual add + RMSNorm.  One block per row; rounds after the add, like the fused
-// all-reduce epilogue.  residual_out may alias residual.
+// residual add + RMSNorm.  One block per row, each thread holding VPT vectors of 8
+// bf16 in registers (every load of the row is in flight at once); rounds after the
+// add, like the fused all-reduce epilogue.  residual_out may alias residual.
 // ---------------------------------------------------------------------------
-__global__ void k_add_rmsnorm(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* residual,
-                              __nv_bfloat16* residual_out, const __nv_bfloat16* __restrict__ gamma,
-                              __nv_bfloat16* __restrict__ out, int H, float eps) {
-  extern __shared__ float rowbuf[];
+template <int VPT>
+__global__ void __launch_bounds__(1024) k_add_rmsnorm(const __nv_bfloat16* __restrict__ x,
+                                                      const __nv_bfloat16* residual, __nv_bfloat16* residual_out,
+                                                      const __nv_bfloat16* __restrict__ gamma,
+                                                      __nv_bfloat16* __restrict__ out, int H, float eps) {
   __shared__ float warp_sums[32];
   const size_t row = blockIdx.x;
+  float v[VPT][8];
   float sq = 0.0f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    float v = bf(x[row * H + i]);
-    if (residual) v = bf(__float2bfloat16_rn(v + bf(residual[row * H + i])));
-    rowbuf[i] = v;
-    sq += v * v;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int i = (j * blockDim.x + threadIdx.x) * 8;
+    if (i < H) {
+      uint4 xv = *reinterpret_cast<const uint4*>(x + row * H + i);
+      uint4 rv = make_uint4(0, 0, 0, 0);
+      if (residual) rv = *reinterpret_cast<const uint4*>(residual + row * H + i);
+      const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xv);
+      const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 a = __bfloat1622float2(x2[e]);
+        if (residual) {
+          float2 r = __bfloat1622float2(r2[e]);
+          a.x = bf(__float2bfloat16_rn(a.x + r.x));
+          a.y = bf(__float2bfloat16_rn(a.y + r.y));
+        }
+        v[j][2 * e] = a.x;
+        v[j][2 * e + 1] = a.y;
+        sq += a.x * a.x + a.y * a.y;
+      }
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
@@ -96,46 +112,89 @@ __global__ void k_add_rmsnorm(const __nv_bfloat16* __restrict__ x, const __nv_bf
   float total = 0.0f;
   for (int w = 0; w < int(blockDim.x + 31) / 32; ++w) total += warp_sums[w];
   const float scale = rsqrtf(total / float(H) + eps);
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    float v = rowbuf[i];
-    if (residual_out) residual_out[row * H + i] = __float2bfloat16_rn(v);
-    out[row * H + i] = __float2bfloat16_rn(v * scale * bf(gamma[i]));
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int i = (j * blockDim.x + threadIdx.x) * 8;
+    if (i < H) {
+      uint4 gv = *reinterpret_cast<const uint4*>(gamma + i);
+      const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv);
+      uint4 ov, rv;
+      uint32_t* o32 = reinterpret_cast<uint32_t*>(&ov);
+      uint32_t* r32 = reinterpret_cast<uint32_t*>(&rv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 g = __bfloat1622float2(g2[e]);
+        __nv_bfloat162 o = __floats2bfloat162_rn(v[j][2 * e] * scale * g.x, v[j][2 * e + 1] * scale * g.y);
+        __nv_bfloat162 r = __floats2bfloat162_rn(v[j][2 * e], v[j][2 * e + 1]);
+        o32[e] = *reinterpret_cast<uint32_t*>(&o);
+        r32[e] = *reinterpret_cast<uint32_t*>(&r);
+      }
+      *reinterpret_cast<uint4*>(out + row * H + i) = ov;
+      if (residual_out) *reinterpret_cast<uint4*>(residual_out + row * H + i) = rv;
+    }
   }
 }
 
-// out[b, i] = silu(gu[b, i]) * gu[b, F + i]
+// out[b, i] = silu(gate_i) * up_i.  block == 0: gu[b] = [gate | up]; block > 0: gu[b]
+// is made of [block gate | block up] column groups (the decode GEMM's SwiGLU layout).
 __global__ void k_silu_mul(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ out, int F,
-                           size_t total) {
+                           size_t total, int block) {
   for (size_t idx = size_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < total; idx += size_t(gridDim.x) * blockDim.x) {
     size_t b = idx / F, i = idx % F;
-    float g = bf(gu[b * 2 * F + i]), u = bf(gu[b * 2 * F + F + i]);
+    size_t gi = block ? (i / block) * 2 * block + i % block : i;
+    size_t ui = block ? gi + block : F + i;
+    float g = bf(gu[b * 2 * F + gi]), u = bf(gu[b * 2 * F + ui]);
     out[idx] = __float2bfloat16_rn(g / (1.0f + expf(-g)) * u);
   }
 }
 
-// (max, argmax) of each row; ties take the lowest index.  One block per row.
-__global__ void k_row_argmax(const __nv_bfloat16* __restrict__ logits, int V, int index_offset,
-                             float* __restrict__ out) {
+// (max, argmax) of each row; ties take the lowest index.  One block of 1024 threads
+// per row; each thread first loads its vectors of 8 (all in flight), then scans them.
+__device__ __forceinline__ void better(float& best, int& bi, float v, int i) {
+  if (v > best || (v == best && i < bi)) {
+    best = v;
+    bi = i;
+  }
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(1024) k_row_argmax(const __nv_bfloat16* __restrict__ logits, int V,
+                                                     int index_offset, float* __restrict__ out) {
   __shared__ float sv[32];
   __shared__ int si[32];
   const size_t row = blockIdx.x;
+  const __nv_bfloat16* base = logits + row * V;
   float best = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    float v = bf(logits[row * V + i]);
-    if (v > best || (v == best && i < bi)) {
-      best = v;
-      bi = i;
+  uint4 vec[VPT];
+  const bool aligned = (reinterpret_cast<uintptr_t>(base) & 15) == 0;
+  const int nvec = aligned ? V / 8 : 0;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int w = j * blockDim.x + threadIdx.x;
+    vec[j] = w < nvec ? *reinterpret_cast<const uint4*>(base + size_t(w) * 8) : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int w = j * blockDim.x + threadIdx.x;
+    if (w < nvec) {
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&vec[j]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) better(best, bi, bf(e[k]), w * 8 + k);
     }
+  }
+  for (int i = nvec * 8 + threadIdx.x; i < V; i += blockDim.x) better(best, bi, bf(base[i]), i);  // tail
+  // rows longer than the vectors held in registers
+  for (int w = VPT * blockDim.x + threadIdx.x; w < nvec; w += blockDim.x) {
+    uint4 q = *reinterpret_cast<const uint4*>(base + size_t(w) * 8);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&q);
+    for (int k = 0; k < 8; ++k) better(best, bi, bf(e[k]), w * 8 + k);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     float ov = __shfl_xor_sync(0xffffffffu, best, o);
     int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > best || (ov == best && oi < bi)) {
-      best = ov;
-      bi = oi;
-    }
+    better(best, bi, ov, oi);
   }
   if ((threadIdx.x & 31) == 0) {
     sv[threadIdx.x >> 5] = best;
@@ -143,11 +202,7 @@ __global__ void k_row_argmax(const __nv_bfloat16* __restrict__ logits, int V, in
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    for (int w = 1; w < int(blockDim.x + 31) / 32; ++w)
-      if (sv[w] > best || (sv[w] == best && si[w] < bi)) {
-        best = sv[w];
-        bi = si[w];
-      }
+    for (int w = 1; w < int(blockDim.x + 31) / 32; ++w) better(best, bi, sv[w], si[w]);
     out[row * 2] = best;
     out[row * 2 + 1] = float(bi + index_offset);
   }
@@ -175,8 +230,8 @@ void rope_qkv_cache(const at::Tensor& qkv, const at::Tensor& cos_t, const at::Te
       Hkv, Lmax);
 }
 
-int attn_splits(int B, int Hkv, int max_len, int sms) { return sn::attn::splits(B, Hkv, max_len, sms); }
-
+// workspace: float32, sn::attn::scratch_floats() long, its first kCounterSlots ints zero
+// before the first call (every completed call leaves them zero).
 void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                       const at::Tensor& lengths, at::Tensor& out, at::Tensor& workspace, int max_len, double scale) {
   check_bf16(q, "q");
@@ -185,73 +240,71 @@ void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::
   if (q.size(2) != kHead) throw std::invalid_argument("head_dim must be 128");
   if (Hq % Hkv) throw std::invalid_argument("query heads must be a multiple of KV heads");
   int G = Hq / Hkv;
+  if (G != 1 && G != 2 && G != 4 && G != 8 && G != 16) throw std::invalid_argument("unsupported GQA group size");
+  if (B * Hkv > sn::attn::kCounterSlots) throw std::invalid_argument("too many (sequence, KV head) pairs");
+  if (max_len > Lmax) throw std::invalid_argument("max_len exceeds the cache length");
   c10::cuda::CUDAGuard guard(q.device());
   int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
-  int nsplit = attn_splits(B, Hkv, max_len, sms);
-  int chunk = ((max_len + nsplit - 1) / nsplit + kTile - 1) / kTile * kTile;
-  size_t need = size_t(B) * Hq * nsplit * (kHead + 2);
-  if (workspace.scalar_type() != at::kFloat || size_t(workspace.numel()) < need)
+  size_t need = sn::attn::scratch_floats(B, Hq, Hkv, max_len, sms);
+  if (workspace.scalar_type() != at::kFloat || !workspace.is_contiguous() || size_t(workspace.numel()) < need)
     throw std::invalid_argument("workspace too small for the attention partials");
-  float* part_o = workspace.data_ptr<float>();
-  float* part_ml = part_o + size_t(B) * Hq * nsplit * kHead;
-  auto st = stream_of(q);
-  float scale_log2 = float(scale) * kLog2e;
-  dim3 grid(B * Hkv, nsplit);
-#define SN_ATT(GG)                                                                                          \
-  case GG:                                                                                                  \
-    k_decode_attn<GG><<<grid, 128, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()),           \
-                                            reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr()),     \
-                                            reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr()),     \
-                                            lengths.data_ptr<int>(), part_o, part_ml, Hkv, Lmax, chunk,     \
-                                            scale_log2);                                                    \
-    break;
-  switch (G) {
-    SN_ATT(1)
-    SN_ATT(2)
-    SN_ATT(4)
-    SN_ATT(8)
-    SN_ATT(16)
-    default:
-      throw std::invalid_argument("unsupported GQA group size");
-  }
-#undef SN_ATT
-  k_decode_combine<<<B * Hq, kHead, 0, st>>>(part_o, part_ml, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
-                                              nsplit);
+  cudaError_t e = sn::attn::launch_decode_attention(
+      reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr()),
+      reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr()), lengths.data_ptr<int>(),
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), workspace.data_ptr<float>(), B, Hq, Hkv, Lmax, max_len,
+      float(scale), sms, stream_of(q));
+  if (e != cudaSuccess) throw std::runtime_error(std::string("decode_attention launch: ") + cudaGetErrorString(e));
 }
 
 size_t attention_workspace_floats(int B, int Hq, int Hkv, int max_len, int sms) {
-  return size_t(B) * Hq * attn_splits(B, Hkv, max_len, sms) * (kHead + 2);
+  return sn::attn::scratch_floats(B, Hq, Hkv, max_len, sms);
 }
 
 void add_rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual,
                  const c10::optional<at::Tensor>& residual_out, const at::Tensor& gamma, at::Tensor& out, double eps) {
   check_bf16(x, "x");
+  check_bf16(out, "out");
+  check_bf16(gamma, "gamma");
+  if (residual) check_bf16(*residual, "residual");
+  if (residual_out) check_bf16(*residual_out, "residual_out");
   int rows = int(x.size(0)), H = int(x.size(1));
+  if (H % 8 || H > 1024 * 8 * 8) throw std::invalid_argument("add_rmsnorm needs H a multiple of 8, at most 65536");
   c10::cuda::CUDAGuard guard(x.device());
-  k_add_rmsnorm<<<rows, 256, H * sizeof(float), stream_of(x)>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
-      residual ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr,
-      residual_out ? reinterpret_cast<__nv_bfloat16*>(residual_out->data_ptr()) : nullptr,
-      reinterpret_cast<const __nv_bfloat16*>(gamma.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), H,
-      float(eps));
+  const int vecs = H / 8;
+  const int threads = std::min(1024, (vecs + 31) / 32 * 32);
+  const int vpt = (vecs + threads - 1) / threads;
+  auto xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  auto rp = residual ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr;
+  auto rop = residual_out ? reinterpret_cast<__nv_bfloat16*>(residual_out->data_ptr()) : nullptr;
+  auto gp = reinterpret_cast<const __nv_bfloat16*>(gamma.data_ptr());
+  auto op = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  auto st = stream_of(x);
+  if (vpt == 1) k_add_rmsnorm<1><<<rows, threads, 0, st>>>(xp, rp, rop, gp, op, H, float(eps));
+  else if (vpt == 2) k_add_rmsnorm<2><<<rows, threads, 0, st>>>(xp, rp, rop, gp, op, H, float(eps));
+  else if (vpt <= 4) k_add_rmsnorm<4><<<rows, threads, 0, st>>>(xp, rp, rop, gp, op, H, float(eps));
+  else k_add_rmsnorm<8><<<rows, threads, 0, st>>>(xp, rp, rop, gp, op, H, float(eps));
 }
 
-void silu_mul(const at::Tensor& gu, at::Tensor& out) {
+void silu_mul(const at::Tensor& gu, at::Tensor& out, int block) {
   check_bf16(gu, "gate_up");
   int F = int(gu.size(1) / 2);
+  if (block < 0 || (block && F % block)) throw std::invalid_argument("silu_mul block must divide the feature count");
   size_t total = size_t(gu.size(0)) * F;
   c10::cuda::CUDAGuard guard(gu.device());
   int blocks = int(std::min<size_t>((total + 255) / 256, 148 * 8));
   k_silu_mul<<<blocks, 256, 0, stream_of(gu)>>>(reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()),
-                                                 reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), F, total);
+                                                 reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), F, total, block);
 }
 
 void row_argmax(const at::Tensor& logits, int index_offset, at::Tensor& out) {
   check_bf16(logits, "logits");
   c10::cuda::CUDAGuard guard(logits.device());
-  k_row_argmax<<<int(logits.size(0)), 512, 0, stream_of(logits)>>>(
-      reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), int(logits.size(1)), index_offset,
-      out.data_ptr<float>());
+  const int V = int(logits.size(1));
+  auto lp = reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr());
+  auto st = stream_of(logits);
+  const int rows = int(logits.size(0));
+  if (V <= 1024 * 8 * 2) k_row_argmax<2><<<rows, 1024, 0, st>>>(lp, V, index_offset, out.data_ptr<float>());
+  else k_row_argmax<4><<<rows, 1024, 0, st>>>(lp, V, index_offset, out.data_ptr<float>());
 }
 
 }  // namespace
@@ -262,6 +315,6 @@ void register_decode(py::module_& m) {
   m.def("attention_workspace_floats", &attention_workspace_floats);
   m.def("add_rmsnorm", &add_rmsnorm, py::arg("x"), py::arg("residual"), py::arg("residual_out"), py::arg("gamma"),
         py::arg("out"), py::arg("eps"));
-  m.def("silu_mul", &silu_mul);
+  m.def("silu_mul", &silu_mul, py::arg("gate_up"), py::arg("out"), py::arg("block") = 0);
   m.def("row_argmax", &row_argmax);
 }

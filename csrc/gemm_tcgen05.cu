@@ -40,6 +40,40 @@ namespace py = pybind11;
 
 namespace sn {
 namespace tc {
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void* lib = dlopen("libcuda.so.1", RTLD_NOW | RTLD_GLOBAL);
+    if (!lib) throw std::runtime_error("libcuda.so.1 not found");
+    fn = reinterpret_cast<EncodeFn>(dlsym(lib, "cuTensorMapEncodeTiled"));
+    if (!fn) throw std::runtime_error("cuTensorMapEncodeTiled not found");
+  }
+  return fn;
+}
+
+CUtensorMap make_map(const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows, int elem_bytes) {
+  if (elem_bytes != 1 && elem_bytes != 2) throw std::invalid_argument("TMA maps are over 1- or 2-byte elements");
+  if (reinterpret_cast<uintptr_t>(base) % 16 || (ld * elem_bytes) % 16)
+    throw std::invalid_argument("TMA needs 16-byte alignment");
+  if (box_rows < 1 || box_rows > 256) throw std::invalid_argument("TMA box rows must be 1..256");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * elem_bytes};
+  cuuint32_t box[2] = {uint32_t(128 / elem_bytes), box_rows};  // 128 bytes: one swizzle row
+  cuuint32_t elem[2] = {1, 1};
+  CUresult r = encode_fn()(&map, elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                           const_cast<void*>(base), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
+  return map;
+}
+
 namespace {
 
 constexpr int kThreads = 192;   // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
@@ -58,6 +92,10 @@ struct GemmParams {
   // ag copy role
   const char* shard;
   int copy_ctas;
+  // fp8: UE8M0 scale chunks (512 bytes per 128 rows and 128 K), laid out [row block][K block]
+  const uint8_t* sfa;       // A's (ag: this rank's shard's)
+  const uint8_t* sfb;
+  uint64_t sfa_slot_off;    // ag: byte offset of the pushed shard's scales inside a push slot
 };
 
 struct Seq {
@@ -87,14 +125,22 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* f, uint32_t want, cons
   return true;
 }
 
-template <int BN, int STAGES>
+// F8: A and B are e4m3 with UE8M0 block scales (kind::mxf8f6f4.block_scale); one K
+// block is 128 elements instead of 64, the tiles have the same bytes.
+template <int BN, int STAGES, bool F8>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a2,
            const __grid_constant__ CUtensorMap map_b, GemmParams p) {
-  using S = Smem<BN, STAGES>;
+  using S = Smem<BN, STAGES, F8>;
+  constexpr int kBKe = F8 ? 128 : kBK;          // K elements per stage
+  constexpr int kEsz = F8 ? 1 : 2;              // bytes per element
+  constexpr uint32_t kTmemCols = F8 ? 512u : uint32_t(2 * BN);
+  constexpr uint32_t kSfaCol = 2 * BN, kSfbCol = 2 * BN + 4;  // fp8 scale columns after the accumulators
+  static_assert(!F8 || 2 * BN + 4 + BN / 32 <= 512, "accumulators and scale columns must fit TMEM");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* epi_stage = smem + STAGES * S::kStageBytes;  // S::kEpiStageBytes
+  uint8_t* sf_smem = smem + STAGES * S::kStageBytes;             // STAGES x S::kSfBytes
+  uint8_t* epi_stage = sf_smem + STAGES * S::kSfBytes;           // S::kEpiStageBytes
   uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + S::kEpiStageBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
@@ -133,7 +179,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---- copy CTAs (all-gather): push this rank's shard to every peer, flag per chunk
   if (int(blockIdx.x) < copy_ctas) {
     const int chunks = p.shard_rows / kBM;
-    const uint64_t chunk_packs = uint64_t(kBM) * p.K * 2 / kPack;
+    const uint64_t chunk_packs = uint64_t(kBM) * p.K * kEsz / kPack;
+    const uint64_t sf_packs = F8 ? uint64_t(p.K / kBKe) * 512 / kPack : 0;  // the chunk's scales
     for (int c = blockIdx.x; c < chunks; c += copy_ctas) {
       const Pack16* src = reinterpret_cast<const Pack16*>(p.shard) + uint64_t(c) * chunk_packs;
       for (uint64_t i = threadIdx.x; i < chunk_packs; i += blockDim.x) {
@@ -141,6 +188,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = 1; k < W; ++k) {
           const int q = (rank + k) % W;
           m.st_remote(reinterpret_cast<Pack16*>(slot(p, q, parity, rank)) + uint64_t(c) * chunk_packs + i, v);
+        }
+      }
+      if (F8) {
+        const Pack16* ssrc = reinterpret_cast<const Pack16*>(p.sfa) + uint64_t(c) * sf_packs;
+        for (uint64_t i = threadIdx.x; i < sf_packs; i += blockDim.x) {
+          Pack16 v = m.ld_input(ssrc + i);
+          for (int k = 1; k < W; ++k) {
+            const int q = (rank + k) % W;
+            m.st_remote(reinterpret_cast<Pack16*>(slot(p, q, parity, rank) + p.sfa_slot_off) +
+                            uint64_t(c) * sf_packs + i, v);
+          }
         }
       }
       __syncthreads();
@@ -156,7 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int cta = blockIdx.x - copy_ctas, ncta = gridDim.x - copy_ctas;
   const int tiles_m = (p.M + kBM - 1) / kBM, tiles_n = (p.N + BN - 1) / BN;
   const int tiles = tiles_m * tiles_n;
-  const int kblocks = p.K / kBK;
+  const int kblocks = p.K / kBKe;
   const int bps = fused ? p.shard_rows / kBM : 1;  // row blocks per shard
   // Tile order.  Tiles go in bands of kGroupM row blocks; inside a band the row block
   // varies fastest, so the ~148 tiles in flight cover a compact 16 x 9 block whose A
@@ -189,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(drain, 1);
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&map_a);
     prefetch_tmap(&map_b);
@@ -211,10 +269,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         tile_coord(t, m0, n0);
         const CUtensorMap* amap = &map_a;
         int arow = m0;
+        const uint8_t* sfa_src = F8 ? p.sfa + size_t(m0 / kBM) * kblocks * 512 : nullptr;
         if (p.mode == 1) {
           const int shard = m0 / p.shard_rows, r_in = m0 % p.shard_rows;
           if (shard == rank) {
             arow = r_in;
+            if (F8) sfa_src = p.sfa + size_t(r_in / kBM) * kblocks * 512;
           } else {
             if (!wait_flag(gflag(p, rank, shard, r_in / kBM), seq, octx, uint32_t(shard))) {
               *err = kTcFlagTimeout;
@@ -224,6 +284,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             asm volatile("fence.proxy.async.global;" ::: "memory");  // peer's stores before TMA reads
             amap = &map_a2;
             arow = int((parity * W + shard) * p.slot_rows) + r_in;
+            if (F8)
+              sfa_src = reinterpret_cast<const uint8_t*>(slot(p, rank, parity, shard) + p.sfa_slot_off) +
+                        size_t(r_in / kBM) * kblocks * 512;
           }
         }
         for (int kb = 0; kb < kblocks; ++kb) {
@@ -233,9 +296,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
-          mbar_expect_tx(&full[stage], S::kStageBytes);
-          tma_load_2d(sa, amap, kb * kBK, arow, &full[stage]);
-          tma_load_2d(sb, &map_b, kb * kBK, n0, &full[stage]);
+          mbar_expect_tx(&full[stage], S::kStageBytes + S::kSfBytes);
+          tma_load_2d(sa, amap, kb * kBKe, arow, &full[stage]);
+          tma_load_2d(sb, &map_b, kb * kBKe, n0, &full[stage]);
+          if (F8) {
+            uint8_t* sfs = sf_smem + stage * S::kSfBytes;
+            bulk_load(sfs, sfa_src + size_t(kb) * 512, 512, &full[stage]);
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j)
+              bulk_load(sfs + 512 * (1 + j), p.sfb + (size_t(n0 / 128 + j) * kblocks + kb) * 512, 512, &full[stage]);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -246,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16(BN);
+      const uint32_t idesc = F8 ? idesc_mxf8(BN) : idesc_bf16(BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -265,10 +335,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
           const uint64_t adesc = smem_desc_sw128(sa), bdesc = smem_desc_sw128(sb);
+          if (F8) {
+            // scales of this K block -> TMEM (ordered before the MMAs below by the
+            // tcgen05 pipeline of this thread), then four K=32 steps
+            uint8_t* sfs = sf_smem + stage * S::kSfBytes;
+            tmem_cp_sf(tmem_base + kSfaCol, smem_desc_sf(sfs));
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            // +32 bytes per 16-element K step inside the 128-byte swizzle atom
-            mma_bf16(d, adesc + uint64_t(2 * k), bdesc + uint64_t(2 * k), idesc, (kb | k) ? 1u : 0u);
+            for (int j = 0; j < BN / 128; ++j) tmem_cp_sf(tmem_base + kSfbCol + 4 * j, smem_desc_sf(sfs + 512 * (1 + j)));
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_mxf8(d, adesc + uint64_t(2 * k), bdesc + uint64_t(2 * k), idesc, tmem_base + kSfaCol,
+                       tmem_base + kSfbCol, uint32_t(k), (kb | k) ? 1u : 0u);
+          } else {
+#pragma unroll
+            for (int k = 0; k < kBK / 16; ++k) {
+              // +32 bytes per 16-element K step inside the 128-byte swizzle atom
+              mma_bf16(d, adesc + uint64_t(2 * k), bdesc + uint64_t(2 * k), idesc, (kb | k) ? 1u : 0u);
+            }
           }
           mma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -400,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 2 * BN);
+    tmem_dealloc(tmem_base, kTmemCols);
   }
   if (threadIdx.x == 0) {
     if (err_local) atomicExch(p.err, err_local);
@@ -411,42 +494,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeFn encode_fn() {
-  static EncodeFn fn = nullptr;
-  if (!fn) {
-    void* lib = dlopen("libcuda.so.1", RTLD_NOW | RTLD_GLOBAL);
-    if (!lib) throw std::runtime_error("libcuda.so.1 not found");
-    fn = reinterpret_cast<EncodeFn>(dlsym(lib, "cuTensorMapEncodeTiled"));
-    if (!fn) throw std::runtime_error("cuTensorMapEncodeTiled not found");
-  }
-  return fn;
-}
-
-// 2-D bf16 map over `rows` x `cols` (row pitch `ld` elements), box `box_rows` x 64,
-// 128-byte swizzle.
-CUtensorMap make_map(const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
-  if (reinterpret_cast<uintptr_t>(base) % 16 || (ld * 2) % 16) throw std::invalid_argument("TMA needs 16-byte alignment");
-  CUtensorMap map;
-  cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {ld * 2};
-  cuuint32_t box[2] = {uint32_t(kBK), box_rows};
-  cuuint32_t elem[2] = {1, 1};
-  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, elem,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string(int(r)));
-  return map;
-}
-
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool F8 = false>
 void launch(const CUtensorMap& a, const CUtensorMap& a2, const CUtensorMap& b, const GemmParams& p, int grid,
             cudaStream_t s) {
-  using S = Smem<BN, STAGES>;
-  auto kern = k_gemm<BN, STAGES>;
+  using S = Smem<BN, STAGES, F8>;
+  static_assert(S::kBytes <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
+  auto kern = k_gemm<BN, STAGES, F8>;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
@@ -566,10 +619,128 @@ void gemm_rs(const RegionDesc& reg, const at::Tensor& A, const at::Tensor& B, at
   launch<256, 4>(ma, ma, mb, p, std::min(tiles, sms), s);
 }
 
+// ---------------------------------------------------------------------------
+// Block-scaled fp8 (e4m3 operands, UE8M0 scales per 128 rows and 128 K of each operand
+// -- 1 x 128 for activations, 128 x 128 for weights, both expanded to per-row chunks;
+// layout in fp8_quant.cu).  BN = 128: two 128-column accumulators plus the scale
+// columns fit TMEM's 512 columns.
+// ---------------------------------------------------------------------------
+namespace {
+
+void check_fp8_mat(const at::Tensor& t, const char* name) {
+  if (!t.is_cuda() || t.element_size() != 1 || t.dim() != 2 || t.stride(1) != 1)
+    throw std::invalid_argument(std::string(name) + " must be a row-major 2-D CUDA tensor of 1-byte (e4m3) elements");
+}
+
+void check_sf(const at::Tensor& sf, int rows, int K, const char* name) {
+  const int64_t need = int64_t((rows + 127) / 128) * (K / 128) * 512;
+  if (!sf.is_cuda() || sf.element_size() != 1 || !sf.is_contiguous() || sf.numel() < need ||
+      reinterpret_cast<uintptr_t>(sf.data_ptr()) % 16)
+    throw std::invalid_argument(std::string(name) + ": scales must be a contiguous 16-byte aligned CUDA byte tensor of " +
+                                std::to_string(need) + " bytes");
+}
+
+constexpr int kF8BN = 128, kF8Stages = 6;
+
+}  // namespace
+
+void gemm_fp8(const at::Tensor& A, const at::Tensor& sfa, const at::Tensor& B, const at::Tensor& sfb, at::Tensor& C,
+              at::Tensor& err, int max_ctas) {
+  check_fp8_mat(A, "A");
+  check_fp8_mat(B, "B");
+  check_mat(C, "C");
+  const int M = int(A.size(0)), K = int(A.size(1)), N = int(B.size(0));
+  if (B.size(1) != K || C.size(0) != M || C.size(1) != N) throw std::invalid_argument("shape mismatch");
+  if (K % 128 || N % 128) throw std::invalid_argument("fp8 GEMM needs K and N multiples of 128");
+  check_sf(sfa, M, K, "sfa");
+  check_sf(sfb, N, K, "sfb");
+  c10::cuda::CUDAGuard guard(A.device());
+  GemmParams p = base_params(M, N, K, C, err);
+  p.sfa = static_cast<const uint8_t*>(sfa.data_ptr());
+  p.sfb = static_cast<const uint8_t*>(sfb.data_ptr());
+  CUtensorMap ma = make_map(A.data_ptr(), M, K, A.stride(0), kBM, 1);
+  CUtensorMap mb = make_map(B.data_ptr(), N, K, B.stride(0), kF8BN, 1);
+  auto s = at::cuda::getCurrentCUDAStream(A.device().index()).stream();
+  int sms = max_ctas > 0 ? max_ctas : sm_count(A.device().index());
+  const int tiles = ((M + 127) / 128) * (N / kF8BN);
+  launch<kF8BN, kF8Stages, true>(ma, ma, mb, p, std::min(tiles, sms), s);
+}
+
+void ag_gemm_fp8(const RegionDesc& reg, const at::Tensor& xq_shard, const at::Tensor& sfa_shard, const at::Tensor& B,
+                 const at::Tensor& sfb, at::Tensor& C, at::Tensor& err, int copy_ctas, int max_ctas) {
+  check_fp8_mat(xq_shard, "xq_shard");
+  check_fp8_mat(B, "B");
+  check_mat(C, "C");
+  const int W = reg.world;
+  const int shard_rows = int(xq_shard.size(0)), K = int(xq_shard.size(1)), N = int(B.size(0));
+  const int M = shard_rows * W;
+  if (!xq_shard.is_contiguous() || B.size(1) != K || C.size(0) != M || C.size(1) != N)
+    throw std::invalid_argument("ag_gemm_fp8 shapes: xq_shard [T/W, K], B [N, K], C [T, N]");
+  if (shard_rows % kBM || K % 128 || N % kF8BN) throw std::invalid_argument("ag_gemm_fp8 needs T/W % 128, K % 128, N % 128");
+  check_sf(sfa_shard, shard_rows, K, "sfa_shard");
+  check_sf(sfb, N, K, "sfb");
+  const uint64_t data_bytes = uint64_t(shard_rows) * K;
+  const uint64_t sf_bytes = uint64_t(shard_rows / 128) * (K / 128) * 512;
+  if (reg.push_cap % uint64_t(K) || reg.push_cap < data_bytes + sf_bytes)
+    throw std::invalid_argument("the fp8 shard and its scales do not fit a push slot (raise max_gather_bytes)");
+  if (shard_rows / kBM > kGFlags) throw std::invalid_argument("too many chunks");
+  c10::cuda::CUDAGuard guard(xq_shard.device());
+  GemmParams p = base_params(M, N, K, C, err);
+  p.mode = 1;
+  p.reg = reg;
+  p.shard_rows = shard_rows;
+  p.slot_rows = int(reg.push_cap / uint64_t(K));
+  p.shard = static_cast<const char*>(xq_shard.data_ptr());
+  p.copy_ctas = W > 1 ? std::max(1, copy_ctas) : 0;
+  p.sfa = static_cast<const uint8_t*>(sfa_shard.data_ptr());
+  p.sfb = static_cast<const uint8_t*>(sfb.data_ptr());
+  p.sfa_slot_off = data_bytes;
+  CUtensorMap ma = make_map(xq_shard.data_ptr(), shard_rows, K, K, kBM, 1);
+  CUtensorMap ma2 = make_map(reg.base[reg.rank] + reg.push_off, uint64_t(2) * W * p.slot_rows, K, K, kBM, 1);
+  CUtensorMap mb = make_map(B.data_ptr(), N, K, B.stride(0), kF8BN, 1);
+  auto s = at::cuda::getCurrentCUDAStream(xq_shard.device().index()).stream();
+  int sms = max_ctas > 0 ? max_ctas : sm_count(xq_shard.device().index());
+  const int tiles = (M / kBM) * (N / kF8BN);
+  launch<kF8BN, kF8Stages, true>(ma, ma2, mb, p, std::min(tiles, sms - p.copy_ctas) + p.copy_ctas, s);
+}
+
+void gemm_rs_fp8(const RegionDesc& reg, const at::Tensor& A, const at::Tensor& sfa, const at::Tensor& B,
+                 const at::Tensor& sfb, at::Tensor& C_shard, at::Tensor& err, int max_ctas) {
+  check_fp8_mat(A, "A");
+  check_fp8_mat(B, "B");
+  check_mat(C_shard, "C_shard");
+  const int W = reg.world;
+  const int M = int(A.size(0)), K = int(A.size(1)), N = int(B.size(0));
+  if (B.size(1) != K || M % W || C_shard.size(0) != M / W || C_shard.size(1) != N)
+    throw std::invalid_argument("gemm_rs_fp8 shapes: A [T, K], B [N, K], C_shard [T/W, N]");
+  const int shard_rows = M / W;
+  if (shard_rows % kBM || K % 128 || N % kF8BN) throw std::invalid_argument("gemm_rs_fp8 needs T/W % 128, K % 128, N % 128");
+  check_sf(sfa, M, K, "sfa");
+  check_sf(sfb, N, K, "sfb");
+  if (uint64_t(shard_rows) * N * 2 > reg.push_cap) throw std::invalid_argument("the partial does not fit a push slot");
+  if ((shard_rows / kBM) * (N / kF8BN) > kGFlags) throw std::invalid_argument("too many tiles per shard");
+  c10::cuda::CUDAGuard guard(A.device());
+  GemmParams p = base_params(M, N, K, C_shard, err);
+  p.mode = 2;
+  p.reg = reg;
+  p.shard_rows = shard_rows;
+  p.sfa = static_cast<const uint8_t*>(sfa.data_ptr());
+  p.sfb = static_cast<const uint8_t*>(sfb.data_ptr());
+  CUtensorMap ma = make_map(A.data_ptr(), M, K, A.stride(0), kBM, 1);
+  CUtensorMap mb = make_map(B.data_ptr(), N, K, B.stride(0), kF8BN, 1);
+  auto s = at::cuda::getCurrentCUDAStream(A.device().index()).stream();
+  int sms = max_ctas > 0 ? max_ctas : sm_count(A.device().index());
+  const int tiles = (M / kBM) * (N / kF8BN);
+  launch<kF8BN, kF8Stages, true>(ma, ma, mb, p, std::min(tiles, sms), s);
+}
+
 }  // namespace tc
 }  // namespace sn
 
 void register_gemm(py::module_& m) {
   m.def("gemm", &sn::tc::gemm, py::arg("A"), py::arg("B"), py::arg("C"), py::arg("err"), py::arg("bn") = 256,
         py::arg("max_ctas") = 0, "C = A @ B.T on tcgen05 tensor cores (bf16 in, fp32 accumulate)");
+  m.def("gemm_fp8", &sn::tc::gemm_fp8, py::arg("A"), py::arg("sfa"), py::arg("B"), py::arg("sfb"), py::arg("C"),
+        py::arg("err"), py::arg("max_ctas") = 0,
+        "C = (A * sfa) @ (B * sfb).T: e4m3 operands with UE8M0 block scales (kind::mxf8f6f4), bf16 out");
 }

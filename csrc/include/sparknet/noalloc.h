@@ -33,14 +33,17 @@ extern "C" {
 //   scale    softmax scale (usually 1/sqrt(128))
 // Returns 0 on success, or a nonzero code with a message from
 // sparknet_noalloc_last_error(): 1 bad argument, 2 problem too large for the built-in
-// scratch, 3 CUDA error.  Launches two kernels on `stream`; allocates nothing.
+// scratch, 3 CUDA error.  Launches one kernel on `stream`; allocates nothing.
 //
 // The first call on a device looks up the device address of the scratch array (a
 // CUDA runtime query, done once per device with that device current); make that
 // first call outside any stream capture.  Every call, on every stream, shares the
 // one scratch array, so calls that may overlap on the GPU (different streams, no
-// ordering between them) race and must not be issued.  Each call writes every scratch
-// entry it later reads, so nothing needs clearing between calls.
+// ordering between them) race and must not be issued.  The scratch starts with a
+// fixed block of per-(sequence, KV head) counters that must be zero when a call
+// starts: static device storage starts zeroed and every call that completes leaves
+// them zero, so the caller clears nothing.  The partials after them are written
+// before they are read in every call.
 __attribute__((visibility("default"))) int sparknet_decode_attention_noalloc(
     const void* q, const void* k_cache, const void* v_cache, const int32_t* lengths, void* out, int B, int Hq,
     int Hkv, int Lmax, int max_len, float scale, cudaStream_t stream);

@@ -152,23 +152,99 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// --- block-scaled fp8 (kind::mxf8f6f4, e4m3 x e4m3, UE8M0 scales every 32 K) -----
+// One K block is 128 fp8 = one 128-byte swizzle row, like 64 bf16: the tile shapes and
+// descriptors of the bf16 path carry over; each K block adds a 512-byte scale chunk per
+// 128 rows of A and of B (layout in fp8_quant.cu), staged into TMEM by tcgen05.cp.
+
+// Bulk (non-tensor) copy global -> this CTA's shared memory, completing on `bar`.
+// 16-byte aligned addresses, size a multiple of 16.  No multicast.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Descriptor of a 512-byte scale chunk for tcgen05.cp: K-major, no swizzle, 32 rows of
+// 16 bytes, 8-row core matrices 128 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_sf(const void* chunk) {
+  uint64_t d = 0;
+  d |= (uint64_t(smem_u32(chunk)) >> 4) & 0x3FFFull;
+  d |= 1ull << 16;                // leading byte offset (one core matrix along K)
+  d |= (128ull >> 4) << 32;       // stride byte offset: next 8 rows
+  d |= 1ull << 46;                // descriptor version (sm100)
+  return d;                       // layout 0: no swizzle
+}
+
+// 32 TMEM lanes x 128 bits from shared memory, replicated into all four lane quarters.
+__device__ __forceinline__ void tmem_cp_sf(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Instruction descriptor: e4m3 x e4m3 -> f32, K-major, UE8M0 scales, M = 128, N = n.
+__host__ __device__ constexpr uint32_t idesc_mxf8(int n) {
+  return (0u << 7) | (0u << 10)           // A, B e4m3
+         | (uint32_t(n >> 3) << 17)       // N / 8
+         | (1u << 23)                     // scale format UE8M0
+         | (uint32_t(kBM >> 4) << 24);    // M / 16
+}
+
+// One K=32 step; `sf_id` (instruction descriptor) selects the scale byte of this step
+// in the TMEM columns.  The scale addresses are plain column addresses.  (With 1 x 128
+// and 128 x 128 scales all four bytes of a column hold the same exponent, so the step's
+// byte choice cannot change the result.)
+__device__ __forceinline__ void mma_mxf8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t tsfa, uint32_t tsfb, uint32_t sf_id, uint32_t accumulate) {
+  const uint32_t id = idesc | (sf_id << 29) | (sf_id << 4);
+  const uint32_t sa = tsfa, sb = tsfb;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(id), "r"(accumulate), "r"(sa), "r"(sb)
+      : "memory");
+}
+
 // Shared-memory plan of the tile loop.
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool F8 = false>
 struct Smem {
-  static constexpr int kABytes = kBM * kBK * 2;
-  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kABytes = kBM * 128;        // 128 rows x 128 bytes (64 bf16 or 128 fp8)
+  static constexpr int kBBytes = BN * 128;
   static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kSfBytes = F8 ? 512 * (1 + BN / 128) : 0;  // scale chunks of A and B per stage
   // epilogue staging: per epilogue warp, 32 rows x 64 bf16 columns, rows padded to
   // 144 bytes so row-per-thread writes and 16-byte-per-lane reads avoid bank conflicts
   static constexpr int kStageRowBytes = 144;
   static constexpr int kEpiStageBytes = 4 * 32 * kStageRowBytes;
-  static constexpr int kBytes = STAGES * kStageBytes + kEpiStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kBytes =
+      STAGES * (kStageBytes + kSfBytes) + kEpiStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
+
+// Host: 2-D tensor map over `rows` x `cols` (row pitch `ld` elements) of 2-byte
+// (bf16) or 1-byte (fp8) elements, box `box_rows` x 128 bytes, 128-byte swizzle, zero
+// fill out of bounds.
+CUtensorMap make_map(const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows,
+                     int elem_bytes = 2);
 
 struct TileCoord {
   int m0, n0;

@@ -11,9 +11,14 @@ add+RMSNorm kernel with the same rounding points.  The vocabulary projection is
 column-parallel; each rank takes the argmax of its shard and the (value, index)
 pairs are all-gathered (greedy sampling).
 
-Weights are random (N(0, 0.02)); there are no checkpoints.  Non-collective GEMMs
-use torch (cuBLAS); attention, RoPE + KV-cache writes, SwiGLU and the argmax are
-this package's kernels.  A decode step is one CUDA graph replay.
+Weights are random (N(0, 0.02)); there are no checkpoints.  They are stored in
+``nn.Linear`` layout ``[out, in]``; the gate/up weight interleaves 64-row blocks of gate
+and up (``sparknet.ops.interleave_gate_up``).  With ``gemm="sparknet"`` (the default
+with ``comm="sparknet"``) every projection is this package's tcgen05 decode GEMM and
+SwiGLU runs in the gate/up GEMM's epilogue; ``gemm="cublas"`` (the default of the
+NCCL control arm) uses ``torch.mm`` and a separate SwiGLU kernel.  Attention, RoPE +
+KV-cache writes, the norms and the argmax are this package's kernels.  A decode step
+is one CUDA graph replay.
 """
 
 from __future__ import annotations
@@ -25,6 +30,7 @@ import torch
 import torch.distributed as dist
 
 from .. import _native
+from ..ops.decode_gemm import INTERLEAVE_ROWS, DecodeGemm
 
 
 @dataclass(frozen=True)
@@ -63,13 +69,19 @@ class TPLlama:
     """One rank's shard of the model plus its KV cache and decode buffers."""
 
     def __init__(self, cfg: LlamaConfig, *, rank: int, world: int, device, batch: int, max_len: int,
-                 comm: str = "sparknet", runtime=None, group=None, seed: int = 0):
+                 comm: str = "sparknet", runtime=None, group=None, seed: int = 0, gemm: str | None = None):
         if cfg.heads % world or cfg.kv_heads % world or cfg.ffn % world or cfg.vocab % world:
             raise ValueError(f"model does not shard evenly over {world} GPUs")
         if comm not in ("sparknet", "nccl"):
             raise ValueError("comm must be 'sparknet' or 'nccl'")
         if comm == "sparknet" and world > 1 and runtime is None:
             raise ValueError("comm='sparknet' needs the NVLink runtime")
+        gemm = gemm or ("sparknet" if comm == "sparknet" else "cublas")
+        if gemm not in ("sparknet", "cublas"):
+            raise ValueError("gemm must be 'sparknet' or 'cublas'")
+        if (cfg.ffn // world) % INTERLEAVE_ROWS:
+            raise ValueError("the FFN shard must be a multiple of 64 features")
+        self.gemm = gemm
         self.cfg, self.rank, self.world, self.device = cfg, rank, world, torch.device(device)
         self.batch, self.max_len, self.comm, self.runtime, self.group = batch, max_len, comm, runtime, group
         self.C = _native.load()
@@ -86,23 +98,29 @@ class TPLlama:
         for _ in range(cfg.layers):
             self.layers.append({
                 "ln1": torch.ones(H, dtype=torch.bfloat16, device=dev),
-                "wqkv": _normal((H, (self.hq + 2 * self.hkv) * D), dev, generator=gen),
-                "wo": _normal((self.hq * D, H), dev, generator=gen),
+                "wqkv": _normal(((self.hq + 2 * self.hkv) * D, H), dev, generator=gen),
+                "wo": _normal((H, self.hq * D), dev, generator=gen),
                 "ln2": torch.ones(H, dtype=torch.bfloat16, device=dev),
-                "wgu": _normal((H, 2 * self.f), dev, generator=gen),
-                "wdown": _normal((self.f, H), dev, generator=gen),
+                "wgu": _normal((2 * self.f, H), dev, generator=gen),   # [64 gate; 64 up] row blocks
+                "wdown": _normal((H, self.f), dev, generator=gen),
                 "k": torch.zeros((batch, max_len, self.hkv, D), dtype=torch.bfloat16, device=dev),
                 "v": torch.zeros((batch, max_len, self.hkv, D), dtype=torch.bfloat16, device=dev),
             })
         self.norm = torch.ones(H, dtype=torch.bfloat16, device=dev)
-        self.lm_head = _normal((H, self.v), dev, generator=gen)
+        self.lm_head = _normal((self.v, H), dev, generator=gen)
         inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, D // 2, dtype=torch.float64) * 2 / D))
         ang = torch.arange(max_len, dtype=torch.float64)[:, None] * inv[None, :]
         self.cos = ang.cos().float().to(dev).contiguous()
         self.sin = ang.sin().float().to(dev).contiguous()
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
-        self.workspace = torch.empty(int(self.C.attention_workspace_floats(batch, self.hq, self.hkv, max_len, sms)),
+        # zeroed: the attention kernel's split counters sit at its front
+        self.workspace = torch.zeros(int(self.C.attention_workspace_floats(batch, self.hq, self.hkv, max_len, sms)),
                                      dtype=torch.float32, device=dev)
+        self.mm = DecodeGemm(dev)
+        if gemm == "sparknet":
+            for n, k in (((self.hq + 2 * self.hkv) * D, H), (H, self.hq * D), (2 * self.f, H), (H, self.f),
+                         (self.v, H)):
+                self.mm.reserve(batch, n, k)
         # static decode buffers (graph inputs/outputs)
         self.tokens = torch.zeros(batch, dtype=torch.int64, device=dev)
         self.positions = torch.zeros(batch, dtype=torch.int32, device=dev)
@@ -150,6 +168,19 @@ class TPLlama:
         dist.all_gather_into_tensor(self.best_all, self.best, group=self.group)
         return self.best_all
 
+    def _linear(self, x, w, out):
+        if self.gemm == "sparknet":
+            self.mm(x, w, out)
+        else:
+            torch.mm(x, w.t(), out=out)
+
+    def _swiglu(self, x, w, out):
+        if self.gemm == "sparknet":
+            self.mm(x, w, out, swiglu=True)
+        else:
+            torch.mm(x, w.t(), out=self.gu)
+            self.C.silu_mul(self.gu, out, INTERLEAVE_ROWS)
+
     def step_kernels(self) -> None:
         """One decode step on the current stream: tokens -> next tokens (in place)."""
         C, cfg = self.C, self.cfg
@@ -157,17 +188,16 @@ class TPLlama:
         C.add_rmsnorm(self.res, None, None, self.layers[0]["ln1"], self.x, cfg.eps)
         scale = 1.0 / math.sqrt(cfg.head_dim)
         for i, L in enumerate(self.layers):
-            torch.mm(self.x, L["wqkv"], out=self.qkv)
+            self._linear(self.x, L["wqkv"], self.qkv)
             C.rope_qkv_cache(self.qkv, self.cos, self.sin, self.positions, self.q, L["k"], L["v"], self.hq, self.hkv)
             C.decode_attention(self.q, L["k"], L["v"], self.lengths, self.attn, self.workspace, self.max_len, scale)
-            torch.mm(self.attn.view(self.batch, -1), L["wo"], out=self.partial)
+            self._linear(self.attn.view(self.batch, -1), L["wo"], self.partial)
             self._add_norm(self.partial, L["ln2"])
-            torch.mm(self.x, L["wgu"], out=self.gu)
-            C.silu_mul(self.gu, self.act)
-            torch.mm(self.act, L["wdown"], out=self.partial)
+            self._swiglu(self.x, L["wgu"], self.act)
+            self._linear(self.act, L["wdown"], self.partial)
             nxt = self.layers[i + 1]["ln1"] if i + 1 < len(self.layers) else self.norm
             self._add_norm(self.partial, nxt)
-        torch.mm(self.x, self.lm_head, out=self.logits)
+        self._linear(self.x, self.lm_head, self.logits)
         C.row_argmax(self.logits, self.rank * self.v, self.best)
         allb = self._gather_best().view(self.world, self.batch, 2)
         winner = allb[:, :, 0].argmax(dim=0)                                     # first maximal rank
@@ -201,10 +231,14 @@ class TPLlama:
         self.graph = None
 
     def launches_per_step(self) -> int:
-        """This package's kernel launches in one step (GEMMs, index/copy ops excluded)."""
-        per_layer = 1 + 2 + 1 + 2 * (1 if self.world == 1 or self.comm == "sparknet" else 1)
+        """This package's kernel launches in one step (torch index/copy ops and cuBLAS
+        GEMMs excluded): per layer RoPE, attention, two norms (fused with the
+        all-reduce on the NVLink arm), and with ``gemm="sparknet"`` four GEMMs (SwiGLU
+        fused), else the SwiGLU kernel."""
+        per_layer = 1 + 1 + 2 + (4 if self.gemm == "sparknet" else 1)
         own_gather = 1 if (self.world > 1 and self.comm == "sparknet") else 0
-        return 1 + self.cfg.layers * per_layer + 1 + own_gather
+        lm_head = 1 if self.gemm == "sparknet" else 0
+        return 1 + self.cfg.layers * per_layer + lm_head + 1 + own_gather
 
 
 class _null:

@@ -550,6 +550,45 @@ class NvlinkAllReduce:
                 self._mark_stream(capturing)
         return out
 
+    def ag_gemm_fp8(self, xq_shard: torch.Tensor, sfa_shard: torch.Tensor, w: torch.Tensor, sfw: torch.Tensor, *,
+                    out: Optional[torch.Tensor] = None, copy_ctas: int = 8) -> torch.Tensor:
+        """Block-scaled fp8 ``all_gather(x_shard) @ w.T`` in one kernel, bf16 out.
+
+        ``xq_shard``/``sfa_shard`` and ``w``/``sfw`` come from
+        ``sparknet.ops.fp8.quantize_act`` / ``quantize_weight`` (e4m3 with UE8M0 scales
+        per 1 x 128 and 128 x 128).  The shard's rows and scales cross NVLink in fp8,
+        half the bytes of the bf16 gather.
+        """
+        with self._lock:
+            self.check_health()
+            self._live()
+            capturing = torch.cuda.is_current_stream_capturing()
+            with torch.cuda.device(self.device):
+                if out is None:
+                    out = torch.empty((xq_shard.shape[0] * self.world_size, w.shape[0]), dtype=torch.bfloat16,
+                                      device=self.device)
+                self._order_stream(capturing)
+                self._comm.ag_gemm_fp8(xq_shard, sfa_shard, w, sfw, out, self._gemm_err(), int(copy_ctas), 0)
+                self._mark_stream(capturing)
+        return out
+
+    def gemm_rs_fp8(self, aq: torch.Tensor, sfa: torch.Tensor, w: torch.Tensor, sfw: torch.Tensor, *,
+                    out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Block-scaled fp8 ``reduce_scatter(a @ w.T)`` in one kernel; bf16 partials and
+        output, summed in fixed rank order."""
+        with self._lock:
+            self.check_health()
+            self._live()
+            capturing = torch.cuda.is_current_stream_capturing()
+            with torch.cuda.device(self.device):
+                if out is None:
+                    out = torch.empty((aq.shape[0] // self.world_size, w.shape[0]), dtype=torch.bfloat16,
+                                      device=self.device)
+                self._order_stream(capturing)
+                self._comm.gemm_rs_fp8(aq, sfa, w, sfw, out, self._gemm_err(), 0)
+                self._mark_stream(capturing)
+        return out
+
     def gemm_error(self) -> int:
         """The fused GEMMs' error word (0 = healthy; synchronises)."""
         return int(self._gemm_err().item())

@@ -45,10 +45,14 @@ def test_decode_attention(device, native, B, Hq, Hkv, L):
     lengths = torch.randint(1, L + 1, (B,), dtype=torch.int32, device=device)
     lengths[0] = L
     sms = torch.cuda.get_device_properties(device).multi_processor_count
-    ws = torch.empty(native.attention_workspace_floats(B, Hq, Hkv, L, sms), dtype=torch.float32, device=device)
+    ws = torch.zeros(native.attention_workspace_floats(B, Hq, Hkv, L, sms), dtype=torch.float32, device=device)
     out = torch.empty(B, Hq, 128, dtype=torch.bfloat16, device=device)
     native.decode_attention(q, kc, vc, lengths, out, ws, L, 1 / math.sqrt(128))
+    again = torch.empty_like(out)
+    native.decode_attention(q, kc, vc, lengths, again, ws, L, 1 / math.sqrt(128))  # counters were left at zero
     torch.cuda.synchronize()
+    assert torch.equal(out, again)
+    assert not ws[:4096].view(torch.int32).any()
     G = Hq // Hkv
     for b in range(B):
         n = int(lengths[b])
@@ -76,6 +80,14 @@ def test_add_rmsnorm_silu_argmax(device, native):
     torch.cuda.synchronize()
     g_, u_ = gu.float()[:, :1000], gu.float()[:, 1000:]
     torch.testing.assert_close(act.float(), torch.nn.functional.silu(g_) * u_, rtol=1e-2, atol=1e-2)
+    # interleaved [64 gate | 64 up] column groups
+    gu = torch.randn(3, 2 * 1024, device=device).to(torch.bfloat16)
+    act = torch.empty(3, 1024, dtype=torch.bfloat16, device=device)
+    native.silu_mul(gu, act, 64)
+    torch.cuda.synchronize()
+    v = gu.float().view(3, 16, 2, 64)
+    want = (torch.nn.functional.silu(v[:, :, 0]) * v[:, :, 1]).reshape(3, 1024)
+    torch.testing.assert_close(act.float(), want, rtol=1e-2, atol=1e-2)
     logits = torch.randn(4, 16032, device=device).to(torch.bfloat16)
     best = torch.empty(4, 2, dtype=torch.float32, device=device)
     native.row_argmax(logits, 1000, best)
@@ -84,11 +96,12 @@ def test_add_rmsnorm_silu_argmax(device, native):
     assert torch.equal(best[:, 0], vals) and torch.equal(best[:, 1].long(), idx + 1000)
 
 
-def test_tiny_model_step_matches_torch(device, native):
+@pytest.mark.parametrize("gemm", ["sparknet", "cublas"])
+def test_tiny_model_step_matches_torch(device, native, gemm):
     from sparknet.models.llama import LlamaConfig, TPLlama
 
     cfg = LlamaConfig.tiny(layers=2)
-    m = TPLlama(cfg, rank=0, world=1, device=device, batch=2, max_len=32)
+    m = TPLlama(cfg, rank=0, world=1, device=device, batch=2, max_len=32, gemm=gemm)
     m.fill_prompt_cache(5)
     m.tokens.copy_(torch.tensor([3, 9], device=device))
     tokens0, pos0 = m.tokens.clone(), m.positions.clone().long()
@@ -101,8 +114,10 @@ def test_tiny_model_step_matches_torch(device, native):
     rms = lambda v, g: v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + cfg.eps) * f(g)  # noqa: E731
     res = f(m.embed[tokens0])
     x = rms(res, m.layers[0]["ln1"])
+    from sparknet.ops.decode_gemm import split_gate_up
+
     for i, L in enumerate(m.layers):
-        qkv = (x @ f(L["wqkv"])).view(2, -1, 128)
+        qkv = (x @ f(L["wqkv"]).T).view(2, -1, 128)
         q, k, v = qkv[:, :m.hq], qkv[:, m.hq:m.hq + m.hkv], qkv[:, m.hq + m.hkv:]
         q, k = rope_ref(q, m.cos, m.sin, pos0), rope_ref(k, m.cos, m.sin, pos0)
         outs = []
@@ -113,12 +128,35 @@ def test_tiny_model_step_matches_torch(device, native):
             s = torch.einsum("hd,nhd->hn", q[b], kk) / math.sqrt(128)
             outs.append(torch.einsum("hn,nhd->hd", s.softmax(-1), vv))
         attn = torch.stack(outs).view(2, -1)
-        res = res + attn @ f(L["wo"])
+        res = res + attn @ f(L["wo"]).T
         x = rms(res, L["ln2"])
-        gu = x @ f(L["wgu"])
-        act = torch.nn.functional.silu(gu[:, :m.f]) * gu[:, m.f:]
-        res = res + act @ f(L["wdown"])
+        gate, up = split_gate_up(L["wgu"])
+        act = torch.nn.functional.silu(x @ f(gate).T) * (x @ f(up).T)
+        res = res + act @ f(L["wdown"]).T
         x = rms(res, m.layers[i + 1]["ln1"] if i + 1 < len(m.layers) else m.norm)
-    logits = x @ f(m.lm_head)
+    logits = x @ f(m.lm_head).T
     torch.testing.assert_close(m.logits.float(), logits, rtol=5e-2, atol=5e-2)
     assert torch.equal(m.positions.long(), pos0 + 1)
+
+
+@pytest.mark.parametrize("M,N,K,swiglu,max_splits", [
+    (1, 1280, 8192, False, 0), (8, 8192, 1024, False, 0), (8, 7168, 8192, True, 0), (33, 1000, 512, False, 0),
+    (64, 2048, 3584, False, 0), (16, 512, 1024, False, 1), (200, 384, 256, True, 0), (8, 16032, 8192, False, 0)])
+def test_decode_gemm(device, native, M, N, K, swiglu, max_splits):
+    from sparknet.ops.decode_gemm import DecodeGemm, split_gate_up
+
+    gen = torch.Generator(device=device).manual_seed(M * 7 + N)
+    x = torch.randn(M, K, generator=gen, device=device).to(torch.bfloat16)
+    w = (0.02 * torch.randn(N, K, generator=gen, device=device)).to(torch.bfloat16)
+    op = DecodeGemm(device, max_splits=max_splits)
+    y = op(x, w, swiglu=swiglu)
+    y2 = op(x, w, swiglu=swiglu)
+    op.check()
+    assert torch.equal(y, y2), "split-K reduction must not depend on CTA finishing order"
+    if swiglu:
+        gate, up = split_gate_up(w)
+        want = torch.nn.functional.silu(x.float() @ gate.float().T) * (x.float() @ up.float().T)
+    else:
+        want = x.float() @ w.float().T
+    torch.testing.assert_close(y.float(), want, rtol=2e-2, atol=2e-2)
+    assert not op.counters.any()

@@ -47,3 +47,34 @@ def test_gemm_throughput(device, native):
     print(f"\nGEMM {M}x{N}x{K} TFLOP/s: {res}")
     gemm(a, b, c, check=True)
     assert res["tcgen05"] > 100
+
+
+def test_fp8_gemm_throughput(device, native):
+    """Block-scaled fp8 tcgen05 GEMM at a prefill shape; prints TFLOP/s beside bf16."""
+    from sparknet.ops import fp8
+    from sparknet.ops.gemm import gemm
+
+    M, N, K = 8192, 7168, 8192
+    x = torch.randn(M, K, device=device).to(torch.bfloat16)
+    w = (0.02 * torch.randn(N, K, device=device)).to(torch.bfloat16)
+    xq, sx = fp8.quantize_act(x)
+    wq, sw = fp8.quantize_weight(w)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=device)
+
+    def t(fn, reps=10):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record()
+        for _ in range(reps):
+            fn()
+        en.record()
+        en.synchronize()
+        return st.elapsed_time(en) / reps
+
+    f8 = 2 * M * N * K / (t(lambda: fp8.gemm_fp8(xq, sx, wq, sw, y)) * 1e-3) / 1e12
+    bf = 2 * M * N * K / (t(lambda: gemm(x, w, y)) * 1e-3) / 1e12
+    print(f"\nGEMM {M}x{N}x{K} TFLOP/s: fp8 block-scaled {f8:.0f}, bf16 {bf:.0f}")
+    fp8.gemm_fp8(xq, sx, wq, sw, y, check=True)
+    assert f8 > 0

@@ -49,7 +49,7 @@ def test_noalloc_attention_matches_allocating_entry_point(device):
         k = torch.randn(B, Lmax, Hkv, 128, generator=g, device=device).to(torch.bfloat16)
         v = torch.randn(B, Lmax, Hkv, 128, generator=g, device=device).to(torch.bfloat16)
         lengths = torch.randint(1, L + 1, (B,), dtype=torch.int32, device=device, generator=g)
-        ws = torch.empty(native.attention_workspace_floats(B, Hq, Hkv, L, sms), dtype=torch.float32, device=device)
+        ws = torch.zeros(native.attention_workspace_floats(B, Hq, Hkv, L, sms), dtype=torch.float32, device=device)
         want = torch.empty(B, Hq, 128, dtype=torch.bfloat16, device=device)
         native.decode_attention(q, k, v, lengths, want, ws, L, scale)
         got = torch.full_like(want, float("nan"))

@@ -72,6 +72,35 @@ def main():
         failures.append(f"gemm_rs relative error {err}")
     if rt.gemm_error() or rt.failure():
         failures.append(f"error word {rt.gemm_error()} / {rt.failure()}")
+    # -- block-scaled fp8 forms, against fp32 matmuls of the dequantised operands
+    from sparknet.ops import fp8
+
+    xq, sx = fp8.quantize_act(x)
+    wq, sw = fp8.quantize_weight(w)
+    got = rt.ag_gemm_fp8(xq, sx, wq, sw)
+    xd = fp8.dequantize(xq, sx)
+    parts = [torch.empty_like(xd) for _ in range(world)]
+    dist.all_gather(parts, xd)
+    want = torch.cat(parts) @ fp8.dequantize(wq, sw).T
+    torch.cuda.synchronize()
+    err = (got.float() - want).abs().max().item() / max(1e-6, want.abs().max().item())
+    if err > 1e-2:
+        failures.append(f"ag_gemm_fp8 relative error {err}")
+    aq, sa = fp8.quantize_act(a)
+    w2q, s2 = fp8.quantize_weight(w[:512].contiguous())
+    got = rt.gemm_rs_fp8(aq, sa, w2q, s2)
+    ad, wd = fp8.dequantize(aq, sa), fp8.dequantize(w2q, s2)
+    fa = [torch.empty_like(ad) for _ in range(world)]
+    fw = [torch.empty_like(wd) for _ in range(world)]
+    dist.all_gather(fa, ad)
+    dist.all_gather(fw, wd)
+    ref = sum(fa[s] @ fw[s].T for s in range(world))[rank * (t // world):(rank + 1) * (t // world)]
+    torch.cuda.synchronize()
+    err = (got.float() - ref).abs().max().item() / max(1e-6, ref.abs().max().item())
+    if err > 1e-2:
+        failures.append(f"gemm_rs_fp8 relative error {err}")
+    if rt.gemm_error() or rt.failure():
+        failures.append(f"error word (fp8) {rt.gemm_error()} / {rt.failure()}")
     results["correct"] = not failures
     # -- timing at the prefill shapes
     if os.environ.get("SPARKNET_PREFILL_BENCH", "1") == "1" and not failures:
@@ -93,6 +122,23 @@ def main():
             base = timed(lambda: gemm_rs_reference(a, w))
             cases[name] = {"fused_ms": fused, "nccl_cublas_ms": base, "flops": 2 * T * H * kk,
                            "nvlink_bytes_out": (world - 1) * (T // world) * H * 2}
+        # fp8 block-scaled forms (operands quantised outside the timed region)
+        from sparknet.ops import fp8
+
+        xq, sx = fp8.quantize_act(x)
+        for name, n in (("ag_gemm_qkv_fp8", qkv_n), ("ag_gemm_gate_up_fp8", gu_n)):
+            wq, sw = fp8.quantize_weight((0.02 * torch.randn(n, H, generator=g, device=device)).to(torch.bfloat16))
+            out = torch.empty(T, n, dtype=torch.bfloat16, device=device)
+            fused = timed(lambda: rt.ag_gemm_fp8(xq, sx, wq, sw, out=out))
+            cases[name] = {"fused_ms": fused, "nccl_cublas_ms": cases[name[:-4]]["nccl_cublas_ms"],
+                           "flops": 2 * T * H * n, "nvlink_bytes_in": (world - 1) * (T // world) * H}
+        for name, kk in (("gemm_rs_o_fp8", H // world), ("gemm_rs_down_fp8", F // world)):
+            aq, sa = fp8.quantize_act(torch.randn(T, kk, generator=g, device=device).to(torch.bfloat16))
+            wq, sw = fp8.quantize_weight((0.02 * torch.randn(H, kk, generator=g, device=device)).to(torch.bfloat16))
+            out = torch.empty(T // world, H, dtype=torch.bfloat16, device=device)
+            fused = timed(lambda: rt.gemm_rs_fp8(aq, sa, wq, sw, out=out))
+            cases[name] = {"fused_ms": fused, "nccl_cublas_ms": cases[name[:-4]]["nccl_cublas_ms"],
+                           "flops": 2 * T * H * kk, "nvlink_bytes_out": (world - 1) * (T // world) * H * 2}
         gathered = [None] * world
         dist.all_gather_object(gathered, cases, group=cpu)
         for name in cases:
