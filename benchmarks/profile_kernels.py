@@ -49,6 +49,32 @@ def _time(fn, warmup: int, iters: int, device) -> list[float]:
     return out
 
 
+def _gemm_stamps(x, w, y, swiglu, device) -> dict:
+    """Phase timing of one cold decode-GEMM launch from per-CTA %globaltimer stamps:
+    entry (relative to the first CTA's), set-up, first data, streaming, MMA drain, park
+    + cluster barrier, reduce; p50 / max over CTAs in µs."""
+    C = _native_mod()
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    info = C.skinny_plan(x.shape[0], w.shape[0], x.shape[1], sms, 0)
+    ctas = info[2] * info[4]
+    st = torch.zeros(ctas * 8, dtype=torch.int64, device=device)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    flush.fill_(1)
+    torch.cuda.synchronize(device)
+    C.skinny_gemm(x, w, y, err, 1 if swiglu else 0, 0, False, st)
+    torch.cuda.synchronize(device)
+    t = st.view(ctas, 8).double().cpu() / 1000.0
+    t0 = t[:, 0].min()
+    names = ["entry", "setup", "wait_prev", "first_data", "stream", "mma_drain", "park_sync", "reduce_exit"]
+    out = {}
+    for i, n in enumerate(names):
+        d = (t[:, 0] - t0) if i == 0 else (t[:, i] - t[:, i - 1])
+        out[n] = {"p50": round(float(d.median()), 2), "max": round(float(d.max()), 2)}
+    out["span"] = round(float(t[:, 7].max() - t0), 2)
+    return out
+
+
 def _native_mod():
     from sparknet import _native
 
@@ -84,8 +110,11 @@ def main() -> int:
     ap.add_argument("kernel", choices=["allreduce", "fused_norm", "allgather", "reduce_scatter", "gemm", "attention",
                                        "decode_gemm", "cublas_decode_gemm"])
     ap.add_argument("--swiglu", action="store_true", help="decode_gemm: fused SwiGLU epilogue")
-    ap.add_argument("--tune", type=int, nargs=2, default=None, metavar=("CTAS_PER_SM", "ROTATION"),
-                    help="decode_gemm: skinny_tune(ctas_per_sm, rotation) before running")
+    ap.add_argument("--tune", type=int, default=0, metavar="CTAS_PER_SM",
+                    help="decode_gemm: skinny_tune(ctas_per_sm) before running (0 = default)")
+    ap.add_argument("--pdl", action="store_true", help="decode_gemm: programmatic dependent launch")
+    ap.add_argument("--stamps", action="store_true",
+                    help="decode_gemm: per-CTA %%globaltimer phase stamps of one cold launch (µs percentiles)")
     ap.add_argument("--world", type=int, default=8)
     ap.add_argument("--bytes", type=int, default=2 << 20, help="bytes per rank (collectives)")
     ap.add_argument("--algorithm", default="", help="oneshot/twoshot (all-reduce, fused norm), ll/push (gather)")
@@ -159,9 +188,10 @@ def main() -> int:
         w = ws[0]
         if args.kernel == "decode_gemm":
             if args.tune:
-                _native_mod().skinny_tune(*args.tune)
+                _native_mod().skinny_tune(args.tune)
                 row["tune"] = args.tune
-            op = DecodeGemm(device)
+            op = DecodeGemm(device, pdl=args.pdl)
+            row["pdl"] = args.pdl
             y = op(x, w, swiglu=args.swiglu)
             fn = lambda: op(x, w, y, swiglu=args.swiglu)  # noqa: E731
             fns = [lambda w=w: op(x, w, y, swiglu=args.swiglu) for w in ws]
@@ -174,6 +204,8 @@ def main() -> int:
         row["graph_us"] = _time_graph(fns, 20, device)
         if args.kernel == "decode_gemm":
             op.check()
+            if args.stamps:
+                row["phases_us"] = _gemm_stamps(x, ws[-1], y, args.swiglu, device)
         row.update(m=M, n=N, k=K, swiglu=args.swiglu, weight_bytes=N * K * 2, copies=copies)
         row["weight_tbs"] = N * K * 2 / (row["graph_us"] * 1e-6) / 1e12
     else:

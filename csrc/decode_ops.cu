@@ -79,6 +79,7 @@ __global__ void __launch_bounds__(1024) k_add_rmsnorm(const __nv_bfloat16* __res
                                                       const __nv_bfloat16* __restrict__ gamma,
                                                       __nv_bfloat16* __restrict__ out, int H, float eps) {
   __shared__ float warp_sums[32];
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // a PDL-launched successor may start early
   const size_t row = blockIdx.x;
   float v[VPT][8];
   float sq = 0.0f;

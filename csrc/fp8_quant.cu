@@ -27,17 +27,16 @@ namespace py = pybind11;
 
 namespace {
 
-constexpr float kE4M3Max = 448.0f;
-
-// UE8M0 exponent of the smallest power of two s with amax / s <= 448.
+// UE8M0 exponent of the smallest power of two s with amax / s <= 448, exactly: with
+// amax = m * 2^E (1 <= m < 2) and 448 = 1.75 * 2^8, amax <= 448 * 2^k holds from
+// k = E - 8 when m <= 1.75 (mantissa field <= 0x600000), else from k = E - 7.
 __device__ __forceinline__ uint32_t ue8m0_for(float amax) {
   if (!(amax > 0.0f)) return 127u;  // zero (or NaN) block: scale 1
-  const float t = amax * (1.0f / kE4M3Max);
-  const uint32_t bits = __float_as_uint(t);
-  uint32_t e = (bits >> 23) & 0xFFu;
-  if (e == 0u) return 1u;                    // below the normal range: smallest scale used
-  if (bits & 0x7FFFFFu) ++e;                 // round the exponent up
-  return e > 254u ? 254u : e;
+  const uint32_t bits = __float_as_uint(amax);
+  const int exp_field = int((bits >> 23) & 0xFFu);
+  if (exp_field == 0) return 1u;                                   // subnormal amax: smallest scale
+  int e = exp_field - 8 + ((bits & 0x7FFFFFu) > 0x600000u ? 1 : 0);  // 127 + k
+  return uint32_t(e < 1 ? 1 : (e > 254 ? 254 : e));
 }
 
 // 2^(127 - e): multiplying by it divides by the scale exactly.

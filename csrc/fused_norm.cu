@@ -221,7 +221,10 @@ SN_DEV void fused_body(const Job& j, int algo) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(1024) k_fused(Job j, int algo) { fused_body<D>(j, algo); }
+__global__ void __launch_bounds__(1024) k_fused(Job j, int algo) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // a PDL-launched successor may start early
+  fused_body<D>(j, algo);
+}
 
 template <int D>
 __global__ void __launch_bounds__(1024) k_fused_emu(Job j, EmuViews e, int algo) {

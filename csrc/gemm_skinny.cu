@@ -21,6 +21,7 @@
 // Reference: none (the reference has no model GEMMs).
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <cooperative_groups.h>
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <torch/extension.h>
@@ -32,6 +33,7 @@
 #include "sparknet/tc_gemm.cuh"
 
 namespace py = pybind11;
+namespace cg = cooperative_groups;
 
 namespace sn {
 namespace tc {
@@ -41,7 +43,7 @@ constexpr int kSkThreads = 128;
 constexpr int kWRows = 128;                      // weight rows per tile (MMA M)
 constexpr int kWStage = kWRows * kBK * 2;        // 16 KB of weights per stage
 constexpr int kMaxTokens = 256;
-constexpr int kRedBatch = 8;                     // split partials loaded at once by the last CTA
+constexpr int kMaxSplits = 16;                   // cluster size (non-portable above 8)
 
 struct SkinnyParams {
   int M, N, K;        // tokens, weight rows, reduction
@@ -51,16 +53,34 @@ struct SkinnyParams {
   int splits;
   int tiles;          // weight tiles
   int mode;           // 0 plain, 1 SwiGLU over interleaved gate/up tiles
-  int rot;            // K-block rotation per weight tile (spreads concurrent reads over channels)
   __nv_bfloat16* Y;
   int ldy;
-  float* ws;          // [splits][tiles][mp / 16][128][16] fp32 partials
-  int* counters;      // [tiles], zero between launches (the last CTA resets its tile)
   uint32_t* err;
+  uint64_t* stamps;   // optional: kStamps %globaltimer values per CTA (phase timing), or null
 };
+
+constexpr int kStamps = 8;
+
+__device__ __forceinline__ void stamp(const SkinnyParams& p, int i) {
+  if (p.stamps) {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    p.stamps[(size_t(blockIdx.y) * gridDim.x + blockIdx.x) * kStamps + i] = t;
+  }
+}
 
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
+// grid (splits, tiles), cluster (splits, 1, 1): the K splits of one weight tile are one
+// thread-block cluster.  After the main loop each CTA parks its fp32 partial tile in
+// its own shared memory; after a cluster barrier, CTA r sums rows r, r + S, ... of the
+// tile over the S partials through distributed shared memory, in split order, and
+// writes them; a second cluster barrier keeps every partial alive until all reads are
+// done.  No global scratch, no atomics.
+//
+// Programmatic dependent launch: the weight tiles of the first stages are requested
+// before griddepcontrol.wait (weights do not depend on the previous kernel); the
+// activation tiles and everything after come after it.
 __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ CUtensorMap map_w,
                                                        const __grid_constant__ CUtensorMap map_x,
                                                        SkinnyParams p) {
@@ -72,17 +92,20 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
   uint64_t* empty = full + p.stages;
   uint64_t* done = empty + p.stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-  int* last_flag = reinterpret_cast<int*>(tmem_slot + 1);
-  float* xchg = reinterpret_cast<float*>(base + p.stages * stage_bytes + 1024);  // [64][17] SwiGLU exchange
+  float* part = reinterpret_cast<float*>(base);  // [128][mp + 1] fp32, over the stage buffers once they are idle
 
+  cg::cluster_group cluster = cg::this_cluster();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x, split = blockIdx.y;
+  const int split = blockIdx.x, tile = blockIdx.y;
+  const int S = int(cluster.num_blocks());  // == splits
   const int kb0 = split * p.kb_per_split;
-  const int nkb = min(p.kb_per_split, p.K / kBK - kb0);
+  const int nkb = max(0, min(p.kb_per_split, p.K / kBK - kb0));
   volatile uint32_t* err = p.err;
   const uint32_t ncols = p.mp <= 32 ? 32u : (p.mp <= 64 ? 64u : (p.mp <= 128 ? 128u : 256u));
+  const int pitch = p.mp + 1;  // padded row of the parked partial
 
   if (threadIdx.x == 0) {
+    stamp(p, 0);  // entry
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -97,17 +120,25 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0 && lane == 0) {
+    stamp(p, 1);  // set-up done (barriers, TMEM)
     prefetch_tmap(&map_w);
     prefetch_tmap(&map_x);
-    for (int i = 0; i < nkb; ++i) {
+    const int pre = min(nkb, p.stages);
+    for (int i = 0; i < pre; ++i) {  // weights first: independent of the previous kernel
+      mbar_expect_tx(&full[i], stage_bytes);
+      tma_load_2d(base + i * stage_bytes, &map_w, (kb0 + i) * kBK, tile * kWRows, &full[i]);
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    stamp(p, 2);  // previous kernel complete
+    for (int i = 0; i < pre; ++i) tma_load_2d(base + i * stage_bytes + kWStage, &map_x, (kb0 + i) * kBK, 0, &full[i]);
+    for (int i = pre; i < nkb; ++i) {
       const int s = i % p.stages;
       const uint32_t ph = (i / p.stages) & 1;
-      if (i >= p.stages && !mbar_wait(&empty[s], ph ^ 1, err)) break;
+      if (!mbar_wait(&empty[s], ph ^ 1, err)) break;
       uint8_t* st = base + s * stage_bytes;
-      const int kb = kb0 + (i + tile * p.rot) % nkb;
       mbar_expect_tx(&full[s], stage_bytes);
-      tma_load_2d(st, &map_w, kb * kBK, tile * kWRows, &full[s]);
-      tma_load_2d(st + kWStage, &map_x, kb * kBK, 0, &full[s]);
+      tma_load_2d(st, &map_w, (kb0 + i) * kBK, tile * kWRows, &full[s]);
+      tma_load_2d(st + kWStage, &map_x, (kb0 + i) * kBK, 0, &full[s]);
     }
   } else if (warp == 1 && lane == 0) {
     const uint32_t idesc = idesc_bf16(p.mp);
@@ -115,6 +146,7 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
       const int s = i % p.stages;
       const uint32_t ph = (i / p.stages) & 1;
       if (!mbar_wait(&full[s], ph, err)) break;
+      if (i == 0) stamp(p, 3);  // first stage landed
       tc_fence_after();
       uint8_t* st = base + s * stage_bytes;
       const uint64_t adesc = smem_desc_sw128(st), bdesc = smem_desc_sw128(st + kWStage);
@@ -123,98 +155,60 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
         mma_bf16(tmem, adesc + 2 * k, bdesc + 2 * k, idesc, (i | k) != 0);
       mma_commit(&empty[s]);
     }
+    stamp(p, 4);  // last stage landed, last MMA issued
     mma_commit(done);  // also after an early exit: arrives once issued MMAs retire
   }
   __syncwarp();
-  const bool ok = mbar_wait(done, 0, err);
+  mbar_wait(done, 0, err);
   tc_fence_after();
+  if (threadIdx.x == 64) stamp(p, 5);  // accumulator complete
 
-  // TMEM lane = weight row within the tile; warp w may read lanes 32w..32w+31.
+  // TMEM lane = weight row within the tile; warp w may read lanes 32w..32w+31.  Park
+  // the partial (all stage reads and MMAs are complete: `done` fired).
   const int row = warp * 32 + lane;
   const uint32_t lane_addr = tmem + (uint32_t(warp * 32) << 16);
   const int chunks = p.mp / 16;
-  auto final_store = [&](int c, const float* v) {
-    if (p.mode == 0) {
-      const int n = tile * kWRows + row;
-      if (n < p.N) {
+  for (int c = 0; c < chunks; ++c) {
+    float v[16];
+    tmem_ld16(lane_addr + c * 16, v);
+    if (nkb == 0) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          if (c * 16 + j < p.M) p.Y[size_t(c * 16 + j) * p.ldy + n] = __float2bfloat16_rn(v[j]);
-      }
-    } else {
-      // rows 64..127 (warps 2, 3) hold `up`, rows 0..63 `gate` of the same features
-      if (row >= 64) {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) xchg[(row - 64) * 17 + j] = v[j];
-      }
-      __syncthreads();
-      if (row < 64) {
-        const int f = tile * 64 + row;
-#pragma unroll
-        for (int j = 0; j < 16; ++j)
-          if (c * 16 + j < p.M)
-            p.Y[size_t(c * 16 + j) * p.ldy + f] = __float2bfloat16_rn(silu(v[j]) * xchg[row * 17 + j]);
-      }
-      __syncthreads();
+      for (int j = 0; j < 16; ++j) v[j] = 0.0f;
     }
-  };
+#pragma unroll
+    for (int j = 0; j < 16; ++j) part[row * pitch + c * 16 + j] = v[j];
+  }
+  tc_fence_before();
+  cluster.sync();  // every split's partial is parked
+  if (threadIdx.x == 64) stamp(p, 6);
 
-  if (p.splits == 1) {
-    for (int c = 0; c < chunks; ++c) {
-      float v[16];
-      tmem_ld16(lane_addr + c * 16, v);
-      final_store(c, v);
+  if (p.mode == 0) {
+    // this CTA's rows: r = split, split + S, ...; thread -> (row, column) pairs
+    const int my_rows = (kWRows - split + S - 1) / S;
+    for (int e = threadIdx.x; e < my_rows * p.M; e += blockDim.x) {
+      const int r = split + (e / p.M) * S, m = e % p.M;
+      const int n = tile * kWRows + r;
+      float acc = 0.0f;
+      for (int s = 0; s < S; ++s) acc += cluster.map_shared_rank(part, s)[r * pitch + m];
+      if (n < p.N) p.Y[size_t(m) * p.ldy + n] = __float2bfloat16_rn(acc);
     }
   } else {
-    float* mine = p.ws + (size_t(split) * p.tiles + tile) * chunks * kWRows * 16;
-    for (int c = 0; c < chunks; ++c) {
-      float v[16];
-      tmem_ld16(lane_addr + c * 16, v);
-      float4* dst = reinterpret_cast<float4*>(mine + (size_t(c) * kWRows + row) * 16);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) __stcg(dst + j, make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) *last_flag = atomicAdd(&p.counters[tile], 1) == p.splits - 1;
-    __syncthreads();
-    if (*last_flag) {
-      __threadfence();
-      for (int c = 0; c < chunks; ++c) {
-        float v[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = 0.0f;
-        // fixed split order; kRedBatch splits' loads in flight before any add
-        for (int s0 = 0; s0 < p.splits; s0 += kRedBatch) {
-          float4 t[kRedBatch][4];
-#pragma unroll
-          for (int b = 0; b < kRedBatch; ++b) {
-            const float4* src = reinterpret_cast<const float4*>(
-                p.ws + ((size_t(s0 + b) * p.tiles + tile) * chunks * kWRows + size_t(c) * kWRows + row) * 16);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) t[b][j] = s0 + b < p.splits ? __ldcg(src + j) : make_float4(0, 0, 0, 0);
-          }
-#pragma unroll
-          for (int b = 0; b < kRedBatch; ++b) {
-            if (s0 + b < p.splits) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                v[4 * j] += t[b][j].x;
-                v[4 * j + 1] += t[b][j].y;
-                v[4 * j + 2] += t[b][j].z;
-                v[4 * j + 3] += t[b][j].w;
-              }
-            }
-          }
-        }
-        final_store(c, v);
+    // SwiGLU: rows 0..63 gate, 64..127 up of the same 64 features
+    const int my_rows = (64 - split + S - 1) / S;
+    for (int e = threadIdx.x; e < my_rows * p.M; e += blockDim.x) {
+      const int r = split + (e / p.M) * S, m = e % p.M;
+      float g = 0.0f, u = 0.0f;
+      for (int s = 0; s < S; ++s) {
+        const float* ps = cluster.map_shared_rank(part, s);
+        g += ps[r * pitch + m];
+        u += ps[(r + 64) * pitch + m];
       }
-      if (threadIdx.x == 0) p.counters[tile] = 0;
+      p.Y[size_t(m) * p.ldy + tile * 64 + r] = __float2bfloat16_rn(silu(g) * u);
     }
   }
-  (void)ok;
-  tc_fence_before();
-  __syncthreads();
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  cluster.sync();  // partials stay readable until every CTA of the cluster is done
+  if (threadIdx.x == 64) stamp(p, 7);  // exit
   if (warp == 1) tmem_dealloc(tmem, ncols);
 }
 
@@ -222,9 +216,8 @@ struct Plan {
   int mp, stages, splits, kb_per_split, tiles, smem;
 };
 
-// Tuning (process-wide): CTAs per SM (0: by token count) and K-block rotation.
+// Tuning (process-wide): CTAs per SM (0: by token count) and the split cap.
 int g_cps = 0;
-int g_rot = 0;
 
 Plan plan(int M, int N, int K, int sms, int max_splits) {
   Plan pl;
@@ -234,12 +227,12 @@ Plan plan(int M, int N, int K, int sms, int max_splits) {
   const int stage = kWStage + x_stage;
   // two CTAs per SM while the token tile is small, one beyond
   const int ctas_per_sm = g_cps > 0 ? g_cps : (pl.mp <= 64 ? 2 : 1);
-  const int budget = (224 / ctas_per_sm) * 1024 - 1024 /*align*/ - 1024 /*barriers*/ - 64 * 17 * 4;
+  const int budget = (224 / ctas_per_sm) * 1024 - 1024 /*align*/ - 1024 /*barriers*/;
   pl.stages = std::max(2, std::min(12, budget / stage));
-  pl.smem = 1024 + pl.stages * stage + 1024 + 64 * 17 * 4;
+  pl.smem = 1024 + pl.stages * stage + 1024;
   const int kbs = K / kBK;
   int splits = std::max(1, sms * ctas_per_sm / pl.tiles);  // one wave
-  splits = std::min({splits, kbs, max_splits > 0 ? max_splits : 16});
+  splits = std::min({splits, kbs, max_splits > 0 ? std::min(max_splits, kMaxSplits) : kMaxSplits});
   pl.kb_per_split = (kbs + splits - 1) / splits;
   pl.splits = (kbs + pl.kb_per_split - 1) / pl.kb_per_split;
   return pl;
@@ -252,15 +245,8 @@ void check_mat(const at::Tensor& t, const char* name) {
 
 }  // namespace
 
-// Floats of fp32 workspace and ints of counters a call with these shapes needs.
-std::pair<int64_t, int64_t> skinny_workspace(int M, int N, int K, int sms, int max_splits) {
-  Plan pl = plan(M, N, K, sms, max_splits);
-  if (pl.splits == 1) return {0, pl.tiles};
-  return {int64_t(pl.splits) * pl.tiles * pl.mp * kWRows, pl.tiles};
-}
-
-void skinny_gemm(const at::Tensor& X, const at::Tensor& W, at::Tensor& Y, at::Tensor& ws, at::Tensor& counters,
-                 at::Tensor& err, int mode, int max_splits) {
+void skinny_gemm(const at::Tensor& X, const at::Tensor& W, at::Tensor& Y, at::Tensor& err, int mode, int max_splits,
+                 bool pdl, const c10::optional<at::Tensor>& stamps) {
   check_mat(X, "X");
   check_mat(W, "W");
   check_mat(Y, "Y");
@@ -272,16 +258,13 @@ void skinny_gemm(const at::Tensor& X, const at::Tensor& W, at::Tensor& Y, at::Te
   if (mode == 1 && (N % kWRows || Y.size(0) != M || Y.size(1) != N / 2))
     throw std::invalid_argument("SwiGLU mode: W rows a multiple of 128 and Y [M, N/2]");
   if (mode != 0 && mode != 1) throw std::invalid_argument("mode must be 0 or 1");
-  if (ws.scalar_type() != at::kFloat || counters.scalar_type() != at::kInt || !ws.is_cuda() || !counters.is_cuda())
-    throw std::invalid_argument("workspace must be CUDA float32 and counters CUDA int32");
   const int dev = X.device().index();
   c10::cuda::CUDAGuard guard(X.device());
   int sms = 0;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   Plan pl = plan(M, N, K, sms, max_splits);
-  const int64_t need_ws = pl.splits == 1 ? 0 : int64_t(pl.splits) * pl.tiles * pl.mp * kWRows;
-  if (ws.numel() < need_ws || counters.numel() < pl.tiles)
-    throw std::invalid_argument("workspace or counters too small (see skinny_workspace)");
+  if (size_t(kWRows) * (pl.mp + 1) * 4 > size_t(pl.stages) * (kWStage + pl.mp * kBK * 2))
+    throw std::logic_error("decode GEMM: the parked partial does not fit the stage buffers");
 
   SkinnyParams p;
   p.M = M;
@@ -293,29 +276,42 @@ void skinny_gemm(const at::Tensor& X, const at::Tensor& W, at::Tensor& Y, at::Te
   p.splits = pl.splits;
   p.tiles = pl.tiles;
   p.mode = mode;
-  p.rot = g_rot;
   p.Y = reinterpret_cast<__nv_bfloat16*>(Y.data_ptr());
   p.ldy = int(Y.stride(0));
-  p.ws = ws.data_ptr<float>();
-  p.counters = counters.data_ptr<int>();
   p.err = reinterpret_cast<uint32_t*>(err.data_ptr());
+  p.stamps = nullptr;
+  if (stamps) {
+    if (!stamps->is_cuda() || stamps->element_size() != 8 || stamps->numel() < int64_t(pl.splits) * pl.tiles * kStamps)
+      throw std::invalid_argument("stamps must be a CUDA 8-byte tensor of splits * tiles * 8 entries");
+    p.stamps = reinterpret_cast<uint64_t*>(stamps->data_ptr());
+  }
   CUtensorMap mw = make_map(W.data_ptr(), N, K, W.stride(0), kWRows);
   CUtensorMap mx = make_map(X.data_ptr(), M, K, X.stride(0), pl.mp);
   static int attr_done[64] = {0};
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
     cudaFuncSetAttribute(k_skinny, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    cudaFuncSetAttribute(k_skinny, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     attr_done[dev] = 1;
   }
-  auto s = at::cuda::getCurrentCUDAStream(dev).stream();
-  k_skinny<<<dim3(pl.tiles, pl.splits), kSkThreads, pl.smem, s>>>(mw, mx, p);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.splits, pl.tiles, 1);
+  cfg.blockDim = dim3(kSkThreads, 1, 1);
+  cfg.dynamicSmemBytes = size_t(pl.smem);
+  cfg.stream = at::cuda::getCurrentCUDAStream(dev).stream();
+  cudaLaunchAttribute attrs[2];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = pl.splits;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 2;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k_skinny, mw, mx, p);
   if (e != cudaSuccess) throw std::runtime_error(std::string("skinny_gemm launch: ") + cudaGetErrorString(e));
 }
 
-void skinny_tune(int ctas_per_sm, int rotation) {
-  g_cps = ctas_per_sm;
-  g_rot = rotation;
-}
+void skinny_tune(int ctas_per_sm) { g_cps = ctas_per_sm; }
 
 std::vector<int> skinny_plan(int M, int N, int K, int sms, int max_splits) {
   Plan pl = plan(M, N, K, sms, max_splits);
@@ -326,13 +322,11 @@ std::vector<int> skinny_plan(int M, int N, int K, int sms, int max_splits) {
 }  // namespace sn
 
 void register_skinny(py::module_& m) {
-  m.def("skinny_gemm", &sn::tc::skinny_gemm, py::arg("X"), py::arg("W"), py::arg("Y"), py::arg("ws"),
-        py::arg("counters"), py::arg("err"), py::arg("mode") = 0, py::arg("max_splits") = 0,
-        "Y = X @ W.T for few token rows (tcgen05, split-K, optional SwiGLU epilogue)");
-  m.def("skinny_workspace", &sn::tc::skinny_workspace, py::arg("M"), py::arg("N"), py::arg("K"), py::arg("sms"),
-        py::arg("max_splits") = 0);
-  m.def("skinny_tune", &sn::tc::skinny_tune, py::arg("ctas_per_sm") = 0, py::arg("rotation") = 0,
-        "process-wide decode GEMM tuning: CTAs per SM (0 = by token count) and K-block rotation per tile");
+  m.def("skinny_gemm", &sn::tc::skinny_gemm, py::arg("X"), py::arg("W"), py::arg("Y"), py::arg("err"),
+        py::arg("mode") = 0, py::arg("max_splits") = 0, py::arg("pdl") = false, py::arg("stamps") = py::none(),
+        "Y = X @ W.T for few token rows (tcgen05, split-K reduced in a cluster, optional SwiGLU epilogue)");
+  m.def("skinny_tune", &sn::tc::skinny_tune, py::arg("ctas_per_sm") = 0,
+        "process-wide decode GEMM tuning: CTAs per SM (0 = by token count)");
   m.def("skinny_plan", &sn::tc::skinny_plan, py::arg("M"), py::arg("N"), py::arg("K"), py::arg("sms"),
         py::arg("max_splits") = 0);
 }

@@ -41,7 +41,7 @@ static inline size_t scratch_floats(int B, int Hq, int Hkv, int max_len, int sms
 }
 
 // ---------------------------------------------------------------------------
-// Split-KV decode attention.  grid (B * Hkv, nsplit), block 128 threads.
+// Split-KV decode attention.  grid (B * Hkv, nsplit), block 256 threads.
 // q: [B, Hq, 128] with Hq = G * Hkv; caches [B, Lmax, Hkv, 128]; lengths [B]; out
 // [B, Hq, 128].  Each block streams its span of keys in tiles of 32 keys: the K and
 // V rows of two tiles are in flight at once (cp.async, 16 bytes per copy, double
@@ -62,23 +62,31 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool va
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
+constexpr int kAttnThreads = 256;  // 8 warps
+
 template <int G>
-static __global__ void __launch_bounds__(128) k_decode_attn(const __nv_bfloat16* __restrict__ q,
-                                                            const __nv_bfloat16* __restrict__ k_cache,
-                                                            const __nv_bfloat16* __restrict__ v_cache,
-                                                            const int* __restrict__ lengths,
-                                                            __nv_bfloat16* __restrict__ out, int* counters,
-                                                            float* part_o, float* part_ml, int Hkv, int Lmax,
-                                                            int chunk, float scale_log2) {
-  __shared__ float qs[G][kHead];
+static __global__ void __launch_bounds__(kAttnThreads) k_decode_attn(const __nv_bfloat16* __restrict__ q,
+                                                                     const __nv_bfloat16* __restrict__ k_cache,
+                                                                     const __nv_bfloat16* __restrict__ v_cache,
+                                                                     const int* __restrict__ lengths,
+                                                                     __nv_bfloat16* __restrict__ out, int* counters,
+                                                                     float* part_o, float* part_ml, int Hkv, int Lmax,
+                                                                     int chunk, float scale_log2) {
+  // Roles.  Scores: warp w owns heads w, w + 8 (G = 16); lane = key of the tile.  P V:
+  // thread t owns dimensions 2*(t % 64), +1 of heads t / 64, t / 64 + 4, ...
+  constexpr int kHW = (G + 7) / 8;     // heads per warp in the score phase
+  constexpr int kHT = (G + 3) / 4;     // heads per thread in the P V phase
+  __shared__ __align__(16) float qs[G][kHead];
   __shared__ __align__(16) __nv_bfloat16 kt[2][kTile][kRowPad];
   __shared__ __align__(16) __nv_bfloat16 vt[2][kTile][kRowPad];
-  __shared__ float ps[G][kTile];
+  __shared__ __align__(16) float ps[G][kTile];
   __shared__ float corr[G];
   __shared__ float mls[G][2];
   __shared__ int last;
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // a PDL-launched successor may start early
   const int b = blockIdx.x / Hkv, h = blockIdx.x % Hkv, s = blockIdx.y, nsplit = gridDim.y;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int dp = t & 63, hg = t >> 6;
   const int Hq = G * Hkv;
   const int len = min(lengths[b], Lmax);
   const int start = s * chunk, end = min(start + chunk, len);
@@ -87,13 +95,13 @@ static __global__ void __launch_bounds__(128) k_decode_attn(const __nv_bfloat16*
   const __nv_bfloat16* kbase = k_cache + (size_t(b) * Lmax * Hkv + h) * kHead;
   const __nv_bfloat16* vbase = v_cache + (size_t(b) * Lmax * Hkv + h) * kHead;
 
-  // one tile = 32 keys x 256 bytes of K and of V = 1024 copies of 16 bytes, 8 per thread
+  // one tile = 32 keys x 256 bytes of K and of V = 1024 copies of 16 bytes, 4 per thread
   auto issue = [&](int tile_idx) {
     if (tile_idx < ntiles) {
       const int k0 = start + tile_idx * kTile, buf = tile_idx & 1;
 #pragma unroll
-      for (int r = 0; r < (kTile * kHead / 8) / 128; ++r) {
-        const int i = r * 128 + t, key = i / (kHead / 8), c = i % (kHead / 8);
+      for (int r = 0; r < (kTile * kHead / 8) / kAttnThreads; ++r) {
+        const int i = r * kAttnThreads + t, key = i / (kHead / 8), c = i % (kHead / 8);
         const bool valid = k0 + key < end;
         const size_t off = size_t(valid ? k0 + key : start) * row_stride + c * 8;
         cp_async16(&kt[buf][key][c * 8], kbase + off, valid);
@@ -104,97 +112,133 @@ static __global__ void __launch_bounds__(128) k_decode_attn(const __nv_bfloat16*
   };
   issue(0);
   issue(1);
-  for (int i = t; i < G * kHead; i += blockDim.x) {
-    int g = i / kHead, d = i % kHead;
+  for (int i = t; i < G * kHead; i += kAttnThreads) {
+    const int g = i / kHead, d = i % kHead;
     qs[g][d] = bf(q[(size_t(b) * Hq + h * G + g) * kHead + d]) * scale_log2;
   }
-  // per-head running max / sum live in the warp that owns the head (g = warp + 4j)
-  float m[(G + 3) / 4], l[(G + 3) / 4];
+  float m[kHW], l[kHW];
 #pragma unroll
-  for (int j = 0; j < (G + 3) / 4; ++j) {
+  for (int j = 0; j < kHW; ++j) {
     m[j] = -INFINITY;
     l[j] = 0.0f;
   }
-  float acc[G];
+  float2 acc[kHT];
 #pragma unroll
-  for (int g = 0; g < G; ++g) acc[g] = 0.0f;
+  for (int i = 0; i < kHT; ++i) acc[i] = make_float2(0.0f, 0.0f);
 
   for (int it = 0; it < ntiles; ++it) {
     const int buf = it & 1;
     const int nk = min(kTile, end - (start + it * kTile));
     cp_async_wait1();
     __syncthreads();
-    // scores and online softmax: warp w owns heads w, w + 4, ...; lane = key
+    // scores + online softmax, one K row per lane, loaded once for the warp's heads
+    if (warp < G) {
+      float dot[kHW];
 #pragma unroll
-    for (int j = 0; j < (G + 3) / 4; ++j) {
-      const int g = warp + 4 * j;
-      if (g < G) {
-        float sc = -INFINITY;
-        if (lane < nk) {
-          float dot = 0.0f;
+      for (int j = 0; j < kHW; ++j) dot[j] = 0.0f;
 #pragma unroll
-          for (int c = 0; c < kHead / 8; ++c) {
-            uint4 kv = *reinterpret_cast<const uint4*>(&kt[buf][lane][c * 8]);
-            const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kv);
+      for (int c = 0; c < kHead / 8; ++c) {
+        const uint4 kv = *reinterpret_cast<const uint4*>(&kt[buf][lane][c * 8]);
+        const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kv);
+        float kf[8];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              float2 kf = __bfloat1622float2(k2[e]);
-              dot += qs[g][c * 8 + 2 * e] * kf.x + qs[g][c * 8 + 2 * e + 1] * kf.y;
-            }
-          }
-          sc = dot;
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(k2[e]);
+          kf[2 * e] = f.x;
+          kf[2 * e + 1] = f.y;
         }
-        float tmax = sc;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
-        const float mnew = fmaxf(m[j], tmax);
-        const float p = lane < nk ? exp2f(sc - mnew) : 0.0f;
-        float psum = p;
+        for (int j = 0; j < kHW; ++j) {
+          const int g = warp + 8 * j;
+          if (g < G) {
+            const float4 qa = *reinterpret_cast<const float4*>(&qs[g][c * 8]);
+            const float4 qb = *reinterpret_cast<const float4*>(&qs[g][c * 8 + 4]);
+            dot[j] += qa.x * kf[0] + qa.y * kf[1] + qa.z * kf[2] + qa.w * kf[3] + qb.x * kf[4] + qb.y * kf[5] +
+                      qb.z * kf[6] + qb.w * kf[7];
+          }
+        }
+      }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
-        const float cf = exp2f(m[j] - mnew);  // m = -inf first: exp2(-inf) = 0
-        l[j] = l[j] * cf + psum;
-        m[j] = mnew;
-        ps[g][lane] = p;
-        if (lane == 0) corr[g] = cf;
+      for (int j = 0; j < kHW; ++j) {
+        const int g = warp + 8 * j;
+        if (g < G) {
+          const float sc = lane < nk ? dot[j] : -INFINITY;
+          float tmax = sc;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
+          const float mnew = fmaxf(m[j], tmax);
+          const float pr = lane < nk ? exp2f(sc - mnew) : 0.0f;
+          float psum = pr;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+          const float cf = exp2f(m[j] - mnew);  // m = -inf first: exp2(-inf) = 0
+          l[j] = l[j] * cf + psum;
+          m[j] = mnew;
+          ps[g][lane] = pr;
+          if (lane == 0) corr[g] = cf;
+        }
       }
     }
     __syncthreads();
-    // P V: thread t owns dimension t of every head of the group
+    // P V: a V pair loaded once, used for every head of the thread
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float a = acc[g] * corr[g];
-      for (int key = 0; key < nk; ++key) a += ps[g][key] * bf(vt[buf][key][t]);
-      acc[g] = a;
+    for (int i = 0; i < kHT; ++i) {
+      const int g = hg + 4 * i;
+      if (g < G) {
+        const float cf = corr[g];
+        acc[i].x *= cf;
+        acc[i].y *= cf;
+      }
     }
-    __syncthreads();  // buffer `buf` is free again
+    for (int key = 0; key < nk; ++key) {
+      const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vt[buf][key][2 * dp]));
+#pragma unroll
+      for (int i = 0; i < kHT; ++i) {
+        const int g = hg + 4 * i;
+        if (g < G) {
+          const float pr = ps[g][key];
+          acc[i].x = fmaf(pr, v.x, acc[i].x);
+          acc[i].y = fmaf(pr, v.y, acc[i].y);
+        }
+      }
+    }
+    __syncthreads();  // buffer `buf` and ps are free again
     issue(it + 2);
   }
+  if (warp < G && lane == 0) {
 #pragma unroll
-  for (int j = 0; j < (G + 3) / 4; ++j) {
-    const int g = warp + 4 * j;
-    if (g < G && lane == 0) {
-      mls[g][0] = m[j];
-      mls[g][1] = l[j];
+    for (int j = 0; j < kHW; ++j) {
+      const int g = warp + 8 * j;
+      if (g < G) {
+        mls[g][0] = m[j];
+        mls[g][1] = l[j];
+      }
     }
   }
   __syncthreads();
   const size_t head0 = size_t(b) * Hq + h * G;
   if (nsplit == 1) {
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float L = mls[g][1];
-      out[(head0 + g) * kHead + t] = __float2bfloat16_rn(L > 0.0f ? acc[g] / L : 0.0f);
+    for (int i = 0; i < kHT; ++i) {
+      const int g = hg + 4 * i;
+      if (g < G) {
+        const float L = mls[g][1], inv = L > 0.0f ? 1.0f / L : 0.0f;
+        *reinterpret_cast<__nv_bfloat162*>(out + (head0 + g) * kHead + 2 * dp) =
+            __floats2bfloat162_rn(acc[i].x * inv, acc[i].y * inv);
+      }
     }
     return;
   }
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const size_t row = (head0 + g) * nsplit + s;
-    __stcg(part_o + row * kHead + t, acc[g]);
-    if (t == 0) {
-      __stcg(part_ml + row * 2, mls[g][0]);
-      __stcg(part_ml + row * 2 + 1, mls[g][1]);
+  for (int i = 0; i < kHT; ++i) {
+    const int g = hg + 4 * i;
+    if (g < G) {
+      const size_t row = (head0 + g) * nsplit + s;
+      __stcg(reinterpret_cast<float2*>(part_o + row * kHead + 2 * dp), acc[i]);
+      if (dp == 0) {
+        __stcg(part_ml + row * 2, mls[g][0]);
+        __stcg(part_ml + row * 2 + 1, mls[g][1]);
+      }
     }
   }
   __threadfence();
@@ -204,15 +248,15 @@ static __global__ void __launch_bounds__(128) k_decode_attn(const __nv_bfloat16*
   if (!last) return;
   __threadfence();
   // Merge the spans of each head in span order.  Every load is issued before any sum
-  // depends on it: (max, sum) pairs first (one per thread), then the weights in shared
-  // memory, then the partial outputs in batches of kMergeBatch spans.
+  // depends on it: (max, sum) pairs first, then the weights in shared memory, then the
+  // partial outputs in batches of kMergeBatch spans.
   asm volatile("cp.async.wait_all;" ::: "memory");
   float(*wts)[kMaxSplits] = reinterpret_cast<float(*)[kMaxSplits]>(&kt[0][0][0]);  // K tiles are free now
   static_assert(sizeof(float) * G * kMaxSplits <= sizeof(kt), "merge weights must fit the K tile buffers");
   __shared__ float lsum[G];
-  for (int i = t; i < G * nsplit; i += blockDim.x) {
+  for (int i = t; i < G * nsplit; i += kAttnThreads) {
     const int g = i / nsplit, sp = i % nsplit;
-    wts[g][sp] = __ldcg(part_ml + ((head0 + g) * nsplit + sp) * 2);      // max (log2 units)
+    wts[g][sp] = __ldcg(part_ml + ((head0 + g) * nsplit + sp) * 2);  // max (log2 units)
   }
   __syncthreads();
   if (t < G) {
@@ -228,20 +272,26 @@ static __global__ void __launch_bounds__(128) k_decode_attn(const __nv_bfloat16*
     lsum[t] = L;
   }
   __syncthreads();
-#pragma unroll 1
-  for (int g = 0; g < G; ++g) {
-    const float* po = part_o + (head0 + g) * nsplit * kHead + t;
-    float o = 0.0f;
-    for (int sp0 = 0; sp0 < nsplit; sp0 += kMergeBatch) {
-      float v[kMergeBatch];
 #pragma unroll
-      for (int j = 0; j < kMergeBatch; ++j) v[j] = sp0 + j < nsplit ? __ldcg(po + (sp0 + j) * kHead) : 0.0f;
+  for (int i = 0; i < kHT; ++i) {
+    const int g = hg + 4 * i;
+    if (g >= G) continue;
+    const float* po = part_o + (head0 + g) * nsplit * kHead + 2 * dp;
+    float2 o = make_float2(0.0f, 0.0f);
+    for (int sp0 = 0; sp0 < nsplit; sp0 += kMergeBatch) {
+      float2 v[kMergeBatch];
 #pragma unroll
       for (int j = 0; j < kMergeBatch; ++j)
-        if (sp0 + j < nsplit) o += v[j] * wts[g][sp0 + j];
+        v[j] = sp0 + j < nsplit ? __ldcg(reinterpret_cast<const float2*>(po + (sp0 + j) * kHead)) : make_float2(0, 0);
+#pragma unroll
+      for (int j = 0; j < kMergeBatch; ++j)
+        if (sp0 + j < nsplit) {
+          o.x += v[j].x * wts[g][sp0 + j];
+          o.y += v[j].y * wts[g][sp0 + j];
+        }
     }
-    const float L = lsum[g];
-    out[(head0 + g) * kHead + t] = __float2bfloat16_rn(L > 0.0f ? o / L : 0.0f);
+    const float L = lsum[g], inv = L > 0.0f ? 1.0f / L : 0.0f;
+    *reinterpret_cast<__nv_bfloat162*>(out + (head0 + g) * kHead + 2 * dp) = __floats2bfloat162_rn(o.x * inv, o.y * inv);
   }
   if (t == 0) counters[blockIdx.x] = 0;
 }
@@ -265,8 +315,8 @@ static inline cudaError_t launch_decode_attention(const __nv_bfloat16* q, const 
   switch (G) {
 #define SN_ATT(GG)                                                                                              \
   case GG:                                                                                                      \
-    k_decode_attn<GG><<<grid, 128, 0, st>>>(q, k_cache, v_cache, lengths, out, counters, part_o, part_ml, Hkv,   \
-                                            Lmax, chunk, scale_log2);                                           \
+    k_decode_attn<GG><<<grid, kAttnThreads, 0, st>>>(q, k_cache, v_cache, lengths, out, counters, part_o,     \
+                                                     part_ml, Hkv, Lmax, chunk, scale_log2);                    \
     break;
     SN_ATT(1)
     SN_ATT(2)

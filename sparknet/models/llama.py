@@ -69,7 +69,8 @@ class TPLlama:
     """One rank's shard of the model plus its KV cache and decode buffers."""
 
     def __init__(self, cfg: LlamaConfig, *, rank: int, world: int, device, batch: int, max_len: int,
-                 comm: str = "sparknet", runtime=None, group=None, seed: int = 0, gemm: str | None = None):
+                 comm: str = "sparknet", runtime=None, group=None, seed: int = 0, gemm: str | None = None,
+                 pdl: bool = True):
         if cfg.heads % world or cfg.kv_heads % world or cfg.ffn % world or cfg.vocab % world:
             raise ValueError(f"model does not shard evenly over {world} GPUs")
         if comm not in ("sparknet", "nccl"):
@@ -116,11 +117,7 @@ class TPLlama:
         # zeroed: the attention kernel's split counters sit at its front
         self.workspace = torch.zeros(int(self.C.attention_workspace_floats(batch, self.hq, self.hkv, max_len, sms)),
                                      dtype=torch.float32, device=dev)
-        self.mm = DecodeGemm(dev)
-        if gemm == "sparknet":
-            for n, k in (((self.hq + 2 * self.hkv) * D, H), (H, self.hq * D), (2 * self.f, H), (H, self.f),
-                         (self.v, H)):
-                self.mm.reserve(batch, n, k)
+        self.mm = DecodeGemm(dev, pdl=pdl)
         # static decode buffers (graph inputs/outputs)
         self.tokens = torch.zeros(batch, dtype=torch.int64, device=dev)
         self.positions = torch.zeros(batch, dtype=torch.int32, device=dev)

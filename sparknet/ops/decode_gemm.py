@@ -3,16 +3,17 @@
 ``w`` is in ``nn.Linear`` layout ``[out_features, in_features]`` (bf16, K-major) and
 ``x`` is ``[tokens, in_features]`` with 1..256 tokens.  The kernel (``csrc/gemm_skinny.cu``)
 streams the weight through TMA into 128-row tiles that are the MMA's M side, splits K
-so one wave covers the GPU, and reduces the split partials in a fixed order.
+so one wave covers the GPU, and sums the split partials of a tile inside a thread-block
+cluster through distributed shared memory, in a fixed order (no global scratch).
 
 ``swiglu=True`` fuses the SwiGLU activation: ``w`` is a gate/up weight in the
 interleaved layout :func:`interleave_gate_up` builds ([64 gate rows; 64 up rows] per
 128-row tile) and the result is ``silu(x @ gate.T) * (x @ up.T)`` of width
 ``out_features / 2``, with no intermediate tensor.
 
-Split-K partials need a workspace; :class:`DecodeGemm` owns one per device and stream
-and grows it outside graph capture only (call :meth:`DecodeGemm.reserve` with the
-largest shape before capturing).
+With ``pdl=True`` the launch uses programmatic dependent launch: the kernel may start
+while the previous kernel on the stream is finishing and streams its first weight tiles
+before it waits for that kernel's results (weights never depend on it).
 """
 
 from __future__ import annotations
@@ -41,36 +42,24 @@ def split_gate_up(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 
 
 class DecodeGemm:
-    """Workspace owner for the decode GEMM on one device."""
+    """The decode GEMM on one device (holds the error word)."""
 
-    def __init__(self, device, max_splits: int = 0):
+    def __init__(self, device, max_splits: int = 0, pdl: bool = False):
         self.device = torch.device(device)
         if self.device.index is None:
             self.device = torch.device("cuda", torch.cuda.current_device())
         self.C = _native.load()
-        self.sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.max_splits = int(max_splits)
-        self.ws = torch.empty(0, dtype=torch.float32, device=self.device)
-        self.counters = torch.zeros(0, dtype=torch.int32, device=self.device)
+        self.pdl = bool(pdl)
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
-
-    def reserve(self, m: int, n: int, k: int) -> None:
-        """Grow the workspace for an ``[m, k] x [n, k]^T`` call (not during capture)."""
-        ws, cnt = self.C.skinny_workspace(m, n, k, self.sms, self.max_splits)
-        if ws > self.ws.numel() or cnt > self.counters.numel():
-            if torch.cuda.is_current_stream_capturing():
-                raise RuntimeError("decode GEMM workspace must be reserved before CUDA graph capture")
-            self.ws = torch.empty(max(ws, self.ws.numel()), dtype=torch.float32, device=self.device)
-            self.counters = torch.zeros(max(cnt, self.counters.numel()), dtype=torch.int32, device=self.device)
 
     def __call__(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, *,
                  swiglu: bool = False) -> torch.Tensor:
-        M, K = x.shape
+        M = x.shape[0]
         N = w.shape[0]
         if out is None:
             out = torch.empty((M, N // 2 if swiglu else N), dtype=torch.bfloat16, device=x.device)
-        self.reserve(M, N, K)
-        self.C.skinny_gemm(x, w, out, self.ws, self.counters, self.err, 1 if swiglu else 0, self.max_splits)
+        self.C.skinny_gemm(x, w, out, self.err, 1 if swiglu else 0, self.max_splits, self.pdl)
         return out
 
     def check(self) -> None:
@@ -86,7 +75,7 @@ _default: dict = {}
 
 def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, *, swiglu: bool = False) -> torch.Tensor:
     """``x @ w.T`` (or the fused SwiGLU of an interleaved gate/up weight) for decode."""
-    key = (x.device.index, torch.cuda.current_stream(x.device).cuda_stream)
+    key = x.device.index
     op = _default.get(key)
     if op is None:
         op = _default[key] = DecodeGemm(x.device)

@@ -45,13 +45,18 @@ def quantize_weight(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return q, sf
 
 
-def scales_to_dense(sf: torch.Tensor, rows: int, k: int) -> torch.Tensor:
-    """fp32 ``[rows, k // 128]`` scale of every (row, 128-column block)."""
+def scale_exponents(sf: torch.Tensor, rows: int, k: int) -> torch.Tensor:
+    """UE8M0 exponent byte ``[rows, k // 128]`` of every (row, 128-column block)."""
     kb = k // 128
     rb = (rows + 127) // 128
     chunk = sf[: rb * kb * 512].view(rb, kb, 32, 4, 4)            # [rb, kb, i, g, j] (row = 32 g + i)
-    e = chunk[..., 0].permute(0, 3, 2, 1).reshape(rb * 128, kb)     # byte j = 0: the block's exponent
-    return torch.exp2(e[:rows].float() - 127.0)
+    return chunk[..., 0].permute(0, 3, 2, 1).reshape(rb * 128, kb)[:rows]  # byte j = 0: the block's exponent
+
+
+def scales_to_dense(sf: torch.Tensor, rows: int, k: int) -> torch.Tensor:
+    """fp32 ``[rows, k // 128]`` scale 2^(e - 127) of every (row, 128-column block) (exact)."""
+    e = scale_exponents(sf, rows, k).to(torch.int32) - 127
+    return torch.ldexp(torch.ones(e.shape, dtype=torch.float32, device=e.device), e)
 
 
 def dequantize(q: torch.Tensor, sf: torch.Tensor) -> torch.Tensor:
@@ -77,4 +82,5 @@ def gemm_fp8(aq: torch.Tensor, sfa: torch.Tensor, bq: torch.Tensor, sfb: torch.T
     return out
 
 
-__all__ = ["dequantize", "gemm_fp8", "quantize_act", "quantize_weight", "scale_bytes", "scales_to_dense"]
+__all__ = ["dequantize", "gemm_fp8", "quantize_act", "quantize_weight", "scale_bytes", "scale_exponents",
+           "scales_to_dense"]

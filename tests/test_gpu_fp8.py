@@ -11,10 +11,13 @@ pytestmark = pytest.mark.gpu
 
 
 def _ue8m0(amax: torch.Tensor) -> torch.Tensor:
-    """Exponent of the smallest power of two s with amax / s <= 448 (fp32 math)."""
-    t = amax.double() / 448.0
-    e = torch.ceil(torch.log2(t.clamp_min(2.0 ** -126))) + 127
-    return torch.where(amax > 0, e.clamp(1, 254), torch.full_like(e, 127.0))
+    """Exponent of the smallest power of two s with amax / s <= 448, as integers: from
+    the float's exponent and mantissa (no transcendental functions)."""
+    m, ex = torch.frexp(amax.double().cpu())        # amax = m * 2^ex, 0.5 <= m < 1
+    # amax <= 448 * 2^k  <=>  k >= log2(amax / 448); with amax = (2m) * 2^(ex-1) and 448 = 1.75 * 2^8
+    k = (ex.to(torch.int64) - 1 - 8) + (2 * m > 1.75).to(torch.int64)
+    e = (k + 127).clamp(1, 254)
+    return torch.where(amax.cpu() > 0, e, torch.full_like(e, 127))
 
 
 @pytest.mark.parametrize("rows,k", [(200, 256), (128, 1024), (8, 128)])
@@ -26,7 +29,7 @@ def test_quantize_act(device, native, rows, k):
     torch.cuda.synchronize()
     amax = x.float().abs().view(rows, k // 128, 128).amax(-1)
     want_e = _ue8m0(amax)
-    got_e = torch.log2(fp8.scales_to_dense(sf, rows, k).double()) + 127
+    got_e = fp8.scale_exponents(sf, rows, k).to(torch.int64).cpu()
     assert torch.equal(got_e, want_e)
     deq = fp8.dequantize(q, sf)
     scale = fp8.scales_to_dense(sf, rows, k).repeat_interleave(128, 1)
@@ -44,8 +47,8 @@ def test_quantize_weight(device, native):
     torch.cuda.synchronize()
     s = fp8.scales_to_dense(sf, N, K)
     amax = w.float().abs().view(N // 128, 128, K // 128, 128).amax((1, 3))
-    want = torch.exp2(_ue8m0(amax) - 127).float().repeat_interleave(128, 0)
-    assert torch.equal(s, want)
+    want_e = _ue8m0(amax).repeat_interleave(128, 0)
+    assert torch.equal(fp8.scale_exponents(sf, N, K).to(torch.int64).cpu(), want_e)
     deq = fp8.dequantize(q, sf)
     scale = s.repeat_interleave(128, 1)
     assert ((deq - w.float()).abs() <= w.float().abs() * 2 ** -4 + scale * 2 ** -9).all()
