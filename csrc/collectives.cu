@@ -163,11 +163,11 @@ SN_DEV void allreduce_body(const Job& j, int algo) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(1024) k_allreduce(Job j, int algo) {
+__global__ void __launch_bounds__(kMaxThreads) k_allreduce(Job j, int algo) {
   allreduce_body<D>(j, algo);
 }
 template <int D>
-__global__ void __launch_bounds__(1024) k_allreduce_emu(Job j, EmuViews e, int algo) {
+__global__ void __launch_bounds__(kMaxThreads) k_allreduce_emu(Job j, EmuViews e, int algo) {
   allreduce_body<D>(emulated(j, e), algo);
 }
 
@@ -192,9 +192,9 @@ SN_DEV void reducescatter_body(const Job& j) {
   leave(j, seq);
 }
 template <int D>
-__global__ void __launch_bounds__(1024) k_reducescatter(Job j) { reducescatter_body<D>(j); }
+__global__ void __launch_bounds__(kMaxThreads) k_reducescatter(Job j) { reducescatter_body<D>(j); }
 template <int D>
-__global__ void __launch_bounds__(1024) k_reducescatter_emu(Job j, EmuViews e) {
+__global__ void __launch_bounds__(kMaxThreads) k_reducescatter_emu(Job j, EmuViews e) {
   reducescatter_body<D>(emulated(j, e));
 }
 
@@ -244,8 +244,8 @@ SN_DEV void gather_body(const Job& j, int algo, int op) {
   leave(j, seq);
 }
 
-__global__ void __launch_bounds__(1024) k_gather(Job j, int algo, int op) { gather_body(j, algo, op); }
-__global__ void __launch_bounds__(1024) k_gather_emu(Job j, EmuViews e, int algo, int op) {
+__global__ void __launch_bounds__(kMaxThreads) k_gather(Job j, int algo, int op) { gather_body(j, algo, op); }
+__global__ void __launch_bounds__(kMaxThreads) k_gather_emu(Job j, EmuViews e, int algo, int op) {
   gather_body(emulated(j, e), algo, op);
 }
 

@@ -114,6 +114,8 @@ class Comm {
 
   // -- geometry (rank-invariant: depends on sizes and world only) ---------------
   LaunchGeom geom(uint64_t items, int threads, int max_blocks) const {
+    if (threads < 32 || threads > kMaxThreads || threads % 32)
+      throw std::invalid_argument("threads must be a multiple of 32 between 32 and " + std::to_string(kMaxThreads));
     LaunchGeom g;
     g.threads = threads;
     int cap = max_blocks > 0 ? max_blocks : sms_;
@@ -311,7 +313,9 @@ class Comm {
       throw std::invalid_argument("tokens exceed fused one-shot capacity");
     }
     int cta_packs = int(H / elems / cluster);
-    if (cta_packs > 1024) throw std::invalid_argument("hidden too large for the cluster size");
+    if (cta_packs > kMaxThreads)
+      throw std::invalid_argument("hidden too large for the cluster size (at most " + std::to_string(kMaxThreads) +
+                                  " packs of 16 bytes per CTA: use a larger cluster)");
     LaunchGeom g;
     g.threads = std::max(32, (cta_packs + 31) / 32 * 32);
     int nclusters = int(std::min<int64_t>(T, max_clusters > 0 ? max_clusters : 64));
@@ -476,6 +480,7 @@ void register_gemm(py::module_& m);
 void register_decode(py::module_& m);
 void register_skinny(py::module_& m);
 void register_fp8(py::module_& m);
+void register_microbench(py::module_& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   using namespace sn;
@@ -560,4 +565,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_decode(m);
   register_skinny(m);
   register_fp8(m);
+  register_microbench(m);
 }

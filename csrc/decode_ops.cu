@@ -3,12 +3,13 @@
 //   rope_qkv_cache : split the fused QKV projection, rotate q and k (RoPE, rotate-half
 //                    form, cos/sin from a table), write k and v into the KV cache at
 //                    each sequence's position, emit the rotated q.
-//   decode_attention (+ combine): split-KV flash decoding for grouped-query attention
-//                    (one query token per sequence).  Each block takes one (sequence,
+//   decode_attention : split-KV flash decoding for grouped-query attention, one query
+//                    token per sequence, one launch.  Each block takes one (sequence,
 //                    KV head) and one span of the cache, keeps the group's G query
 //                    heads in shared memory, and writes unnormalised partial outputs
-//                    and (max, sum) pairs into a workspace; the combine kernel merges
-//                    the spans with their log-sum-exp weights.
+//                    and (max, sum) pairs into a workspace; the last block of each
+//                    (sequence, KV head) merges the spans with their log-sum-exp
+//                    weights (kernels in attention_kernels.cuh).
 //   add_rmsnorm    : residual add + RMSNorm of rows (the unfused epilogue, used by the
 //                    NCCL arm and the first layer), same rounding points as the fused
 //                    all-reduce kernel.
@@ -234,7 +235,8 @@ void rope_qkv_cache(const at::Tensor& qkv, const at::Tensor& cos_t, const at::Te
 // workspace: float32, sn::attn::scratch_floats() long, its first kCounterSlots ints zero
 // before the first call (every completed call leaves them zero).
 void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
-                      const at::Tensor& lengths, at::Tensor& out, at::Tensor& workspace, int max_len, double scale) {
+                      const at::Tensor& lengths, at::Tensor& out, at::Tensor& workspace, int max_len, double scale,
+                      bool pdl) {
   check_bf16(q, "q");
   check_bf16(out, "out");
   int B = int(q.size(0)), Hq = int(q.size(1)), Hkv = int(k_cache.size(2)), Lmax = int(k_cache.size(1));
@@ -253,7 +255,7 @@ void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::
       reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr()),
       reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr()), lengths.data_ptr<int>(),
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), workspace.data_ptr<float>(), B, Hq, Hkv, Lmax, max_len,
-      float(scale), sms, stream_of(q));
+      float(scale), sms, stream_of(q), pdl);
   if (e != cudaSuccess) throw std::runtime_error(std::string("decode_attention launch: ") + cudaGetErrorString(e));
 }
 
@@ -312,7 +314,10 @@ void row_argmax(const at::Tensor& logits, int index_offset, at::Tensor& out) {
 
 void register_decode(py::module_& m) {
   m.def("rope_qkv_cache", &rope_qkv_cache);
-  m.def("decode_attention", &decode_attention);
+  m.def("decode_attention", &decode_attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("lengths"),
+        py::arg("out"), py::arg("workspace"), py::arg("max_len"), py::arg("scale"), py::arg("pdl") = false,
+        "split-KV decode attention; pdl: programmatic dependent launch (keys below lengths[b] - 1 may be "
+        "prefetched while the previous kernel runs, so that kernel must not write them)");
   m.def("attention_workspace_floats", &attention_workspace_floats);
   m.def("add_rmsnorm", &add_rmsnorm, py::arg("x"), py::arg("residual"), py::arg("residual_out"), py::arg("gamma"),
         py::arg("out"), py::arg("eps"));

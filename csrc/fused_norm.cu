@@ -140,16 +140,11 @@ SN_DEV void fused_body(const Job& j, int algo) {
       if (t % W != r) continue;
       const uint64_t i = t * row_packs + tpack;
       const uint64_t slot_pack = (t / W) * row_packs + tpack;
-      Acc a;
-      acc_zero<D>(a);
-      for (uint32_t s = 0; s < W && ok; ++s) {
-        Pack16 v;
-        if (s == r) v = pack_canon<D>(m.ld_input(x + i));
-        else ok = take<D>(m, reinterpret_cast<Pack16*>(lam_slot(j, r, parity, s)) + slot_pack, v, c, s);
-        acc_add<D>(a, v);
-      }
+      Pack16 xs[kMaxRanks];
+      const Pack16 own = pack_canon<D>(m.ld_input(x + i));
+      ok = take_all<DevMem, D>(m, j, c, parity, slot_pack, peers_mask(W, r), xs, 1, 1);
       if (!ok) break;
-      Pack16 y = pack_canon<D>(acc_round<D>(a));
+      Pack16 y = pack_canon<D>(sum_rank_order<D>(own, xs, W, r));
       for (uint32_t k = 1; k < W; ++k) {
         uint32_t q = (r + k) % W;
         m.st_remote(reinterpret_cast<Pack16*>(lam_slot(j, q, parity, r)) + half + slot_pack, y);
@@ -177,15 +172,10 @@ SN_DEV void fused_body(const Job& j, int algo) {
                        owner);
         }
       } else {
-        Acc a;
-        acc_zero<D>(a);
-        for (uint32_t s = 0; s < W && ok; ++s) {
-          Pack16 v;
-          if (s == r) v = pack_canon<D>(m.ld_input(x + i));
-          else ok = take<D>(m, reinterpret_cast<Pack16*>(lam_slot(j, r, parity, s)) + i, v, c, s);
-          acc_add<D>(a, v);
-        }
-        sum = acc_round<D>(a);
+        Pack16 xs[kMaxRanks];
+        const Pack16 own = pack_canon<D>(m.ld_input(x + i));
+        ok = take_all<DevMem, D>(m, j, c, parity, i, peers_mask(W, r), xs, 1, 1);
+        if (ok) sum = sum_rank_order<D>(own, xs, W, r);
       }
       // residual add (rounded once, as the unfused add would be)
       Acc a;
@@ -221,13 +211,13 @@ SN_DEV void fused_body(const Job& j, int algo) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(1024) k_fused(Job j, int algo) {
+__global__ void __launch_bounds__(kMaxThreads) k_fused(Job j, int algo) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // a PDL-launched successor may start early
   fused_body<D>(j, algo);
 }
 
 template <int D>
-__global__ void __launch_bounds__(1024) k_fused_emu(Job j, EmuViews e, int algo) {
+__global__ void __launch_bounds__(kMaxThreads) k_fused_emu(Job j, EmuViews e, int algo) {
   fused_body<D>(emulated(j, e, blockIdx.y), algo);
 }
 

@@ -162,6 +162,9 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
   mbar_wait(done, 0, err);
   tc_fence_after();
   if (threadIdx.x == 64) stamp(p, 5);  // accumulator complete
+  // a PDL-launched successor may launch now: it still waits for this grid to finish
+  // before it reads anything this kernel writes
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // TMEM lane = weight row within the tile; warp w may read lanes 32w..32w+31.  Park
   // the partial (all stage reads and MMAs are complete: `done` fired).
@@ -182,14 +185,19 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
   cluster.sync();  // every split's partial is parked
   if (threadIdx.x == 64) stamp(p, 6);
 
+  // Every DSMEM load of an output element is issued before the fixed-order sum.
   if (p.mode == 0) {
     // this CTA's rows: r = split, split + S, ...; thread -> (row, column) pairs
     const int my_rows = (kWRows - split + S - 1) / S;
     for (int e = threadIdx.x; e < my_rows * p.M; e += blockDim.x) {
       const int r = split + (e / p.M) * S, m = e % p.M;
       const int n = tile * kWRows + r;
+      float v[kMaxSplits];
+#pragma unroll
+      for (int s = 0; s < kMaxSplits; ++s) v[s] = s < S ? cluster.map_shared_rank(part, s)[r * pitch + m] : 0.0f;
       float acc = 0.0f;
-      for (int s = 0; s < S; ++s) acc += cluster.map_shared_rank(part, s)[r * pitch + m];
+#pragma unroll
+      for (int s = 0; s < kMaxSplits; ++s) acc += v[s];
       if (n < p.N) p.Y[size_t(m) * p.ldy + n] = __float2bfloat16_rn(acc);
     }
   } else {
@@ -197,16 +205,22 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
     const int my_rows = (64 - split + S - 1) / S;
     for (int e = threadIdx.x; e < my_rows * p.M; e += blockDim.x) {
       const int r = split + (e / p.M) * S, m = e % p.M;
+      float vg[kMaxSplits], vu[kMaxSplits];
+#pragma unroll
+      for (int s = 0; s < kMaxSplits; ++s) {
+        const float* ps = cluster.map_shared_rank(part, s < S ? s : 0);
+        vg[s] = s < S ? ps[r * pitch + m] : 0.0f;
+        vu[s] = s < S ? ps[(r + 64) * pitch + m] : 0.0f;
+      }
       float g = 0.0f, u = 0.0f;
-      for (int s = 0; s < S; ++s) {
-        const float* ps = cluster.map_shared_rank(part, s);
-        g += ps[r * pitch + m];
-        u += ps[(r + 64) * pitch + m];
+#pragma unroll
+      for (int s = 0; s < kMaxSplits; ++s) {
+        g += vg[s];
+        u += vu[s];
       }
       p.Y[size_t(m) * p.ldy + tile * 64 + r] = __float2bfloat16_rn(silu(g) * u);
     }
   }
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   cluster.sync();  // partials stay readable until every CTA of the cluster is done
   if (threadIdx.x == 64) stamp(p, 7);  // exit
   if (warp == 1) tmem_dealloc(tmem, ncols);

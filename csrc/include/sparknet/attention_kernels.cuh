@@ -110,8 +110,16 @@ static __global__ void __launch_bounds__(kAttnThreads) k_decode_attn(const __nv_
     }
     cp_async_commit();  // possibly empty: keeps the group count uniform
   };
-  issue(0);
-  issue(1);
+  // Programmatic dependent launch: K/V tiles wholly below the newest key (lengths[b] - 1,
+  // the one the preceding RoPE kernel writes) are requested before griddepcontrol.wait;
+  // q and everything else after it.  Without PDL the wait returns at once.
+  auto safe = [&](int tile_idx) { return tile_idx < ntiles && start + (tile_idx + 1) * kTile <= len - 1; };
+  const bool pre0 = safe(0), pre1 = pre0 && safe(1);
+  if (pre0) issue(0);
+  if (pre1) issue(1);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (!pre0) issue(0);
+  if (!pre1) issue(1);
   for (int i = t; i < G * kHead; i += kAttnThreads) {
     const int g = i / kHead, d = i % kHead;
     qs[g][d] = bf(q[(size_t(b) * Hq + h * G + g) * kHead + d]) * scale_log2;
@@ -302,7 +310,8 @@ static __global__ void __launch_bounds__(kAttnThreads) k_decode_attn(const __nv_
 static inline cudaError_t launch_decode_attention(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
                                                   const __nv_bfloat16* v_cache, const int* lengths,
                                                   __nv_bfloat16* out, float* scratch, int B, int Hq, int Hkv,
-                                                  int Lmax, int max_len, float scale, int sms, cudaStream_t st) {
+                                                  int Lmax, int max_len, float scale, int sms, cudaStream_t st,
+                                                  bool pdl = false) {
   if (Hkv <= 0 || Hq % Hkv || B * Hkv > kCounterSlots) return cudaErrorInvalidValue;
   const int G = Hq / Hkv;
   const int nsplit = splits(B, Hkv, max_len, sms);
@@ -311,13 +320,21 @@ static inline cudaError_t launch_decode_attention(const __nv_bfloat16* q, const 
   float* part_o = scratch + kCounterSlots;
   float* part_ml = part_o + size_t(B) * Hq * nsplit * kHead;
   const float scale_log2 = scale * kLog2e;
-  const dim3 grid(B * Hkv, nsplit);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(B * Hkv, nsplit, 1);
+  cfg.blockDim = dim3(kAttnThreads, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
   switch (G) {
-#define SN_ATT(GG)                                                                                              \
-  case GG:                                                                                                      \
-    k_decode_attn<GG><<<grid, kAttnThreads, 0, st>>>(q, k_cache, v_cache, lengths, out, counters, part_o,     \
-                                                     part_ml, Hkv, Lmax, chunk, scale_log2);                    \
-    break;
+#define SN_ATT(GG)                                                                                       \
+  case GG:                                                                                               \
+    return cudaLaunchKernelEx(&cfg, k_decode_attn<GG>, q, k_cache, v_cache, lengths, out, counters, part_o, \
+                              part_ml, Hkv, Lmax, chunk, scale_log2);
     SN_ATT(1)
     SN_ATT(2)
     SN_ATT(4)
@@ -327,7 +344,6 @@ static inline cudaError_t launch_decode_attention(const __nv_bfloat16* q, const 
     default:
       return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
 }
 
 }  // namespace attn

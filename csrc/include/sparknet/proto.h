@@ -21,9 +21,11 @@
 #if defined(__CUDACC__)
 #define SN_HD __host__ __device__ __forceinline__
 #define SN_DEV __device__ __forceinline__
+#define SN_UNROLL _Pragma("unroll")
 #else
 #define SN_HD inline
 #define SN_DEV inline
+#define SN_UNROLL
 #endif
 
 namespace sn {
@@ -34,6 +36,8 @@ namespace sn {
 constexpr int kAbiVersion = 4;       // bumped when Layout/Ctrl/Status change
 constexpr int kMaxRanks = 8;         // one NVSwitch box
 constexpr int kMaxBlocks = 256;      // per launch (grid.x)
+constexpr int kMaxThreads = 512;     // per block of the collective kernels: a thread may hold
+                                     // every peer's pack at once (128 registers available)
 constexpr int kPack = 16;            // bytes moved per vector access
 constexpr int kGFlags = 4096;        // per-source chunk/tile flags of the fused GEMMs
 constexpr size_t kPage = 4096;
@@ -434,6 +438,57 @@ SN_HD char* lam_slot(const Job& j, uint32_t owner, uint32_t parity, uint32_t src
 // only after it completed collective s+1, which needed this rank's pushes for s+1,
 // which this rank issues only after its kernel for s (reads and clears) finished.
 // ---------------------------------------------------------------------------
+// Lowest set bit of a non-zero mask (portable between host and device).
+SN_HD uint32_t lowest_bit(uint32_t mask) {
+  uint32_t s = 0;
+  while (!((mask >> s) & 1u)) ++s;
+  return s;
+}
+
+// Consume pack `off` of this rank's Lamport slots [parity][s] for every source s in
+// `mask`: each sweep issues one load per outstanding source before testing any of
+// them, so all sources cost one memory round trip together instead of one each; each
+// slot is re-armed with the sentinel once every source's data is in hand.  xs[s]
+// receives source s's pack.  False if a wait ran out (the failure names the lowest
+// source still outstanding).
+template <class M, int D>
+SN_HD bool take_all(M& m, const Job& j, const OpCtx& c, uint32_t parity, uint64_t off, uint32_t mask,
+                    Pack16 (&xs)[kMaxRanks], uint64_t gtid, uint64_t ti) {
+  const uint32_t r = j.rank;
+  uint32_t pending = mask;
+  WaitState w;
+  while (pending) {
+SN_UNROLL
+    for (uint32_t s = 0; s < uint32_t(kMaxRanks); ++s)
+      if ((pending >> s) & 1u) xs[s] = m.ld_poll(reinterpret_cast<Pack16*>(lam_slot(j, r, parity, s)) + off);
+SN_UNROLL
+    for (uint32_t s = 0; s < uint32_t(kMaxRanks); ++s)
+      if (((pending >> s) & 1u) && pack_arrived<D>(xs[s])) {
+        pending &= ~(1u << s);
+        trace_arrival(m, c, gtid, ti, s);
+      }
+    if (pending && !keep_waiting(m, w, c, lowest_bit(pending))) return false;
+  }
+SN_UNROLL
+  for (uint32_t s = 0; s < uint32_t(kMaxRanks); ++s)
+    if ((mask >> s) & 1u) m.st_local(reinterpret_cast<Pack16*>(lam_slot(j, r, parity, s)) + off, pack_fill(kSentinel));
+  return true;
+}
+
+SN_HD uint32_t peers_mask(uint32_t W, uint32_t r) { return ((W >= 32u ? 0u : (1u << W)) - 1u) & ~(1u << r); }
+
+// Rank-order fp32 sum of the own pack and the peers' packs from take_all.  The loop
+// index is a constant after unrolling, so xs stays in registers.
+template <int D>
+SN_HD Pack16 sum_rank_order(const Pack16& own, const Pack16 (&xs)[kMaxRanks], uint32_t W, uint32_t r) {
+  Acc a;
+  acc_zero<D>(a);
+SN_UNROLL
+  for (uint32_t s = 0; s < uint32_t(kMaxRanks); ++s)
+    if (s < W) acc_add<D>(a, s == r ? own : xs[s]);
+  return acc_round<D>(a);
+}
+
 template <class M, int D>
 SN_HD bool oneshot_allreduce(M& m, const Job& j, const OpCtx& c, uint64_t gtid, uint64_t gstride) {
   const uint64_t packs = j.nbytes / kPack;
@@ -448,27 +503,12 @@ SN_HD bool oneshot_allreduce(M& m, const Job& j, const OpCtx& c, uint64_t gtid, 
       m.st_remote(reinterpret_cast<Pack16*>(lam_slot(j, q, parity, r)) + i, v);
     }
   }
+  const uint32_t peers = peers_mask(W, r);
   for (uint64_t i = gtid; i < packs; i += gstride) {
-    Acc a;
-    acc_zero<D>(a);
-    for (uint32_t s = 0; s < W; ++s) {
-      Pack16 x;
-      if (s == r) {
-        x = pack_canon<D>(m.ld_input(in + i));
-      } else {
-        Pack16* slot = reinterpret_cast<Pack16*>(lam_slot(j, r, parity, s)) + i;
-        WaitState w;
-        for (;;) {
-          x = m.ld_poll(slot);
-          if (pack_arrived<D>(x)) break;
-          if (!keep_waiting(m, w, c, s)) return false;
-        }
-        trace_arrival(m, c, gtid, i, s);
-        m.st_local(slot, pack_fill(kSentinel));
-      }
-      acc_add<D>(a, x);
-    }
-    m.st_output(out + i, acc_round<D>(a));
+    Pack16 xs[kMaxRanks];
+    const Pack16 own = pack_canon<D>(m.ld_input(in + i));
+    if (!take_all<M, D>(m, j, c, parity, i, peers, xs, gtid, i)) return false;
+    m.st_output(out + i, sum_rank_order<D>(own, xs, W, r));
   }
   return true;
 }
@@ -505,25 +545,10 @@ SN_HD bool twoshot_allreduce(M& m, const Job& j, const OpCtx& c, uint64_t gtid, 
   for (uint64_t p = gtid; p < chunk; p += gstride) {
     uint64_t i = uint64_t(r) * chunk + p;
     if (i >= packs) continue;
-    Acc a;
-    acc_zero<D>(a);
-    for (uint32_t s = 0; s < W; ++s) {
-      Pack16 x;
-      if (s == r) {
-        x = pack_canon<D>(m.ld_input(in + i));
-      } else {
-        Pack16* slot = reinterpret_cast<Pack16*>(lam_slot(j, r, parity, s)) + p;
-        WaitState w;
-        for (;;) {
-          x = m.ld_poll(slot);
-          if (pack_arrived<D>(x)) break;
-          if (!keep_waiting(m, w, c, s)) return false;
-        }
-        m.st_local(slot, pack_fill(kSentinel));
-      }
-      acc_add<D>(a, x);
-    }
-    Pack16 y = pack_canon<D>(acc_round<D>(a));
+    Pack16 xs[kMaxRanks];
+    const Pack16 own = pack_canon<D>(m.ld_input(in + i));
+    if (!take_all<M, D>(m, j, c, parity, p, peers_mask(W, r), xs, gtid, p)) return false;
+    Pack16 y = pack_canon<D>(sum_rank_order<D>(own, xs, W, r));
     m.st_output(out + i, y);
     for (uint32_t k = 1; k < W; ++k) {
       uint32_t q = (r + k) % W;
@@ -532,21 +557,16 @@ SN_HD bool twoshot_allreduce(M& m, const Job& j, const OpCtx& c, uint64_t gtid, 
   }
   // gather the other owners' results
   for (uint64_t p = gtid; p < chunk; p += gstride) {
-    for (uint32_t k = 1; k < W; ++k) {
-      uint32_t s = (r + W - k) % W;
-      uint64_t i = uint64_t(s) * chunk + p;
-      if (i >= packs) continue;
-      Pack16* slot = reinterpret_cast<Pack16*>(lam_slot(j, r, parity, s)) + half + p;
-      Pack16 x;
-      WaitState w;
-      for (;;) {
-        x = m.ld_poll(slot);
-        if (pack_arrived<D>(x)) break;
-        if (!keep_waiting(m, w, c, s)) return false;
-      }
-      m.st_local(slot, pack_fill(kSentinel));
-      m.st_output(out + i, x);
-    }
+    uint32_t mask = 0;
+SN_UNROLL
+    for (uint32_t s = 0; s < uint32_t(kMaxRanks); ++s)
+      if (s < W && s != r && uint64_t(s) * chunk + p < packs) mask |= 1u << s;
+    if (!mask) continue;
+    Pack16 xs[kMaxRanks];
+    if (!take_all<M, D>(m, j, c, parity, half + p, mask, xs, gtid, ~0ull)) return false;
+SN_UNROLL
+    for (uint32_t s = 0; s < uint32_t(kMaxRanks); ++s)
+      if ((mask >> s) & 1u) m.st_output(out + uint64_t(s) * chunk + p, xs[s]);
   }
   return true;
 }
@@ -570,26 +590,12 @@ SN_HD bool reduce_scatter(M& m, const Job& j, const OpCtx& c, uint64_t gtid, uin
       m.st_remote(reinterpret_cast<Pack16*>(lam_slot(j, q, parity, r)) + p, v);
     }
   }
+  const uint32_t peers = peers_mask(W, r);
   for (uint64_t p = gtid; p < chunk; p += gstride) {
-    Acc a;
-    acc_zero<D>(a);
-    for (uint32_t s = 0; s < W; ++s) {
-      Pack16 x;
-      if (s == r) {
-        x = pack_canon<D>(m.ld_input(in + uint64_t(r) * peer_stride + p));
-      } else {
-        Pack16* slot = reinterpret_cast<Pack16*>(lam_slot(j, r, parity, s)) + p;
-        WaitState w;
-        for (;;) {
-          x = m.ld_poll(slot);
-          if (pack_arrived<D>(x)) break;
-          if (!keep_waiting(m, w, c, s)) return false;
-        }
-        m.st_local(slot, pack_fill(kSentinel));
-      }
-      acc_add<D>(a, x);
-    }
-    m.st_output(out + p, acc_round<D>(a));
+    Pack16 xs[kMaxRanks];
+    const Pack16 own = pack_canon<D>(m.ld_input(in + uint64_t(r) * peer_stride + p));
+    if (!take_all<M, D>(m, j, c, parity, p, peers, xs, gtid, ~0ull)) return false;
+    m.st_output(out + p, sum_rank_order<D>(own, xs, W, r));
   }
   return true;
 }
@@ -628,19 +634,24 @@ SN_HD bool allgather_ll(M& m, const Job& j, const OpCtx& c, uint64_t gtid, uint6
     }
     m.st_output8(j.out + gather_dst(j, r, u * 8), d);
   }
+  const uint32_t peers = peers_mask(W, r);
   for (uint64_t u = gtid; u < units; u += gstride) {
-    for (uint32_t k = 1; k < W; ++k) {
-      uint32_t s = (r + W - k) % W;
-      Pack16* slot = reinterpret_cast<Pack16*>(j.v.base[r] + j.L.ll(parity, s)) + u;
-      Pack16 x;
-      WaitState w;
-      for (;;) {
-        x = m.ld_poll(slot);
-        if (x.w[1] == flag && x.w[3] == flag) break;
-        if (!keep_waiting(m, w, c, s)) return false;
-      }
-      uint32_t d[2] = {x.w[0], x.w[2]};
-      m.st_output8(j.out + gather_dst(j, s, u * 8), d);
+    // every outstanding source polled per sweep (one round trip for all of them)
+    uint32_t pending = peers;
+    WaitState w;
+    while (pending) {
+      Pack16 xs[kMaxRanks];
+SN_UNROLL
+      for (uint32_t s = 0; s < uint32_t(kMaxRanks); ++s)
+        if ((pending >> s) & 1u) xs[s] = m.ld_poll(reinterpret_cast<Pack16*>(j.v.base[r] + j.L.ll(parity, s)) + u);
+SN_UNROLL
+      for (uint32_t s = 0; s < uint32_t(kMaxRanks); ++s)
+        if (((pending >> s) & 1u) && xs[s].w[1] == flag && xs[s].w[3] == flag) {
+          pending &= ~(1u << s);
+          uint32_t d[2] = {xs[s].w[0], xs[s].w[2]};
+          m.st_output8(j.out + gather_dst(j, s, u * 8), d);
+        }
+      if (pending && !keep_waiting(m, w, c, lowest_bit(pending))) return false;
     }
   }
   return true;
@@ -663,13 +674,17 @@ SN_HD bool block_barrier_leader(M& m, const Job& j, const OpCtx& c, uint32_t blo
     uint32_t q = (r + k) % W;
     m.st_release_u32(reinterpret_cast<uint32_t*>(j.v.base[q] + j.L.flag(block, r)), gen);
   }
-  for (uint32_t k = 1; k < W; ++k) {
-    uint32_t s = (r + k) % W;
-    const uint32_t* f = reinterpret_cast<const uint32_t*>(j.v.base[r] + j.L.flag(block, s));
-    WaitState w;
-    while (int32_t(m.ld_acquire_u32(f) - gen) < 0) {
-      if (!keep_waiting(m, w, c, s)) return false;
-    }
+  uint32_t pending = peers_mask(W, r);
+  WaitState w;
+  while (pending) {
+    uint32_t seen[kMaxRanks];
+SN_UNROLL
+    for (uint32_t s = 0; s < uint32_t(kMaxRanks); ++s)
+      if ((pending >> s) & 1u) seen[s] = m.ld_acquire_u32(reinterpret_cast<const uint32_t*>(j.v.base[r] + j.L.flag(block, s)));
+SN_UNROLL
+    for (uint32_t s = 0; s < uint32_t(kMaxRanks); ++s)
+      if (((pending >> s) & 1u) && int32_t(seen[s] - gen) >= 0) pending &= ~(1u << s);
+    if (pending && !keep_waiting(m, w, c, lowest_bit(pending))) return false;
   }
   return true;
 }

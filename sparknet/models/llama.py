@@ -117,6 +117,7 @@ class TPLlama:
         # zeroed: the attention kernel's split counters sit at its front
         self.workspace = torch.zeros(int(self.C.attention_workspace_floats(batch, self.hq, self.hkv, max_len, sms)),
                                      dtype=torch.float32, device=dev)
+        self.pdl = bool(pdl)
         self.mm = DecodeGemm(dev, pdl=pdl)
         # static decode buffers (graph inputs/outputs)
         self.tokens = torch.zeros(batch, dtype=torch.int64, device=dev)
@@ -187,7 +188,8 @@ class TPLlama:
         for i, L in enumerate(self.layers):
             self._linear(self.x, L["wqkv"], self.qkv)
             C.rope_qkv_cache(self.qkv, self.cos, self.sin, self.positions, self.q, L["k"], L["v"], self.hq, self.hkv)
-            C.decode_attention(self.q, L["k"], L["v"], self.lengths, self.attn, self.workspace, self.max_len, scale)
+            C.decode_attention(self.q, L["k"], L["v"], self.lengths, self.attn, self.workspace, self.max_len, scale,
+                               self.pdl)
             self._linear(self.attn.view(self.batch, -1), L["wo"], self.partial)
             self._add_norm(self.partial, L["ln2"])
             self._swiglu(self.x, L["wgu"], self.act)

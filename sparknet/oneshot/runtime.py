@@ -200,8 +200,8 @@ class NvlinkAllReduce:
             raise ValueError(f"unsupported world size {self.world_size}; supported: {SUPPORTED_WORLD_SIZES}")
         if int(max_size) < PACK_BYTES or int(max_size) % PACK_BYTES:
             raise ValueError("max_size must be a positive multiple of 16 bytes")
-        if int(threads) % 32 or not 32 <= int(threads) <= 1024:
-            raise ValueError("threads must be a multiple of 32 between 32 and 1024")
+        if int(threads) % 32 or not 32 <= int(threads) <= 512:
+            raise ValueError("threads must be a multiple of 32 between 32 and 512")
         if int(blocks) < 0:
             raise ValueError("blocks must be 0 (automatic) or positive")
         problems = removed_setting_problems(os.environ)

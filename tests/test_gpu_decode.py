@@ -49,7 +49,8 @@ def test_decode_attention(device, native, B, Hq, Hkv, L):
     out = torch.empty(B, Hq, 128, dtype=torch.bfloat16, device=device)
     native.decode_attention(q, kc, vc, lengths, out, ws, L, 1 / math.sqrt(128))
     again = torch.empty_like(out)
-    native.decode_attention(q, kc, vc, lengths, again, ws, L, 1 / math.sqrt(128))  # counters were left at zero
+    # counters were left at zero; programmatic dependent launch computes the same
+    native.decode_attention(q, kc, vc, lengths, again, ws, L, 1 / math.sqrt(128), True)
     torch.cuda.synchronize()
     assert torch.equal(out, again)
     assert not ws[:4096].view(torch.int32).any()
