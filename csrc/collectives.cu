@@ -13,6 +13,7 @@
 // is exercised end to end without two processes spinning on one device.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <stdexcept>
 #include <string>
 
@@ -256,8 +257,16 @@ void check(cudaError_t e, const char* what) {
 template <typename... KArgs, typename... Args>
 void launch(void (*kernel)(KArgs...), const LaunchGeom& g, cudaStream_t stream, Args... args) {
   if (g.emulate) {
+    // every emulated rank's blocks must be co-resident: cap the blocks per rank by the
+    // kernel's occupancy at this block size (the kernels stride over gridDim.x, and all
+    // emulated ranks share the grid, so they see the same block count)
+    int dev = 0, sms = 0, per_sm = 0;
+    check(cudaGetDevice(&dev), "cudaGetDevice");
+    check(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "SM count");
+    check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, g.threads, 0), "occupancy");
+    const int blocks = std::max(1, std::min(g.blocks, (per_sm * sms) / std::max(1, g.ranks)));
     void* argv[] = {static_cast<void*>(&args)...};
-    check(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kernel), dim3(g.blocks, g.ranks),
+    check(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kernel), dim3(blocks, g.ranks),
                                       dim3(g.threads), argv, 0, stream),
           "cooperative launch");
   } else {

@@ -16,6 +16,7 @@
 // reading every CTA's partial through distributed shared memory in CTA order, so all
 // ranks and all CTAs of a row compute the same scale bit for bit.  Clusters loop over
 // rows (persistent), so the grid never exceeds what is resident.
+#include <algorithm>
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
@@ -237,13 +238,18 @@ void launch_cluster(void (*kernel)(KArgs...), const LaunchGeom& g, cudaStream_t 
   attrs[0].val.clusterDim.y = 1;
   attrs[0].val.clusterDim.z = 1;
   int n = 1;
-  if (g.emulate) {
-    attrs[1].id = cudaLaunchAttributeCooperative;
-    attrs[1].val.cooperative = 1;
-    n = 2;
-  }
   cfg.attrs = attrs;
   cfg.numAttrs = n;
+  if (g.emulate) {
+    // every emulated rank's clusters must be co-resident: cap by the clusters that fit
+    int fit = 0;
+    check(cudaOccupancyMaxActiveClusters(&fit, kernel, &cfg), "cluster occupancy");
+    const int per_rank = std::max(1, std::min(int(g.blocks / g.cluster), fit / std::max(1, g.ranks)));
+    cfg.gridDim = dim3(per_rank * g.cluster, g.ranks);
+    attrs[1].id = cudaLaunchAttributeCooperative;
+    attrs[1].val.cooperative = 1;
+    cfg.numAttrs = 2;
+  }
   check(cudaLaunchKernelEx(&cfg, kernel, args...), "fused norm launch");
 }
 

@@ -159,6 +159,30 @@ class _StatusView:
         self._words[record * self.WORDS + index] = value
 
 
+# Rates measured on B200 that size the all-gather -> GEMM split between copy CTAs and
+# GEMM CTAs: one CTA pushing 16-byte packs to a peer over NVLink sustains ~20 GB/s
+# (benchmarks/microbench_nvlink.py, store, 4 packs in flight), and the tcgen05 GEMM
+# sustains ~9 TFLOP/s per SM in bf16 (1343.9 TFLOP/s over 148 SMs) and ~10.7 in
+# block-scaled fp8.
+PUSH_GBS_PER_CTA = 20.0
+BF16_GEMM_TFLOPS_PER_SM = 9.0
+FP8_GEMM_TFLOPS_PER_SM = 10.7
+
+
+def copy_ctas_for(shard_bytes: int, world: int, flops: int, *, sms: int = 148,
+                  gemm_tflops_per_sm: float = BF16_GEMM_TFLOPS_PER_SM) -> int:
+    """Copy CTAs for the fused all-gather -> GEMM so that pushing the shard to the
+    ``world - 1`` peers takes about as long as the GEMM on the remaining SMs:
+    c / (sms - c) = (bytes / push rate) / (flops / GEMM rate per SM).  Clamped to
+    [4, sms / 2]; rank-invariant (shapes and world only)."""
+    if world <= 1:
+        return 0
+    t_push = (world - 1) * shard_bytes / (PUSH_GBS_PER_CTA * 1e9)      # seconds with one CTA
+    t_gemm = flops / (gemm_tflops_per_sm * 1e12)                          # seconds with one SM
+    c = sms * t_push / (t_push + t_gemm)
+    return int(max(4, min(sms // 2, round(c))))
+
+
 class NvlinkAllReduce:
     """One-shot / two-shot / NVLS collectives over NVLink symmetric memory."""
 
@@ -511,13 +535,18 @@ class NvlinkAllReduce:
         return self._gemm_err_word
 
     def ag_gemm(self, x_shard: torch.Tensor, w: torch.Tensor, *, out: Optional[torch.Tensor] = None,
-                copy_ctas: int = 16) -> torch.Tensor:
+                copy_ctas: Optional[int] = None) -> torch.Tensor:
         """``all_gather(x_shard, dim=0) @ w.T`` in one kernel (sequence-parallel prefill).
 
         ``x_shard`` is this rank's ``[T/W, K]`` rows, ``w`` this rank's ``[N, K]``
         column shard (K-major).  Copy CTAs push the shard to every peer chunk by chunk
-        while tcgen05 tiles consume own rows first and peers' rows as they land.
+        while tcgen05 tiles consume own rows first and peers' rows as they land.  The
+        number of copy CTAs defaults to :func:`copy_ctas_for` (push time balanced against
+        GEMM time).
         """
+        if copy_ctas is None:
+            copy_ctas = copy_ctas_for(x_shard.numel() * x_shard.element_size(), self.world_size,
+                                      2 * x_shard.shape[0] * self.world_size * x_shard.shape[1] * w.shape[0])
         with self._lock:
             self.check_health()
             self._live()
@@ -551,7 +580,7 @@ class NvlinkAllReduce:
         return out
 
     def ag_gemm_fp8(self, xq_shard: torch.Tensor, sfa_shard: torch.Tensor, w: torch.Tensor, sfw: torch.Tensor, *,
-                    out: Optional[torch.Tensor] = None, copy_ctas: int = 8) -> torch.Tensor:
+                    out: Optional[torch.Tensor] = None, copy_ctas: Optional[int] = None) -> torch.Tensor:
         """Block-scaled fp8 ``all_gather(x_shard) @ w.T`` in one kernel, bf16 out.
 
         ``xq_shard``/``sfa_shard`` and ``w``/``sfw`` come from
@@ -559,6 +588,10 @@ class NvlinkAllReduce:
         per 1 x 128 and 128 x 128).  The shard's rows and scales cross NVLink in fp8,
         half the bytes of the bf16 gather.
         """
+        if copy_ctas is None:
+            copy_ctas = copy_ctas_for(xq_shard.numel() + sfa_shard.numel(), self.world_size,
+                                      2 * xq_shard.shape[0] * self.world_size * xq_shard.shape[1] * w.shape[0],
+                                      gemm_tflops_per_sm=FP8_GEMM_TFLOPS_PER_SM)
         with self._lock:
             self.check_health()
             self._live()

@@ -87,3 +87,16 @@ def test_crossover_from_timings():
         {"world_size": 8, "nbytes": 1 << 18, "algorithm": "twoshot", "p50_us": 8.0},
     ]
     assert crossover_from_timings(rows) == {8: 1 << 16}
+
+
+def test_ag_gemm_copy_ctas_balance():
+    from sparknet.oneshot.runtime import copy_ctas_for
+
+    T, H = 8192, 8192
+    shard = T // 8 * H * 2
+    small = copy_ctas_for(shard, 8, 2 * T * H * 1280)      # QKV: little GEMM per gathered byte
+    large = copy_ctas_for(shard, 8, 2 * T * H * 7168)      # gate/up: GEMM-bound
+    assert 4 <= large < small <= 74
+    assert copy_ctas_for(shard, 1, 2 * T * H * 1280) == 0
+    assert copy_ctas_for(1 << 30, 8, 1) == 74              # clamped to half the SMs
+    assert copy_ctas_for(1, 8, 1 << 50) == 4

@@ -111,9 +111,12 @@ def main():
             w = (0.02 * torch.randn(n, H, generator=g, device=device)).to(torch.bfloat16)
             out = torch.empty(T, n, dtype=torch.bfloat16, device=device)
             fused = timed(lambda: rt.ag_gemm(x, w, out=out))
+            fused16 = timed(lambda: rt.ag_gemm(x, w, out=out, copy_ctas=16))
             base = timed(lambda: ag_gemm_reference(x, w))
             cases[name] = {"fused_ms": fused, "nccl_cublas_ms": base, "flops": 2 * T * H * n,
                            "nvlink_bytes_in": (world - 1) * (T // world) * H * 2}
+            cases[name + "_copy16"] = {"fused_ms": fused16, "nccl_cublas_ms": base, "flops": 2 * T * H * n,
+                                       "nvlink_bytes_in": (world - 1) * (T // world) * H * 2}
         for name, kk in (("gemm_rs_o", H // world), ("gemm_rs_down", F // world)):
             a = torch.randn(T, kk, generator=g, device=device).to(torch.bfloat16)
             w = (0.02 * torch.randn(H, kk, generator=g, device=device)).to(torch.bfloat16)
