@@ -15,7 +15,9 @@
 //
 // Epilogues: mode 0 writes Y; mode 1 is SwiGLU over a gate/up weight whose 128-row
 // tiles are [64 gate rows; 64 up rows] of the same 64 features, and writes
-// Y[m, f] = silu(gate) * up for the N/2 features (no intermediate tensor).
+// Y[m, f] = silu(gate) * up for the N/2 features (no intermediate tensor); mode 2 is the
+// QKV projection with RoPE (rotate-half, fp32) and the KV-cache write, one 128-row
+// tile per head (no qkv tensor, no separate RoPE kernel).
 //
 // Every mbarrier wait is bounded (sets the error word and unwinds).
 // Reference: none (the reference has no model GEMMs).
@@ -52,10 +54,21 @@ struct SkinnyParams {
   int kb_per_split;   // K blocks (64) per split
   int splits;
   int tiles;          // weight tiles
-  int mode;           // 0 plain, 1 SwiGLU over interleaved gate/up tiles
+  int mode;           // 0 plain, 1 SwiGLU over interleaved gate/up tiles, 2 QKV + RoPE + KV cache
   __nv_bfloat16* Y;
   int ldy;
   uint32_t* err;
+  // mode 2: tile h < hq is query head h, then hkv key heads, then hkv value heads (128 rows
+  // = head_dim each); q and k are rotated (rotate-half RoPE, pair (d, d + 64)) with
+  // cos/sin[pos][d] and written to q_out [M, hq, 128] and k_cache / v_cache
+  // [M, lmax, hkv, 128] at position positions[m]
+  __nv_bfloat16* q_out;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  const float* cos_t;
+  const float* sin_t;
+  const int* positions;
+  int hq, hkv, lmax;
   uint64_t* stamps;   // optional: kStamps %globaltimer values per CTA (phase timing), or null
 };
 
@@ -200,6 +213,39 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
       for (int s = 0; s < kMaxSplits; ++s) acc += v[s];
       if (n < p.N) p.Y[size_t(m) * p.ldy + n] = __float2bfloat16_rn(acc);
     }
+  } else if (p.mode == 2) {
+    // one head per tile: rows r and r + 64 form a RoPE pair
+    const int my_rows = (64 - split + S - 1) / S;
+    for (int e = threadIdx.x; e < my_rows * p.M; e += blockDim.x) {
+      const int r = split + (e / p.M) * S, m = e % p.M;
+      float va[kMaxSplits], vb[kMaxSplits];
+#pragma unroll
+      for (int s = 0; s < kMaxSplits; ++s) {
+        const float* ps = cluster.map_shared_rank(part, s < S ? s : 0);
+        va[s] = s < S ? ps[r * pitch + m] : 0.0f;
+        vb[s] = s < S ? ps[(r + 64) * pitch + m] : 0.0f;
+      }
+      float x1 = 0.0f, x2 = 0.0f;
+#pragma unroll
+      for (int s = 0; s < kMaxSplits; ++s) {
+        x1 += va[s];
+        x2 += vb[s];
+      }
+      const int pos = p.positions[m];
+      __nv_bfloat16* dst;
+      if (tile < p.hq + p.hkv) {  // q or k: rotate
+        const float c = p.cos_t[size_t(pos) * 64 + r], sn = p.sin_t[size_t(pos) * 64 + r];
+        const float y1 = x1 * c - x2 * sn, y2 = x2 * c + x1 * sn;
+        x1 = y1;
+        x2 = y2;
+      }
+      if (tile < p.hq) dst = p.q_out + (size_t(m) * p.hq + tile) * kWRows;
+      else if (tile < p.hq + p.hkv)
+        dst = p.k_cache + ((size_t(m) * p.lmax + pos) * p.hkv + (tile - p.hq)) * kWRows;
+      else dst = p.v_cache + ((size_t(m) * p.lmax + pos) * p.hkv + (tile - p.hq - p.hkv)) * kWRows;
+      dst[r] = __float2bfloat16_rn(x1);
+      dst[r + 64] = __float2bfloat16_rn(x2);
+    }
   } else {
     // SwiGLU: rows 0..63 gate, 64..127 up of the same 64 features
     const int my_rows = (64 - split + S - 1) / S;
@@ -257,50 +303,11 @@ void check_mat(const at::Tensor& t, const char* name) {
     throw std::invalid_argument(std::string(name) + " must be a row-major 2-D CUDA bfloat16 tensor");
 }
 
-}  // namespace
-
-void skinny_gemm(const at::Tensor& X, const at::Tensor& W, at::Tensor& Y, at::Tensor& err, int mode, int max_splits,
-                 bool pdl, const c10::optional<at::Tensor>& stamps) {
-  check_mat(X, "X");
-  check_mat(W, "W");
-  check_mat(Y, "Y");
-  const int M = int(X.size(0)), K = int(X.size(1)), N = int(W.size(0));
-  if (W.size(1) != K) throw std::invalid_argument("X and W must share K");
-  if (M < 1 || M > kMaxTokens) throw std::invalid_argument("skinny_gemm takes 1..256 token rows");
-  if (K % kBK) throw std::invalid_argument("K must be a multiple of 64");
-  if (mode == 0 && (Y.size(0) != M || Y.size(1) != N)) throw std::invalid_argument("Y must be [M, N]");
-  if (mode == 1 && (N % kWRows || Y.size(0) != M || Y.size(1) != N / 2))
-    throw std::invalid_argument("SwiGLU mode: W rows a multiple of 128 and Y [M, N/2]");
-  if (mode != 0 && mode != 1) throw std::invalid_argument("mode must be 0 or 1");
-  const int dev = X.device().index();
-  c10::cuda::CUDAGuard guard(X.device());
-  int sms = 0;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  Plan pl = plan(M, N, K, sms, max_splits);
+void launch_skinny(const at::Tensor& W, const at::Tensor& X, const SkinnyParams& p, const Plan& pl, int dev, bool pdl) {
   if (size_t(kWRows) * (pl.mp + 1) * 4 > size_t(pl.stages) * (kWStage + pl.mp * kBK * 2))
     throw std::logic_error("decode GEMM: the parked partial does not fit the stage buffers");
-
-  SkinnyParams p;
-  p.M = M;
-  p.N = N;
-  p.K = K;
-  p.mp = pl.mp;
-  p.stages = pl.stages;
-  p.kb_per_split = pl.kb_per_split;
-  p.splits = pl.splits;
-  p.tiles = pl.tiles;
-  p.mode = mode;
-  p.Y = reinterpret_cast<__nv_bfloat16*>(Y.data_ptr());
-  p.ldy = int(Y.stride(0));
-  p.err = reinterpret_cast<uint32_t*>(err.data_ptr());
-  p.stamps = nullptr;
-  if (stamps) {
-    if (!stamps->is_cuda() || stamps->element_size() != 8 || stamps->numel() < int64_t(pl.splits) * pl.tiles * kStamps)
-      throw std::invalid_argument("stamps must be a CUDA 8-byte tensor of splits * tiles * 8 entries");
-    p.stamps = reinterpret_cast<uint64_t*>(stamps->data_ptr());
-  }
-  CUtensorMap mw = make_map(W.data_ptr(), N, K, W.stride(0), kWRows);
-  CUtensorMap mx = make_map(X.data_ptr(), M, K, X.stride(0), pl.mp);
+  CUtensorMap mw = make_map(W.data_ptr(), p.N, p.K, W.stride(0), kWRows);
+  CUtensorMap mx = make_map(X.data_ptr(), p.M, p.K, X.stride(0), pl.mp);
   static int attr_done[64] = {0};
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
     cudaFuncSetAttribute(k_skinny, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
@@ -322,7 +329,103 @@ void skinny_gemm(const at::Tensor& X, const at::Tensor& W, at::Tensor& Y, at::Te
   cfg.attrs = attrs;
   cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, k_skinny, mw, mx, p);
-  if (e != cudaSuccess) throw std::runtime_error(std::string("skinny_gemm launch: ") + cudaGetErrorString(e));
+  if (e != cudaSuccess) throw std::runtime_error(std::string("decode GEMM launch: ") + cudaGetErrorString(e));
+}
+
+}  // namespace
+
+void skinny_gemm(const at::Tensor& X, const at::Tensor& W, at::Tensor& Y, at::Tensor& err, int mode, int max_splits,
+                 bool pdl, const c10::optional<at::Tensor>& stamps) {
+  check_mat(X, "X");
+  check_mat(W, "W");
+  check_mat(Y, "Y");
+  const int M = int(X.size(0)), K = int(X.size(1)), N = int(W.size(0));
+  if (W.size(1) != K) throw std::invalid_argument("X and W must share K");
+  if (M < 1 || M > kMaxTokens) throw std::invalid_argument("skinny_gemm takes 1..256 token rows");
+  if (K % kBK) throw std::invalid_argument("K must be a multiple of 64");
+  if (mode == 0 && (Y.size(0) != M || Y.size(1) != N)) throw std::invalid_argument("Y must be [M, N]");
+  if (mode == 1 && (N % kWRows || Y.size(0) != M || Y.size(1) != N / 2))
+    throw std::invalid_argument("SwiGLU mode: W rows a multiple of 128 and Y [M, N/2]");
+  if (mode != 0 && mode != 1) throw std::invalid_argument("mode must be 0 or 1");
+  const int dev = X.device().index();
+  c10::cuda::CUDAGuard guard(X.device());
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  Plan pl = plan(M, N, K, sms, max_splits);
+  SkinnyParams p;
+  memset(&p, 0, sizeof(p));
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.mp = pl.mp;
+  p.stages = pl.stages;
+  p.kb_per_split = pl.kb_per_split;
+  p.splits = pl.splits;
+  p.tiles = pl.tiles;
+  p.mode = mode;
+  p.Y = reinterpret_cast<__nv_bfloat16*>(Y.data_ptr());
+  p.ldy = int(Y.stride(0));
+  p.err = reinterpret_cast<uint32_t*>(err.data_ptr());
+  p.stamps = nullptr;
+  if (stamps) {
+    if (!stamps->is_cuda() || stamps->element_size() != 8 || stamps->numel() < int64_t(pl.splits) * pl.tiles * kStamps)
+      throw std::invalid_argument("stamps must be a CUDA 8-byte tensor of splits * tiles * 8 entries");
+    p.stamps = reinterpret_cast<uint64_t*>(stamps->data_ptr());
+  }
+  launch_skinny(W, X, p, pl, dev, pdl);
+}
+
+// QKV projection for decode with RoPE and the KV-cache write in the epilogue:
+// X [M, K] x W [(hq + 2 hkv) * 128, K]^T; q -> q_out [M, hq, 128] (rotated), k (rotated)
+// and v -> k_cache / v_cache [M, lmax, hkv, 128] at positions[m].
+void skinny_qkv_rope(const at::Tensor& X, const at::Tensor& W, const at::Tensor& cos_t, const at::Tensor& sin_t,
+                     const at::Tensor& positions, at::Tensor& q_out, at::Tensor& k_cache, at::Tensor& v_cache,
+                     at::Tensor& err, int hq, int hkv, bool pdl) {
+  check_mat(X, "X");
+  check_mat(W, "W");
+  const int M = int(X.size(0)), K = int(X.size(1)), N = int(W.size(0));
+  if (W.size(1) != K) throw std::invalid_argument("X and W must share K");
+  if (N != (hq + 2 * hkv) * kWRows) throw std::invalid_argument("W must have (hq + 2 hkv) * 128 rows");
+  if (M < 1 || M > kMaxTokens || K % kBK) throw std::invalid_argument("1..256 tokens and K a multiple of 64");
+  auto bf16c = [](const at::Tensor& t) {
+    return t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous();
+  };
+  if (!bf16c(q_out) || q_out.numel() != int64_t(M) * hq * kWRows) throw std::invalid_argument("q_out [M, hq, 128] bf16");
+  if (!bf16c(k_cache) || !bf16c(v_cache) || k_cache.dim() != 4 || k_cache.size(0) != M || k_cache.size(2) != hkv ||
+      k_cache.size(3) != kWRows || !k_cache.sizes().equals(v_cache.sizes()))
+    throw std::invalid_argument("k_cache / v_cache [M, lmax, hkv, 128] bf16");
+  if (!cos_t.is_cuda() || cos_t.scalar_type() != at::kFloat || !cos_t.is_contiguous() || cos_t.size(1) != 64 ||
+      !sin_t.sizes().equals(cos_t.sizes()) || sin_t.scalar_type() != at::kFloat)
+    throw std::invalid_argument("cos/sin tables [lmax, 64] float32");
+  if (!positions.is_cuda() || positions.scalar_type() != at::kInt || positions.numel() != M)
+    throw std::invalid_argument("positions [M] int32");
+  const int dev = X.device().index();
+  c10::cuda::CUDAGuard guard(X.device());
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  Plan pl = plan(M, N, K, sms, 0);
+  SkinnyParams p;
+  memset(&p, 0, sizeof(p));
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.mp = pl.mp;
+  p.stages = pl.stages;
+  p.kb_per_split = pl.kb_per_split;
+  p.splits = pl.splits;
+  p.tiles = pl.tiles;
+  p.mode = 2;
+  p.err = reinterpret_cast<uint32_t*>(err.data_ptr());
+  p.q_out = reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr());
+  p.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache.data_ptr());
+  p.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache.data_ptr());
+  p.cos_t = cos_t.data_ptr<float>();
+  p.sin_t = sin_t.data_ptr<float>();
+  p.positions = positions.data_ptr<int>();
+  p.hq = hq;
+  p.hkv = hkv;
+  p.lmax = int(k_cache.size(1));
+  launch_skinny(W, X, p, pl, dev, pdl);
 }
 
 void skinny_tune(int ctas_per_sm) { g_cps = ctas_per_sm; }
@@ -339,6 +442,10 @@ void register_skinny(py::module_& m) {
   m.def("skinny_gemm", &sn::tc::skinny_gemm, py::arg("X"), py::arg("W"), py::arg("Y"), py::arg("err"),
         py::arg("mode") = 0, py::arg("max_splits") = 0, py::arg("pdl") = false, py::arg("stamps") = py::none(),
         "Y = X @ W.T for few token rows (tcgen05, split-K reduced in a cluster, optional SwiGLU epilogue)");
+  m.def("skinny_qkv_rope", &sn::tc::skinny_qkv_rope, py::arg("X"), py::arg("W"), py::arg("cos"), py::arg("sin"),
+        py::arg("positions"), py::arg("q_out"), py::arg("k_cache"), py::arg("v_cache"), py::arg("err"),
+        py::arg("hq"), py::arg("hkv"), py::arg("pdl") = false,
+        "decode QKV projection with RoPE and the KV-cache write fused into the epilogue");
   m.def("skinny_tune", &sn::tc::skinny_tune, py::arg("ctas_per_sm") = 0,
         "process-wide decode GEMM tuning: CTAs per SM (0 = by token count)");
   m.def("skinny_plan", &sn::tc::skinny_plan, py::arg("M"), py::arg("N"), py::arg("K"), py::arg("sms"),

@@ -176,14 +176,22 @@ __global__ void __launch_bounds__(kThreads, 1)
              uint32_t(p.mode == 1 ? kOpAgGemm : kOpGemmRs)};
   const int copy_ctas = p.mode == 1 ? p.copy_ctas : 0;
 
-  // ---- copy CTAs (all-gather): push this rank's shard to every peer, flag per chunk
+  // ---- copy CTAs (all-gather): push this rank's shard to every peer, flag per chunk.
+  // Every copy CTA takes a slice of every chunk (chunk by chunk, in order), so all of
+  // them push however few chunks a shard has; the last CTA to finish its slice of a
+  // chunk (a counter in this rank's control words) raises the chunk's flag at every
+  // peer.  Each CTA orders its peer stores before its count with a system-scope fence;
+  // the last one fences after observing the count, before the release of the flags.
   if (int(blockIdx.x) < copy_ctas) {
     const int chunks = p.shard_rows / kBM;
     const uint64_t chunk_packs = uint64_t(kBM) * p.K * kEsz / kPack;
     const uint64_t sf_packs = F8 ? uint64_t(p.K / kBKe) * 512 / kPack : 0;  // the chunk's scales
-    for (int c = blockIdx.x; c < chunks; c += copy_ctas) {
+    const uint64_t lo = chunk_packs * blockIdx.x / copy_ctas, hi = chunk_packs * (blockIdx.x + 1) / copy_ctas;
+    const uint64_t slo = sf_packs * blockIdx.x / copy_ctas, shi = sf_packs * (blockIdx.x + 1) / copy_ctas;
+    Ctrl* ctrl = ctrl_of(p);
+    for (int c = 0; c < chunks; ++c) {
       const Pack16* src = reinterpret_cast<const Pack16*>(p.shard) + uint64_t(c) * chunk_packs;
-      for (uint64_t i = threadIdx.x; i < chunk_packs; i += blockDim.x) {
+      for (uint64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
         Pack16 v = m.ld_input(src + i);
         for (int k = 1; k < W; ++k) {
           const int q = (rank + k) % W;
@@ -192,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (F8) {
         const Pack16* ssrc = reinterpret_cast<const Pack16*>(p.sfa) + uint64_t(c) * sf_packs;
-        for (uint64_t i = threadIdx.x; i < sf_packs; i += blockDim.x) {
+        for (uint64_t i = slo + threadIdx.x; i < shi; i += blockDim.x) {
           Pack16 v = m.ld_input(ssrc + i);
           for (int k = 1; k < W; ++k) {
             const int q = (rank + k) % W;
@@ -203,7 +211,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncthreads();
       if (threadIdx.x == 0) {
-        for (int k = 1; k < W; ++k) m.st_release_u32(gflag(p, (rank + k) % W, rank, c), seq);
+        m.fence_sys();
+        const uint32_t prev = atomicAdd(&ctrl->chunk_count[c], 1u);
+        if (prev == uint32_t(copy_ctas) - 1u) {
+          m.fence_sys();
+          ctrl->chunk_count[c] = 0;  // every slice counted: re-armed for the next collective
+          for (int k = 1; k < W; ++k) m.st_release_u32(gflag(p, (rank + k) % W, rank, c), seq);
+        }
       }
     }
     __syncthreads();
@@ -574,7 +588,7 @@ void ag_gemm(const RegionDesc& reg, const at::Tensor& x_shard, const at::Tensor&
   const uint64_t row_bytes = uint64_t(K) * 2;
   if (reg.push_cap % row_bytes || reg.push_cap / row_bytes < uint64_t(shard_rows))
     throw std::invalid_argument("the shard does not fit a push slot (raise max_gather_bytes)");
-  if (shard_rows / kBM > kGFlags) throw std::invalid_argument("too many chunks");
+  if (shard_rows / kBM > kChunkCounters) throw std::invalid_argument("too many 128-row chunks per shard");
   c10::cuda::CUDAGuard guard(x_shard.device());
   GemmParams p = base_params(M, N, K, C, err);
   p.mode = 1;
@@ -683,7 +697,7 @@ void ag_gemm_fp8(const RegionDesc& reg, const at::Tensor& xq_shard, const at::Te
   const uint64_t sf_bytes = uint64_t(shard_rows / 128) * (K / 128) * 512;
   if (reg.push_cap % uint64_t(K) || reg.push_cap < data_bytes + sf_bytes)
     throw std::invalid_argument("the fp8 shard and its scales do not fit a push slot (raise max_gather_bytes)");
-  if (shard_rows / kBM > kGFlags) throw std::invalid_argument("too many chunks");
+  if (shard_rows / kBM > kChunkCounters) throw std::invalid_argument("too many 128-row chunks per shard");
   c10::cuda::CUDAGuard guard(xq_shard.device());
   GemmParams p = base_params(M, N, K, C, err);
   p.mode = 1;

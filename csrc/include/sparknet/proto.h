@@ -33,9 +33,10 @@ namespace sn {
 // ---------------------------------------------------------------------------
 // Limits and ABI
 // ---------------------------------------------------------------------------
-constexpr int kAbiVersion = 4;       // bumped when Layout/Ctrl/Status change
+constexpr int kAbiVersion = 5;       // bumped when Layout/Ctrl/Status change
 constexpr int kMaxRanks = 8;         // one NVSwitch box
 constexpr int kMaxBlocks = 256;      // per launch (grid.x)
+constexpr int kChunkCounters = 1024; // fused all-gather->GEMM: 128-row chunks per shard
 constexpr int kMaxThreads = 512;     // per block of the collective kernels: a thread may hold
                                      // every peer's pack at once (128 registers available)
 constexpr int kPack = 16;            // bytes moved per vector access
@@ -65,6 +66,7 @@ struct Ctrl {
   uint32_t ops;                    // collectives completed (stats)
   uint32_t bar_count[kMaxBlocks];  // per-block barrier generation (push/flag protocols)
   uint32_t mc_count[kMaxBlocks];   // per-block multicast barrier target
+  uint32_t chunk_count[kChunkCounters];  // fused all-gather->GEMM: copy CTAs done with a chunk
 };
 static_assert(sizeof(Ctrl) <= kPage * 3, "ctrl must fit its pages");
 

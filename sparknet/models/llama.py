@@ -186,8 +186,13 @@ class TPLlama:
         C.add_rmsnorm(self.res, None, None, self.layers[0]["ln1"], self.x, cfg.eps)
         scale = 1.0 / math.sqrt(cfg.head_dim)
         for i, L in enumerate(self.layers):
-            self._linear(self.x, L["wqkv"], self.qkv)
-            C.rope_qkv_cache(self.qkv, self.cos, self.sin, self.positions, self.q, L["k"], L["v"], self.hq, self.hkv)
+            if self.gemm == "sparknet":  # RoPE and the KV-cache write in the GEMM epilogue
+                self.mm.qkv_rope(self.x, L["wqkv"], self.cos, self.sin, self.positions, self.q, L["k"], L["v"],
+                                 self.hq, self.hkv)
+            else:
+                self._linear(self.x, L["wqkv"], self.qkv)
+                C.rope_qkv_cache(self.qkv, self.cos, self.sin, self.positions, self.q, L["k"], L["v"], self.hq,
+                                 self.hkv)
             C.decode_attention(self.q, L["k"], L["v"], self.lengths, self.attn, self.workspace, self.max_len, scale,
                                self.pdl)
             self._linear(self.attn.view(self.batch, -1), L["wo"], self.partial)
@@ -231,10 +236,11 @@ class TPLlama:
 
     def launches_per_step(self) -> int:
         """This package's kernel launches in one step (torch index/copy ops and cuBLAS
-        GEMMs excluded): per layer RoPE, attention, two norms (fused with the
-        all-reduce on the NVLink arm), and with ``gemm="sparknet"`` four GEMMs (SwiGLU
-        fused), else the SwiGLU kernel."""
-        per_layer = 1 + 1 + 2 + (4 if self.gemm == "sparknet" else 1)
+        GEMMs excluded): per layer attention and two norms (fused with the all-reduce on
+        the NVLink arm), plus four GEMMs with RoPE and SwiGLU fused (``gemm="sparknet"``)
+        or the RoPE and SwiGLU kernels (cuBLAS arm)."""
+        # sparknet: QKV+RoPE, O, gate/up+SwiGLU, down GEMMs; cuBLAS arm: RoPE and SwiGLU kernels
+        per_layer = 1 + 2 + (4 if self.gemm == "sparknet" else 2)
         own_gather = 1 if (self.world > 1 and self.comm == "sparknet") else 0
         lm_head = 1 if self.gemm == "sparknet" else 0
         return 1 + self.cfg.layers * per_layer + lm_head + 1 + own_gather

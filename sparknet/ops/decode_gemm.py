@@ -62,6 +62,17 @@ class DecodeGemm:
         self.C.skinny_gemm(x, w, out, self.err, 1 if swiglu else 0, self.max_splits, self.pdl)
         return out
 
+    def qkv_rope(self, x: torch.Tensor, w: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                 positions: torch.Tensor, q_out: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                 hq: int, hkv: int) -> None:
+        """Decode QKV projection with RoPE and the KV-cache write in the epilogue.
+
+        ``w`` is ``[(hq + 2 hkv) * 128, K]`` (q heads, then k heads, then v heads);
+        rotated q goes to ``q_out [M, hq, 128]``, rotated k and plain v to
+        ``k_cache`` / ``v_cache [M, lmax, hkv, 128]`` at ``positions [M]`` (int32);
+        ``cos`` / ``sin`` are ``[lmax, 64]`` float32 (rotate-half form)."""
+        self.C.skinny_qkv_rope(x, w, cos, sin, positions, q_out, k_cache, v_cache, self.err, hq, hkv, self.pdl)
+
     def check(self) -> None:
         torch.cuda.synchronize(self.device)
         code = int(self.err.item())

@@ -164,3 +164,32 @@ def test_decode_gemm(device, native, M, N, K, swiglu, max_splits):
     y3 = DecodeGemm(device, max_splits=max_splits, pdl=True)(x, w, swiglu=swiglu)
     torch.cuda.synchronize()
     assert torch.equal(y, y3)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv", [(8, 8, 1), (3, 16, 2), (1, 8, 8)])
+def test_decode_qkv_rope_epilogue(device, native, B, Hq, Hkv):
+    from sparknet.ops.decode_gemm import DecodeGemm
+
+    K, L = 1024, 48
+    g = torch.Generator(device=device).manual_seed(B * 100 + Hq)
+    x = torch.randn(B, K, generator=g, device=device).to(torch.bfloat16)
+    w = (0.05 * torch.randn((Hq + 2 * Hkv) * 128, K, generator=g, device=device)).to(torch.bfloat16)
+    ang = torch.arange(L, dtype=torch.float64)[:, None] / (5e5 ** (torch.arange(64, dtype=torch.float64) * 2 / 128))
+    cos, sin = ang.cos().float().to(device), ang.sin().float().to(device)
+    pos = torch.randint(0, L, (B,), dtype=torch.int32, device=device)
+    q = torch.empty(B, Hq, 128, dtype=torch.bfloat16, device=device)
+    kc = torch.zeros(B, L, Hkv, 128, dtype=torch.bfloat16, device=device)
+    vc = torch.zeros_like(kc)
+    op = DecodeGemm(device, pdl=True)
+    op.qkv_rope(x, w, cos, sin, pos, q, kc, vc, Hq, Hkv)
+    op.check()
+    qkv = (x.float() @ w.float().T).view(B, Hq + 2 * Hkv, 128)
+    p = pos.long()
+    torch.testing.assert_close(q.float(), rope_ref(qkv[:, :Hq], cos, sin, p), rtol=2e-2, atol=2e-2)
+    for b in range(B):
+        torch.testing.assert_close(kc[b, p[b]].float(), rope_ref(qkv[b:b + 1, Hq:Hq + Hkv], cos, sin, p[b:b + 1])[0],
+                                   rtol=2e-2, atol=2e-2)
+        torch.testing.assert_close(vc[b, p[b]].float(), qkv[b, Hq + Hkv:], rtol=2e-2, atol=2e-2)
+        others = torch.ones(L, dtype=torch.bool, device=device)
+        others[p[b]] = False
+        assert not kc[b, others].any() and not vc[b, others].any(), "wrote outside the token's position"
