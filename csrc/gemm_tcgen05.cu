@@ -79,6 +79,7 @@ namespace {
 constexpr int kThreads = 192;   // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int kEpiWarps = 4;
 constexpr int kGroupM = 16;     // row blocks per rasterisation band
+constexpr int kCopyPpt = 4;     // all-gather copy CTAs: packs in flight per thread
 
 struct GemmParams {
   int M, N, K;
@@ -177,25 +178,41 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int copy_ctas = p.mode == 1 ? p.copy_ctas : 0;
 
   // ---- copy CTAs (all-gather): push this rank's shard to every peer, flag per chunk.
-  // Every copy CTA takes a slice of every chunk (chunk by chunk, in order), so all of
-  // them push however few chunks a shard has; the last CTA to finish its slice of a
-  // chunk (a counter in this rank's control words) raises the chunk's flag at every
-  // peer.  Each CTA orders its peer stores before its count with a system-scope fence;
-  // the last one fences after observing the count, before the release of the flags.
+  // Work units are chunks, split into `slices` pieces only when there are fewer chunks
+  // than copy CTAs (slices = copy_ctas / chunks), taken in chunk order.  An unsplit
+  // chunk's CTA raises the chunk's flag at every peer itself (a system-scope release,
+  // cumulative over the CTA's stores after the barrier).  For a split chunk, each CTA
+  // orders its stores before its count with a system-scope fence, and the CTA that
+  // completes the count (a counter in this rank's control words, reset by that CTA)
+  // fences again and raises the flags.
   if (int(blockIdx.x) < copy_ctas) {
     const int chunks = p.shard_rows / kBM;
+    const int slices = max(1, copy_ctas / max(1, chunks));
     const uint64_t chunk_packs = uint64_t(kBM) * p.K * kEsz / kPack;
     const uint64_t sf_packs = F8 ? uint64_t(p.K / kBKe) * 512 / kPack : 0;  // the chunk's scales
-    const uint64_t lo = chunk_packs * blockIdx.x / copy_ctas, hi = chunk_packs * (blockIdx.x + 1) / copy_ctas;
-    const uint64_t slo = sf_packs * blockIdx.x / copy_ctas, shi = sf_packs * (blockIdx.x + 1) / copy_ctas;
     Ctrl* ctrl = ctrl_of(p);
-    for (int c = 0; c < chunks; ++c) {
+    for (int u = blockIdx.x; u < chunks * slices; u += copy_ctas) {
+      const int c = u / slices, sl = u % slices;
+      const uint64_t lo = chunk_packs * sl / slices, hi = chunk_packs * (sl + 1) / slices;
+      const uint64_t slo = sf_packs * sl / slices, shi = sf_packs * (sl + 1) / slices;
       const Pack16* src = reinterpret_cast<const Pack16*>(p.shard) + uint64_t(c) * chunk_packs;
-      for (uint64_t i = lo + threadIdx.x; i < hi; i += blockDim.x) {
-        Pack16 v = m.ld_input(src + i);
-        for (int k = 1; k < W; ++k) {
-          const int q = (rank + k) % W;
-          m.st_remote(reinterpret_cast<Pack16*>(slot(p, q, parity, rank)) + uint64_t(c) * chunk_packs + i, v);
+      // kCopyPpt packs in flight per thread before the stores
+      for (uint64_t i0 = lo + threadIdx.x; i0 < hi; i0 += uint64_t(kCopyPpt) * blockDim.x) {
+        Pack16 v[kCopyPpt];
+#pragma unroll
+        for (int k2 = 0; k2 < kCopyPpt; ++k2) {
+          const uint64_t i = i0 + uint64_t(k2) * blockDim.x;
+          if (i < hi) v[k2] = m.ld_input(src + i);
+        }
+#pragma unroll
+        for (int k2 = 0; k2 < kCopyPpt; ++k2) {
+          const uint64_t i = i0 + uint64_t(k2) * blockDim.x;
+          if (i < hi)
+            for (int k = 1; k < W; ++k) {
+              const int q = (rank + k) % W;
+              m.st_remote(reinterpret_cast<Pack16*>(slot(p, q, parity, rank)) + uint64_t(c) * chunk_packs + i,
+                          v[k2]);
+            }
         }
       }
       if (F8) {
@@ -211,13 +228,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncthreads();
       if (threadIdx.x == 0) {
-        m.fence_sys();
-        const uint32_t prev = atomicAdd(&ctrl->chunk_count[c], 1u);
-        if (prev == uint32_t(copy_ctas) - 1u) {
+        bool raise = slices == 1;
+        if (!raise) {
           m.fence_sys();
-          ctrl->chunk_count[c] = 0;  // every slice counted: re-armed for the next collective
-          for (int k = 1; k < W; ++k) m.st_release_u32(gflag(p, (rank + k) % W, rank, c), seq);
+          const uint32_t prev = atomicAdd(&ctrl->chunk_count[c], 1u);
+          if (prev == uint32_t(slices) - 1u) {
+            m.fence_sys();
+            ctrl->chunk_count[c] = 0;  // every slice counted: re-armed for the next collective
+            raise = true;
+          }
         }
+        if (raise)
+          for (int k = 1; k < W; ++k) m.st_release_u32(gflag(p, (rank + k) % W, rank, c), seq);
       }
     }
     __syncthreads();

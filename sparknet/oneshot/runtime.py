@@ -165,6 +165,7 @@ class _StatusView:
 # sustains ~9 TFLOP/s per SM in bf16 (1343.9 TFLOP/s over 148 SMs) and ~10.7 in
 # block-scaled fp8.
 PUSH_GBS_PER_CTA = 20.0
+MIN_COPY_CTAS = 16        # fewer measured slower at TP2 and TP8 on every prefill shape
 BF16_GEMM_TFLOPS_PER_SM = 9.0
 FP8_GEMM_TFLOPS_PER_SM = 10.7
 
@@ -174,13 +175,13 @@ def copy_ctas_for(shard_bytes: int, world: int, flops: int, *, sms: int = 148,
     """Copy CTAs for the fused all-gather -> GEMM so that pushing the shard to the
     ``world - 1`` peers takes about as long as the GEMM on the remaining SMs:
     c / (sms - c) = (bytes / push rate) / (flops / GEMM rate per SM).  Clamped to
-    [4, sms / 2]; rank-invariant (shapes and world only)."""
+    [16, sms / 2]; rank-invariant (shapes and world only)."""
     if world <= 1:
         return 0
     t_push = (world - 1) * shard_bytes / (PUSH_GBS_PER_CTA * 1e9)      # seconds with one CTA
     t_gemm = flops / (gemm_tflops_per_sm * 1e12)                          # seconds with one SM
     c = sms * t_push / (t_push + t_gemm)
-    return int(max(4, min(sms // 2, round(c))))
+    return int(max(MIN_COPY_CTAS, min(sms // 2, round(c))))
 
 
 class NvlinkAllReduce:

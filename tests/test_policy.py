@@ -96,7 +96,7 @@ def test_ag_gemm_copy_ctas_balance():
     shard = T // 8 * H * 2
     small = copy_ctas_for(shard, 8, 2 * T * H * 1280)      # QKV: little GEMM per gathered byte
     large = copy_ctas_for(shard, 8, 2 * T * H * 7168)      # gate/up: GEMM-bound
-    assert 4 <= large < small <= 74
+    assert 16 <= large < small <= 74
     assert copy_ctas_for(shard, 1, 2 * T * H * 1280) == 0
     assert copy_ctas_for(1 << 30, 8, 1) == 74              # clamped to half the SMs
-    assert copy_ctas_for(1, 8, 1 << 50) == 4
+    assert copy_ctas_for(1, 8, 1 << 50) == 16
