@@ -34,8 +34,7 @@ SN_DEV uint32_t enter(const Job& j) {
   uint32_t epoch, poison;
   m.ld_volatile_pair(&ctrl->epoch, epoch, poison);
   if (poison) return 0u;
-  uint32_t seq = epoch + 1u;
-  return seq ? seq : 1u;  // keep 0 as "poisoned"; wrap skips it on every rank alike
+  return next_seq(epoch);  // 0 stays "poisoned"; the wrap keeps the parity alternating
 }
 
 SN_DEV void leave(const Job& j, uint32_t seq) {

@@ -89,8 +89,7 @@ SN_DEV void fused_body(const Job& j, int algo) {
   uint32_t epoch, poison;
   m.ld_volatile_pair(&ctrl->epoch, epoch, poison);
   if (poison) return;
-  uint32_t seq = epoch + 1u;
-  if (!seq) seq = 1u;
+  const uint32_t seq = next_seq(epoch);
   OpCtx c{ctrl, j.v.status, seq, j.rank, blockIdx.x, kOpFusedNorm};
 
   constexpr int kElems = 16 / (Codec<D>::kLanes == 2 ? 2 : 4);   // elements per pack

@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (fused) {
       uint32_t epoch, poison;
       m.ld_volatile_pair(&ctrl_of(p)->epoch, epoch, poison);
-      sq.seq = poison ? 0u : (epoch + 1u ? epoch + 1u : 1u);
+      sq.seq = poison ? 0u : next_seq(epoch);
       sq.parity = sq.seq & 1u;
     }
   }

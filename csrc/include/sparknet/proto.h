@@ -752,6 +752,15 @@ SN_HD void push_receive(M& m, const Job& j, const OpCtx& c, bool exchange, uint6
 // before its increment of `done`, so no block can read the new value early, and the
 // next collective on this rank starts only after this kernel completes.  No fence is
 // needed: the kernel boundary publishes the new epoch to the next launch.
+// Sequence number of the collective after `epoch`.  0 is reserved (a poisoned rank's
+// kernels leave with it), so the wrap after 0xFFFFFFFF goes to 2, not 1: consecutive
+// collectives keep alternating their slot parity (seq & 1) across the wrap, which the
+// two-parity reuse argument of the Lamport and LL slots needs.
+SN_HD uint32_t next_seq(uint32_t epoch) {
+  const uint32_t s = epoch + 1u;
+  return s ? s : 2u;
+}
+
 template <class M>
 SN_HD void finish_op(M& m, Ctrl* ctrl, uint32_t seq, uint32_t nblocks) {
   uint32_t old = m.atomic_add_u32(&ctrl->done, 1u);

@@ -76,6 +76,10 @@ void sim_group_chaos(void* handle, uint32_t permille, uint32_t max_spin, uint32_
 uint32_t sim_failed_seq(void* handle, int rank) { return static_cast<Group*>(handle)->status[rank].failed_seq; }
 uint32_t sim_failed_peer(void* handle, int rank) { return static_cast<Group*>(handle)->status[rank].peer; }
 uint32_t sim_epoch(void* handle, int rank) { return ctrl_of(static_cast<Group*>(handle), rank)->epoch; }
+void sim_set_epoch(void* handle, uint32_t epoch) {
+  Group* g = static_cast<Group*>(handle);
+  for (int r = 0; r < g->world; ++r) ctrl_of(g, r)->epoch = epoch;
+}
 uint32_t sim_poison(void* handle, int rank) { return ctrl_of(static_cast<Group*>(handle), rank)->poison; }
 
 // op: 1 all-reduce, 2 all-gather, 3 reduce-scatter, 4 exchange, 5 barrier
@@ -110,8 +114,7 @@ int sim_collective(void* handle, int op, int algo, int dtype, int blocks, uint32
         j.skip_rank = skip_rank;
         sn::Ctrl* ctrl = ctrl_of(g, r);
         if (m.ld_volatile_u32(&ctrl->poison)) return;
-        uint32_t seq = m.ld_volatile_u32(&ctrl->epoch) + 1u;
-        if (!seq) seq = 1u;
+        const uint32_t seq = sn::next_seq(m.ld_volatile_u32(&ctrl->epoch));
         sn::OpCtx c{ctrl, j.v.status, seq, uint32_t(r), uint32_t(b), uint32_t(op)};
         const uint64_t gtid = uint64_t(b), gstride = uint64_t(blocks);
         if (g->world == 1) {
@@ -211,10 +214,11 @@ uint32_t canon(int dtype, uint32_t b) {
   return b == 0xffffu ? (b ^ 1u) : b;
 }
 
-int check(int world, int blocks, int ops, uint32_t seed, uint32_t chaos, int ring4) {
+int check(int world, int blocks, int ops, uint32_t seed, uint32_t chaos, int ring4, uint32_t start_epoch = 0) {
   const uint64_t cap = 256 * 1024;
   void* g = sim_group_create(world, cap, cap, cap);
   sim_group_chaos(g, chaos, 8, 4, ring4);
+  sim_set_epoch(g, start_epoch);
   std::mt19937 rng(seed);
   std::normal_distribution<float> normal(0.0f, 1.0f);
   int bad = 0;
@@ -243,9 +247,16 @@ int check(int world, int blocks, int ops, uint32_t seed, uint32_t chaos, int rin
     std::vector<const void*> ip(world);
     std::vector<void*> op_(world);
     for (int r = 0; r < world; ++r) { ip[r] = in[r].data(); op_[r] = out[r].data(); }
+    const uint32_t before = sim_epoch(g, 0);
     int f = sim_collective(g, op, algo, dtype, blocks, seed + k, nbytes, ip.data(), op_.data(), 0, 0, nbytes, nbytes,
                            -1, 5000000);
     if (f) { printf("op %d (kind %d) reported a failure\n", k, op); ++bad; continue; }
+    const uint32_t after = sim_epoch(g, 0);
+    if (world > 1 && (after == 0 || ((after ^ before) & 1u) == 0u)) {
+      printf("op %d: sequence %u after %u does not alternate parity\n", k, after, before);
+      ++bad;
+      break;
+    }
     // oracle
     for (int r = 0; r < world && !bad; ++r) {
       if (op == 1 || op == 3) {
@@ -304,9 +315,9 @@ int timeout_case(int world) {
 int main(int argc, char** argv) {
   if (argc >= 2 && !strcmp(argv[1], "check") && argc >= 8)
     return check(atoi(argv[2]), atoi(argv[3]), atoi(argv[4]), uint32_t(atoi(argv[5])), uint32_t(atoi(argv[6])),
-                 atoi(argv[7]));
+                 atoi(argv[7]), argc >= 9 ? uint32_t(strtoul(argv[8], nullptr, 0)) : 0u);
   if (argc >= 3 && !strcmp(argv[1], "timeout")) return timeout_case(atoi(argv[2]));
-  fprintf(stderr, "usage: simulate check <world> <blocks> <ops> <seed> <chaos> <ring4> | timeout <world>\n");
+  fprintf(stderr, "usage: simulate check <world> <blocks> <ops> <seed> <chaos> <ring4> [start_epoch] | timeout <world>\n");
   return 2;
 }
 #endif

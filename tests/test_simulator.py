@@ -144,3 +144,13 @@ def test_missing_rank_times_out_and_reset_recovers(sanitized):
         out = subprocess.run([str(sanitized["asan"]), "timeout", str(world)], capture_output=True, text=True,
                              timeout=60)
         assert out.returncode == 0, out.stdout + out.stderr
+
+
+def test_sequence_wrap_keeps_parity_alternating(sanitized):
+    """Start 40 collectives before the 32-bit sequence wraps and run past it: results stay
+    exact, every rank keeps the same epoch, and each collective's slot parity differs
+    from the previous one's (0 is skipped by jumping to 2)."""
+    out = subprocess.run([str(sanitized["asan"]), "check", "4", "2", "100", "77", "60", "0", str(0xFFFFFFFF - 40)],
+                         capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stdout + out.stderr
+    assert "passed" in out.stdout
