@@ -309,10 +309,11 @@ void launch_skinny(const at::Tensor& W, const at::Tensor& X, const SkinnyParams&
   CUtensorMap mw = make_map(W.data_ptr(), p.N, p.K, W.stride(0), kWRows);
   CUtensorMap mx = make_map(X.data_ptr(), p.M, p.K, X.stride(0), pl.mp);
   static int attr_done[64] = {0};
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    cudaFuncSetAttribute(k_skinny, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    cudaFuncSetAttribute(k_skinny, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    attr_done[dev] = 1;
+  if (dev < 0 || dev >= 64 || !attr_done[dev]) {  // function attributes belong to each device's context
+    cudaError_t e = cudaFuncSetAttribute(k_skinny, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k_skinny, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("decode GEMM attributes: ") + cudaGetErrorString(e));
+    if (dev >= 0 && dev < 64) attr_done[dev] = 1;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.splits, pl.tiles, 1);

@@ -536,10 +536,14 @@ void launch(const CUtensorMap& a, const CUtensorMap& a2, const CUtensorMap& b, c
   using S = Smem<BN, STAGES, F8>;
   static_assert(S::kBytes <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
   auto kern = k_gemm<BN, STAGES, F8>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
-    attr = true;
+  // function attributes belong to each device's context: set once per device
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("gemm smem attribute: ") + cudaGetErrorString(e));
+    if (dev >= 0 && dev < 64) attr_done[dev] = true;
   }
   kern<<<grid, kThreads, S::kBytes, s>>>(a, a2, b, p);
   cudaError_t e = cudaGetLastError();

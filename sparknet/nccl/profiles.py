@@ -60,6 +60,14 @@ PROFILES: dict[str, dict[str, Any]] = {
         "limits": dict(_LIMITS),
         "evidence": "bench.py and probe receipts on 8x B200 (profiles/ summaries)",
     },
+    "nvlink-8": {
+        "transport": "nvlink",
+        "node_counts": (8,),
+        "status": "product on a full box: as nvlink, pinned to tensor-parallel size 8 (every GPU of an HGX B200)",
+        "nccl": {"NCCL_NVLS_ENABLE": None, "NCCL_P2P_LEVEL": None, "NCCL_ALGO": None, "NCCL_PROTO": None},
+        "limits": dict(_LIMITS),
+        "evidence": "bench.py --gpus 8 and the decode benchmark on 8x B200",
+    },
     "nvlink-nvls": {
         "transport": "nvlink-nvls",
         "node_counts": (2, 4, 8),

@@ -32,7 +32,8 @@ def test_reference_control_env_is_verbatim():
 def test_profile_lookup_and_applicability():
     with pytest.raises(ValueError):
         nccl.profile("tp4-ring")
-    assert nccl.profiles_for("nvlink", 8) == ["nvlink"]
+    assert nccl.profiles_for("nvlink", 8) == ["nvlink", "nvlink-8"]
+    assert nccl.profiles_for("nvlink", 4) == ["nvlink"]
     assert "nvlink-nccl-only" in nccl.profiles_for("nccl-nvlink", 2)
     assert nccl.profile_problems("nvlink-nvls", "nvlink-nvls", 1)
     assert nccl.profile_problems("nvlink", "nccl-nvlink", 8)
