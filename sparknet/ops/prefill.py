@@ -2,6 +2,8 @@
 
 ``ag_gemm(runtime, x_shard, w)``  = all_gather(x_shard, dim 0) @ w.T   (QKV, gate/up)
 ``gemm_rs(runtime, a, w)``        = reduce_scatter(a @ w.T, dim 0)     (O, down)
+``ag_gemm_fp8`` / ``gemm_rs_fp8``   the same on block-scaled fp8 operands
+                                   (``sparknet.ops.fp8.quantize_act`` / ``quantize_weight``)
 
 Both run as one kernel launch on every rank (see ``csrc/gemm_tcgen05.cu``); the
 unfused equivalents (NCCL collective + cuBLAS GEMM) are ``ag_gemm_reference`` and
@@ -22,6 +24,16 @@ def gemm_rs(runtime, a: torch.Tensor, w: torch.Tensor, **kw) -> torch.Tensor:
     return runtime.gemm_rs(a, w, **kw)
 
 
+def ag_gemm_fp8(runtime, xq_shard: torch.Tensor, sx: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
+                **kw) -> torch.Tensor:
+    return runtime.ag_gemm_fp8(xq_shard, sx, wq, sw, **kw)
+
+
+def gemm_rs_fp8(runtime, aq: torch.Tensor, sa: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor,
+                **kw) -> torch.Tensor:
+    return runtime.gemm_rs_fp8(aq, sa, wq, sw, **kw)
+
+
 def ag_gemm_reference(x_shard: torch.Tensor, w: torch.Tensor, group=None) -> torch.Tensor:
     world = dist.get_world_size(group)
     full = torch.empty((x_shard.shape[0] * world, x_shard.shape[1]), dtype=x_shard.dtype, device=x_shard.device)
@@ -37,4 +49,4 @@ def gemm_rs_reference(a: torch.Tensor, w: torch.Tensor, group=None) -> torch.Ten
     return out
 
 
-__all__ = ["ag_gemm", "ag_gemm_reference", "gemm_rs", "gemm_rs_reference"]
+__all__ = ["ag_gemm", "ag_gemm_fp8", "ag_gemm_reference", "gemm_rs", "gemm_rs_fp8", "gemm_rs_reference"]
