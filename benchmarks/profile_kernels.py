@@ -107,8 +107,8 @@ def _time_graph(fns, reps: int, device) -> float:
 
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("kernel", choices=["allreduce", "fused_norm", "allgather", "reduce_scatter", "gemm", "attention",
-                                       "decode_gemm", "cublas_decode_gemm"])
+    ap.add_argument("kernel", choices=["allreduce", "fused_norm", "allgather", "reduce_scatter", "gemm", "gemm_fp8",
+                                       "attention", "decode_gemm", "cublas_decode_gemm"])
     ap.add_argument("--swiglu", action="store_true", help="decode_gemm: fused SwiGLU epilogue")
     ap.add_argument("--tune", type=int, default=0, metavar="CTAS_PER_SM",
                     help="decode_gemm: skinny_tune(ctas_per_sm) before running (0 = default)")
@@ -177,6 +177,18 @@ def main() -> int:
         samples = _time(fn, args.warmup, args.iters, device)
         gemm(a, b, c, block_n=args.block_n, check=True)
         row.update(m=M, n=N, k=K, block_n=args.block_n, flops=2 * M * N * K)
+        row["tflops"] = 2 * M * N * K / (statistics.median(samples) * 1e-6) / 1e12
+    elif args.kernel == "gemm_fp8":
+        from sparknet.ops import fp8
+
+        M, N, K = args.m, args.n, args.k
+        xq, sx = fp8.quantize_act(torch.randn(M, K, generator=gen, device=device).bfloat16())
+        wq, sw = fp8.quantize_weight((0.02 * torch.randn(N, K, generator=gen, device=device)).bfloat16())
+        c = torch.empty(M, N, dtype=torch.bfloat16, device=device)
+        fn = lambda: fp8.gemm_fp8(xq, sx, wq, sw, c)  # noqa: E731
+        samples = _time(fn, args.warmup, args.iters, device)
+        fp8.gemm_fp8(xq, sx, wq, sw, c, check=True)
+        row.update(m=M, n=N, k=K, flops=2 * M * N * K)
         row["tflops"] = 2 * M * N * K / (statistics.median(samples) * 1e-6) / 1e12
     elif args.kernel in ("decode_gemm", "cublas_decode_gemm"):
         from sparknet.ops.decode_gemm import DecodeGemm, plan
