@@ -38,8 +38,9 @@ ROOT = Path(__file__).resolve().parent
 HEADLINE_SIZES = (10 * 1024, 60 * 1024, 480 * 1024, 2 * 1024 * 1024)
 CALLS_PER_GRAPH = 256
 METRIC = "bf16 all-reduce p50 µs (max over ranks) @10K–2MiB, 2/4/8 B200; TP8 decode tok/s"
-# BASELINE.md published one-shot numbers (GB10 + RoCE), geometric mean of the four
-# headline sizes, by world size; the bar on B200 is the NCCL arm measured alongside.
+# The reference's published one-shot latencies (GB10 + RoCE; its README.md:29-42),
+# geometric mean of the four headline sizes, by world size; the bar on B200 is the
+# NCCL arm measured alongside.
 PUBLISHED_GEOMEAN_US = {2: (10.9 * 17.0 * 43.1 * 137.1) ** 0.25, 4: (16.9 * 28.0 * 94.0 * 307.7) ** 0.25}
 
 
