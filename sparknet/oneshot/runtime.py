@@ -221,6 +221,9 @@ class NvlinkAllReduce:
         self._capture_id = 0
         self._calls = {"oneshot": 0, "twoshot": 0, "nvls": 0, "all_gather": 0, "reduce_scatter": 0,
                        "exchange": 0, "fused_norm": 0}
+        # host-side accounting of issued collectives (a captured graph counts once, at capture)
+        self._peer_bytes = 0      # bytes this rank sent to each peer over NVLink (P2P stores)
+        self._nvls_bytes = 0      # bytes moved through the multicast alias
         if self.world_size not in SUPPORTED_WORLD_SIZES:
             raise ValueError(f"unsupported world size {self.world_size}; supported: {SUPPORTED_WORLD_SIZES}")
         if int(max_size) < PACK_BYTES or int(max_size) % PACK_BYTES:
@@ -481,6 +484,7 @@ class NvlinkAllReduce:
                 self._order_stream(capturing)
                 self._comm.all_reduce([src], [dst], ALGO_CODES[algo], self._threads, self._blocks)
                 self._calls[algo] += 1
+                self._account_reduce(algo, nbytes)
                 if dst is not out:
                     out.copy_(dst)
                 self._mark_stream(capturing)
@@ -524,6 +528,7 @@ class NvlinkAllReduce:
                 self._comm.fused_norm([inp], [residual], gamma, float(eps), [out], [residual_out],
                                       ALGO_CODES[algorithm], cluster, 0)
                 self._calls["fused_norm"] += 1
+                self._account_reduce(algorithm, nbytes)
                 self._mark_stream(capturing)
         if not capturing:
             self.check_health()
@@ -558,6 +563,7 @@ class NvlinkAllReduce:
                                       device=self.device)
                 self._order_stream(capturing)
                 self._comm.ag_gemm(x_shard, w, out, self._gemm_err(), int(copy_ctas), 0)
+                self._peer_bytes += x_shard.numel() * x_shard.element_size()
                 self._mark_stream(capturing)
         return out
 
@@ -577,6 +583,7 @@ class NvlinkAllReduce:
                     out = torch.empty((a.shape[0] // self.world_size, w.shape[0]), dtype=a.dtype, device=self.device)
                 self._order_stream(capturing)
                 self._comm.gemm_rs(a, w, out, self._gemm_err(), 0)
+                self._peer_bytes += out.numel() * out.element_size()   # each owner's rows of the partial
                 self._mark_stream(capturing)
         return out
 
@@ -603,6 +610,7 @@ class NvlinkAllReduce:
                                       device=self.device)
                 self._order_stream(capturing)
                 self._comm.ag_gemm_fp8(xq_shard, sfa_shard, w, sfw, out, self._gemm_err(), int(copy_ctas), 0)
+                self._peer_bytes += xq_shard.numel() + sfa_shard.numel()
                 self._mark_stream(capturing)
         return out
 
@@ -620,6 +628,7 @@ class NvlinkAllReduce:
                                       device=self.device)
                 self._order_stream(capturing)
                 self._comm.gemm_rs_fp8(aq, sfa, w, sfw, out, self._gemm_err(), 0)
+                self._peer_bytes += out.numel() * out.element_size()
                 self._mark_stream(capturing)
         return out
 
@@ -723,6 +732,10 @@ class NvlinkAllReduce:
         self._comm.all_gather([src], [dst], shard_bytes, row_bytes, dst_row_stride, dst_src_stride,
                               GATHER_CODES[algo], self._threads, self._blocks)
         self._calls["all_gather"] += 1
+        if algo == "nvls":
+            self._nvls_bytes += shard_bytes
+        else:
+            self._peer_bytes += shard_bytes * (2 if algo == "ll" else 1)  # LL8 carries a flag per word
 
     def all_gather(self, inp: torch.Tensor, *, dim: int = -1, out: Optional[torch.Tensor] = None,
                    stream: object = None, sliced: bool = False) -> torch.Tensor:
@@ -864,6 +877,7 @@ class NvlinkAllReduce:
                         if not capturing:
                             self.check_health()
                 self._calls["reduce_scatter"] += 1
+                self._peer_bytes += chunk
                 if dst is not out:
                     out.copy_(dst)
                 self._mark_stream(capturing)
@@ -941,6 +955,7 @@ class NvlinkAllReduce:
         self._comm.exchange([src], [dst], chunk_bytes, src_stride, dst_stride, total_src_bytes,
                             valid_out_bytes, bool(copy_self), self._threads, self._blocks)
         self._calls["exchange"] += 1
+        self._peer_bytes += chunk_bytes
 
     def should_all_to_all_rows(self, inp: torch.Tensor, rows: int) -> bool:
         self._live()
@@ -1016,6 +1031,14 @@ class NvlinkAllReduce:
             self._capture_id = 0
             self._last_stream = None
 
+    def _account_reduce(self, algo: str, nbytes: int) -> None:
+        if algo == "oneshot":
+            self._peer_bytes += nbytes
+        elif algo == "twoshot":
+            self._peer_bytes += 2 * nbytes // max(1, self.world_size)
+        elif algo == "nvls":
+            self._nvls_bytes += nbytes
+
     def stats(self) -> dict[str, Any]:
         lam, ll, push = self._caps
         info: dict[str, Any] = {
@@ -1026,6 +1049,8 @@ class NvlinkAllReduce:
             "push_slot_bytes": push, "timeout_ms": self.timeout_ms, "threads": self._threads,
             "blocks": self._blocks, "multicast": self.has_multicast,
             "calls": dict(self._calls), "ops_posted": sum(self._calls.values()),
+            "bytes_pushed_per_peer": self._peer_bytes, "nvls_bytes": self._nvls_bytes,
+            "nvls_ops": self._calls.get("nvls", 0),
             "oneshot_max_bytes": self.policy.oneshot_limit(self.world_size),
         }
         if self._comm is not None:
