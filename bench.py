@@ -233,18 +233,26 @@ def run_allreduce(args, rank, world, device, cpu_group):
             times.append((start, end))
         return times
 
+    # clocks: the sampler starts before the warm-up (nvidia-smi takes a moment to begin);
+    # only samples stamped in the timed window (or nearest to a short one) count
+    sampler = ClockSampler(clocks_gpus(world), interval_ms=20).start() if rank == 0 else None
+    if sampler:
+        time.sleep(0.5)  # nvidia-smi takes a moment to begin sampling
     for _ in range(args.warmup):
         one_step(False)
     torch.cuda.synchronize()
     dist.barrier(group=cpu_group)
-    sampler = ClockSampler(clocks_gpus(world)).start() if rank == 0 else None
     torch.cuda.synchronize()
     dist.barrier(group=cpu_group)
+    if sampler:
+        sampler.mark_start()
     t0 = time.perf_counter()
     recorded = [one_step(True) for _ in range(args.steps)]
     torch.cuda.synchronize()
     dist.barrier(group=cpu_group)
     wall = time.perf_counter() - t0
+    if sampler:
+        sampler.mark_end()
     clocks = sampler.stop() if sampler else None
     per_rank = [[st.elapsed_time(en) for (st, en) in step] for step in recorded]  # ms [step][size]
     gathered = gather_floats([v for step in per_rank for v in step], cpu_group)

@@ -57,15 +57,20 @@ def run_decode_bench(args, rank, world, device, cpu_group):
     dist.barrier(group=cpu_group)
     from sparknet.utils.clocks import ClockSampler
 
-    sampler = ClockSampler(list(range(world))).start() if rank == 0 else None
+    sampler = ClockSampler(list(range(world)), interval_ms=50).start() if rank == 0 else None
+    time.sleep(0.3)  # nvidia-smi takes a moment to begin sampling
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     dist.barrier(group=cpu_group)
     torch.cuda.synchronize()
+    if sampler:
+        sampler.mark_start()
     start.record()
     for _ in range(args.steps):
         model.replay()
     end.record()
     end.synchronize()
+    if sampler:
+        sampler.mark_end()
     dist.barrier(group=cpu_group)
     clocks = sampler.stop() if sampler else None
     ms = start.elapsed_time(end)

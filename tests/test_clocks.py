@@ -1,0 +1,38 @@
+"""Clock-sample summaries (CPU): busy samples only, throttle reasons, the timed window."""
+
+from datetime import datetime
+
+from sparknet.utils import clocks
+
+
+def _row(index, sm, util, reasons=("Not Active",) * 4, ts=None):
+    stamp = ts.strftime("%Y/%m/%d %H:%M:%S.%f")[:-3] if ts else "2026/12/02 10:00:00.000"
+    return ", ".join([str(index), f"{sm} MHz", "1965 MHz", "900.00 W", f"{util} %", *reasons, stamp])
+
+
+def test_summary_uses_busy_samples_and_reasons():
+    text = "\n".join([_row(0, 120, 0), _row(0, 1900, 95), _row(0, 1850, 97),
+                      _row(0, 1300, 99, ("Not Active", "Not Active", "Not Active", "Active"))])
+    s = clocks.summarize(text)
+    assert s["sm_mhz"] == 1850 and s["sm_max_mhz"] == 1965
+    assert s["reasons"] == ["sw_power_cap"] and not s["rejected"]
+    hot = clocks.summarize(_row(0, 1500, 90, ("Not Active", "Active", "Not Active", "Not Active")))
+    assert hot["rejected"] and hot["reasons"] == ["hw_thermal_slowdown"]
+
+
+def test_idle_only_reports_no_clock():
+    s = clocks.summarize("\n".join([_row(0, 120, 0), _row(0, 345, 0)]))
+    assert s["sm_mhz"] is None and s["sm_mhz_any"] == 232.5
+
+
+def test_window_keeps_inside_or_nearest_samples():
+    t = datetime(2026, 12, 2, 10, 0, 0, 500000)
+    base = t.timestamp()
+    rows = [_row(0, 1000, 50, ts=datetime.fromtimestamp(base - 2)),
+            _row(0, 1900, 90, ts=datetime.fromtimestamp(base + 0.01)),
+            _row(0, 1000, 50, ts=datetime.fromtimestamp(base + 3))]
+    s = clocks.summarize("\n".join(rows), window=(base, base + 0.02))
+    assert s["sm_mhz"] == 1900 and s["samples_in_window"] == 1 and s["samples"] == 1
+    # a window between samples takes the ones within the slack
+    s = clocks.summarize("\n".join(rows), window=(base + 0.05, base + 0.06), slack_s=0.1)
+    assert s["samples_in_window"] == 0 and s["sm_mhz"] == 1900
