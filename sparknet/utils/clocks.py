@@ -54,6 +54,7 @@ def summarize(csv_text: str, gpus: list[int] | None = None, window: tuple[float,
     if gpus is not None:
         rows = [r for r in rows if int(r[0]) in gpus]
     in_window = None
+    loaded = False  # rows stamped inside the timed window are under load by construction
     if window is not None:
         t0, t1 = window
         stamped = [(r, _stamp(r[9]) if len(r) > 9 else None) for r in rows]
@@ -61,13 +62,16 @@ def summarize(csv_text: str, gpus: list[int] | None = None, window: tuple[float,
         near = [r for r, t in stamped if t is not None and t0 - slack_s <= t <= t1 + slack_s]
         in_window = len(inside)
         rows = inside or near
+        loaded = bool(inside)
     mhz, busy_mhz, max_mhz, reasons = [], [], None, set()
     for row in rows:
         sm, smax, util = _num(row[1]), _num(row[2]), _num(row[4])
         if sm is None:
             continue
         mhz.append(sm)
-        if util is not None and util > 0:
+        # NVML's utilisation averages over longer than a short window: inside the
+        # window a sample counts as loaded whatever it says
+        if loaded or (util is not None and util > 0):
             busy_mhz.append(sm)
         if smax is not None:
             max_mhz = smax if max_mhz is None else max(max_mhz, smax)

@@ -36,3 +36,15 @@ def test_window_keeps_inside_or_nearest_samples():
     # a window between samples takes the ones within the slack
     s = clocks.summarize("\n".join(rows), window=(base + 0.05, base + 0.06), slack_s=0.1)
     assert s["samples_in_window"] == 0 and s["sm_mhz"] == 1900
+
+
+def test_samples_inside_the_window_count_as_loaded():
+    t = datetime(2026, 12, 2, 10, 0, 0, 500000)
+    base = t.timestamp()
+    rows = [_row(0, 1965, 0, ts=datetime.fromtimestamp(base + 0.01)),
+            _row(0, 1965, 0, ts=datetime.fromtimestamp(base + 0.03))]
+    s = clocks.summarize("\n".join(rows), window=(base, base + 0.04))
+    assert s["sm_mhz"] == 1965 and s["samples_under_load"] == 2
+    # nearest samples outside the window still need the utilisation
+    s = clocks.summarize("\n".join(rows), window=(base + 0.1, base + 0.12), slack_s=0.2)
+    assert s["samples_in_window"] == 0 and s["sm_mhz"] is None
