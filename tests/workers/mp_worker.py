@@ -165,7 +165,54 @@ def main():
                 expect(torch.equal(o, want), f"graph replay {step}")
     expect(rt.failure() is None, f"health: {rt.failure()}")
     results["checks"] += 1
-    results["stats"] = {k: v for k, v in rt.stats().items() if k in ("calls", "epoch", "transport")}
+    # ineligible inputs are refused on every rank alike (the caller then uses NCCL)
+    expect(not rt.should_allreduce(torch.zeros(64, dtype=torch.int32, device=device)), "int32 eligible")
+    expect(not rt.should_allreduce(torch.zeros(7, dtype=torch.bfloat16, device=device)), "14 bytes eligible")
+    expect(not rt.should_allreduce(torch.zeros(64, 2, dtype=torch.bfloat16, device=device).t()), "strided eligible")
+    big = (rt.dispatch_max_bytes // 2) + 8
+    expect(not rt.should_allreduce(torch.zeros(big, dtype=torch.bfloat16, device=device)), "over dispatch eligible")
+    results["checks"] += 1
+    # eager calls alternating between two streams stay ordered (sequence numbers are shared)
+    s1, s2 = torch.cuda.Stream(device=device), torch.cuda.Stream(device=device)
+    xs = [torch.randn(4096, generator=gen, device=device).to(torch.bfloat16) for _ in range(6)]
+    torch.cuda.synchronize()
+    outs = []
+    for i, x in enumerate(xs):
+        with torch.cuda.stream(s1 if i % 2 == 0 else s2):
+            outs.append(rt.all_reduce(x))
+    torch.cuda.synchronize()
+    for x, o in zip(xs, outs):
+        expect(torch.equal(o, rank_order_sum(gather_all(x, world))), "alternating streams")
+    results["checks"] += 1
+    # all-gather and all-reduce of two sizes mixed in one graph, replayed with new inputs
+    ag_in = [torch.randn(n, generator=gen, device=device).to(torch.bfloat16) for n in (1024, 65536)]
+    ar_in = [torch.randn(n, generator=gen, device=device).to(torch.bfloat16) for n in (2048, 131072)]
+    ag_out = [torch.empty(world * x.numel(), dtype=x.dtype, device=device) for x in ag_in]
+    ar_out = [torch.empty_like(x) for x in ar_in]
+    stream.wait_stream(torch.cuda.current_stream())
+    mixed = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(mixed, stream=stream), rt.capture(stream=stream):
+        for a, ao, b, bo in zip(ag_in, ag_out, ar_in, ar_out):
+            rt.all_gather(a, dim=0, out=ao)
+            rt.all_reduce(b, out=bo)
+    for step in range(3):
+        for t in ag_in + ar_in:
+            t.mul_(-1)
+        mixed.replay()
+        torch.cuda.synchronize()
+        for a, ao in zip(ag_in, ag_out):
+            expect(torch.equal(ao, torch.cat(gather_all(a, world))), f"mixed graph all_gather {step}")
+        for b, bo in zip(ar_in, ar_out):
+            want = rank_order_sum(gather_all(b, world))
+            if rt.algorithm_for(b.numel() * 2, b.dtype) == "nvls":
+                expect(torch.allclose(bo.float(), want.float(), rtol=2e-2, atol=2e-2), f"mixed graph nvls {step}")
+            else:
+                expect(torch.equal(bo, want), f"mixed graph all_reduce {step}")
+    del mixed
+    expect(rt.failure() is None, f"health after mixed graph: {rt.failure()}")
+    results["checks"] += 1
+    results["stats"] = {k: v for k, v in rt.stats().items()
+                        if k in ("calls", "epoch", "transport", "bytes_pushed_per_peer", "nvls_bytes")}
     if rt.trace_path:
         from sparknet.oneshot import trace
 
