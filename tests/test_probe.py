@@ -2,13 +2,11 @@
 reference's tests/test_probe.py."""
 
 import copy
+import importlib
 import json
-import subprocess
 from pathlib import Path
 
 import pytest
-
-import importlib
 
 from sparknet.probe import container, counters, doctor, failstop, fleet, summary
 from sparknet.topology import gpumap
