@@ -115,6 +115,7 @@ def run_decode_bench(args, rank, world, device, cpu_group):
         "data": "synthetic: random-init weights, random KV cache for a 1024-token prompt, random tokens",
         "config": {"model": "Llama-3-70B-shaped (80 layers, hidden 8192, 64/8 heads, FFN 28672, vocab 128256)",
                    "global_batch": batch, "seq_len": PROMPT, "parallelism": f"tp{world}", "comm": comm,
+                   "gemm": model.gemm, "programmatic_dependent_launch": model.pdl,
                    "l2": "weights per step far exceed L2 (126 MB)"},
         "gpu_launches": model.launches_per_step() * args.steps,
         "clocks": clocks,
