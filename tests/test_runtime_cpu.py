@@ -1,0 +1,52 @@
+"""Host-side rules of the runtime that need no GPU: refused settings, timeout bounds,
+device normalisation, support detection, alignment (CPU only)."""
+
+import pytest
+
+torch = pytest.importorskip("torch")
+
+
+def test_reference_settings_are_refused_with_a_reason():
+    from sparknet.oneshot.runtime import REMOVED_SETTINGS, removed_setting_problems
+
+    assert removed_setting_problems({}) == []
+    env = {"SPARKNET_ROCE_HCA": "mlx5_0", "SPARKNET_ROCE_TIMEOUT_MS": "100", "SPARKNET_TIMEOUT_MS": "100"}
+    problems = removed_setting_problems(env)
+    assert len(problems) == 2
+    assert any("SPARKNET_ROCE_HCA" in p and "NVLink" in p for p in problems)
+    assert any("renamed: set SPARKNET_TIMEOUT_MS" in p for p in problems)
+    assert all(name.startswith("SPARKNET_ROCE_") for name in REMOVED_SETTINGS)
+
+
+def test_timeout_bounds():
+    from sparknet.oneshot.runtime import MAX_TIMEOUT_MS, checked_timeout_ms
+
+    assert checked_timeout_ms(1) == 1 and checked_timeout_ms("250") == 250
+    assert checked_timeout_ms(MAX_TIMEOUT_MS) == MAX_TIMEOUT_MS  # microseconds fit 32 bits
+    for bad in (0, -5, MAX_TIMEOUT_MS + 1):
+        with pytest.raises(ValueError):
+            checked_timeout_ms(bad)
+
+
+def test_devices_and_support_on_a_cpu_host():
+    from sparknet.oneshot.runtime import align_up, is_supported, normalize_device
+
+    assert normalize_device(3) == torch.device("cuda", 3)
+    assert normalize_device("cuda:1") == torch.device("cuda", 1)
+    with pytest.raises(ValueError):
+        normalize_device("cpu")
+    if not torch.cuda.is_available():
+        assert is_supported() is False
+    assert align_up(0, 16) == 0 and align_up(1, 16) == 16 and align_up(4096, 4096) == 4096
+
+
+def test_codes_match_the_native_protocol():
+    """The op and algorithm codes the runtime passes are the ones the kernels read."""
+    from sparknet import _native
+    from sparknet.oneshot.runtime import ALGO_CODES, GATHER_CODES
+
+    assert ALGO_CODES == {"oneshot": 0, "twoshot": 1, "nvls": 2}
+    assert GATHER_CODES == {"ll": 0, "push": 1, "nvls": 2}
+    if _native.available():
+        C = _native.load()
+        assert int(C.MAX_RANKS) == 8 and int(C.ABI_VERSION) >= 5
