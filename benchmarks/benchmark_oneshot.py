@@ -2,6 +2,11 @@
 """NVLink collectives vs NCCL, eager and graph-replayed, interleaved arms.
 
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 benchmarks/benchmark_oneshot.py --sizes 10240 61440 491520 2097152
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 benchmarks/benchmark_oneshot.py --fused-norm-tokens 1 8 32 128 256
+
+With ``--fused-norm-tokens`` the arms are the decode epilogue instead: the fused NVLink
+all-reduce + residual add + RMSNorm (hidden 8192, bf16, eps 1e-5) against NCCL's
+all-reduce followed by this package's add + RMSNorm kernel (the same rounding points).
 
 Method (after the reference's ``benchmarks/benchmark_oneshot.py``):
 
@@ -63,6 +68,9 @@ def main() -> int:
     ap.add_argument("--samples-per-block", type=int, default=3)
     ap.add_argument("--calls", type=int, default=64)
     ap.add_argument("--arms", nargs="+", default=list(ARMS), choices=ARMS)
+    ap.add_argument("--fused-norm-tokens", type=int, nargs="*", default=[],
+                    help="time the fused all-reduce + residual + RMSNorm for these token counts instead")
+    ap.add_argument("--hidden", type=int, default=8192)
     ap.add_argument("--output", default="")
     args = ap.parse_args()
 
@@ -77,7 +85,9 @@ def main() -> int:
     rt = AllReduce.from_exchange_group(exchange_group=cpu, device=device, max_size=max(8 << 20, max(args.sizes)))
     rt.prepare((torch.bfloat16,))
     rows = []
-    for nbytes in args.sizes:
+    if args.fused_norm_tokens:
+        rows = fused_norm_rows(args, rt, rank, world, device, cpu)
+    for nbytes in ([] if args.fused_norm_tokens else args.sizes):
         gen = torch.Generator(device=device).manual_seed(nbytes + rank)
         x = torch.randn(nbytes // 2, generator=gen, device=device).to(torch.bfloat16)
         out = torch.empty_like(x)
@@ -157,6 +167,73 @@ def main() -> int:
     dist.barrier(group=cpu)
     dist.destroy_process_group()
     return 0
+
+
+def fused_norm_rows(args, rt, rank, world, device, cpu) -> list:
+    """Interleaved arms for the decode epilogue: residual += all_reduce(x); y = RMSNorm(residual) * gamma."""
+    from sparknet import _native
+
+    C = _native.load()
+    H, eps = args.hidden, 1e-5
+    rows = []
+    for tokens in args.fused_norm_tokens:
+        gen = torch.Generator(device=device).manual_seed(1000 * tokens + rank)
+        x = torch.randn(tokens, H, generator=gen, device=device).to(torch.bfloat16)
+        res = torch.randn(tokens, H, generator=torch.Generator(device=device).manual_seed(tokens), device=device)
+        res = res.to(torch.bfloat16)
+        gamma = (1 + 0.02 * torch.randn(H, generator=torch.Generator(device=device).manual_seed(7),
+                                        device=device)).to(torch.bfloat16)
+        out_f, res_f = torch.empty_like(x), torch.empty_like(res)
+        out_n, res_n, xn = torch.empty_like(x), torch.empty_like(res), x.clone()
+
+        def fused():
+            rt.all_reduce_residual_rmsnorm(x, res, gamma, eps, out=out_f, residual_out=res_f)
+
+        def unfused():
+            xn.copy_(x)
+            dist.all_reduce(xn)
+            C.add_rmsnorm(xn, res, res_n, gamma, out_n, eps)
+
+        fused()
+        unfused()
+        torch.cuda.synchronize()
+        if not torch.allclose(out_f.float(), out_n.float(), rtol=2e-2, atol=2e-2):
+            raise RuntimeError(f"fused and unfused epilogues disagree at {tokens} tokens")
+        arms = {"nvlink-fused": fused, "nccl-unfused": unfused}
+        graphs = {}
+        stream = torch.cuda.Stream(device=device)
+        for name, fn in arms.items():
+            stream.wait_stream(torch.cuda.current_stream())
+            g = torch.cuda.CUDAGraph()
+            ctx = rt.capture(stream=stream) if name.startswith("nvlink") else _Null()
+            with torch.cuda.graph(g, stream=stream), ctx:
+                for _ in range(args.calls):
+                    fn()
+            graphs[name] = g
+        samples = {name: [] for name in arms}
+        for block in range(args.blocks):
+            order = list(arms) if block % 2 == 0 else list(reversed(list(arms)))
+            for name in order:
+                for _ in range(args.samples_per_block):
+                    dist.barrier(group=cpu)
+                    rt.barrier()
+                    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    st.record()
+                    graphs[name].replay()
+                    en.record()
+                    en.synchronize()
+                    samples[name].append(st.elapsed_time(en) * 1000.0 / args.calls)
+        rt.check_health()
+        gathered = [None] * world
+        dist.all_gather_object(gathered, samples, group=cpu)
+        row = {"tokens": tokens, "hidden": H}
+        for name in arms:
+            paired = [max(g[name][i] for g in gathered) for i in range(len(samples[name]))]
+            row[name + "-graph"] = {"median_us": statistics.median(paired), "samples": len(paired)}
+        rows.append(row)
+        del graphs
+        torch.cuda.synchronize()
+    return rows
 
 
 class _Null:
