@@ -166,6 +166,35 @@ template <int D>
 __global__ void __launch_bounds__(kMaxThreads) k_allreduce(Job j, int algo) {
   allreduce_body<D>(j, algo);
 }
+
+// The one-rank all-reduce (kLocal): the sum over one rank is the input itself, so
+// the call is a copy with three arguments instead of the collective's Job.  It is
+// launched with programmatic stream serialisation: in a chain of calls (a graph of
+// back-to-back all-reduces) each launch is scheduled while the previous kernel
+// runs, and griddepcontrol.wait holds this grid's first access until that kernel
+// has finished and its writes are visible.  The trigger comes after the wait, so
+// at most two copies are resident at a time.  No peers, no waits: it cannot hang.
+constexpr int kCopyPpt = 4;  // packs in flight per thread
+__global__ void __launch_bounds__(kMaxThreads) k_copy_local(const Pack16* __restrict__ in,
+                                                             Pack16* __restrict__ out, uint64_t packs) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  DevMem m;
+  const uint64_t stride = uint64_t(gridDim.x) * blockDim.x;
+  for (uint64_t base = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; base < packs; base += stride * kCopyPpt) {
+    Pack16 v[kCopyPpt];
+    SN_UNROLL
+    for (int k = 0; k < kCopyPpt; ++k) {
+      const uint64_t i = base + uint64_t(k) * stride;
+      if (i < packs) v[k] = m.ld_input(in + i);
+    }
+    SN_UNROLL
+    for (int k = 0; k < kCopyPpt; ++k) {
+      const uint64_t i = base + uint64_t(k) * stride;
+      if (i < packs) m.st_output(out + i, v[k]);
+    }
+  }
+}
 template <int D>
 __global__ void __launch_bounds__(kMaxThreads) k_allreduce_emu(Job j, EmuViews e, int algo) {
   allreduce_body<D>(emulated(j, e), algo);
@@ -291,6 +320,32 @@ void launch_allreduce(const Job& j, const EmuViews* e, int dtype, int algo, cons
     default:
       throw std::invalid_argument("unsupported all-reduce dtype");
   }
+}
+
+void launch_copy_local(const char* in, char* out, uint64_t nbytes, int threads, int max_blocks, cudaStream_t s) {
+  if (nbytes % kPack || reinterpret_cast<uintptr_t>(in) % kPack || reinterpret_cast<uintptr_t>(out) % kPack)
+    throw std::invalid_argument("the one-rank all-reduce copies 16-byte aligned packs");
+  if (threads < 32 || threads > kMaxThreads || threads % 32 || max_blocks < 1)
+    throw std::invalid_argument("local copy: bad launch geometry");
+  const uint64_t packs = nbytes / kPack;
+  if (packs == 0) return;
+  // two packs per thread before the grid reaches its cap, up to kCopyPpt after it
+  const uint64_t per_block = uint64_t(threads) * 2;
+  const int blocks = int(std::max<uint64_t>(1, std::min<uint64_t>((packs + per_block - 1) / per_block,
+                                                                   uint64_t(max_blocks))));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  check(cudaLaunchKernelEx(&cfg, k_copy_local, reinterpret_cast<const Pack16*>(in), reinterpret_cast<Pack16*>(out),
+                           packs),
+        "local copy launch");
 }
 
 void launch_reducescatter(const Job& j, const EmuViews* e, int dtype, const LaunchGeom& g, cudaStream_t s) {

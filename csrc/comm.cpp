@@ -175,6 +175,13 @@ class Comm {
     const at::Tensor& in = ins[0];
     uint64_t nbytes = uint64_t(in.numel()) * in.element_size();
     if (nbytes % kPack) throw std::invalid_argument("all-reduce size must be a multiple of 16 bytes");
+    if (algo == kLocal) {
+      if (world_ != 1 || emulate_) throw std::invalid_argument("the local all-reduce is the one-rank case");
+      if (in.data_ptr() == outs[0].data_ptr()) return;  // in place: the input already is the sum
+      launch_copy_local(ptr_of(in), static_cast<char*>(outs[0].data_ptr()), nbytes, threads ? threads : 512,
+                        max_blocks > 0 ? max_blocks : 2 * sms_, at::cuda::getCurrentCUDAStream(device_).stream());
+      return;
+    }
     if (algo == kNvls && !view_.mc) throw std::invalid_argument("NVLS is not available on this communicator");
     if (algo == kNvls && nbytes > view_.mc_cap) throw std::invalid_argument("message exceeds the NVLS buffer");
     if (algo == kOneShot && nbytes > L_.lam_cap) throw std::invalid_argument("message exceeds one-shot capacity");

@@ -27,6 +27,9 @@ struct LaunchGeom {
 };
 
 void launch_allreduce(const Job& j, const EmuViews* e, int dtype, int algo, const LaunchGeom& g, cudaStream_t s);
+// One-rank all-reduce (kLocal): `nbytes` from `in` to `out` in one kernel launched
+// with programmatic stream serialisation; grid capped at `max_blocks`.
+void launch_copy_local(const char* in, char* out, uint64_t nbytes, int threads, int max_blocks, cudaStream_t s);
 void launch_reducescatter(const Job& j, const EmuViews* e, int dtype, const LaunchGeom& g, cudaStream_t s);
 void launch_gather(const Job& j, const EmuViews* e, int algo, int op, const LaunchGeom& g, cudaStream_t s);
 void launch_fused_norm(const Job& j, const EmuViews* e, int dtype, int algo, const LaunchGeom& g, cudaStream_t s);

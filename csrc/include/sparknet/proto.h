@@ -45,7 +45,8 @@ constexpr size_t kPage = 4096;
 constexpr uint32_t kSentinel = 0xFFFFFFFFu;  // "not yet written" in Lamport slots
 
 enum DType : int { kF16 = 0, kBF16 = 1, kF32 = 2 };
-enum Algo : int { kOneShot = 0, kTwoShot = 1, kNvls = 2 };
+// kLocal: the one-rank all-reduce, a copy (no protocol)
+enum Algo : int { kOneShot = 0, kTwoShot = 1, kNvls = 2, kLocal = 3 };
 enum FailKind : int { kFailNone = 0, kFailTimeout = 1, kFailPoisoned = 2, kFailIterations = 3 };
 
 SN_HD size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }

@@ -61,7 +61,7 @@ DEFAULT_TIMEOUT_MS = 10_000
 MAX_TIMEOUT_MS = (2**32 - 1) // 1000
 LL_CAP = 1024 * 1024
 
-ALGO_CODES = {"oneshot": 0, "twoshot": 1, "nvls": 2}
+ALGO_CODES = {"oneshot": 0, "twoshot": 1, "nvls": 2, "local": 3}
 GATHER_CODES = {"ll": 0, "push": 1, "nvls": 2}
 FAIL_KINDS = {1: "timed out", 2: "was poisoned", 3: "exceeded its poll limit"}
 OP_NAMES = {1: "all-reduce", 2: "all-gather", 3: "reduce-scatter", 4: "exchange", 5: "barrier",
@@ -219,7 +219,7 @@ class NvlinkAllReduce:
         self._last_stream = None
         self._capture_stream = None
         self._capture_id = 0
-        self._calls = {"oneshot": 0, "twoshot": 0, "nvls": 0, "all_gather": 0, "reduce_scatter": 0,
+        self._calls = {"oneshot": 0, "twoshot": 0, "nvls": 0, "local": 0, "all_gather": 0, "reduce_scatter": 0,
                        "exchange": 0, "fused_norm": 0}
         # host-side accounting of issued collectives (a captured graph counts once, at capture)
         self._peer_bytes = 0      # bytes this rank sent to each peer over NVLink (P2P stores)
@@ -374,6 +374,8 @@ class NvlinkAllReduce:
             algo = "oneshot" if nbytes <= self.policy.oneshot_limit(self.world_size) else "twoshot"
         if algo == "nvls" and not self.has_multicast:
             algo = "twoshot"  # rank-invariant: multicast availability was agreed collectively
+        if self.world_size == 1:
+            algo = "local"  # one rank: the sum is the input, one copy kernel
         return algo
 
     def prepare_channels(self, channel_ids: Sequence[str]) -> None:
@@ -472,6 +474,8 @@ class NvlinkAllReduce:
                 raise ValueError("out must be a contiguous tensor on the input's device matching the input")
             nbytes = inp.numel() * inp.element_size()
             algo = algorithm or self.algorithm_for(nbytes, inp.dtype)
+            if algo not in ALGO_CODES or (algo == "local" and self.world_size != 1):
+                raise ValueError(f"all-reduce algorithm {algo!r} is not available at world size {self.world_size}")
             with torch.cuda.device(self.device), self._stream_ctx(stream):
                 capturing = torch.cuda.is_current_stream_capturing()
                 if out is None:

@@ -45,8 +45,24 @@ def test_codes_match_the_native_protocol():
     from sparknet import _native
     from sparknet.oneshot.runtime import ALGO_CODES, GATHER_CODES
 
-    assert ALGO_CODES == {"oneshot": 0, "twoshot": 1, "nvls": 2}
+    assert ALGO_CODES == {"oneshot": 0, "twoshot": 1, "nvls": 2, "local": 3}
     assert GATHER_CODES == {"ll": 0, "push": 1, "nvls": 2}
     if _native.available():
         C = _native.load()
         assert int(C.MAX_RANKS) == 8 and int(C.ABI_VERSION) >= 5
+
+
+def test_one_rank_all_reduce_is_the_local_copy():
+    """At world size 1 the policy's choice becomes the copy kernel (an explicit
+    algorithm passed to all_reduce still wins)."""
+    from sparknet.oneshot.runtime import NvlinkAllReduce
+    from sparknet.policy import NVLINK_POLICY
+
+    rt = NvlinkAllReduce.__new__(NvlinkAllReduce)
+    rt.policy = NVLINK_POLICY
+    rt.has_multicast = False
+    for world, want in ((1, "local"), (2, "oneshot"), (8, "oneshot")):
+        rt.world_size = world
+        assert rt.algorithm_for(10240, torch.bfloat16) == want
+    rt.world_size = 1
+    assert rt.algorithm_for(8 << 20, torch.bfloat16) == "local"
