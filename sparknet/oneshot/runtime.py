@@ -217,6 +217,9 @@ class NvlinkAllReduce:
         self._prepared: set[torch.dtype] = set()
         self._stream_event = torch.cuda.Event()
         self._last_stream = None
+        self._current_stream = None
+        self._algo_cache: dict[tuple[int, torch.dtype], str] = {}  # the policy's choice per size
+        self._algo_cache_policy = None
         self._capture_stream = None
         self._capture_id = 0
         self._calls = {"oneshot": 0, "twoshot": 0, "nvls": 0, "local": 0, "all_gather": 0, "reduce_scatter": 0,
@@ -368,6 +371,20 @@ class NvlinkAllReduce:
         return 0 < nbytes <= limit and nbytes % PACK_BYTES == 0
 
     def algorithm_for(self, nbytes: int, dtype: torch.dtype) -> str:
+        """The all-reduce algorithm for ``nbytes`` of ``dtype`` (memoised per policy object)."""
+        cache = getattr(self, "_algo_cache", None)
+        if cache is None:
+            return self._choose_algorithm(nbytes, dtype)
+        if self._algo_cache_policy is not self.policy or len(cache) > 4096:
+            cache.clear()
+            self._algo_cache_policy = self.policy
+        key = (int(nbytes), dtype)
+        algo = cache.get(key)
+        if algo is None:
+            algo = cache[key] = self._choose_algorithm(nbytes, dtype)
+        return algo
+
+    def _choose_algorithm(self, nbytes: int, dtype: torch.dtype) -> str:
         algo = self.policy.all_reduce_backend(int(nbytes), str(dtype).replace("torch.", ""),
                                               world=self.world_size)
         if algo == "nccl":  # above dispatch but within capacity: the runtime still carries it
@@ -410,8 +427,13 @@ class NvlinkAllReduce:
         self.check_health()
 
     # -- stream ordering -----------------------------------------------------------------
+    # Collectives share the symmetric slots and the device epoch, so they run one at a
+    # time.  On one stream that is the stream's own order; when a call arrives on another
+    # stream, the new stream first waits for everything the previous one holds (the last
+    # collective included).  The event is recorded only at such a switch, not per call.
     def _order_stream(self, capturing: bool) -> None:
         current = torch.cuda.current_stream(self.device)
+        self._current_stream = current
         if capturing:
             cid = capture_id(current)
             if cid != self._capture_id:
@@ -420,15 +442,14 @@ class NvlinkAllReduce:
             elif current != self._capture_stream:
                 raise RuntimeError("NVLink collectives must all be captured on one stream")
             return
-        if self._last_stream is not None and current != self._last_stream:
+        last = self._last_stream
+        if last is not None and current != last:
+            self._stream_event.record(last)
             current.wait_event(self._stream_event)
 
     def _mark_stream(self, capturing: bool) -> None:
-        if capturing:
-            return
-        current = torch.cuda.current_stream(self.device)
-        self._stream_event.record(current)
-        self._last_stream = current
+        if not capturing:
+            self._last_stream = self._current_stream
 
     def _aligned_scratch(self, which: int, like: torch.Tensor) -> torch.Tensor:
         if self._align_buffers is None:

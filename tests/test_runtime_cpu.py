@@ -66,3 +66,17 @@ def test_one_rank_all_reduce_is_the_local_copy():
         assert rt.algorithm_for(10240, torch.bfloat16) == want
     rt.world_size = 1
     assert rt.algorithm_for(8 << 20, torch.bfloat16) == "local"
+
+
+def test_algorithm_choice_is_memoised_per_policy():
+    from sparknet.oneshot.runtime import NvlinkAllReduce
+    from sparknet.policy import NVLINK_POLICY, CollectivePolicy
+
+    rt = NvlinkAllReduce.__new__(NvlinkAllReduce)
+    rt.policy, rt.has_multicast, rt.world_size = NVLINK_POLICY, False, 8
+    rt._algo_cache, rt._algo_cache_policy = {}, None
+    first = rt.algorithm_for(2 << 20, torch.bfloat16)
+    assert rt.algorithm_for(2 << 20, torch.bfloat16) == first and len(rt._algo_cache) == 1
+    # a different policy object is consulted afresh, not answered from the old entries
+    rt.policy = CollectivePolicy(2 << 20, 8 << 20, 16 << 20, force="twoshot")
+    assert rt.algorithm_for(10240, torch.bfloat16) == "twoshot" and len(rt._algo_cache) == 1
