@@ -55,6 +55,8 @@ def parse_args(argv=None):
     p.add_argument("--reference-env", choices=("stock", "profile"), default="stock")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--algorithm", default=None, help="force oneshot|twoshot|nvls (ours)")
+    p.add_argument("--pdl", action="store_true",
+                   help="ours: launch the collectives with programmatic dependent launch")
     p.add_argument("--batch", type=int, default=8, help="decode: sequences per step")
     p.add_argument("--layers", type=int, default=80, help="decode: decoder layers")
     p.add_argument("--json-out", default="")
@@ -140,7 +142,8 @@ def clocks_gpus(world: int) -> list[int]:
 class Arm:
     """One implementation: how to all-reduce, align ranks and capture."""
 
-    def __init__(self, impl: str, rank: int, world: int, device, cpu_group, algorithm: str | None):
+    def __init__(self, impl: str, rank: int, world: int, device, cpu_group, algorithm: str | None,
+                 pdl: bool = False):
         self.impl, self.rank, self.world, self.device = impl, rank, world, device
         self.algorithm = algorithm
         self.launches_per_call = 1
@@ -149,6 +152,8 @@ class Arm:
             from sparknet.oneshot import AllReduce
 
             self.rt = AllReduce.from_exchange_group(exchange_group=cpu_group, device=device)
+            if pdl:
+                self.rt.set_pdl(True)
             self.rt.prepare((torch.bfloat16,))
             self.native_path = _native.loaded_path()
             self.align_buf = torch.zeros(8, dtype=torch.bfloat16, device=device)
@@ -181,7 +186,7 @@ def run_allreduce(args, rank, world, device, cpu_group):
     ClockSampler = _local("clocks").ClockSampler
     L2Flusher, geomean = _local("timing").L2Flusher, _local("timing").geomean
 
-    arm = Arm(args.impl, rank, world, device, cpu_group, args.algorithm)
+    arm = Arm(args.impl, rank, world, device, cpu_group, args.algorithm, pdl=args.pdl)
     flush = L2Flusher(device)
     sizes = [int(s) for s in args.sizes]
     gen = torch.Generator(device=device)
@@ -307,6 +312,7 @@ def run_allreduce(args, rank, world, device, cpu_group):
     if args.impl == "ours":
         result["algorithms"] = {str(s): (args.algorithm or arm.rt.algorithm_for(s, torch.bfloat16)) for s in sizes}
         result["native_extension"] = arm.native_path
+        result["pdl"] = bool(arm.rt.pdl)
     else:
         result["impl"] = "reference"
         result["reference_arm"] = ("PolicyCommunicator(runtime=None): clone + torch.distributed.all_reduce (NCCL), "

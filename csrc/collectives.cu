@@ -26,6 +26,18 @@ namespace {
 
 SN_DEV Ctrl* ctrl_of(const Job& j) { return reinterpret_cast<Ctrl*>(j.v.base[j.rank] + j.L.ctrl_off); }
 
+// Programmatic dependent launch (Job::pdl): wait until the previous kernel on the
+// stream has finished and its writes are visible (the epoch it published included),
+// then let the next programmatically serialised launch be scheduled.  The trigger
+// comes from blocks that are already running, so a successor can only take SM slots
+// once this whole grid is resident: no block of a collective waits on peers while
+// one of its own blocks is kept off the GPU.
+SN_DEV void pdl_enter(const Job& j) {
+  if (!j.pdl) return;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Returns the sequence number of this collective, or 0 if the rank is poisoned.
 SN_DEV uint32_t enter(const Job& j) {
   DevMem m;
@@ -136,6 +148,7 @@ SN_DEV void copy_body(const Job& j) {
 
 template <int D>
 SN_DEV void allreduce_body(const Job& j, int algo) {
+  pdl_enter(j);
   if (j.world == 1) {
     if (j.in != j.out) copy_body(j);
     return;
@@ -205,6 +218,7 @@ __global__ void __launch_bounds__(kMaxThreads) k_allreduce_emu(Job j, EmuViews e
 // ---------------------------------------------------------------------------
 template <int D>
 SN_DEV void reducescatter_body(const Job& j) {
+  pdl_enter(j);
   uint32_t seq = enter(j);
   if (!seq) return;
   DevMem m;
@@ -253,6 +267,7 @@ SN_DEV void nvls_allgather(const Job& j, const OpCtx& c, uint64_t gtid, uint64_t
 }
 
 SN_DEV void gather_body(const Job& j, int algo, int op) {
+  pdl_enter(j);
   uint32_t seq = enter(j);
   if (!seq) return;
   DevMem m;
@@ -297,6 +312,18 @@ void launch(void (*kernel)(KArgs...), const LaunchGeom& g, cudaStream_t stream, 
     check(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kernel), dim3(blocks, g.ranks),
                                       dim3(g.threads), argv, 0, stream),
           "cooperative launch");
+  } else if (g.pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(g.blocks);
+    cfg.blockDim = dim3(g.threads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    check(cudaLaunchKernelEx(&cfg, kernel, args...), "collective launch (PDL)");
   } else {
     kernel<<<dim3(g.blocks), dim3(g.threads), 0, stream>>>(args...);
     check(cudaGetLastError(), "collective launch");

@@ -129,6 +129,7 @@ class Comm {
     g.ranks = world_;
     g.emulate = emulate_;
     g.cluster = 1;
+    g.pdl = pdl_ && !emulate_;
     return g;
   }
 
@@ -142,6 +143,7 @@ class Comm {
     j.nbytes = nbytes;
     j.valid_out_bytes = -1;
     j.skip_rank = skip_rank_;
+    j.pdl = (pdl_ && !emulate_) ? 1u : 0u;
     j.trace = trace_d_;
     return j;
   }
@@ -331,6 +333,7 @@ class Comm {
     g.cluster = cluster;
     g.ranks = world_;
     g.emulate = emulate_;
+    g.pdl = pdl_ && !emulate_;
     Job j = job(nbytes);
     j.in = ptr_of(x);
     j.out = static_cast<char*>(outs[0].data_ptr());
@@ -455,6 +458,12 @@ class Comm {
     skip_rank_ = r;
   }
 
+  // Launch the collective kernels with programmatic stream serialisation (each waits
+  // for its predecessor on the stream before touching anything, then lets its own
+  // successor be scheduled).  Emulated groups always launch cooperatively, never so.
+  void set_pdl(bool on) { pdl_ = on; }
+  bool pdl() const { return pdl_ && !emulate_; }
+
   int rank() const { return rank_; }
   int world() const { return world_; }
   bool emulated() const { return emulate_; }
@@ -472,6 +481,7 @@ class Comm {
   Status* status_h_ = nullptr;
   Status* status_d_ = nullptr;
   int skip_rank_ = -1;
+  bool pdl_ = false;
   void* trace_host_ = nullptr;
   uint64_t* trace_d_ = nullptr;
 };
@@ -557,6 +567,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("failed_seq", &Comm::failed_seq, py::arg("which") = 0)
       .def("set_timeout_us", &Comm::set_timeout_us)
       .def("set_skip_rank", &Comm::set_skip_rank)
+      .def("set_pdl", &Comm::set_pdl)
+      .def_property_readonly("pdl", &Comm::pdl)
       .def("set_trace", &Comm::set_trace)
       .def("status_address", &Comm::status_address)
       .def("ctrl", &Comm::ctrl, py::arg("which") = 0)

@@ -213,6 +213,9 @@ SN_DEV void fused_body(const Job& j, int algo) {
 template <int D>
 __global__ void __launch_bounds__(kMaxThreads) k_fused(Job j, int algo) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // a PDL-launched successor may start early
+  // launched with PDL itself: nothing (the epoch included) is read before the previous
+  // kernel on the stream has finished
+  if (j.pdl) asm volatile("griddepcontrol.wait;" ::: "memory");
   fused_body<D>(j, algo);
 }
 
@@ -237,6 +240,11 @@ void launch_cluster(void (*kernel)(KArgs...), const LaunchGeom& g, cudaStream_t 
   attrs[0].val.clusterDim.y = 1;
   attrs[0].val.clusterDim.z = 1;
   int n = 1;
+  if (g.pdl && !g.emulate) {
+    attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[1].val.programmaticStreamSerializationAllowed = 1;
+    n = 2;
+  }
   cfg.attrs = attrs;
   cfg.numAttrs = n;
   if (g.emulate) {

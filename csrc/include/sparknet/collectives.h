@@ -19,11 +19,12 @@ struct EmuViews {
 };
 
 struct LaunchGeom {
-  int blocks;
-  int threads;
-  int ranks;      // grid.y for emulated launches
-  bool emulate;
-  int cluster;    // thread-block cluster size (fused kernels), 1 = none
+  int blocks = 1;
+  int threads = 32;
+  int ranks = 1;        // grid.y for emulated launches
+  bool emulate = false;
+  int cluster = 1;      // thread-block cluster size (fused kernels), 1 = none
+  bool pdl = false;     // programmatic stream serialisation (never for emulated launches)
 };
 
 void launch_allreduce(const Job& j, const EmuViews* e, int dtype, int algo, const LaunchGeom& g, cudaStream_t s);

@@ -33,7 +33,7 @@ namespace sn {
 // ---------------------------------------------------------------------------
 // Limits and ABI
 // ---------------------------------------------------------------------------
-constexpr int kAbiVersion = 5;       // bumped when Layout/Ctrl/Status change
+constexpr int kAbiVersion = 6;       // bumped when Layout/Ctrl/Status/Job change
 constexpr int kMaxRanks = 8;         // one NVSwitch box
 constexpr int kMaxBlocks = 256;      // per launch (grid.x)
 constexpr int kChunkCounters = 1024; // fused all-gather->GEMM: 128-row chunks per shard
@@ -420,6 +420,11 @@ struct Job {
   // Test hook (emulated groups only): this rank's blocks return at entry, as if
   // the rank never launched the collective.  -1 = none.
   int32_t skip_rank;
+  // 1: launched with programmatic stream serialisation.  The kernel waits for the
+  // previous kernel on its stream (griddepcontrol.wait) before its first access and
+  // then lets the next such launch be scheduled (launch_dependents): the successor
+  // can only start once every block of this grid is resident.
+  uint32_t pdl;
   // Trace ring (device pointer of the pinned trace file's records), or null.
   uint64_t* trace;
 };

@@ -68,6 +68,7 @@ OP_NAMES = {1: "all-reduce", 2: "all-gather", 3: "reduce-scatter", 4: "exchange"
             6: "fused all-reduce+RMSNorm"}
 
 ENV_TIMEOUT_MS = "SPARKNET_TIMEOUT_MS"
+ENV_PDL = "SPARKNET_PDL"
 ENV_DISPATCH = "SPARKNET_ALLREDUCE_DISPATCH_MAX_BYTES"
 # Settings of the reference's RoCE transport have no meaning on NVLink; refused with
 # the reason instead of silently ignored.
@@ -319,6 +320,7 @@ class NvlinkAllReduce:
             self._comm.set_trace(address, trace.file_bytes())
             logger.info("collective trace %s", self.trace_path)
         self.has_multicast = bool(self._comm.has_multicast)
+        self.set_pdl(os.environ.get(ENV_PDL, "0") == "1")
         if self.rank == 0:
             logger.info("NVLink collectives ready: world=%d region=%d MiB multicast=%s max_size=%d",
                         self.world_size, region_bytes >> 20, self.has_multicast, self.max_size)
@@ -670,6 +672,21 @@ class NvlinkAllReduce:
         """
         self.timeout_ms = checked_timeout_ms(timeout_ms)
         self._comm.set_timeout_us(1000 * self.timeout_ms)
+
+    def set_pdl(self, enabled: bool) -> None:
+        """Launch the collective kernels with programmatic dependent launch.
+
+        Each collective is then scheduled while the previous kernel on its stream still
+        runs; it waits (``griddepcontrol.wait``) until that kernel has finished before it
+        reads its sequence number, and lets its own successor be scheduled once all of
+        its blocks are running, so a chain of collectives (a graph) overlaps every
+        launch with the previous call.  Off by default (``SPARKNET_PDL=1`` turns it on).
+        The one-rank copy always uses it.  Affects the calls issued after it, and graphs
+        captured after it.
+        """
+        self._live()
+        self._comm.set_pdl(bool(enabled))
+        self.pdl = bool(self._comm.pdl)
 
     def failure(self) -> Optional[str]:
         """The failure report, or None while healthy (a pinned-memory read, no sync)."""
@@ -1071,7 +1088,8 @@ class NvlinkAllReduce:
             "transport": "nvlink-p2p" + ("+nvls" if self.has_multicast else ""),
             "max_size": self.max_size, "dispatch_max_bytes": self.dispatch_max_bytes,
             "max_gather_bytes": self.max_gather_bytes, "lamport_slot_bytes": lam, "ll_slot_bytes": ll,
-            "push_slot_bytes": push, "timeout_ms": self.timeout_ms, "threads": self._threads,
+            "push_slot_bytes": push, "timeout_ms": self.timeout_ms, "pdl": getattr(self, "pdl", False),
+            "threads": self._threads,
             "blocks": self._blocks, "multicast": self.has_multicast,
             "calls": dict(self._calls), "ops_posted": sum(self._calls.values()),
             "bytes_pushed_per_peer": self._peer_bytes, "nvls_bytes": self._nvls_bytes,

@@ -5,7 +5,9 @@ with programmatic dependent launch.  Checks: every dtype and size returns the in
 exact bits (special values included); in place is a no-op; a misaligned input goes
 through the alignment scratch; a CUDA graph of chained calls, each reading the
 previous call's output, ends with the input's bits (each launch waits for its
-predecessor); the protocol path still runs when forced.  Writes one JSON file.
+predecessor); the protocol path still runs when forced; with programmatic dependent
+launch on, a sequence of collectives (all-reduce, all-gather, fused norm,
+reduce-scatter, barrier) gives the bits it gives without.  Writes one JSON file.
 """
 
 import json
@@ -116,6 +118,49 @@ def main():
         expect(False, "unknown algorithm accepted")
     except ValueError:
         pass
+    results["checks"] += 1
+
+    # programmatic dependent launch for the collective kernels: the same sequence of
+    # collectives (protocol paths forced where one rank would copy) gives the same bits
+    # with and without it, eagerly and replayed from a graph
+    tokens, hidden = 16, 8192
+    xa = torch.randn(tokens, hidden, generator=gen, device=device).to(torch.bfloat16)
+    res = torch.randn(tokens, hidden, generator=gen, device=device).to(torch.bfloat16)
+    gamma = torch.randn(hidden, generator=gen, device=device).to(torch.bfloat16)
+    outs = {k: torch.empty(tokens, hidden, device=device, dtype=torch.bfloat16)
+            for k in ("ar", "ag", "rs", "norm", "res")}
+
+    def sequence():
+        rt.all_reduce(xa, out=outs["ar"], algorithm="oneshot")
+        rt.all_gather(outs["ar"], dim=0, out=outs["ag"])
+        rt.all_reduce_residual_rmsnorm(outs["ag"], res, gamma, 1e-5, out=outs["norm"], residual_out=outs["res"])
+        rt.reduce_scatter(outs["norm"], out=outs["rs"])
+        rt.barrier()
+
+    sequence()
+    torch.cuda.synchronize()
+    want = {k: v.clone() for k, v in outs.items()}
+    rt.set_pdl(True)
+    expect(rt.pdl and rt.stats()["pdl"], "set_pdl(True) took effect")
+    for v in outs.values():
+        v.fill_(float("nan"))
+    sequence()
+    torch.cuda.synchronize()
+    expect(all(same_bits(outs[k], want[k]) for k in want), "PDL eager sequence")
+    stream.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream), rt.capture(stream=stream):
+        for _ in range(8):
+            sequence()
+    for rep in range(3):
+        for v in outs.values():
+            v.fill_(float("nan"))
+        torch.cuda.synchronize()
+        graph.replay()
+        torch.cuda.synchronize()
+        expect(all(same_bits(outs[k], want[k]) for k in want), f"PDL graph replay {rep}")
+    del graph
+    rt.set_pdl(False)
     results["checks"] += 1
 
     torch.cuda.synchronize()
