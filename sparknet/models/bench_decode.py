@@ -41,6 +41,8 @@ def run_decode_bench(args, rank, world, device, cpu_group):
 
         runtime = AllReduce.from_exchange_group(exchange_group=cpu_group, device=device,
                                                 max_size=max(8 << 20, batch * cfg.hidden * 2 * 2))
+        if getattr(args, "pdl", False):
+            runtime.set_pdl(True)  # the fused all-reduce + norm launches during the GEMM before it
         runtime.prepare((torch.bfloat16,))
     t0 = time.perf_counter()
     model = TPLlama(cfg, rank=rank, world=world, device=device, batch=batch, max_len=max_len, comm=comm,
@@ -116,6 +118,7 @@ def run_decode_bench(args, rank, world, device, cpu_group):
         "config": {"model": "Llama-3-70B-shaped (80 layers, hidden 8192, 64/8 heads, FFN 28672, vocab 128256)",
                    "global_batch": batch, "seq_len": PROMPT, "parallelism": f"tp{world}", "comm": comm,
                    "gemm": model.gemm, "programmatic_dependent_launch": model.pdl,
+                   "collective_pdl": bool(runtime.pdl) if runtime is not None else False,
                    "l2": "weights per step far exceed L2 (126 MB)"},
         "gpu_launches": model.launches_per_step() * args.steps,
         "clocks": clocks,
