@@ -123,12 +123,12 @@ SN_DEV void fused_body(const Job& j, int algo) {
         uint32_t q = uint32_t(t % W);
         if (q != r) {
           uint64_t slot_pack = (t / W) * row_packs + tpack;
-          m.st_remote(reinterpret_cast<Pack16*>(lam_slot(j, q, parity, r)) + slot_pack, v);
+          m.st_remote(lam_pack(j, q, parity, r, slot_pack), v);
         }
       } else {
         for (uint32_t k = 1; k < W; ++k) {
           uint32_t q = (r + k) % W;
-          m.st_remote(reinterpret_cast<Pack16*>(lam_slot(j, q, parity, r)) + i, v);
+          m.st_remote(lam_pack(j, q, parity, r, i), v);
         }
       }
     }
@@ -147,7 +147,7 @@ SN_DEV void fused_body(const Job& j, int algo) {
       Pack16 y = pack_canon<D>(sum_rank_order<D>(own, xs, W, r));
       for (uint32_t k = 1; k < W; ++k) {
         uint32_t q = (r + k) % W;
-        m.st_remote(reinterpret_cast<Pack16*>(lam_slot(j, q, parity, r)) + half + slot_pack, y);
+        m.st_remote(lam_pack(j, q, parity, r, half + slot_pack), y);
       }
       // keep the own sum for step 3 in the output buffer (overwritten there)
       m.st_local(out + i, y);
@@ -168,7 +168,7 @@ SN_DEV void fused_body(const Job& j, int algo) {
           sum = m.ld_peer_data(out + i);
         } else {
           uint64_t slot_pack = (t / W) * row_packs + tpack;
-          ok = take<D>(m, reinterpret_cast<Pack16*>(lam_slot(j, r, parity, owner)) + half + slot_pack, sum, c,
+          ok = take<D>(m, lam_pack(j, r, parity, owner, half + slot_pack), sum, c,
                        owner);
         }
       } else {

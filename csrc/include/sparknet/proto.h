@@ -47,7 +47,8 @@ constexpr uint32_t kSentinel = 0xFFFFFFFFu;  // "not yet written" in Lamport slo
 enum DType : int { kF16 = 0, kBF16 = 1, kF32 = 2 };
 // kLocal: the one-rank all-reduce, a copy (no protocol)
 enum Algo : int { kOneShot = 0, kTwoShot = 1, kNvls = 2, kLocal = 3 };
-enum FailKind : int { kFailNone = 0, kFailTimeout = 1, kFailPoisoned = 2, kFailIterations = 3 };
+// kFailBounds: a slot access outside its area (builds with SN_BOUNDS_CHECK only)
+enum FailKind : int { kFailNone = 0, kFailTimeout = 1, kFailPoisoned = 2, kFailIterations = 3, kFailBounds = 4 };
 
 SN_HD size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
@@ -68,6 +69,7 @@ struct Ctrl {
   uint32_t bar_count[kMaxBlocks];  // per-block barrier generation (push/flag protocols)
   uint32_t mc_count[kMaxBlocks];   // per-block multicast barrier target
   uint32_t chunk_count[kChunkCounters];  // fused all-gather->GEMM: copy CTAs done with a chunk
+  alignas(16) uint32_t sink[8];    // bounds-checked builds: where a rejected slot access goes
 };
 static_assert(sizeof(Ctrl) <= kPage * 3, "ctrl must fit its pages");
 
@@ -434,6 +436,63 @@ SN_HD char* lam_slot(const Job& j, uint32_t owner, uint32_t parity, uint32_t src
   return j.v.base[owner] + j.L.lam(parity, src);
 }
 
+// Slot accessors: every access of the protocols to a peer-written area (Lamport, LL
+// and bulk-push slots, per-block flags) takes its address from one of these.  Builds
+// with SN_BOUNDS_CHECK check the owner and source ranks (< world), the parity (< 2)
+// and that the whole pack (or flag) lies inside its slot.  A violation is recorded in
+// the pinned status (kind kFailBounds, `peer` = which check, `block` = the offending
+// pack index, low 32 bits), poisons the rank, and redirects the access to a sink in
+// the control page: the collective then ends poisoned, and no neighbouring slot is
+// touched.  Without the macro the accessors are plain address arithmetic.
+enum BoundsCheck : uint32_t { kBoundsLam = 1, kBoundsLL = 2, kBoundsPush = 3, kBoundsFlag = 4 };
+
+#if defined(SN_BOUNDS_CHECK)
+SN_HD uint32_t* bounds_violation(const Job& j, uint32_t owner, uint32_t which, uint64_t index) {
+  Status* st = j.v.status;
+  if (st && st->failed_seq == 0u) {
+    st->kind = kFailBounds;
+    st->peer = which;
+    st->block = uint32_t(index);
+    st->waited_us = 0u;
+    st->op = 0u;
+    st->failed_seq = 0xFFFFFFFFu;  // the sequence is not known at the access
+  }
+  volatile uint32_t* poison = &reinterpret_cast<Ctrl*>(j.v.base[j.rank] + j.L.ctrl_off)->poison;
+  *poison = 1u;
+  char* base = owner < j.world ? j.v.base[owner] : j.v.base[j.rank];
+  return reinterpret_cast<Ctrl*>(base + j.L.ctrl_off)->sink;
+}
+#define SN_SLOT_CHECK(ok, j, owner, which, index, T) \
+  if (!(ok)) return reinterpret_cast<T*>(bounds_violation(j, owner, which, index))
+#else
+#define SN_SLOT_CHECK(ok, j, owner, which, index, T) (void)0
+#endif
+
+// Pack `pack` of Lamport slot [parity][src] in `owner`'s region.
+SN_HD Pack16* lam_pack(const Job& j, uint32_t owner, uint32_t parity, uint32_t src, uint64_t pack) {
+  SN_SLOT_CHECK(owner < j.world && src < j.world && parity < 2u && (pack + 1u) * kPack <= j.L.lam_cap, j, owner,
+                kBoundsLam, pack, Pack16);
+  return reinterpret_cast<Pack16*>(j.v.base[owner] + j.L.lam(parity, src)) + pack;
+}
+// 16-byte unit `unit` of LL slot [parity][src] (2 x ll_cap bytes) in `owner`'s region.
+SN_HD Pack16* ll_pack(const Job& j, uint32_t owner, uint32_t parity, uint32_t src, uint64_t unit) {
+  SN_SLOT_CHECK(owner < j.world && src < j.world && parity < 2u && (unit + 1u) * kPack <= 2u * j.L.ll_cap, j, owner,
+                kBoundsLL, unit, Pack16);
+  return reinterpret_cast<Pack16*>(j.v.base[owner] + j.L.ll(parity, src)) + unit;
+}
+// Pack `pack` of bulk-push slot [parity][src] in `owner`'s region.
+SN_HD Pack16* push_pack(const Job& j, uint32_t owner, uint32_t parity, uint32_t src, uint64_t pack) {
+  SN_SLOT_CHECK(owner < j.world && src < j.world && parity < 2u && (pack + 1u) * kPack <= j.L.push_cap, j, owner,
+                kBoundsPush, pack, Pack16);
+  return reinterpret_cast<Pack16*>(j.v.base[owner] + j.L.push(parity, src)) + pack;
+}
+// Barrier flag [block][src] in `owner`'s region.
+SN_HD uint32_t* flag_word(const Job& j, uint32_t owner, uint32_t block, uint32_t src) {
+  SN_SLOT_CHECK(owner < j.world && src < j.world && block < uint32_t(kMaxBlocks), j, owner, kBoundsFlag, block,
+                uint32_t);
+  return reinterpret_cast<uint32_t*>(j.v.base[owner] + j.L.flag(block, src));
+}
+
 // ---------------------------------------------------------------------------
 // One-shot all-reduce (Lamport push).  Every thread owns packs i = gtid, gtid +
 // gstride, ...: it pushes its (canonicalised) input pack into slot [parity][rank]
@@ -468,7 +527,7 @@ SN_HD bool take_all(M& m, const Job& j, const OpCtx& c, uint32_t parity, uint64_
   while (pending) {
 SN_UNROLL
     for (uint32_t s = 0; s < uint32_t(kMaxRanks); ++s)
-      if ((pending >> s) & 1u) xs[s] = m.ld_poll(reinterpret_cast<Pack16*>(lam_slot(j, r, parity, s)) + off);
+      if ((pending >> s) & 1u) xs[s] = m.ld_poll(lam_pack(j, r, parity, s, off));
 SN_UNROLL
     for (uint32_t s = 0; s < uint32_t(kMaxRanks); ++s)
       if (((pending >> s) & 1u) && pack_arrived<D>(xs[s])) {
@@ -479,7 +538,7 @@ SN_UNROLL
   }
 SN_UNROLL
   for (uint32_t s = 0; s < uint32_t(kMaxRanks); ++s)
-    if ((mask >> s) & 1u) m.st_local(reinterpret_cast<Pack16*>(lam_slot(j, r, parity, s)) + off, pack_fill(kSentinel));
+    if ((mask >> s) & 1u) m.st_local(lam_pack(j, r, parity, s, off), pack_fill(kSentinel));
   return true;
 }
 
@@ -508,7 +567,7 @@ SN_HD bool oneshot_allreduce(M& m, const Job& j, const OpCtx& c, uint64_t gtid, 
     Pack16 v = pack_canon<D>(m.ld_input(in + i));
     for (uint32_t k = 1; k < W; ++k) {
       uint32_t q = (r + k) % W;
-      m.st_remote(reinterpret_cast<Pack16*>(lam_slot(j, q, parity, r)) + i, v);
+      m.st_remote(lam_pack(j, q, parity, r, i), v);
     }
   }
   const uint32_t peers = peers_mask(W, r);
@@ -546,7 +605,7 @@ SN_HD bool twoshot_allreduce(M& m, const Job& j, const OpCtx& c, uint64_t gtid, 
       uint64_t i = uint64_t(q) * chunk + p;
       if (i >= packs) continue;
       Pack16 v = pack_canon<D>(m.ld_input(in + i));
-      m.st_remote(reinterpret_cast<Pack16*>(lam_slot(j, q, parity, r)) + p, v);
+      m.st_remote(lam_pack(j, q, parity, r, p), v);
     }
   }
   // reduce the own chunk, broadcast the result
@@ -560,7 +619,7 @@ SN_HD bool twoshot_allreduce(M& m, const Job& j, const OpCtx& c, uint64_t gtid, 
     m.st_output(out + i, y);
     for (uint32_t k = 1; k < W; ++k) {
       uint32_t q = (r + k) % W;
-      m.st_remote(reinterpret_cast<Pack16*>(lam_slot(j, q, parity, r)) + half + p, y);
+      m.st_remote(lam_pack(j, q, parity, r, half + p), y);
     }
   }
   // gather the other owners' results
@@ -595,7 +654,7 @@ SN_HD bool reduce_scatter(M& m, const Job& j, const OpCtx& c, uint64_t gtid, uin
     for (uint32_t k = 1; k < W; ++k) {
       uint32_t q = (r + k) % W;
       Pack16 v = pack_canon<D>(m.ld_input(in + uint64_t(q) * peer_stride + p));
-      m.st_remote(reinterpret_cast<Pack16*>(lam_slot(j, q, parity, r)) + p, v);
+      m.st_remote(lam_pack(j, q, parity, r, p), v);
     }
   }
   const uint32_t peers = peers_mask(W, r);
@@ -638,7 +697,7 @@ SN_HD bool allgather_ll(M& m, const Job& j, const OpCtx& c, uint64_t gtid, uint6
     p.w[3] = flag;
     for (uint32_t k = 1; k < W; ++k) {
       uint32_t q = (r + k) % W;
-      m.st_remote(reinterpret_cast<Pack16*>(j.v.base[q] + j.L.ll(parity, r)) + u, p);
+      m.st_remote(ll_pack(j, q, parity, r, u), p);
     }
     m.st_output8(j.out + gather_dst(j, r, u * 8), d);
   }
@@ -651,7 +710,7 @@ SN_HD bool allgather_ll(M& m, const Job& j, const OpCtx& c, uint64_t gtid, uint6
       Pack16 xs[kMaxRanks];
 SN_UNROLL
       for (uint32_t s = 0; s < uint32_t(kMaxRanks); ++s)
-        if ((pending >> s) & 1u) xs[s] = m.ld_poll(reinterpret_cast<Pack16*>(j.v.base[r] + j.L.ll(parity, s)) + u);
+        if ((pending >> s) & 1u) xs[s] = m.ld_poll(ll_pack(j, r, parity, s, u));
 SN_UNROLL
       for (uint32_t s = 0; s < uint32_t(kMaxRanks); ++s)
         if (((pending >> s) & 1u) && xs[s].w[1] == flag && xs[s].w[3] == flag) {
@@ -680,7 +739,7 @@ SN_HD bool block_barrier_leader(M& m, const Job& j, const OpCtx& c, uint32_t blo
   // caller synchronised the block first; release is cumulative): no separate fence.
   for (uint32_t k = 1; k < W; ++k) {
     uint32_t q = (r + k) % W;
-    m.st_release_u32(reinterpret_cast<uint32_t*>(j.v.base[q] + j.L.flag(block, r)), gen);
+    m.st_release_u32(flag_word(j, q, block, r), gen);
   }
   uint32_t pending = peers_mask(W, r);
   WaitState w;
@@ -688,7 +747,7 @@ SN_HD bool block_barrier_leader(M& m, const Job& j, const OpCtx& c, uint32_t blo
     uint32_t seen[kMaxRanks];
 SN_UNROLL
     for (uint32_t s = 0; s < uint32_t(kMaxRanks); ++s)
-      if ((pending >> s) & 1u) seen[s] = m.ld_acquire_u32(reinterpret_cast<const uint32_t*>(j.v.base[r] + j.L.flag(block, s)));
+      if ((pending >> s) & 1u) seen[s] = m.ld_acquire_u32(flag_word(j, r, block, s));
 SN_UNROLL
     for (uint32_t s = 0; s < uint32_t(kMaxRanks); ++s)
       if (((pending >> s) & 1u) && int32_t(seen[s] - gen) >= 0) pending &= ~(1u << s);
@@ -715,7 +774,7 @@ SN_HD void push_send(M& m, const Job& j, const OpCtx& c, bool exchange, uint64_t
       Pack16 v = m.ld_input(reinterpret_cast<const Pack16*>(j.in) + i);
       for (uint32_t k = 1; k < W; ++k) {
         uint32_t q = (r + k) % W;
-        m.st_remote(reinterpret_cast<Pack16*>(j.v.base[q] + j.L.push(parity, r)) + i, v);
+        m.st_remote(push_pack(j, q, parity, r, i), v);
       }
       m.st_output(reinterpret_cast<Pack16*>(j.out + gather_dst(j, r, i * kPack)), v);
       continue;
@@ -725,7 +784,7 @@ SN_HD void push_send(M& m, const Job& j, const OpCtx& c, bool exchange, uint64_t
       uint64_t src_off = uint64_t(q) * j.src_peer_stride + i * kPack;
       if (j.total_src_bytes && src_off >= j.total_src_bytes) continue;
       Pack16 v = m.ld_input(reinterpret_cast<const Pack16*>(j.in + src_off));
-      m.st_remote(reinterpret_cast<Pack16*>(j.v.base[q] + j.L.push(parity, r)) + i, v);
+      m.st_remote(push_pack(j, q, parity, r, i), v);
     }
     if (j.copy_self && (j.valid_out_bytes < 0 || int64_t(i * kPack) < j.valid_out_bytes)) {
       uint64_t src_off = uint64_t(r) * j.src_peer_stride + i * kPack;
@@ -746,7 +805,7 @@ SN_HD void push_receive(M& m, const Job& j, const OpCtx& c, bool exchange, uint6
     if (exchange && j.valid_out_bytes >= 0 && int64_t(i * kPack) >= j.valid_out_bytes) continue;
     for (uint32_t k = 1; k < W; ++k) {
       uint32_t s = (r + W - k) % W;
-      Pack16 v = m.ld_peer_data(reinterpret_cast<const Pack16*>(j.v.base[r] + j.L.push(parity, s)) + i);
+      Pack16 v = m.ld_peer_data(push_pack(j, r, parity, s, i));
       uint64_t dst = exchange ? uint64_t(s) * j.dst_src_stride + i * kPack : gather_dst(j, s, i * kPack);
       m.st_output(reinterpret_cast<Pack16*>(j.out + dst), v);
     }

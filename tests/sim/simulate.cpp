@@ -75,6 +75,15 @@ void sim_group_chaos(void* handle, uint32_t permille, uint32_t max_spin, uint32_
 
 uint32_t sim_failed_seq(void* handle, int rank) { return static_cast<Group*>(handle)->status[rank].failed_seq; }
 uint32_t sim_failed_peer(void* handle, int rank) { return static_cast<Group*>(handle)->status[rank].peer; }
+uint32_t sim_failed_kind(void* handle, int rank) { return static_cast<Group*>(handle)->status[rank].kind; }
+// Region inspection for tests: offsets of the layout's areas and a byte copy.
+uint64_t sim_lam_offset(void* handle, uint32_t parity, uint32_t src) {
+  return static_cast<Group*>(handle)->L.lam(parity, src);
+}
+uint64_t sim_ll_offset(void* handle) { return static_cast<Group*>(handle)->L.ll_off; }
+void sim_read(void* handle, int rank, uint64_t offset, void* dst, uint64_t n) {
+  memcpy(dst, static_cast<Group*>(handle)->regions[rank] + offset, n);
+}
 uint32_t sim_epoch(void* handle, int rank) { return ctrl_of(static_cast<Group*>(handle), rank)->epoch; }
 void sim_set_epoch(void* handle, uint32_t epoch) {
   Group* g = static_cast<Group*>(handle);

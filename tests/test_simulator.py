@@ -22,8 +22,9 @@ pytestmark = pytest.mark.skipif(shutil.which("g++") is None, reason="needs g++")
 
 def build(tmp: Path, name: str, flags: list[str], shared: bool) -> Path:
     out = tmp / name
-    cmd = ["g++", "-std=c++17", "-Wall", "-Wextra", "-Werror", "-g", *flags, *INCLUDES, str(SRC), "-o", str(out),
-           "-lpthread"]
+    # every simulated collective runs with the slot bounds checks of the protocol header on
+    cmd = ["g++", "-std=c++17", "-Wall", "-Wextra", "-Werror", "-g", "-DSN_BOUNDS_CHECK", *flags, *INCLUDES, str(SRC),
+           "-o", str(out), "-lpthread"]
     if shared:
         cmd[1:1] = ["-shared", "-fPIC"]
     else:
@@ -44,6 +45,14 @@ def sim_lib(tmp_path_factory):
                                    ctypes.c_uint32, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p),
                                    ctypes.POINTER(ctypes.c_void_p), ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64,
                                    ctypes.c_uint64, ctypes.c_int, ctypes.c_uint32]
+    lib.sim_lam_offset.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32]
+    lib.sim_lam_offset.restype = ctypes.c_uint64
+    lib.sim_ll_offset.argtypes = [ctypes.c_void_p]
+    lib.sim_ll_offset.restype = ctypes.c_uint64
+    lib.sim_read.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_uint64]
+    for name in ("sim_failed_kind", "sim_failed_peer", "sim_poison"):
+        getattr(lib, name).argtypes = [ctypes.c_void_p, ctypes.c_int]
+        getattr(lib, name).restype = ctypes.c_uint32
     lib.sim_f32_to_bf16.argtypes = [ctypes.c_float]
     lib.sim_f32_to_bf16.restype = ctypes.c_uint16
     lib.sim_f32_to_f16.argtypes = [ctypes.c_float]
@@ -61,11 +70,11 @@ def sanitized(tmp_path_factory):
             "tsan": build(tmp, "sim_tsan", ["-O1", "-fsanitize=thread"], shared=False)}
 
 
-def run_sim(lib, group, op, algo, dtype_code, blocks, tensors_in, tensors_out, nbytes, seed=1):
+def run_sim(lib, group, op, algo, dtype_code, blocks, tensors_in, tensors_out, nbytes, seed=1, timeout_us=5_000_000):
     ins = (ctypes.c_void_p * len(tensors_in))(*[t.data_ptr() for t in tensors_in])
     outs = (ctypes.c_void_p * len(tensors_out))(*[t.data_ptr() for t in tensors_out])
     return lib.sim_collective(group, op, algo, dtype_code, blocks, seed, nbytes, ins, outs, 0, 0, nbytes, nbytes, -1,
-                              5_000_000)
+                              timeout_us)
 
 
 @pytest.mark.parametrize("ring4", [0, 1])
@@ -154,3 +163,34 @@ def test_sequence_wrap_keeps_parity_alternating(sanitized):
                          capture_output=True, text=True, timeout=300)
     assert out.returncode == 0, out.stdout + out.stderr
     assert "passed" in out.stdout
+
+
+def test_slot_overflow_is_caught_by_the_bounds_checks(sim_lib):
+    """A message two packs longer than the Lamport slot (the host-side capacity check
+    bypassed): with the bounds checks on, each rank records kind 4 (bounds) for the
+    Lamport slot check and is poisoned, and the area after each written slot keeps its
+    idle contents: rank 0's pushes fill slot [1][0] of rank 1, followed by the
+    never-written slot [1][1] (sentinel); rank 1's fill slot [1][1] of rank 0, the
+    last Lamport slot, followed by the LL area (zeros).  Without the checks the same
+    call reports success, and the first LL units of rank 0 end up all-ones: the
+    overflow landed there and its consumer re-armed it with the sentinel."""
+    torch = pytest.importorskip("torch")
+    world, lam_cap = 2, 1 << 16
+    n = (lam_cap + 32) // 2
+    xs = [torch.randn(n, generator=torch.Generator().manual_seed(r)).to(torch.bfloat16) for r in range(world)]
+    outs = [torch.empty_like(x) for x in xs]
+    g = sim_lib.sim_group_create(world, lam_cap, 1 << 16, 1 << 16)
+    try:
+        failed = run_sim(sim_lib, g, 1, 0, 1, 2, xs, outs, n * 2, timeout_us=200_000)
+        kinds = [sim_lib.sim_failed_kind(g, r) for r in range(world)]
+        checks = [sim_lib.sim_failed_peer(g, r) for r in range(world)]
+        poisoned = [sim_lib.sim_poison(g, r) for r in range(world)]
+        after_slot = ctypes.create_string_buffer(256)
+        sim_lib.sim_read(g, 1, sim_lib.sim_lam_offset(g, 1, 1), after_slot, 256)
+        after_last = ctypes.create_string_buffer(256)
+        sim_lib.sim_read(g, 0, sim_lib.sim_ll_offset(g), after_last, 256)
+    finally:
+        sim_lib.sim_group_destroy(g)
+    assert failed == world and kinds == [4] * world and checks == [1] * world and poisoned == [1] * world
+    assert after_slot.raw == b"\xff" * 256
+    assert after_last.raw == b"\x00" * 256
