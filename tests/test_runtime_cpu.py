@@ -80,3 +80,48 @@ def test_algorithm_choice_is_memoised_per_policy():
     # a different policy object is consulted afresh, not answered from the old entries
     rt.policy = CollectivePolicy(2 << 20, 8 << 20, 16 << 20, force="twoshot")
     assert rt.algorithm_for(10240, torch.bfloat16) == "twoshot" and len(rt._algo_cache) == 1
+
+
+def test_stream_switch_orders_after_the_previous_stream(monkeypatch):
+    """Eager calls on one stream record nothing; the first call on another stream first
+    records an event on the previous stream and waits for it (everything the previous
+    stream holds, the last collective included)."""
+    from sparknet.oneshot.runtime import NvlinkAllReduce
+
+    log = []
+
+    class FakeStream:
+        def __init__(self, name):
+            self.name = name
+
+        def wait_event(self, event):
+            log.append(("wait", self.name, event))
+
+    class FakeEvent:
+        def record(self, stream):
+            log.append(("record", stream.name))
+
+    a, b = FakeStream("a"), FakeStream("b")
+    current = {"s": a}
+    monkeypatch.setattr(torch.cuda, "current_stream", lambda device=None: current["s"])
+    rt = NvlinkAllReduce.__new__(NvlinkAllReduce)
+    rt.device = torch.device("cuda", 0)
+    rt._last_stream = rt._current_stream = rt._capture_stream = None
+    rt._capture_id = 0
+    rt._stream_event = FakeEvent()
+
+    def call(stream):
+        current["s"] = stream
+        rt._order_stream(False)
+        rt._mark_stream(False)
+
+    call(a)
+    call(a)
+    call(a)
+    assert log == []
+    call(b)
+    assert log == [("record", "a"), ("wait", "b", rt._stream_event)]
+    call(b)
+    assert len(log) == 2
+    call(a)
+    assert log[2:] == [("record", "b"), ("wait", "a", rt._stream_event)]
