@@ -160,11 +160,7 @@ SN_DEV void allreduce_body(const Job& j, int algo) {
   trace_begin(j, c, kOpAllReduce);
   const uint64_t gtid = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const uint64_t gstride = uint64_t(gridDim.x) * blockDim.x;
-  if (j.world == 1) {
-    const Pack16* in = reinterpret_cast<const Pack16*>(j.in);
-    Pack16* out = reinterpret_cast<Pack16*>(j.out);
-    for (uint64_t i = gtid; i < j.nbytes / kPack; i += gstride) m.st_output(out + i, m.ld_input(in + i));
-  } else if (algo == kOneShot) {
+  if (algo == kOneShot) {
     oneshot_allreduce<DevMem, D>(m, j, c, gtid, gstride);
   } else if (algo == kTwoShot) {
     twoshot_allreduce<DevMem, D>(m, j, c, gtid, gstride);

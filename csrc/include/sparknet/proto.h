@@ -431,11 +431,6 @@ struct Job {
   uint64_t* trace;
 };
 
-// Index helpers --------------------------------------------------------------
-SN_HD char* lam_slot(const Job& j, uint32_t owner, uint32_t parity, uint32_t src) {
-  return j.v.base[owner] + j.L.lam(parity, src);
-}
-
 // Slot accessors: every access of the protocols to a peer-written area (Lamport, LL
 // and bulk-push slots, per-block flags) takes its address from one of these.  Builds
 // with SN_BOUNDS_CHECK check the owner and source ranks (< world), the parity (< 2)
