@@ -113,6 +113,7 @@ def main() -> int:
     ap.add_argument("--tune", type=int, default=0, metavar="CTAS_PER_SM",
                     help="decode_gemm: skinny_tune(ctas_per_sm) before running (0 = default)")
     ap.add_argument("--pdl", action="store_true", help="decode_gemm: programmatic dependent launch")
+    ap.add_argument("--cluster", action="store_true", help="attention: spans merged in a thread-block cluster")
     ap.add_argument("--stamps", action="store_true",
                     help="decode_gemm: per-CTA %%globaltimer phase stamps of one cold launch (µs percentiles)")
     ap.add_argument("--world", type=int, default=8)
@@ -233,14 +234,21 @@ def main() -> int:
         out = torch.empty(B, Hq, D, dtype=torch.bfloat16, device=device)
         sms = torch.cuda.get_device_properties(device).multi_processor_count
         ws = torch.zeros(C.attention_workspace_floats(B, Hq, Hkv, Lmax, sms), dtype=torch.float32, device=device)
-        fn = lambda: C.decode_attention(q, k, v, lengths, out, ws, Lmax, D ** -0.5)  # noqa: E731
+        def attend(kk, vv):
+            if args.cluster:
+                C.decode_attention_cluster(q, kk, vv, lengths, out, Lmax, D ** -0.5)
+            else:
+                C.decode_attention(q, kk, vv, lengths, out, ws, Lmax, D ** -0.5)
+
+        fn = lambda: attend(k, v)  # noqa: E731
         samples = _time(fn, args.warmup, args.iters, device)
         kv_bytes = 2 * B * Hkv * L * D * 2
         copies = max(1, min(64, -(-(400 << 20) // kv_bytes)))
         kvs = [(k, v)] + [(torch.randn_like(k), torch.randn_like(v)) for _ in range(copies - 1)]
-        fns = [lambda kk=kk, vv=vv: C.decode_attention(q, kk, vv, lengths, out, ws, Lmax, D ** -0.5) for kk, vv in kvs]
+        fns = [lambda kk=kk, vv=vv: attend(kk, vv) for kk, vv in kvs]
         row["graph_us"] = _time_graph(fns, 20, device)
-        row.update(batch=B, heads=Hq, kv_heads=Hkv, length=L, kv_bytes=kv_bytes, copies=copies)
+        row.update(batch=B, heads=Hq, kv_heads=Hkv, length=L, kv_bytes=kv_bytes, copies=copies,
+                   variant="cluster" if args.cluster else "split")
     med = statistics.median(samples)
     row.update(median_us=med, min_us=min(samples), iters=len(samples))
     if "bytes_per_rank" in row:

@@ -70,7 +70,7 @@ class TPLlama:
 
     def __init__(self, cfg: LlamaConfig, *, rank: int, world: int, device, batch: int, max_len: int,
                  comm: str = "sparknet", runtime=None, group=None, seed: int = 0, gemm: str | None = None,
-                 pdl: bool = True):
+                 pdl: bool = True, attention: str = "split"):
         if cfg.heads % world or cfg.kv_heads % world or cfg.ffn % world or cfg.vocab % world:
             raise ValueError(f"model does not shard evenly over {world} GPUs")
         if comm not in ("sparknet", "nccl"):
@@ -82,7 +82,10 @@ class TPLlama:
             raise ValueError("gemm must be 'sparknet' or 'cublas'")
         if (cfg.ffn // world) % INTERLEAVE_ROWS:
             raise ValueError("the FFN shard must be a multiple of 64 features")
+        if attention not in ("split", "cluster"):
+            raise ValueError("attention must be 'split' (workspace merge) or 'cluster' (cluster merge)")
         self.gemm = gemm
+        self.attention = attention
         self.cfg, self.rank, self.world, self.device = cfg, rank, world, torch.device(device)
         self.batch, self.max_len, self.comm, self.runtime, self.group = batch, max_len, comm, runtime, group
         self.C = _native.load()
@@ -193,8 +196,12 @@ class TPLlama:
                 self._linear(self.x, L["wqkv"], self.qkv)
                 C.rope_qkv_cache(self.qkv, self.cos, self.sin, self.positions, self.q, L["k"], L["v"], self.hq,
                                  self.hkv)
-            C.decode_attention(self.q, L["k"], L["v"], self.lengths, self.attn, self.workspace, self.max_len, scale,
-                               self.pdl)
+            if self.attention == "cluster":
+                C.decode_attention_cluster(self.q, L["k"], L["v"], self.lengths, self.attn, self.max_len, scale,
+                                           self.pdl)
+            else:
+                C.decode_attention(self.q, L["k"], L["v"], self.lengths, self.attn, self.workspace, self.max_len,
+                                   scale, self.pdl)
             self._linear(self.attn.view(self.batch, -1), L["wo"], self.partial)
             self._add_norm(self.partial, L["ln2"])
             self._swiglu(self.x, L["wgu"], self.act)

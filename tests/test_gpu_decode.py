@@ -1,6 +1,7 @@
 """Decode-step kernels against plain PyTorch fp32 references (GPU)."""
 
 import math
+import os
 
 import pytest
 
@@ -58,6 +59,42 @@ def test_decode_attention(device, native, B, Hq, Hkv, L):
     for b in range(B):
         n = int(lengths[b])
         k = kc[b, :n].float().repeat_interleave(G, dim=1)          # [n, Hq, 128]
+        v = vc[b, :n].float().repeat_interleave(G, dim=1)
+        s = torch.einsum("hd,nhd->hn", q[b].float(), k) / math.sqrt(128)
+        ref = torch.einsum("hn,nhd->hd", s.softmax(-1), v)
+        torch.testing.assert_close(out[b].float(), ref, rtol=2e-2, atol=2e-2)
+
+
+EXPERIMENTAL = pytest.mark.skipif(os.environ.get("SPARKNET_TEST_EXPERIMENTAL") != "1",
+                                  reason="kernel not yet run on a GPU: SPARKNET_TEST_EXPERIMENTAL=1 runs it")
+
+
+@EXPERIMENTAL
+@pytest.mark.parametrize("B,Hq,Hkv,L", [(1, 8, 1, 1025), (4, 8, 1, 300), (2, 64, 8, 129), (64, 8, 1, 1280),
+                                        (3, 4, 4, 33), (8, 8, 1, 1296), (2, 16, 1, 40), (1, 1, 1, 7)])
+def test_decode_attention_cluster(device, native, B, Hq, Hkv, L):
+    """The cluster variant against the fp32 reference, and against the split-KV kernel."""
+    Lmax = L + 7
+    q = torch.randn(B, Hq, 128, device=device).to(torch.bfloat16)
+    kc = torch.randn(B, Lmax, Hkv, 128, device=device).to(torch.bfloat16)
+    vc = torch.randn(B, Lmax, Hkv, 128, device=device).to(torch.bfloat16)
+    lengths = torch.randint(1, L + 1, (B,), dtype=torch.int32, device=device)
+    lengths[0] = L
+    out = torch.empty(B, Hq, 128, dtype=torch.bfloat16, device=device)
+    native.decode_attention_cluster(q, kc, vc, lengths, out, L, 1 / math.sqrt(128))
+    again = torch.empty_like(out)
+    native.decode_attention_cluster(q, kc, vc, lengths, again, L, 1 / math.sqrt(128), True)
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    ws = torch.zeros(native.attention_workspace_floats(B, Hq, Hkv, L, sms), dtype=torch.float32, device=device)
+    split = torch.empty_like(out)
+    native.decode_attention(q, kc, vc, lengths, split, ws, L, 1 / math.sqrt(128))
+    torch.cuda.synchronize()
+    assert torch.equal(out, again)  # deterministic: spans merge in span order
+    torch.testing.assert_close(out.float(), split.float(), rtol=1e-2, atol=1e-2)
+    G = Hq // Hkv
+    for b in range(B):
+        n = int(lengths[b])
+        k = kc[b, :n].float().repeat_interleave(G, dim=1)
         v = vc[b, :n].float().repeat_interleave(G, dim=1)
         s = torch.einsum("hd,nhd->hn", q[b].float(), k) / math.sqrt(128)
         ref = torch.einsum("hn,nhd->hd", s.softmax(-1), v)
