@@ -572,10 +572,18 @@ static inline cudaError_t launch_cluster_g(const __nv_bfloat16* q, const __nv_bf
                                            bool pdl) {
   auto kernel = k_decode_attn_cluster<G, S, kClusterNT>;
   const int smem = int(sizeof(ClusterSmem<G, kClusterNT>));
-  // function attributes are per device context and cheap to set again: no allocation
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e == cudaSuccess && S > 8) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  // function attributes belong to each device's context: set once per device (the
+  // first call, which is an eager one before any graph capture)
+  static int attr_done[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64 || !attr_done[dev]) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e == cudaSuccess && S > 8) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+    if (dev >= 0 && dev < 64) attr_done[dev] = 1;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(S, B * Hkv, 1);
   cfg.blockDim = dim3(kAttnThreads, 1, 1);
