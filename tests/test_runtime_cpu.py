@@ -125,3 +125,15 @@ def test_stream_switch_orders_after_the_previous_stream(monkeypatch):
     assert len(log) == 2
     call(a)
     assert log[2:] == [("record", "b"), ("wait", "a", rt._stream_event)]
+
+
+def test_ag_copy_order_setting(monkeypatch):
+    from sparknet.oneshot.runtime import ag_copy_order
+
+    monkeypatch.delenv("SPARKNET_AG_COPY_ORDER", raising=False)
+    assert ag_copy_order() == 0 and ag_copy_order("chunk-major") == 1
+    monkeypatch.setenv("SPARKNET_AG_COPY_ORDER", "chunk-major")
+    assert ag_copy_order() == 1 and ag_copy_order("spread") == 0
+    monkeypatch.setenv("SPARKNET_AG_COPY_ORDER", "diagonal")
+    with pytest.raises(ValueError, match="copy order"):
+        ag_copy_order()
