@@ -46,7 +46,8 @@ def run_decode_bench(args, rank, world, device, cpu_group):
         runtime.prepare((torch.bfloat16,))
     t0 = time.perf_counter()
     model = TPLlama(cfg, rank=rank, world=world, device=device, batch=batch, max_len=max_len, comm=comm,
-                    runtime=runtime, group=None, attention=getattr(args, "attention", "split"))
+                    runtime=runtime, group=None, attention=getattr(args, "attention", "split"),
+                    prefetch=getattr(args, "prefetch", False))
     model.fill_prompt_cache(PROMPT)
     torch.cuda.synchronize()
     init_s = time.perf_counter() - t0
@@ -119,7 +120,7 @@ def run_decode_bench(args, rank, world, device, cpu_group):
                    "global_batch": batch, "seq_len": PROMPT, "parallelism": f"tp{world}", "comm": comm,
                    "gemm": model.gemm, "programmatic_dependent_launch": model.pdl,
                    "collective_pdl": bool(runtime.pdl) if runtime is not None else False,
-                   "attention": model.attention,
+                   "attention": model.attention, "l2_prefetch": model.prefetch,
                    "l2": "weights per step far exceed L2 (126 MB)"},
         "gpu_launches": model.launches_per_step() * args.steps,
         "clocks": clocks,

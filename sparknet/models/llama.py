@@ -70,7 +70,7 @@ class TPLlama:
 
     def __init__(self, cfg: LlamaConfig, *, rank: int, world: int, device, batch: int, max_len: int,
                  comm: str = "sparknet", runtime=None, group=None, seed: int = 0, gemm: str | None = None,
-                 pdl: bool = True, attention: str = "split"):
+                 pdl: bool = True, attention: str = "split", prefetch: bool = False, prefetch_mb: int = 48):
         if cfg.heads % world or cfg.kv_heads % world or cfg.ffn % world or cfg.vocab % world:
             raise ValueError(f"model does not shard evenly over {world} GPUs")
         if comm not in ("sparknet", "nccl"):
@@ -86,6 +86,12 @@ class TPLlama:
             raise ValueError("attention must be 'split' (workspace merge) or 'cluster' (cluster merge)")
         self.gemm = gemm
         self.attention = attention
+        # L2 prefetch of the next GEMM's weights during attention and the all-reduces
+        # (phases that leave HBM idle): O before attention, the first `prefetch_mb` MB
+        # of gate/up before the all-reduce after O, the next layer's QKV (or the LM
+        # head's first `prefetch_mb` MB) before the all-reduce after down.
+        self.prefetch = bool(prefetch)
+        self.prefetch_bytes = int(prefetch_mb) << 20
         self.cfg, self.rank, self.world, self.device = cfg, rank, world, torch.device(device)
         self.batch, self.max_len, self.comm, self.runtime, self.group = batch, max_len, comm, runtime, group
         self.C = _native.load()
@@ -196,6 +202,8 @@ class TPLlama:
                 self._linear(self.x, L["wqkv"], self.qkv)
                 C.rope_qkv_cache(self.qkv, self.cos, self.sin, self.positions, self.q, L["k"], L["v"], self.hq,
                                  self.hkv)
+            if self.prefetch:
+                C.l2_prefetch(L["wo"], -1)
             if self.attention == "cluster":
                 C.decode_attention_cluster(self.q, L["k"], L["v"], self.lengths, self.attn, self.max_len, scale,
                                            self.pdl)
@@ -203,10 +211,15 @@ class TPLlama:
                 C.decode_attention(self.q, L["k"], L["v"], self.lengths, self.attn, self.workspace, self.max_len,
                                    scale, self.pdl)
             self._linear(self.attn.view(self.batch, -1), L["wo"], self.partial)
+            if self.prefetch:
+                C.l2_prefetch(L["wgu"], self.prefetch_bytes)
             self._add_norm(self.partial, L["ln2"])
             self._swiglu(self.x, L["wgu"], self.act)
             self._linear(self.act, L["wdown"], self.partial)
-            nxt = self.layers[i + 1]["ln1"] if i + 1 < len(self.layers) else self.norm
+            last = i + 1 == len(self.layers)
+            if self.prefetch:
+                C.l2_prefetch(self.lm_head if last else self.layers[i + 1]["wqkv"], self.prefetch_bytes if last else -1)
+            nxt = self.norm if last else self.layers[i + 1]["ln1"]
             self._add_norm(self.partial, nxt)
         self._linear(self.x, self.lm_head, self.logits)
         C.row_argmax(self.logits, self.rank * self.v, self.best)
@@ -245,12 +258,14 @@ class TPLlama:
         """This package's kernel launches in one step (torch index/copy ops and cuBLAS
         GEMMs excluded): per layer attention and two norms (fused with the all-reduce on
         the NVLink arm), plus four GEMMs with RoPE and SwiGLU fused (``gemm="sparknet"``)
-        or the RoPE and SwiGLU kernels (cuBLAS arm)."""
+        or the RoPE and SwiGLU kernels (cuBLAS arm), plus three L2 prefetches with
+        ``prefetch=True``."""
         # sparknet: QKV+RoPE, O, gate/up+SwiGLU, down GEMMs; cuBLAS arm: RoPE and SwiGLU kernels
         per_layer = 1 + 2 + (4 if self.gemm == "sparknet" else 2)
         own_gather = 1 if (self.world > 1 and self.comm == "sparknet") else 0
         lm_head = 1 if self.gemm == "sparknet" else 0
-        return 1 + self.cfg.layers * per_layer + lm_head + 1 + own_gather
+        prefetch = 3 * self.cfg.layers if self.prefetch else 0
+        return 1 + self.cfg.layers * per_layer + lm_head + 1 + own_gather + prefetch
 
 
 class _null:
