@@ -87,9 +87,9 @@ class TPLlama:
         self.gemm = gemm
         self.attention = attention
         # L2 prefetch of the next GEMM's weights during attention and the all-reduces
-        # (phases that leave HBM idle): O before attention, the first `prefetch_mb` MB
-        # of gate/up before the all-reduce after O, the next layer's QKV (or the LM
-        # head's first `prefetch_mb` MB) before the all-reduce after down.
+        # (phases that leave HBM idle), at most `prefetch_mb` MB each (L2 is 126 MB): O
+        # before attention, gate/up before the all-reduce after O, the next layer's QKV
+        # (or the LM head) before the all-reduce after down.
         self.prefetch = bool(prefetch)
         self.prefetch_bytes = int(prefetch_mb) << 20
         self.cfg, self.rank, self.world, self.device = cfg, rank, world, torch.device(device)
@@ -203,7 +203,7 @@ class TPLlama:
                 C.rope_qkv_cache(self.qkv, self.cos, self.sin, self.positions, self.q, L["k"], L["v"], self.hq,
                                  self.hkv)
             if self.prefetch:
-                C.l2_prefetch(L["wo"], -1)
+                C.l2_prefetch(L["wo"], self.prefetch_bytes)
             if self.attention == "cluster":
                 C.decode_attention_cluster(self.q, L["k"], L["v"], self.lengths, self.attn, self.max_len, scale,
                                            self.pdl)
@@ -218,7 +218,7 @@ class TPLlama:
             self._linear(self.act, L["wdown"], self.partial)
             last = i + 1 == len(self.layers)
             if self.prefetch:
-                C.l2_prefetch(self.lm_head if last else self.layers[i + 1]["wqkv"], self.prefetch_bytes if last else -1)
+                C.l2_prefetch(self.lm_head if last else self.layers[i + 1]["wqkv"], self.prefetch_bytes)
             nxt = self.norm if last else self.layers[i + 1]["ln1"]
             self._add_norm(self.partial, nxt)
         self._linear(self.x, self.lm_head, self.logits)
