@@ -137,3 +137,18 @@ def test_ag_copy_order_setting(monkeypatch):
     monkeypatch.setenv("SPARKNET_AG_COPY_ORDER", "diagonal")
     with pytest.raises(ValueError, match="copy order"):
         ag_copy_order()
+
+
+def test_entry_point_imports_the_built_extension_in_a_fresh_interpreter():
+    """What the build check runs after compiling: a new interpreter that has not
+    imported torch yet must still import the extension."""
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    if not list((root / "sparknet").glob("_C*.so")):
+        pytest.skip("extension not built")
+    proc = subprocess.run([sys.executable, "-c", "import __graft_entry__ as g; g.import_package(); print('ok')"],
+                          cwd=root, capture_output=True, text=True, timeout=300)
+    assert proc.returncode == 0 and proc.stdout.strip().endswith("ok"), proc.stderr[-2000:]
