@@ -21,6 +21,7 @@ def load():
     if _module is not None:
         return _module
     try:
+        importlib.import_module("torch")  # the extension links libc10 / libtorch: torch loads them
         _module = importlib.import_module("sparknet._C")
     except Exception as exc:  # noqa: BLE001 - re-raised with context below
         _error = exc
