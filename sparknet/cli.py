@@ -6,7 +6,7 @@ Command tree after the reference's (``sparknet/cli.py:332-462``):
   sparknet topology validate|render|example|discover|subset|inventory
   sparknet nccl env|validate|profiles|patches
   sparknet policy show
-  sparknet probe doctor|nvlink|gpudirect|render-command|fleet|summarize|collectives|failstop
+  sparknet probe doctor|nvlink|gpudirect|counters|render-command|fleet|summarize|collectives|failstop
 
 Everything except ``probe collectives`` and ``probe failstop`` runs without torch.
 """
@@ -208,6 +208,26 @@ def cmd_probe_nvlink(args) -> int:
     return 0 if report.get("ready", {}).get("p2p") else 1
 
 
+def cmd_probe_counters(args) -> int:
+    """NVLink counters of every GPU (NVML, read-only): a snapshot, or with --interval the
+    counters that moved over that many seconds; exit 1 if an error counter moved."""
+    import time
+
+    from sparknet.probe import counters
+
+    before = counters.nvlink_counters()
+    if args.interval <= 0:
+        print(json.dumps(before, indent=2, sort_keys=True))
+        return 0
+    time.sleep(args.interval)
+    after = counters.nvlink_counters()
+    errors = counters.error_deltas(before, after)
+    moved = errors if args.errors_only else counters.deltas(before, after)
+    print(json.dumps({"interval_s": args.interval, "deltas": moved, "error_counters_moved": bool(errors)},
+                     indent=2, sort_keys=True))
+    return 1 if errors else 0
+
+
 def _environments(gmap: dict, transport: str, profile: str | None) -> dict[str, dict[str, str]]:
     return {node["name"]: topology.node_environment(gmap, node["name"], transport, profile=profile)
             for node in gmap["nodes"]}
@@ -371,6 +391,10 @@ def parser() -> argparse.ArgumentParser:
         pg = pr.add_parser(name, help="what this host offers the NVLink transport (P2P, NVLS, fabric)")
         pg.add_argument("--json", action="store_true")
         pg.set_defaults(func=cmd_probe_nvlink)
+    pc = pr.add_parser("counters", help="NVLink throughput and error counters (NVML, read-only)")
+    pc.add_argument("--interval", type=float, default=0.0, help="seconds between two snapshots (0: one snapshot)")
+    pc.add_argument("--errors-only", action="store_true", help="with --interval: only the error counters")
+    pc.set_defaults(func=cmd_probe_counters)
 
     def probe_options(parser_):
         parser_.add_argument("--transport", required=True, choices=topology.TRANSPORTS)

@@ -80,3 +80,33 @@ def test_version(capsys):
     with pytest.raises(SystemExit):
         cli.main(["--version"])
     assert "sparknet" in capsys.readouterr().out
+
+
+def test_probe_counters_snapshot_and_deltas(capsys, monkeypatch):
+    from sparknet.probe import nvml as nvml_mod
+    from tests.fake_nvml import FakeNVML
+
+    nv = FakeNVML()
+    monkeypatch.setattr(nvml_mod, "load", lambda: nv)
+    code, out, _ = run(capsys, "probe", "counters")
+    snap = json.loads(out)
+    assert code == 0 and "gpu0.nvlink_tx_kib" in snap and snap["gpu7.nvlink_replay"] == 0
+    # an interval over which only throughput moves: exit 0; an error counter that moves: exit 1
+    import time as time_mod
+
+    def step(seconds):
+        nv.tx[1] += 64
+
+    monkeypatch.setattr(time_mod, "sleep", step)
+    code, out, _ = run(capsys, "probe", "counters", "--interval", "0.1")
+    report = json.loads(out)
+    assert code == 0 and report["deltas"]["gpu1.nvlink_tx_kib"] == 64 and not report["error_counters_moved"]
+
+    def fault(seconds):
+        nv.errors[2] += 1
+
+    monkeypatch.setattr(time_mod, "sleep", fault)
+    code, out, _ = run(capsys, "probe", "counters", "--interval", "0.1", "--errors-only")
+    report = json.loads(out)
+    assert code == 1 and report["deltas"] == {f"gpu2.nvlink_{k}": 1 for k in ("replay", "recovery", "crc_flit",
+                                                                                "crc_data")}
