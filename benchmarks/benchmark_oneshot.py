@@ -4,6 +4,9 @@
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 benchmarks/benchmark_oneshot.py --sizes 10240 61440 491520 2097152
     torchrun --nproc-per-node 8 --master-addr 127.0.0.1 benchmarks/benchmark_oneshot.py --fused-norm-tokens 1 8 32 128 256
 
+``--arms nvlink-graph nvlink-pdl-graph nccl-graph`` adds the NVLink graph captured with
+programmatic dependent launch (each call scheduled while the previous one runs).
+
 With ``--fused-norm-tokens`` the arms are the decode epilogue instead: the fused NVLink
 all-reduce + residual add + RMSNorm (hidden 8192, bf16, eps 1e-5) against NCCL's
 all-reduce followed by this package's add + RMSNorm kernel (the same rounding points).
@@ -40,6 +43,8 @@ ROOT = Path(__file__).resolve().parent.parent
 sys.path.insert(0, str(ROOT))
 
 ARMS = ("nvlink-graph", "nccl-graph", "nvlink-eager", "nccl-eager")
+# also selectable: the NVLink graph captured with programmatic dependent launch
+EXTRA_ARMS = ("nvlink-pdl-graph",)
 
 
 def git_state() -> dict:
@@ -67,7 +72,7 @@ def main() -> int:
     ap.add_argument("--blocks", type=int, default=6)
     ap.add_argument("--samples-per-block", type=int, default=3)
     ap.add_argument("--calls", type=int, default=64)
-    ap.add_argument("--arms", nargs="+", default=list(ARMS), choices=ARMS)
+    ap.add_argument("--arms", nargs="+", default=list(ARMS), choices=ARMS + EXTRA_ARMS)
     ap.add_argument("--fused-norm-tokens", type=int, nargs="*", default=[],
                     help="time the fused all-reduce + residual + RMSNorm for these token counts instead")
     ap.add_argument("--hidden", type=int, default=8192)
@@ -111,7 +116,8 @@ def main() -> int:
         }
         graphs = {}
         stream = torch.cuda.Stream(device=device)
-        for arm, fn in (("nvlink-graph", calls["nvlink-eager"]), ("nccl-graph", calls["nccl-eager"])):
+        for arm, fn in (("nvlink-graph", calls["nvlink-eager"]), ("nvlink-pdl-graph", calls["nvlink-eager"]),
+                        ("nccl-graph", calls["nccl-eager"])):
             if arm not in args.arms:
                 continue
             fn()
@@ -119,9 +125,11 @@ def main() -> int:
             stream.wait_stream(torch.cuda.current_stream())
             g = torch.cuda.CUDAGraph()
             ctx = rt.capture(stream=stream) if arm.startswith("nvlink") else _Null()
+            rt.set_pdl(arm == "nvlink-pdl-graph")  # the launch attribute is recorded in the graph
             with torch.cuda.graph(g, stream=stream), ctx:
                 for _ in range(args.calls):
                     fn()
+            rt.set_pdl(False)
             graphs[arm] = g
         samples = {arm: [] for arm in args.arms}
         for block in range(args.blocks):
