@@ -27,6 +27,8 @@ from .runtime import (
     SUPPORTED_WORLD_SIZES,
     TOPOLOGIES,
     NvlinkAllReduce,
+    discover_hcas,
+    discover_nvlink_gpus,
     is_supported,
 )
 
@@ -34,6 +36,7 @@ AllReduce = NvlinkAllReduce
 
 __all__ = [
     "API_VERSION", "AllReduce", "DEFAULT_MAX_GATHER_BYTES", "DEFAULT_MAX_SIZE", "KernelResolutionFrozenError",
-    "NvlinkAllReduce", "SUPPORTED_DTYPES", "SUPPORTED_WORLD_SIZES", "TOPOLOGIES", "freeze_kernel_resolution",
-    "is_supported", "kernel_resolution_frozen", "thaw_kernel_resolution",
+    "NvlinkAllReduce", "SUPPORTED_DTYPES", "SUPPORTED_WORLD_SIZES", "TOPOLOGIES", "discover_hcas",
+    "discover_nvlink_gpus", "freeze_kernel_resolution", "is_supported", "kernel_resolution_frozen",
+    "thaw_kernel_resolution",
 ]

@@ -124,6 +124,27 @@ def is_supported(device: torch.device | int | str | None = None) -> bool:
     return (major, minor) == (10, 0) and _native.available()
 
 
+def discover_hcas() -> tuple[str, ...]:
+    """The RDMA devices the collectives would use: always none on an NVSwitch box.
+
+    The reference picks up to two active RoCE v2 HCAs here (reference
+    ``sparknet/oneshot/runtime.py:168-189``) because its one-shot path writes over
+    RDMA.  Here every byte of a collective crosses NVLink from inside the kernels, so
+    no RDMA device takes part; the name stays importable for code written against the
+    reference.  The NVLink devices are :func:`discover_nvlink_gpus`.
+    """
+    return ()
+
+
+def discover_nvlink_gpus() -> tuple[int, ...]:
+    """CUDA device indices this process can use for the NVLink collectives: B200s
+    (compute capability 10.0) that reach every other listed device peer to peer."""
+    if not torch.cuda.is_available():
+        return ()
+    gpus = [i for i in range(torch.cuda.device_count()) if torch.cuda.get_device_capability(i) == (10, 0)]
+    return tuple(i for i in gpus if all(i == j or torch.cuda.can_device_access_peer(i, j) for j in gpus))
+
+
 def normalize_device(device: torch.device | int | str) -> torch.device:
     if isinstance(device, int):
         device = torch.device("cuda", device)
@@ -1148,4 +1169,5 @@ class NvlinkAllReduce:
 
 
 __all__ = ["API_VERSION", "DEFAULT_MAX_GATHER_BYTES", "DEFAULT_MAX_SIZE", "SUPPORTED_DTYPES",
-           "SUPPORTED_WORLD_SIZES", "TOPOLOGIES", "NvlinkAllReduce", "is_supported"]
+           "SUPPORTED_WORLD_SIZES", "TOPOLOGIES", "NvlinkAllReduce", "discover_hcas", "discover_nvlink_gpus",
+           "is_supported"]

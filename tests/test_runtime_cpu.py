@@ -152,3 +152,16 @@ def test_entry_point_imports_the_built_extension_in_a_fresh_interpreter():
     proc = subprocess.run([sys.executable, "-c", "import __graft_entry__ as g; g.import_package(); print('ok')"],
                           cwd=root, capture_output=True, text=True, timeout=300)
     assert proc.returncode == 0 and proc.stdout.strip().endswith("ok"), proc.stderr[-2000:]
+
+
+def test_reference_exports_are_importable():
+    """Every name the reference's sparknet.oneshot exports imports here too; on an
+    NVSwitch box no RDMA device takes part, so discover_hcas() finds none."""
+    import sparknet.oneshot as oneshot
+
+    for name in ("API_VERSION", "AllReduce", "DEFAULT_MAX_GATHER_BYTES", "DEFAULT_MAX_SIZE",
+                 "KernelResolutionFrozenError", "SUPPORTED_DTYPES", "SUPPORTED_WORLD_SIZES", "TOPOLOGIES",
+                 "discover_hcas", "freeze_kernel_resolution", "is_supported", "thaw_kernel_resolution"):
+        assert hasattr(oneshot, name), name
+    assert oneshot.discover_hcas() == ()
+    assert oneshot.discover_nvlink_gpus() == ()  # no CUDA device on this host
