@@ -15,4 +15,11 @@ from .counters import deltas, nvlink_counters
 from .doctor import local_problems
 from .nvlink_report import nvlink_report
 
-__all__ = ["deltas", "docker_probe_command", "local_problems", "nvlink_counters", "nvlink_report"]
+# The reference's host capability report (GPUDirect RDMA readiness) is, on an NVSwitch
+# box, the NVLink report: the same question (what does this host offer the
+# collectives' transport) for the transport used here.  `sparknet probe gpudirect`
+# prints it too.
+gpudirect_report = nvlink_report
+
+__all__ = ["deltas", "docker_probe_command", "gpudirect_report", "local_problems", "nvlink_counters",
+           "nvlink_report"]

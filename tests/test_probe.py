@@ -149,3 +149,12 @@ def test_failstop_bounds():
     assert failstop.problems(unnamed, 1000)
     victim = {"rank": 1, "victim": 1, "eager": {"victim": True, "recovered": True}}
     assert failstop.problems(victim, 1000) == []
+
+
+def test_reference_report_names():
+    import sparknet.probe as probe
+    from sparknet.integration.vllm import REQUIRED_API_VERSION
+    from sparknet.oneshot.runtime import API_VERSION
+
+    assert probe.gpudirect_report is probe.nvlink_report
+    assert REQUIRED_API_VERSION == API_VERSION
