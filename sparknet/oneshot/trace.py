@@ -102,6 +102,36 @@ def valid(recs):
     return recs[(recs[:, 2] > 0) & (recs[:, 3] >= recs[:, 2])]
 
 
+def select(recs, *, min_seq: int = 0, max_seq: int | None = None, nbytes: int | None = None, op: int | None = None):
+    """The valid records of a sequence range and, optionally, one payload size or one
+    collective (``OP_*`` code of the runtime)."""
+    r = valid(recs)
+    seq = r[:, 0] & 0xFFFFFFFF
+    keep = seq >= min_seq
+    if max_seq is not None:
+        keep &= seq <= max_seq
+    if nbytes is not None:
+        keep &= r[:, 1] == nbytes
+    if op is not None:
+        keep &= (r[:, 0] >> 32) == op
+    return r[keep]
+
+
+def sizes(recs, top: int = 8) -> dict[int, int]:
+    """Collective counts of the most frequent payload sizes (bytes), most frequent first."""
+    counts: dict[int, int] = {}
+    for size in valid(recs)[:, 1].tolist():
+        counts[int(size)] = counts.get(int(size), 0) + 1
+    return dict(sorted(counts.items(), key=lambda item: -item[1])[:top])
+
+
+def peer_arrival(record, peer: int) -> int:
+    """Nanoseconds from a collective's entry to the arrival of ``peer``'s first pack
+    (this rank's clock), or -1 when the record holds no arrival for that peer."""
+    arrival, entry = int(record[4 + peer]), int(record[2])
+    return arrival - entry if arrival and entry else -1
+
+
 def _percentiles(values) -> dict:
     import numpy as np
 
@@ -159,8 +189,8 @@ def pair_clock(a: tuple[dict, object], b: tuple[dict, object]) -> dict:
     return {"pairs": len(offs), "offset_us": float(np.median(offs)), "delay_us": float(np.median(delays))}
 
 
-def summarize(paths: list[str]) -> dict:
-    traces = [read(p) for p in paths]
+def summarize(paths: list[str], *, min_seq: int = 0, max_seq: int | None = None, nbytes: int | None = None) -> dict:
+    traces = [(h, select(r, min_seq=min_seq, max_seq=max_seq, nbytes=nbytes)) for h, r in (read(p) for p in paths)]
     out = {"ranks": {}, "pairs": {}}
     for h, r in traces:
         out["ranks"][h["rank"]] = {"phases": phases(h, r), "clock_offset_ns": h["clock_offset_ns"],
@@ -175,8 +205,19 @@ def summarize(paths: list[str]) -> dict:
 def main(argv=None) -> int:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("files", nargs="+", help="trace files, one per rank")
+    p.add_argument("--min-seq", type=int, default=0)
+    p.add_argument("--max-seq", type=int)
+    p.add_argument("--nbytes", type=int, help="only collectives of this payload size")
+    p.add_argument("--last-seq", action="store_true", help="print each file's newest sequence and exit")
     args = p.parse_args(argv)
-    print(json.dumps(summarize(args.files), indent=2))
+    if args.last_seq:
+        newest = {}
+        for path in args.files:
+            r = valid(read(path)[1])
+            newest[path] = int((r[:, 0] & 0xFFFFFFFF).max()) if len(r) else 0
+        print(json.dumps(newest, indent=2))
+        return 0
+    print(json.dumps(summarize(args.files, min_seq=args.min_seq, max_seq=args.max_seq, nbytes=args.nbytes), indent=2))
     return 0
 
 

@@ -56,3 +56,33 @@ def test_phases_and_pair_clock(tmp_path):
 def test_enabled_flag():
     assert trace.enabled({"SPARKNET_TRACE": "1"}) and not trace.enabled({"SPARKNET_TRACE": "0"})
     assert not trace.enabled({})
+
+
+def test_select_sizes_and_peer_arrival(tmp_path):
+    path = synthetic(tmp_path, 0, 4, 0, range(1, 41), delay_ns=2500)
+    header, recs = trace.read(path)
+    recs = recs.copy()
+    recs[(np.arange(trace.RECORDS) % 4 == 0) & (recs[:, 2] > 0), 1] = 491520   # every 4th collective is larger
+    assert len(trace.select(recs)) == 40
+    assert len(trace.select(recs, min_seq=11, max_seq=20)) == 10
+    assert len(trace.select(recs, nbytes=491520)) == 10 and len(trace.select(recs, op=1)) == 40
+    assert len(trace.select(recs, op=2)) == 0
+    assert trace.sizes(recs) == {10240: 30, 491520: 10}
+    r = trace.select(recs, min_seq=5, max_seq=5)[0]
+    assert trace.peer_arrival(r, 2) == 2500 and trace.peer_arrival(r, 0) == 0
+    r[4 + 3] = 0
+    assert trace.peer_arrival(r, 3) == -1
+
+
+def test_cli_selection_and_last_seq(tmp_path, capsys):
+    import json
+
+    a = synthetic(tmp_path, 0, 2, 0, range(1, 51))
+    b = synthetic(tmp_path, 1, 2, 300_000, range(1, 51))
+    assert trace.main([a, b, "--min-seq", "21", "--max-seq", "30"]) == 0
+    out = json.loads(capsys.readouterr().out)
+    assert out["ranks"]["0"]["phases"]["collectives"] == 10 and out["pairs"]["0-1"]["pairs"] == 10
+    assert trace.main([a, b, "--nbytes", "999"]) == 0
+    assert json.loads(capsys.readouterr().out)["ranks"]["1"]["phases"]["collectives"] == 0
+    assert trace.main([a, "--last-seq"]) == 0
+    assert json.loads(capsys.readouterr().out) == {a: 50}
