@@ -3,6 +3,7 @@
 from .patchset import export as export_patches, patch_directory, series
 from .profiles import (
     COMMON_ENV,
+    COMMON_IB_ENV,
     PATCH_CONTROLS,
     PROFILES,
     REFERENCE_IB_ENV,
@@ -15,6 +16,6 @@ from .profiles import (
     size_bytes,
 )
 
-__all__ = ["COMMON_ENV", "PATCH_CONTROLS", "PROFILES", "REFERENCE_IB_ENV", "environment", "export_patches",
+__all__ = ["COMMON_ENV", "COMMON_IB_ENV", "PATCH_CONTROLS", "PROFILES", "REFERENCE_IB_ENV", "environment", "export_patches",
            "patch_directory", "problems", "profile", "profile_problems", "profiles_for", "required_patches",
            "series", "size_bytes"]

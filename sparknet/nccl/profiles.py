@@ -33,6 +33,7 @@ REFERENCE_IB_ENV = {
     "NCCL_DEBUG_SUBSYS": "INIT",
     "TORCH_NCCL_ASYNC_ERROR_HANDLING": "1",
 }
+COMMON_IB_ENV = REFERENCE_IB_ENV  # the reference's name for the same environment
 # Every NVLink profile shares these: asynchronous error handling and quiet logs.
 COMMON_ENV = {
     "NCCL_DEBUG": "WARN",
@@ -173,5 +174,5 @@ def problems(env: dict[str, str], *, world: int) -> list[str]:
     return errors
 
 
-__all__ = ["COMMON_ENV", "PATCH_CONTROLS", "PROFILES", "REFERENCE_IB_ENV", "environment", "problems", "profile",
+__all__ = ["COMMON_ENV", "COMMON_IB_ENV", "PATCH_CONTROLS", "PROFILES", "REFERENCE_IB_ENV", "environment", "problems", "profile",
            "profile_problems", "profiles_for", "required_patches", "size_bytes"]
