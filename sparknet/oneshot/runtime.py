@@ -1164,8 +1164,11 @@ class NvlinkAllReduce:
                 self._transport = None
 
     def __del__(self) -> None:  # pragma: no cover - defensive teardown
-        with contextlib.suppress(Exception):
+        # no module globals here: at interpreter exit they may already be gone
+        try:
             self.close()
+        except Exception:  # noqa: BLE001
+            pass
 
 
 __all__ = ["API_VERSION", "DEFAULT_MAX_GATHER_BYTES", "DEFAULT_MAX_SIZE", "SUPPORTED_DTYPES",
