@@ -119,7 +119,9 @@ void map_rw(CUdeviceptr va, size_t bytes, CUmemGenericAllocationHandle h, int de
   a.location.type = CU_MEM_LOCATION_TYPE_DEVICE;
   a.location.id = device;
   a.flags = CU_MEM_ACCESS_FLAGS_PROT_READWRITE;
-  ck(d.cuMemSetAccess(va, bytes, &a, 1), "cuMemSetAccess");
+  const CUresult r = d.cuMemSetAccess(va, bytes, &a, 1);
+  if (r != CUDA_SUCCESS) d.cuMemUnmap(va, bytes);  // leave nothing mapped behind the error
+  ck(r, "cuMemSetAccess");
 }
 
 sockaddr_un abstract_addr(const std::string& name, socklen_t* len) {
@@ -259,11 +261,17 @@ LocalRegion::LocalRegion(int device, size_t bytes, size_t align) : device_(devic
   CUmemAllocationProp p = device_prop(device);
   CUmemGenericAllocationHandle h;
   ck(d.cuMemCreate(&h, bytes_, &p, 0), "cuMemCreate");
+  CUdeviceptr va = 0;
+  try {  // a constructor that throws runs no destructor: release here what it took
+    ck(d.cuMemAddressReserve(&va, bytes_, g, 0, 0), "cuMemAddressReserve");
+    map_rw(va, bytes_, h, device);
+  } catch (...) {
+    if (va) d.cuMemAddressFree(va, bytes_);
+    d.cuMemRelease(h);
+    throw;
+  }
   handle_ = h;
-  CUdeviceptr va;
-  ck(d.cuMemAddressReserve(&va, bytes_, g, 0, 0), "cuMemAddressReserve");
   ptr_ = va;
-  map_rw(va, bytes_, h, device);
 }
 
 LocalRegion::~LocalRegion() {
@@ -296,10 +304,16 @@ uint64_t LocalRegion::map_peer(int fd, size_t bytes) {
   ck(d.cuMemImportFromShareableHandle(&h, reinterpret_cast<void*>(static_cast<uintptr_t>(fd)),
                                       CU_MEM_HANDLE_TYPE_POSIX_FILE_DESCRIPTOR),
      "cuMemImportFromShareableHandle");
-  CUdeviceptr va;
-  ck(d.cuMemAddressReserve(&va, bytes, vmm_granularity(device_), 0, 0), "cuMemAddressReserve(peer)");
-  map_rw(va, bytes, h, device_);
-  peers_.push_back({va, bytes, h});
+  CUdeviceptr va = 0;
+  try {  // the peer is recorded (and released by the destructor) only once it is mapped
+    ck(d.cuMemAddressReserve(&va, bytes, vmm_granularity(device_), 0, 0), "cuMemAddressReserve(peer)");
+    map_rw(va, bytes, h, device_);
+    peers_.push_back({va, bytes, h});
+  } catch (...) {
+    if (va) d.cuMemAddressFree(va, bytes);
+    d.cuMemRelease(h);
+    throw;
+  }
   return va;
 }
 
