@@ -56,6 +56,7 @@ class Comm {
       : rank_(rank), world_(world), device_(device), emulate_(emulate) {
     if (world < 1 || world > kMaxRanks) throw std::invalid_argument("world must be 1..8");
     if (rank < 0 || rank >= world) throw std::invalid_argument("rank out of range");
+    if (!emulate && int(bases.size()) != world) throw std::invalid_argument("need one base address per rank");
     L_ = Layout::make(uint32_t(world), lam_cap, ll_cap, push_cap);
     c10::cuda::CUDAGuard guard(device);
     cudaDeviceProp prop;
@@ -66,12 +67,22 @@ class Comm {
                         cudaHostAllocMapped | cudaHostAllocPortable),
           "cudaHostAlloc(status)");
     memset(status_h_, 0, sizeof(Status) * nstatus);
-    ck_rt(cudaHostGetDevicePointer(reinterpret_cast<void**>(&status_d_), status_h_, 0),
-          "cudaHostGetDevicePointer(status)");
+    const cudaError_t pe = cudaHostGetDevicePointer(reinterpret_cast<void**>(&status_d_), status_h_, 0);
+    if (pe != cudaSuccess) {  // a constructor that throws runs no destructor
+      cudaFreeHost(status_h_);
+      status_h_ = nullptr;
+      ck_rt(pe, "cudaHostGetDevicePointer(status)");
+    }
     for (int i = 0; i < nstatus; ++i) status_h_[i].timeout_us = 10u * 1000u * 1000u;
     if (emulate) {
       // world regions in one device allocation, each rank seeing all of them
-      ck_rt(cudaMalloc(reinterpret_cast<void**>(&emu_blob_), L_.total * world), "cudaMalloc(emulated regions)");
+      const cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&emu_blob_), L_.total * world);
+      if (e != cudaSuccess) {  // a constructor that throws runs no destructor
+        cudaFreeHost(status_h_);
+        status_h_ = nullptr;
+        emu_blob_ = nullptr;
+        ck_rt(e, "cudaMalloc(emulated regions)");
+      }
       for (int w = 0; w < world; ++w) {
         View& v = emu_.v[w];
         memset(&v, 0, sizeof(v));
@@ -80,7 +91,6 @@ class Comm {
       }
       view_ = emu_.v[0];
     } else {
-      if (int(bases.size()) != world) throw std::invalid_argument("need one base address per rank");
       memset(&view_, 0, sizeof(view_));
       for (int q = 0; q < world; ++q) view_.base[q] = reinterpret_cast<char*>(bases[q]);
       view_.status = status_d_;
