@@ -12,6 +12,7 @@
 #include <torch/extension.h>
 
 #include <stdexcept>
+#include <string>
 #include <tuple>
 #include <vector>
 
@@ -59,10 +60,18 @@ std::vector<std::tuple<unsigned long long, unsigned long long, unsigned long lon
     throw std::runtime_error("cudaHostAlloc(ping page) failed");
   memset(page, 0, sizeof(PingPage));
   PingPage* dpage = nullptr;
-  cudaHostGetDevicePointer(reinterpret_cast<void**>(&dpage), page, 0);
-  cudaStream_t s;
-  cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
-  k_clock_probe<<<1, 32, 0, s>>>(dpage, unsigned(rounds), 400000000ull);
+  cudaStream_t s = nullptr;
+  cudaError_t e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&dpage), page, 0);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+  if (e == cudaSuccess) {
+    k_clock_probe<<<1, 32, 0, s>>>(dpage, unsigned(rounds), 400000000ull);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) {  // nothing was launched (or the launch failed): release and report why
+    if (s) cudaStreamDestroy(s);
+    cudaFreeHost(page);
+    throw std::runtime_error(std::string("clock probe set-up: ") + cudaGetErrorString(e));
+  }
   std::vector<std::tuple<unsigned long long, unsigned long long, unsigned long long>> out;
   bool lost = false;
   for (int r = 1; r <= rounds && !lost; ++r) {
