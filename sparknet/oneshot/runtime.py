@@ -198,7 +198,7 @@ class _StatusView:
 # Rates measured on B200 that size the all-gather -> GEMM split between copy CTAs and
 # GEMM CTAs: one CTA pushing 16-byte packs to a peer over NVLink sustains ~20 GB/s
 # (benchmarks/microbench_nvlink.py, store, 4 packs in flight), and the tcgen05 GEMM
-# sustains ~9 TFLOP/s per SM in bf16 (1343.9 TFLOP/s over 148 SMs) and ~10.7 in
+# sustains ~9 TFLOP/s per SM in bf16 (1354.8 TFLOP/s over 148 SMs) and ~10.7 in
 # block-scaled fp8.
 PUSH_GBS_PER_CTA = 20.0
 MIN_COPY_CTAS = 16        # fewer measured slower at TP2 and TP8 on every prefill shape
