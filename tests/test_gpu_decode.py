@@ -259,3 +259,15 @@ def test_prefetch_and_attention_variants_keep_the_step(device, native, attention
         ref.step_kernels()
         torch.cuda.synchronize()
         torch.testing.assert_close(outs[0][0].float(), ref.logits.float(), rtol=5e-2, atol=5e-2)
+
+
+def test_parallel_layer_decode_uses_the_decode_gemm(device, native):
+    """ColumnParallelLinear.decode on few tokens: the tcgen05 decode GEMM, against fp32."""
+    from sparknet.parallel.linear import ColumnParallelLinear
+
+    w = (0.05 * torch.randn(1024, 512, device=device)).to(torch.bfloat16)
+    x = torch.randn(8, 512, device=device).to(torch.bfloat16)
+    layer = ColumnParallelLinear(w, runtime=None)
+    y = layer.decode(x)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(y.float(), x.float() @ w.float().T, rtol=2e-2, atol=2e-2)
