@@ -314,7 +314,10 @@ class Comm {
 
   void fused_norm(const std::vector<at::Tensor>& ins, const std::vector<at::Tensor>& residuals,
                   const at::Tensor& gamma, double eps, const std::vector<at::Tensor>& outs,
-                  const std::vector<at::Tensor>& residual_outs, int algo, int cluster, int max_clusters) {
+                  const std::vector<at::Tensor>& residual_outs, int algo, int cluster, int max_clusters,
+                  bool received = false) {
+    if (received && (emulate_ || algo != kOneShot || world_ < 2))
+      throw std::invalid_argument("a received fused norm is the one-shot form of a real (not emulated) group");
     check_views(ins, outs);
     check_views(residuals, residual_outs);
     require_aligned(gamma, "gamma");
@@ -352,6 +355,7 @@ class Comm {
     j.gamma = ptr_of(gamma);
     j.eps = float(eps);
     j.hidden = uint32_t(H);
+    j.received = received ? 1u : 0u;
     auto stream = at::cuda::getCurrentCUDAStream(device_).stream();
     if (emulate_) {
       EmuViews e = emu_views(ins, outs, &residuals, &residual_outs);
@@ -359,6 +363,20 @@ class Comm {
     } else {
       launch_fused_norm(j, nullptr, dtype_code(x), algo, g, stream);
     }
+  }
+
+  // Decode: partial = x @ w.T on the decode GEMM, whose epilogue pushes every finished
+  // group of the partial into the peers' one-shot slots, then the fused all-reduce +
+  // residual + RMSNorm, which only receives.  Two launches on the current stream; the
+  // one-shot form only (the caller checks the shapes the policy sends here).
+  void gemm_fused_norm(const at::Tensor& x, const at::Tensor& w, at::Tensor& partial, const at::Tensor& residual,
+                       const at::Tensor& gamma, double eps, at::Tensor& out, at::Tensor& residual_out,
+                       at::Tensor& err, int cluster, bool pdl_gemm) {
+    if (emulate_ || world_ < 2) throw std::invalid_argument("the pushing decode GEMM needs a real group of 2..8 ranks");
+    if (x.scalar_type() != at::kBFloat16 || partial.scalar_type() != at::kBFloat16)
+      throw std::invalid_argument("bf16 activations and partial");
+    tc::skinny_gemm_push(view_, L_, rank_, world_, x, w, partial, err, 0, pdl_gemm);
+    fused_norm({partial}, {residual}, gamma, eps, {out}, {residual_out}, kOneShot, cluster, 0, true);
   }
 
   // -- fused prefill GEMMs (tcgen05) ----------------------------------------------
@@ -574,7 +592,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            py::arg("out"), py::arg("err"), py::arg("max_ctas") = 0)
       .def("fused_norm", &Comm::fused_norm, py::arg("ins"), py::arg("residuals"), py::arg("gamma"), py::arg("eps"),
            py::arg("outs"), py::arg("residual_outs"), py::arg("algo"), py::arg("cluster") = 8,
-           py::arg("max_clusters") = 0)
+           py::arg("max_clusters") = 0, py::arg("received") = false)
+      .def("gemm_fused_norm", &Comm::gemm_fused_norm, py::arg("x"), py::arg("w"), py::arg("partial"),
+           py::arg("residual"), py::arg("gamma"), py::arg("eps"), py::arg("out"), py::arg("residual_out"),
+           py::arg("err"), py::arg("cluster") = 8, py::arg("pdl_gemm") = true)
       .def("status", &Comm::status, py::arg("which") = 0)
       .def("failed_seq", &Comm::failed_seq, py::arg("which") = 0)
       .def("set_timeout_us", &Comm::set_timeout_us)

@@ -596,6 +596,72 @@ class NvlinkAllReduce:
             self.check_health()
         return out, residual_out
 
+    def gemm_push_eligible(self, x: torch.Tensor, w: torch.Tensor, cluster: int = 8) -> bool:
+        """Whether ``gemm_all_reduce_residual_rmsnorm`` runs its fused form for these
+        shapes: several ranks, bf16, 1..256 tokens, K a multiple of 64, N a multiple of
+        8 x cluster, a message within the one-shot slot that the fused norm would send
+        one-shot.  Depends on shapes, dtype and world size only (rank-invariant)."""
+        if x.dim() != 2 or w.dim() != 2 or x.shape[1] != w.shape[1]:
+            return False
+        tokens, k, n = x.shape[0], x.shape[1], w.shape[0]
+        nbytes = tokens * n * 2
+        return (self.world_size > 1 and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+                and 1 <= tokens <= 256 and k % 64 == 0 and n % (8 * cluster) == 0
+                and nbytes <= self._caps[0]  # the one-shot slot; the rest is the fused norm's own choice
+                and (self.world_size <= 2 or nbytes <= self.policy.oneshot_limit(self.world_size)
+                     or tokens < self.world_size))
+
+    def gemm_all_reduce_residual_rmsnorm(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor,
+                                         gamma: torch.Tensor, eps: float = 1e-5, *,
+                                         partial: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                                         residual_out: Optional[torch.Tensor] = None, cluster: int = 8,
+                                         pdl: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
+        """Decode row-parallel projection and its collective: ``partial = x @ w.T``,
+        ``residual += all_reduce(partial)``, ``out = rms_norm(residual) * gamma``.
+
+        The decode GEMM's epilogue pushes each finished 16-byte group of ``partial``
+        into every peer's one-shot slot, so the fused all-reduce kernel that follows
+        only receives: the push overlaps the GEMM's other tiles and leaves the
+        collective's critical path.  The results equal the unfused
+        ``linear`` + ``all_reduce_residual_rmsnorm`` bit for bit.  Shapes the one-shot
+        form cannot carry (more than 256 tokens, K not a multiple of 64, N not a
+        multiple of 8 x cluster, a message above the one-shot limit) run that unfused
+        pair instead; the choice depends on shapes and world size only, so every rank
+        makes it alike.  ``pdl`` launches the GEMM with programmatic dependent launch.
+        """
+        tokens = x.shape[0] if x.dim() == 2 else 0
+        n = w.shape[0] if w.dim() == 2 else 0
+        nbytes = tokens * n * 2
+        if partial is None:
+            partial = torch.empty((tokens, n), dtype=torch.bfloat16, device=x.device)
+        if not self.gemm_push_eligible(x, w, cluster):
+            from sparknet.ops.decode_gemm import linear
+
+            linear(x, w, partial)
+            return self.all_reduce_residual_rmsnorm(partial, residual, gamma, eps, out=out,
+                                                    residual_out=residual_out, cluster=cluster)
+        with self._lock:
+            self.check_health()
+            self._live()
+            for t in (x, w, residual, gamma, partial):
+                if not t.is_cuda or t.device != self.device or not t.is_contiguous() or t.data_ptr() % PACK_BYTES:
+                    raise ValueError("tensors must be contiguous, 16-byte aligned, on the runtime device")
+            if residual.shape != (tokens, n) or gamma.shape != (n,) or partial.shape != (tokens, n):
+                raise ValueError("residual and partial [tokens, N], gamma [N]")
+            with torch.cuda.device(self.device):
+                capturing = torch.cuda.is_current_stream_capturing()
+                out = torch.empty_like(residual) if out is None else out
+                residual_out = torch.empty_like(residual) if residual_out is None else residual_out
+                self._order_stream(capturing)
+                self._comm.gemm_fused_norm(x, w, partial, residual, gamma, float(eps), out, residual_out,
+                                           self._gemm_err(), cluster, bool(pdl))
+                self._calls["fused_norm"] += 1
+                self._account_reduce("oneshot", nbytes)
+                self._mark_stream(capturing)
+        if not capturing:
+            self.check_health()
+        return out, residual_out
+
     # -- fused prefill GEMMs (tcgen05) -------------------------------------------------------
     def _gemm_err(self) -> torch.Tensor:
         if getattr(self, "_gemm_err_word", None) is None:
