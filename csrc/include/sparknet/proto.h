@@ -21,7 +21,11 @@
 #if defined(__CUDACC__)
 #define SN_HD __host__ __device__ __forceinline__
 #define SN_DEV __device__ __forceinline__
+#if defined(__CUDA_ARCH__)  // the device pass; the host pass of a .cu file has no such pragma
 #define SN_UNROLL _Pragma("unroll")
+#else
+#define SN_UNROLL
+#endif
 #else
 #define SN_HD inline
 #define SN_DEV inline

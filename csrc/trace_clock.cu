@@ -96,12 +96,6 @@ std::vector<std::tuple<unsigned long long, unsigned long long, unsigned long lon
   return out;
 }
 
-__global__ void k_globaltimer(unsigned long long* out) {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  *out = t;
-}
-
 }  // namespace
 
 void register_trace(py::module_& m) {
