@@ -71,7 +71,7 @@ def _fetch_without_server_worker(rank, world, store_path, results):
 
 
 def spawn(fn, world, tmp_path):
-    manager = mp.Manager()
+    manager = mp.get_context("spawn").Manager()
     results = manager.dict()
     store = str(tmp_path / "store")
     mp.start_processes(fn, args=(world, store, results), nprocs=world, join=True, start_method="spawn")

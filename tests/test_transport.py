@@ -57,7 +57,7 @@ def test_host_staged_regions_shared_across_ranks(tmp_path):
     import torch.multiprocessing as mp
 
     world = 3
-    manager = mp.Manager()
+    manager = mp.get_context("spawn").Manager()
     results = manager.dict()
     mp.start_processes(_worker, args=(world, str(tmp_path / "s"), results), nprocs=world, join=True,
                        start_method="spawn")

@@ -79,7 +79,7 @@ def _worker(rank, world, store, mode, results):
 
 
 def run(mode, tmp_path, world=2):
-    manager = mp.Manager()
+    manager = mp.get_context("spawn").Manager()
     results = manager.dict()
     mp.start_processes(_worker, args=(world, str(tmp_path / "s"), mode, results), nprocs=world, join=True,
                        start_method="spawn")
