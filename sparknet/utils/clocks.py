@@ -11,6 +11,7 @@ reads settings; it never changes a clock, power limit or any other GPU state.
 
 from __future__ import annotations
 
+import atexit
 import csv
 import io
 import os
@@ -112,7 +113,24 @@ class ClockSampler:
         if self.gpus is not None:
             cmd.append("--id=" + ",".join(str(g) for g in self.gpus))
         self._proc = subprocess.Popen(cmd, stdout=self._file, stderr=subprocess.DEVNULL)
+        atexit.register(self._abandon)  # a run that fails before stop() must not leave the sampler running
         return self
+
+    def _abandon(self) -> None:
+        """Stop this sampler's own process (exactly that PID) and drop its file."""
+        proc, self._proc = self._proc, None
+        if proc is not None and proc.poll() is None:
+            proc.terminate()
+            try:
+                proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                proc.kill()
+        if self._file is not None:
+            try:
+                self._file.close()
+                os.unlink(self._file.name)
+            except OSError:
+                pass
 
     def mark_start(self) -> None:
         self._t0 = time.time()
@@ -126,12 +144,14 @@ class ClockSampler:
         if self._t0 is not None and self._t1 is None:
             self.mark_end()
         time.sleep(min(1.0, 2 * self.interval_ms / 1000.0))  # let the sample after the window land
+        atexit.unregister(self._abandon)
         self._proc.terminate()
         try:
             self._proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self._proc.kill()
             self._proc.wait()
+        self._proc = None
         self._file.flush()
         self._file.seek(0)
         text = self._file.read()

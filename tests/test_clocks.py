@@ -48,3 +48,25 @@ def test_samples_inside_the_window_count_as_loaded():
     # nearest samples outside the window still need the utilisation
     s = clocks.summarize("\n".join(rows), window=(base + 0.1, base + 0.12), slack_s=0.2)
     assert s["samples_in_window"] == 0 and s["sm_mhz"] is None
+
+
+def test_sampler_left_running_is_stopped_at_exit(tmp_path, monkeypatch):
+    """A run that fails between start() and stop(): the exit hook ends exactly the
+    sampler's own process (a stand-in nvidia-smi that would sample forever)."""
+    import os
+    import stat
+
+    from sparknet.utils.clocks import ClockSampler
+
+    fake = tmp_path / "nvidia-smi"
+    fake.write_text("#!/bin/sh\nwhile true; do echo '0, 1200, 1965, 500.0, 0x0, Not Active, Not Active, Not Active, Not Active'; sleep 0.05; done\n")
+    fake.chmod(fake.stat().st_mode | stat.S_IEXEC)
+    monkeypatch.setenv("PATH", f"{tmp_path}{os.pathsep}{os.environ['PATH']}")
+    s = ClockSampler([0], interval_ms=50).start()
+    proc, name = s._proc, s._file.name
+    assert proc is not None and proc.poll() is None
+    s._abandon()          # what atexit runs
+    assert proc.poll() is not None and not os.path.exists(name)
+    s2 = ClockSampler([0], interval_ms=50).start()
+    result = s2.stop()    # the normal path still works and unregisters the hook
+    assert result["samples"] >= 0 and s2._proc is None
