@@ -149,6 +149,8 @@ def main(argv=None) -> int:
     parser.add_argument("--output", default="", help="write the JSON result here as well as to stdout")
     parser.add_argument("--runtime-threads", type=int, default=None)
     parser.add_argument("--runtime-blocks", type=int, default=None)
+    parser.add_argument("--pdl", action="store_true",
+                        help="launch the NVLink collectives with programmatic dependent launch")
     args = parser.parse_args(argv)
     if any(n < 8 or n > (64 << 20) or n % 8 for n in args.lengths):
         parser.error("lengths must be multiples of 8 elements between 8 and 64 Mi")
@@ -172,6 +174,8 @@ def main(argv=None) -> int:
             enable_multicast=(args.transport == "nvlink-nvls" or policy.allow_nvls), **geometry)
         if runtime.dispatch_max_bytes != policy.all_reduce_dispatch_bytes:
             raise RuntimeError("runtime did not apply the requested dispatch limit")
+        if args.pdl:
+            runtime.set_pdl(True)
         runtime.prepare((torch.bfloat16, torch.float32, torch.float16), padded_gather=True)
     comm = PolicyCommunicator(runtime, policy, device, world)
     capture_context = (lambda s: runtime.capture(stream=s)) if runtime else (lambda s: nullcontext())
@@ -198,7 +202,7 @@ def main(argv=None) -> int:
                 raise RuntimeError("no probe payload used the NVLink kernels")
             stats = {k: v for k, v in runtime.stats().items() if k not in ("status",)}
     environment = {k: v for k, v in sorted(os.environ.items()) if k.startswith(("SPARKNET_", "NCCL_"))}
-    result = {"rank": rank, "world_size": world, "transport": args.transport,
+    result = {"rank": rank, "world_size": world, "transport": args.transport, "pdl": bool(runtime and runtime.pdl),
               "policy": ({k: (dict(v) if isinstance(v, dict) else v) for k, v in policy.__dict__.items()}
                          if policy else None),
               "runtime": stats, "environment": environment, "passed": True, "checks": checks,
