@@ -78,6 +78,10 @@ extern "C" int sparknet_decode_attention_noalloc(const void* q, const void* k_ca
   if (need > kScratchFloats)
     return fail(2, "problem needs " + std::to_string(need * sizeof(float)) + " bytes of scratch; the built-in scratch is " +
                        std::to_string(SPARKNET_NOALLOC_SCRATCH_BYTES) + " bytes (use the allocating entry point)");
+  // the counters this call uses must be zero when its kernel starts: clear them on the
+  // caller's stream (a device memset: nothing is allocated)
+  e = cudaMemsetAsync(scratch, 0, size_t(B) * Hkv * sizeof(int), stream);
+  if (e != cudaSuccess) return fail(3, std::string("clearing the counters: ") + cudaGetErrorString(e));
   e = sn::attn::launch_decode_attention(static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k_cache),
                                         static_cast<const __nv_bfloat16*>(v_cache), lengths,
                                         static_cast<__nv_bfloat16*>(out), scratch, B, Hq, Hkv, Lmax, max_len, scale, sms,

@@ -4,11 +4,10 @@
 // model code at all); it is an addition of this library.
 //
 // Who it is for: callers that cannot allocate device memory at the moment they run
-// attention.  That includes code being recorded into a CUDA graph (cudaMalloc is not
-// allowed while a stream is capturing), inference engines that reserve nearly all of
-// the GPU's memory up front for their own pool (a stray cudaMalloc there can fail or
-// fragment the pool), and plain C/C++ hosts that have no caching allocator and cannot
-// afford cudaMalloc's implicit device synchronisation on a latency-critical path.
+// attention: inference engines that reserve nearly all of the GPU's memory up front for
+// their own pool (a stray cudaMalloc there can fail or fragment the pool), and plain
+// C/C++ hosts that have no caching allocator and cannot afford cudaMalloc's implicit
+// device synchronisation on a latency-critical path.
 // Such callers pass only their inputs and output; the per-split partial results the
 // kernels need live in a fixed scratch array compiled into the library.
 #pragma once
@@ -33,17 +32,19 @@ extern "C" {
 //   scale    softmax scale (usually 1/sqrt(128))
 // Returns 0 on success, or a nonzero code with a message from
 // sparknet_noalloc_last_error(): 1 bad argument, 2 problem too large for the built-in
-// scratch, 3 CUDA error.  Launches one kernel on `stream`; allocates nothing.
+// scratch, 3 CUDA error.  Clears the call's counters and launches one kernel, both on
+// `stream`; allocates nothing.
 //
 // The first call on a device looks up the device address of the scratch array (a
 // CUDA runtime query, done once per device with that device current); make that
 // first call outside any stream capture.  Every call, on every stream, shares the
 // one scratch array, so calls that may overlap on the GPU (different streams, no
-// ordering between them) race and must not be issued.  The scratch starts with a
-// fixed block of per-(sequence, KV head) counters that must be zero when a call
-// starts: static device storage starts zeroed and every call that completes leaves
-// them zero, so the caller clears nothing.  The partials after them are written
-// before they are read in every call.
+// ordering between them) race and must not be issued.  The scratch keeps the last
+// call's contents.  It starts with a fixed block of per-(sequence, KV head) counters
+// that must be zero when the kernel starts: each call zeroes the B x Hkv counters it
+// uses (cudaMemsetAsync on `stream`, before its kernel), so nothing depends on how an
+// earlier call ended.  The partials after them are written before they are read in
+// every call.
 __attribute__((visibility("default"))) int sparknet_decode_attention_noalloc(
     const void* q, const void* k_cache, const void* v_cache, const int32_t* lengths, void* out, int B, int Hq,
     int Hkv, int Lmax, int max_len, float scale, cudaStream_t stream);

@@ -1,8 +1,8 @@
 """The allocation-free decode-attention entry point (GPU).
 
-Some callers cannot allocate device memory when they run attention: code being
-captured into a CUDA graph, engines that have already reserved the GPU's memory for
-their own pool, C hosts without a caching allocator.  The library exports
+Some callers cannot allocate device memory when they run attention: engines that have
+already reserved the GPU's memory for their own pool, C hosts without a caching
+allocator.  The library exports
 ``sparknet_decode_attention_noalloc``, whose scratch is a fixed array inside the
 library.  This test calls that exported C symbol directly (ctypes), twice in a row,
 and checks each result against the allocating entry point on the same inputs.  It
