@@ -565,6 +565,38 @@ static __global__ void __launch_bounds__(kAttnThreads) k_decode_attn_cluster(
 // waves of the SMs, else 8.
 static inline int cluster_spans(int B, int Hkv, int sms) { return B * Hkv * 16 <= 2 * sms ? 16 : 8; }
 
+// Whether clusters of 16 CTAs of this kernel can be scheduled at all on the current
+// device (the answer depends on the GPU's partitioning): asked once per device.
+template <int G>
+static inline bool cluster16_fits() {
+  static int answer[64] = {0};  // 0 unknown, 1 fits, 2 does not
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (dev >= 0 && dev < 64 && answer[dev]) return answer[dev] == 1;
+  auto kernel = k_decode_attn_cluster<G, 16, kClusterNT>;
+  const int smem = int(sizeof(ClusterSmem<G, kClusterNT>));
+  bool fits = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess &&
+              cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+  if (fits) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(16, 1, 1);
+    cfg.blockDim = dim3(kAttnThreads, 1, 1);
+    cfg.dynamicSmemBytes = size_t(smem);
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 16;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    fits = cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) == cudaSuccess && clusters > 0;
+  }
+  (void)cudaGetLastError();  // clear the error a refused query may leave behind
+  if (dev >= 0 && dev < 64) answer[dev] = fits ? 1 : 2;
+  return fits;
+}
+
 template <int G, int S>
 static inline cudaError_t launch_cluster_g(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
                                            const __nv_bfloat16* v_cache, const int* lengths, __nv_bfloat16* out,
@@ -610,7 +642,19 @@ static inline cudaError_t launch_decode_attention_cluster(const __nv_bfloat16* q
                                                           bool pdl = false) {
   if (Hkv <= 0 || Hq % Hkv || B <= 0 || max_len <= 0 || B * Hkv > 65535) return cudaErrorInvalidValue;
   const int G = Hq / Hkv;
-  const int S = cluster_spans(B, Hkv, sms);
+  int S = cluster_spans(B, Hkv, sms);
+  if (S == 16) {
+    bool fits = false;
+    switch (G) {
+      case 1: fits = cluster16_fits<1>(); break;
+      case 2: fits = cluster16_fits<2>(); break;
+      case 4: fits = cluster16_fits<4>(); break;
+      case 8: fits = cluster16_fits<8>(); break;
+      case 16: fits = cluster16_fits<16>(); break;
+      default: return cudaErrorInvalidValue;
+    }
+    if (!fits) S = 8;  // portable cluster size
+  }
   const int chunk = ((max_len + S - 1) / S + kTile - 1) / kTile * kTile;
   const float scale_log2 = scale * kLog2e;
 #define SN_ATC(GG)                                                                                              \
