@@ -237,6 +237,7 @@ class NvlinkAllReduce:
         policy: Optional[CollectivePolicy] = None,
         enable_multicast: Optional[bool] = None,
         transport=None,
+        pdl: Optional[bool] = None,
     ) -> None:
         self.device = normalize_device(device)
         self.rank = dist.get_rank(group=exchange_group)
@@ -355,7 +356,7 @@ class NvlinkAllReduce:
             self._comm.set_trace(address, trace.file_bytes())
             logger.info("collective trace %s", self.trace_path)
         self.has_multicast = bool(self._comm.has_multicast)
-        self.set_pdl(os.environ.get(ENV_PDL, "0") == "1")
+        self.set_pdl(os.environ.get(ENV_PDL, "0") == "1" if pdl is None else bool(pdl))
         if self.rank == 0:
             logger.info("NVLink collectives ready: world=%d region=%d MiB multicast=%s max_size=%d",
                         self.world_size, region_bytes >> 20, self.has_multicast, self.max_size)
@@ -369,14 +370,17 @@ class NvlinkAllReduce:
         """Build the runtime collectively over ``exchange_group`` (a CPU/gloo group)."""
         if "kernels" in kwargs:
             raise TypeError("the kernels keyword is not supported: the kernels are compiled ahead of time")
-        known = {k: kwargs[k] for k in ("policy", "enable_multicast", "transport") if k in kwargs}
+        known = {k: kwargs[k] for k in ("policy", "enable_multicast", "transport", "pdl") if k in kwargs}
         capacity = max(int(max_size), int(eager_buffer_bytes or 0))
         return cls(exchange_group=exchange_group, device=device, max_size=capacity,
                    max_gather_bytes=max_gather_bytes, threads=threads, blocks=blocks, **known)
 
     @classmethod
     def from_process_group(cls, *, process_group, device, max_size: int = DEFAULT_MAX_SIZE,
-                           max_input_bytes: Optional[int] = None, **kwargs: Any) -> "NvlinkAllReduce":
+                           max_input_bytes: Optional[int] = None, **_ignored: Any) -> "NvlinkAllReduce":
+        """Build the runtime with ``process_group`` as both the rank identity and the
+        setup exchange (a CPU-capable group, e.g. gloo); further keywords are accepted
+        and ignored, as in the reference (``sparknet/oneshot/runtime.py``)."""
         capacity = max(int(max_size), int(max_input_bytes or 0))
         return cls(exchange_group=process_group, device=device, max_size=capacity)
 
