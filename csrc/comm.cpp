@@ -316,8 +316,8 @@ class Comm {
                   const at::Tensor& gamma, double eps, const std::vector<at::Tensor>& outs,
                   const std::vector<at::Tensor>& residual_outs, int algo, int cluster, int max_clusters,
                   bool received = false) {
-    if (received && (emulate_ || algo != kOneShot || world_ < 2))
-      throw std::invalid_argument("a received fused norm is the one-shot form of a real (not emulated) group");
+    if (received && (emulate_ || (algo != kOneShot && algo != kTwoShot) || world_ < 2))
+      throw std::invalid_argument("a received fused norm runs in a real (not emulated) group, one-shot or two-shot");
     check_views(ins, outs);
     check_views(residuals, residual_outs);
     require_aligned(gamma, "gamma");
@@ -366,17 +366,18 @@ class Comm {
   }
 
   // Decode: partial = x @ w.T on the decode GEMM, whose epilogue pushes every finished
-  // group of the partial into the peers' one-shot slots, then the fused all-reduce +
-  // residual + RMSNorm, which only receives.  Two launches on the current stream; the
-  // one-shot form only (the caller checks the shapes the policy sends here).
+  // group of the partial into the peers' slots (one-shot: to every peer; two-shot: each
+  // row to its owner), then the fused all-reduce + residual + RMSNorm, which only
+  // receives.  Two launches on the current stream.
   void gemm_fused_norm(const at::Tensor& x, const at::Tensor& w, at::Tensor& partial, const at::Tensor& residual,
                        const at::Tensor& gamma, double eps, at::Tensor& out, at::Tensor& residual_out,
-                       at::Tensor& err, int cluster, bool pdl_gemm) {
+                       at::Tensor& err, int algo, int cluster, bool pdl_gemm) {
     if (emulate_ || world_ < 2) throw std::invalid_argument("the pushing decode GEMM needs a real group of 2..8 ranks");
+    if (algo != kOneShot && algo != kTwoShot) throw std::invalid_argument("one-shot or two-shot");
     if (x.scalar_type() != at::kBFloat16 || partial.scalar_type() != at::kBFloat16)
       throw std::invalid_argument("bf16 activations and partial");
-    tc::skinny_gemm_push(view_, L_, rank_, world_, x, w, partial, err, 0, pdl_gemm);
-    fused_norm({partial}, {residual}, gamma, eps, {out}, {residual_out}, kOneShot, cluster, 0, true);
+    tc::skinny_gemm_push(view_, L_, rank_, world_, x, w, partial, err, 0, pdl_gemm, algo == kTwoShot);
+    fused_norm({partial}, {residual}, gamma, eps, {out}, {residual_out}, algo, cluster, 0, true);
   }
 
   // -- fused prefill GEMMs (tcgen05) ----------------------------------------------
@@ -595,7 +596,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            py::arg("max_clusters") = 0, py::arg("received") = false)
       .def("gemm_fused_norm", &Comm::gemm_fused_norm, py::arg("x"), py::arg("w"), py::arg("partial"),
            py::arg("residual"), py::arg("gamma"), py::arg("eps"), py::arg("out"), py::arg("residual_out"),
-           py::arg("err"), py::arg("cluster") = 8, py::arg("pdl_gemm") = true)
+           py::arg("err"), py::arg("algo") = 0, py::arg("cluster") = 8, py::arg("pdl_gemm") = true)
       .def("status", &Comm::status, py::arg("which") = 0)
       .def("failed_seq", &Comm::failed_seq, py::arg("which") = 0)
       .def("set_timeout_us", &Comm::set_timeout_us)

@@ -115,8 +115,8 @@ SN_DEV void fused_body(const Job& j, int algo) {
   bool ok = true;
 
   // 1. push: one-shot sends every row to every peer; two-shot sends row t to its owner.
-  //    Skipped when the producer of the input already pushed it (j.received, one-shot).
-  if (active && W > 1 && !(j.received && !twoshot)) {
+  //    Skipped when the producer of the input already pushed it (j.received).
+  if (active && W > 1 && !j.received) {
     for (uint64_t t = cid; t < T; t += nclusters) {
       const uint64_t i = t * row_packs + tpack;
       Pack16 v = pack_canon<D>(m.ld_input(x + i));

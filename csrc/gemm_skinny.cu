@@ -77,6 +77,7 @@ struct SkinnyParams {
   // mode 3: the collective's view (regions of every rank, layout, rank, world); read
   // in place from the kernel parameters, like the collective kernels' Job
   Job pj;
+  int push_twoshot;   // mode 3: push each row to its owner (two-shot) instead of to every peer
 };
 
 constexpr int kStamps = 8;
@@ -256,8 +257,9 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
   } else if (p.mode == 3) {
     // Y in 8-feature groups (CTA `split` takes groups split, split + S, ...), each group
     // summed over the splits in split order exactly as mode 0 sums an element, and
-    // pushed, sentinel-safe, into Lamport slot [parity][rank] of every peer at the
-    // one-shot layout's pack index (token * N / 8 + feature / 8).  The parity is that of
+    // pushed, sentinel-safe, into Lamport slot [parity][rank]: of every peer at the
+    // one-shot layout's pack index (token * N / 8 + feature / 8), or (two-shot) of the
+    // row's owner (token % world) at (token / world) * N / 8 + feature / 8.  The parity is that of
     // the collective that follows this kernel: the epoch read here plus one.  The read
     // comes after griddepcontrol.wait (the main loop waited), so the previous
     // collective has completed on this rank.  A poisoned rank pushes nothing (the
@@ -296,7 +298,14 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
         if (!poison) {
           const Pack16 c = pack_canon<kBF16>(pk);
           const uint64_t idx = uint64_t(m) * row_packs + uint64_t(n0) / 8;
-          for (uint32_t k = 1; k < j.world; ++k) dm.st_remote(lam_pack(j, (j.rank + k) % j.world, parity, j.rank, idx), c);
+          if (p.push_twoshot) {
+            const uint32_t owner = uint32_t(m) % j.world;
+            if (owner != j.rank)
+              dm.st_remote(lam_pack(j, owner, parity, j.rank, uint64_t(m / int(j.world)) * row_packs + uint64_t(n0) / 8),
+                           c);
+          } else {
+            for (uint32_t k = 1; k < j.world; ++k) dm.st_remote(lam_pack(j, (j.rank + k) % j.world, parity, j.rank, idx), c);
+          }
         }
       }
     }
@@ -488,7 +497,7 @@ void skinny_qkv_rope(const at::Tensor& X, const at::Tensor& W, const at::Tensor&
 // [parity][rank] of every peer's region.  The caller launches the receiving fused
 // all-reduce + residual + RMSNorm right after it on the same stream.
 void skinny_gemm_push(const View& view, const Layout& L, int rank, int world, const at::Tensor& X,
-                      const at::Tensor& W, at::Tensor& Y, at::Tensor& err, int max_splits, bool pdl) {
+                      const at::Tensor& W, at::Tensor& Y, at::Tensor& err, int max_splits, bool pdl, bool twoshot) {
   check_mat(X, "X");
   check_mat(W, "W");
   check_mat(Y, "Y");
@@ -501,7 +510,9 @@ void skinny_gemm_push(const View& view, const Layout& L, int rank, int world, co
     throw std::invalid_argument("Y must be a contiguous, 16-byte aligned [M, N] tensor");
   if (world < 2 || world > kMaxRanks || rank < 0 || rank >= world)
     throw std::invalid_argument("the pushing decode GEMM needs 2..8 ranks");
-  if (uint64_t(M) * N * 2 > L.lam_cap) throw std::invalid_argument("M x N exceeds the one-shot slot");
+  if (!twoshot && uint64_t(M) * N * 2 > L.lam_cap) throw std::invalid_argument("M x N exceeds the one-shot slot");
+  if (twoshot && uint64_t((M + world - 1) / world) * N * 2 > L.lam_cap / 2)
+    throw std::invalid_argument("the rows per owner exceed the two-shot slot");
   const int dev = X.device().index();
   c10::cuda::CUDAGuard guard(X.device());
   int sms = 0;
@@ -526,6 +537,7 @@ void skinny_gemm_push(const View& view, const Layout& L, int rank, int world, co
   p.pj.rank = uint32_t(rank);
   p.pj.world = uint32_t(world);
   p.pj.skip_rank = -1;
+  p.push_twoshot = twoshot ? 1 : 0;
   launch_skinny(W, X, p, pl, dev, pdl);
 }
 

@@ -584,8 +584,7 @@ class NvlinkAllReduce:
             tokens, hidden = inp.shape
             nbytes = inp.numel() * inp.element_size()
             if algorithm is None:
-                algorithm = "oneshot" if (self.world_size <= 2 or nbytes <= self.policy.oneshot_limit(
-                    self.world_size) or tokens < self.world_size) else "twoshot"
+                algorithm = self._fused_norm_algorithm(tokens, nbytes)
             with torch.cuda.device(self.device), self._stream_ctx(stream):
                 capturing = torch.cuda.is_current_stream_capturing()
                 out = torch.empty_like(inp) if out is None else out
@@ -600,20 +599,28 @@ class NvlinkAllReduce:
             self.check_health()
         return out, residual_out
 
+    def _fused_norm_algorithm(self, tokens: int, nbytes: int) -> str:
+        """One-shot or two-shot for the fused norm (rank-invariant: sizes and world)."""
+        if self.world_size <= 2 or nbytes <= self.policy.oneshot_limit(self.world_size) or tokens < self.world_size:
+            return "oneshot"
+        return "twoshot"
+
     def gemm_push_eligible(self, x: torch.Tensor, w: torch.Tensor, cluster: int = 8) -> bool:
         """Whether ``gemm_all_reduce_residual_rmsnorm`` runs its fused form for these
         shapes: several ranks, bf16, 1..256 tokens, K a multiple of 64, N a multiple of
-        8 x cluster, a message within the one-shot slot that the fused norm would send
-        one-shot.  Depends on shapes, dtype and world size only (rank-invariant)."""
+        8 x cluster, and the message within the slot of the algorithm the fused norm
+        picks (one-shot: the whole message; two-shot: each owner's rows in half a slot).
+        Depends on shapes, dtype and world size only (rank-invariant)."""
         if x.dim() != 2 or w.dim() != 2 or x.shape[1] != w.shape[1]:
             return False
         tokens, k, n = x.shape[0], x.shape[1], w.shape[0]
         nbytes = tokens * n * 2
-        return (self.world_size > 1 and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
-                and 1 <= tokens <= 256 and k % 64 == 0 and n % (8 * cluster) == 0
-                and nbytes <= self._caps[0]  # the one-shot slot; the rest is the fused norm's own choice
-                and (self.world_size <= 2 or nbytes <= self.policy.oneshot_limit(self.world_size)
-                     or tokens < self.world_size))
+        if not (self.world_size > 1 and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+                and 1 <= tokens <= 256 and k % 64 == 0 and n % (8 * cluster) == 0):
+            return False
+        if self._fused_norm_algorithm(tokens, nbytes) == "oneshot":
+            return nbytes <= self._caps[0]
+        return -(-tokens // self.world_size) * n * 2 <= self._caps[0] // 2
 
     def gemm_all_reduce_residual_rmsnorm(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor,
                                          gamma: torch.Tensor, eps: float = 1e-5, *,
@@ -624,14 +631,14 @@ class NvlinkAllReduce:
         ``residual += all_reduce(partial)``, ``out = rms_norm(residual) * gamma``.
 
         The decode GEMM's epilogue pushes each finished 16-byte group of ``partial``
-        into every peer's one-shot slot, so the fused all-reduce kernel that follows
+        into the peers' slots of the algorithm the fused norm picks (one-shot: every
+        peer; two-shot: the row's owner), so the fused all-reduce kernel that follows
         only receives: the push overlaps the GEMM's other tiles and leaves the
         collective's critical path.  The results equal the unfused
-        ``linear`` + ``all_reduce_residual_rmsnorm`` bit for bit.  Shapes the one-shot
-        form cannot carry (more than 256 tokens, K not a multiple of 64, N not a
-        multiple of 8 x cluster, a message above the one-shot limit) run that unfused
-        pair instead; the choice depends on shapes and world size only, so every rank
-        makes it alike.  ``pdl`` launches the GEMM with programmatic dependent launch.
+        ``linear`` + ``all_reduce_residual_rmsnorm`` bit for bit.  Shapes it cannot
+        carry (:meth:`gemm_push_eligible`) run that unfused pair instead; the choice
+        depends on shapes and world size only, so every rank makes it alike.  ``pdl``
+        launches the GEMM with programmatic dependent launch.
         """
         tokens = x.shape[0] if x.dim() == 2 else 0
         n = w.shape[0] if w.dim() == 2 else 0
@@ -657,10 +664,11 @@ class NvlinkAllReduce:
                 out = torch.empty_like(residual) if out is None else out
                 residual_out = torch.empty_like(residual) if residual_out is None else residual_out
                 self._order_stream(capturing)
+                algorithm = self._fused_norm_algorithm(tokens, nbytes)
                 self._comm.gemm_fused_norm(x, w, partial, residual, gamma, float(eps), out, residual_out,
-                                           self._gemm_err(), cluster, bool(pdl))
+                                           self._gemm_err(), ALGO_CODES[algorithm], cluster, bool(pdl))
                 self._calls["fused_norm"] += 1
-                self._account_reduce("oneshot", nbytes)
+                self._account_reduce(algorithm, nbytes)
                 self._mark_stream(capturing)
         if not capturing:
             self.check_health()

@@ -169,7 +169,7 @@ def test_reference_exports_are_importable():
 
 def test_pushing_gemm_eligibility():
     """When the decode projection runs with its GEMM pushing into the all-reduce: the
-    one-shot shapes of a real group; everything else takes the unfused pair."""
+    shapes a real group's fused norm carries; everything else takes the unfused pair."""
     from sparknet.oneshot.runtime import NvlinkAllReduce
     from sparknet.policy import NVLINK_POLICY
 
@@ -184,7 +184,9 @@ def test_pushing_gemm_eligibility():
     assert not ok(8, 1000, 8192)             # K not a multiple of 64
     assert not ok(8, 1024, 8200)             # N not a multiple of 8 x cluster
     assert not ok(300, 1024, 8192)           # beyond the decode GEMM's 256 rows
-    assert not ok(64, 1024, 8192)            # 1 MiB at W = 8: the fused norm goes two-shot
+    assert ok(64, 1024, 8192)                # 1 MiB at W = 8: two-shot, 8 rows per owner
+    assert rt._fused_norm_algorithm(64, 64 * 8192 * 2) == "twoshot"
+    assert rt._fused_norm_algorithm(8, 8 * 8192 * 2) == "oneshot"
     assert not ok(8, 1024, 8192, torch.float16)
     rt.world_size = 2
     assert ok(64, 1024, 8192)                # two ranks: one-shot up to the slot

@@ -23,18 +23,29 @@ def gemm_pushes_all_reduce(rt, cfg, rank, world, device, results):
     from sparknet.ops.decode_gemm import linear
 
     g = torch.Generator(device=device).manual_seed(11 + rank)
+    # 8 tokens: one-shot; 64 tokens x 8192: two-shot at 4 or more ranks (one-shot at 2)
+    for tokens, n in ((8, 2048), (64, 8192)):
+        xs = torch.randn(tokens, 1024, generator=g, device=device).to(torch.bfloat16)
+        ws = (0.05 * torch.randn(n, 1024, generator=g, device=device)).to(torch.bfloat16)
+        gs = (1 + 0.1 * torch.randn(n, device=device)).to(torch.bfloat16)
+        rs = torch.randn(tokens, n, generator=torch.Generator(device=device).manual_seed(5), device=device)
+        rs = rs.to(torch.bfloat16)
+        if not rt.gemm_push_eligible(xs, ws):
+            results["failures"].append(f"{tokens} x {n} not eligible for the pushing GEMM")
+            continue
+        for call in range(2):  # both slot parities
+            partial = linear(xs, ws)
+            want_out, want_res = rt.all_reduce_residual_rmsnorm(partial, rs.clone(), gs, 1e-5)
+            got_out, got_res = rt.gemm_all_reduce_residual_rmsnorm(xs, ws, rs.clone(), gs, 1e-5)
+            torch.cuda.synchronize()
+            if not (torch.equal(got_out, want_out) and torch.equal(got_res, want_res)):
+                results["failures"].append(f"pushing GEMM differs from the unfused sequence ({tokens} x {n}, "
+                                           f"call {call})")
     x = torch.randn(8, 1024, generator=g, device=device).to(torch.bfloat16)
     w = (0.05 * torch.randn(2048, 1024, generator=g, device=device)).to(torch.bfloat16)
     gamma = (1 + 0.1 * torch.randn(2048, device=device)).to(torch.bfloat16)
     res0 = torch.randn(8, 2048, generator=torch.Generator(device=device).manual_seed(5), device=device)
     res0 = res0.to(torch.bfloat16)
-    for call in range(2):
-        partial = linear(x, w)
-        want_out, want_res = rt.all_reduce_residual_rmsnorm(partial, res0.clone(), gamma, 1e-5)
-        got_out, got_res = rt.gemm_all_reduce_residual_rmsnorm(x, w, res0.clone(), gamma, 1e-5)
-        torch.cuda.synchronize()
-        if not (torch.equal(got_out, want_out) and torch.equal(got_res, want_res)):
-            results["failures"].append(f"pushing GEMM differs from the unfused sequence (call {call})")
     res, out, part = res0.clone(), torch.empty_like(res0), torch.empty_like(res0)
     stream = torch.cuda.Stream(device=device)
     stream.wait_stream(torch.cuda.current_stream())
