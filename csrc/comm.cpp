@@ -312,10 +312,18 @@ class Comm {
     }
   }
 
-  void fused_norm(const std::vector<at::Tensor>& ins, const std::vector<at::Tensor>& residuals,
-                  const at::Tensor& gamma, double eps, const std::vector<at::Tensor>& outs,
-                  const std::vector<at::Tensor>& residual_outs, int algo, int cluster, int max_clusters,
-                  bool received = false) {
+  struct FusedPlan {
+    Job j;
+    LaunchGeom g;
+    int dtype;
+  };
+
+  // Every check of the fused norm, and its launch description; launches nothing (so a
+  // caller can validate before it launches anything that writes into peers' slots).
+  FusedPlan plan_fused_norm(const std::vector<at::Tensor>& ins, const std::vector<at::Tensor>& residuals,
+                            const at::Tensor& gamma, double eps, const std::vector<at::Tensor>& outs,
+                            const std::vector<at::Tensor>& residual_outs, int algo, int cluster, int max_clusters,
+                            bool received) const {
     if (received && (emulate_ || (algo != kOneShot && algo != kTwoShot) || world_ < 2))
       throw std::invalid_argument("a received fused norm runs in a real (not emulated) group, one-shot or two-shot");
     check_views(ins, outs);
@@ -356,12 +364,21 @@ class Comm {
     j.eps = float(eps);
     j.hidden = uint32_t(H);
     j.received = received ? 1u : 0u;
+    return FusedPlan{j, g, dtype_code(x)};
+  }
+
+  void fused_norm(const std::vector<at::Tensor>& ins, const std::vector<at::Tensor>& residuals,
+                  const at::Tensor& gamma, double eps, const std::vector<at::Tensor>& outs,
+                  const std::vector<at::Tensor>& residual_outs, int algo, int cluster, int max_clusters,
+                  bool received = false) {
+    FusedPlan p = plan_fused_norm(ins, residuals, gamma, eps, outs, residual_outs, algo, cluster, max_clusters,
+                                  received);
     auto stream = at::cuda::getCurrentCUDAStream(device_).stream();
     if (emulate_) {
       EmuViews e = emu_views(ins, outs, &residuals, &residual_outs);
-      launch_fused_norm(j, &e, dtype_code(x), algo, g, stream);
+      launch_fused_norm(p.j, &e, p.dtype, algo, p.g, stream);
     } else {
-      launch_fused_norm(j, nullptr, dtype_code(x), algo, g, stream);
+      launch_fused_norm(p.j, nullptr, p.dtype, algo, p.g, stream);
     }
   }
 
@@ -376,8 +393,14 @@ class Comm {
     if (algo != kOneShot && algo != kTwoShot) throw std::invalid_argument("one-shot or two-shot");
     if (x.scalar_type() != at::kBFloat16 || partial.scalar_type() != at::kBFloat16)
       throw std::invalid_argument("bf16 activations and partial");
+    if (residual.sizes() != partial.sizes() || out.sizes() != partial.sizes() ||
+        residual_out.sizes() != partial.sizes() || partial.dim() != 2 || gamma.numel() != partial.size(1))
+      throw std::invalid_argument("residual, out and residual_out like partial [tokens, N]; gamma [N]");
+    // Every check before the first launch: the GEMM writes into the peers' slots, so
+    // nothing may stop the collective that consumes them once it has run.
+    FusedPlan plan = plan_fused_norm({partial}, {residual}, gamma, eps, {out}, {residual_out}, algo, cluster, 0, true);
     tc::skinny_gemm_push(view_, L_, rank_, world_, x, w, partial, err, 0, pdl_gemm, algo == kTwoShot);
-    fused_norm({partial}, {residual}, gamma, eps, {out}, {residual_out}, algo, cluster, 0, true);
+    launch_fused_norm(plan.j, nullptr, plan.dtype, algo, plan.g, at::cuda::getCurrentCUDAStream(device_).stream());
   }
 
   // -- fused prefill GEMMs (tcgen05) ----------------------------------------------

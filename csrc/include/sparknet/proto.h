@@ -431,8 +431,9 @@ struct Job {
   // then lets the next such launch be scheduled (launch_dependents): the successor
   // can only start once every block of this grid is resident.
   uint32_t pdl;
-  // fused norm, one-shot: 1 when every rank's input was already pushed into the peers'
-  // Lamport slots (by the decode GEMM's epilogue); the kernel then only receives.
+  // fused norm: 1 when every rank's input was already pushed into the Lamport slots the
+  // kernel reads (one-shot: every peer's; two-shot: the row owners'), by the decode
+  // GEMM's epilogue; the kernel then skips its own push.
   uint32_t received;
   // Trace ring (device pointer of the pinned trace file's records), or null.
   uint64_t* trace;
