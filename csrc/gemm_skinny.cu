@@ -18,8 +18,9 @@
 // Y[m, f] = silu(gate) * up for the N/2 features (no intermediate tensor); mode 2 is the
 // QKV projection with RoPE (rotate-half, fp32) and the KV-cache write, one 128-row
 // tile per head (no qkv tensor, no separate RoPE kernel); mode 3 writes Y like mode 0
-// and pushes every finished 8-feature group into the peers' one-shot all-reduce slots
-// (the push half of the fused all-reduce + residual + RMSNorm that follows).
+// and pushes every finished 8-feature group into the peers' all-reduce slots, one-shot
+// or two-shot layout (the push half of the fused all-reduce + residual + RMSNorm that
+// follows).
 //
 // Every mbarrier wait is bounded (sets the error word and unwinds).
 // Reference: none (the reference has no model GEMMs).
@@ -259,9 +260,9 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
     // summed over the splits in split order exactly as mode 0 sums an element, and
     // pushed, sentinel-safe, into Lamport slot [parity][rank]: of every peer at the
     // one-shot layout's pack index (token * N / 8 + feature / 8), or (two-shot) of the
-    // row's owner (token % world) at (token / world) * N / 8 + feature / 8.  The parity is that of
-    // the collective that follows this kernel: the epoch read here plus one.  The read
-    // comes after griddepcontrol.wait (the main loop waited), so the previous
+    // row's owner (token % world) at (token / world) * N / 8 + feature / 8.  The parity
+    // is that of the collective that follows this kernel: the epoch read here plus one.
+    // The read comes after griddepcontrol.wait (the main loop waited), so the previous
     // collective has completed on this rank.  A poisoned rank pushes nothing (the
     // collective exits at entry).
     const Job& j = p.pj;
@@ -492,10 +493,11 @@ void skinny_qkv_rope(const at::Tensor& X, const at::Tensor& W, const at::Tensor&
   launch_skinny(W, X, p, pl, dev, pdl);
 }
 
-// Decode GEMM whose epilogue also performs the push of the one-shot all-reduce that
-// follows (mode 3): Y = X W^T, and every 16-byte group of Y goes to slot
-// [parity][rank] of every peer's region.  The caller launches the receiving fused
-// all-reduce + residual + RMSNorm right after it on the same stream.
+// Decode GEMM whose epilogue also performs the push of the all-reduce that follows
+// (mode 3): Y = X W^T, and every 16-byte group of Y goes to slot [parity][rank] of every
+// peer's region (one-shot) or of its row's owner (`twoshot`).  The caller launches the
+// receiving fused all-reduce + residual + RMSNorm right after it on the same stream,
+// having checked its arguments first.
 void skinny_gemm_push(const View& view, const Layout& L, int rank, int world, const at::Tensor& X,
                       const at::Tensor& W, at::Tensor& Y, at::Tensor& err, int max_splits, bool pdl, bool twoshot) {
   check_mat(X, "X");
