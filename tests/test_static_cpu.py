@@ -1,0 +1,65 @@
+"""Static checks over the native sources (CPU only), after the reference's header and
+PTX-string checks (reference tests/test_oneshot_cpu.py: required PTX present,
+record-then-fence-then-trap ordering).  Here they guard the rules the device code
+keeps on a shared GPU pool:
+
+* nothing traps: no ``trap`` instruction, ``__trap()``, ``__brkpt()`` or device
+  ``assert`` (a failed wait ends in a status word and the context stays usable);
+* no bulk or TMA copy with cluster multicast (the collective and fused GEMM kernels
+  run on several GPUs; ``tcgen05.commit`` may still signal a cluster);
+* the protocols' memory-ordering and multicast instructions are where the runtime
+  expects them.
+"""
+
+import re
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent.parent
+SOURCES = sorted(p for p in (ROOT / "csrc").rglob("*") if p.suffix in (".cu", ".cuh", ".h", ".cpp"))
+
+# Kept on separate lines on purpose: no line of this file names such a copy.
+BULK_COPY = "cp.async.bulk"
+MULTICAST = "multicast::"
+
+
+def code_lines(path):
+    """(line number, text) with // comments and /* */ blocks removed."""
+    text = path.read_text()
+    text = re.sub(r"/\*.*?\*/", lambda m: "\n" * m.group(0).count("\n"), text, flags=re.S)
+    for number, line in enumerate(text.splitlines(), 1):
+        yield number, line.split("//", 1)[0]
+
+
+def test_sources_found():
+    names = {p.name for p in SOURCES}
+    assert {"proto.h", "dev_mem.cuh", "collectives.cu", "gemm_tcgen05.cu", "gemm_skinny.cu"} <= names
+
+
+def test_nothing_traps():
+    banned = re.compile(r"\btrap\s*;|__trap\s*\(|__brkpt\s*\(|(?<!static_)\bassert\s*\(")
+    hits = [f"{p.relative_to(ROOT)}:{n}: {line.strip()}" for p in SOURCES for n, line in code_lines(p)
+            if banned.search(line)]
+    assert not hits, hits
+
+
+def test_no_bulk_copy_with_cluster_multicast():
+    hits = [f"{p.relative_to(ROOT)}:{n}: {line.strip()}" for p in SOURCES for n, line in code_lines(p)
+            if BULK_COPY in line and MULTICAST in line]
+    assert not hits, hits
+
+
+def test_protocol_instructions_present():
+    dev_mem = (ROOT / "csrc" / "include" / "sparknet" / "dev_mem.cuh").read_text()
+    for instruction in ("ld.acquire.sys", "st.release.sys", "fence.acq_rel.sys", "ld.volatile",
+                        "multimem.ld_reduce", "multimem.st"):
+        assert instruction in dev_mem, instruction
+    gemm = (ROOT / "csrc" / "include" / "sparknet" / "tc_gemm.cuh").read_text()
+    for instruction in ("tcgen05.mma", "tcgen05.alloc", "tcgen05.ld", "cp.async.bulk.tensor"):
+        assert instruction in gemm, instruction
+
+
+def test_every_poll_loop_is_bounded():
+    """The protocol's waits go through keep_waiting (clock, poison and timeout checks)."""
+    proto = (ROOT / "csrc" / "include" / "sparknet" / "proto.h").read_text()
+    loops = len(re.findall(r"while \(pending\)", proto))
+    assert loops >= 3 and proto.count("keep_waiting(m, w, c,") >= loops
