@@ -63,3 +63,13 @@ def test_every_poll_loop_is_bounded():
     proto = (ROOT / "csrc" / "include" / "sparknet" / "proto.h").read_text()
     loops = len(re.findall(r"while \(pending\)", proto))
     assert loops >= 3 and proto.count("keep_waiting(m, w, c,") >= loops
+
+
+def test_mbarrier_waits_are_bounded():
+    """The one mbarrier wait loop (mbar_wait) gives up after kWaitLimit tries, setting the
+    error word; every tcgen05 kernel waits through it."""
+    users = [p for p in SOURCES if any("mbarrier.try_wait" in line or "mbarrier.test_wait" in line
+                                       for _, line in code_lines(p))]
+    assert [p.name for p in users] == ["tc_gemm.cuh"], users
+    gemm = (ROOT / "csrc" / "include" / "sparknet" / "tc_gemm.cuh").read_text()
+    assert "for (uint32_t i = 0; i < kWaitLimit; ++i)" in gemm and "*err = kTcWaitTimeout;" in gemm
