@@ -271,3 +271,25 @@ def test_parallel_layer_decode_uses_the_decode_gemm(device, native):
     y = layer.decode(x)
     torch.cuda.synchronize()
     torch.testing.assert_close(y.float(), x.float() @ w.float().T, rtol=2e-2, atol=2e-2)
+
+
+def test_ops_decode_attention_wrapper(device, native):
+    """sparknet.ops.decode_attention (split-KV, its own workspace), against fp32, twice."""
+    from sparknet.ops import decode_attention
+
+    B, Hq, Hkv, L = 3, 16, 2, 200
+    for _ in range(2):
+        q = torch.randn(B, Hq, 128, device=device).to(torch.bfloat16)
+        kc = torch.randn(B, L + 8, Hkv, 128, device=device).to(torch.bfloat16)
+        vc = torch.randn(B, L + 8, Hkv, 128, device=device).to(torch.bfloat16)
+        lengths = torch.tensor([L, 17, 150], dtype=torch.int32, device=device)
+        out = decode_attention(q, kc, vc, lengths, L)
+        torch.cuda.synchronize()
+        G = Hq // Hkv
+        for b in range(B):
+            n = int(lengths[b])
+            k = kc[b, :n].float().repeat_interleave(G, dim=1)
+            v = vc[b, :n].float().repeat_interleave(G, dim=1)
+            s = torch.einsum("hd,nhd->hn", q[b].float(), k) / math.sqrt(128)
+            torch.testing.assert_close(out[b].float(), torch.einsum("hn,nhd->hd", s.softmax(-1), v),
+                                       rtol=2e-2, atol=2e-2)
