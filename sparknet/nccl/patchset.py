@@ -16,18 +16,22 @@ README = ("No NCCL patches are applied on B200: NCCL runs unmodified over NVLink
 
 
 def patch_directory() -> Path:
+    """Where the series would live (this package; it ships no patch files)."""
     return Path(__file__).resolve().parent
 
 
 def series() -> list[str]:
+    """The NCCL patch series: empty, stock NCCL serves an NVSwitch box."""
     return []
 
 
 def missing(directory: str | Path | None = None) -> list[str]:
+    """Patches of the series that ``directory`` lacks: none, stock NCCL needs no series."""
     return []
 
 
 def export(directory: str | Path) -> list[Path]:
+    """Write the (empty) patch series and its README into ``directory``; returns the written paths."""
     out = Path(directory)
     out.mkdir(parents=True, exist_ok=True)
     (out / "series").write_text("")

@@ -106,6 +106,7 @@ def size_bytes(value: str) -> int:
 
 
 def profile(name: str) -> dict[str, Any]:
+    """The named NCCL control profile (ValueError naming the known ones otherwise)."""
     try:
         return PROFILES[name]
     except KeyError:
@@ -113,10 +114,12 @@ def profile(name: str) -> dict[str, Any]:
 
 
 def profiles_for(transport: str, world: int) -> list[str]:
+    """The profiles that apply to ``transport`` at ``world`` GPUs."""
     return [n for n, e in PROFILES.items() if e["transport"] == transport and world in e["node_counts"]]
 
 
 def profile_problems(name: str, transport: str, world: int) -> list[str]:
+    """Why profile ``name`` does not fit ``transport`` at ``world`` GPUs (empty when it does)."""
     entry = profile(name)
     errors = []
     if entry["transport"] != transport:
@@ -174,5 +177,5 @@ def problems(env: dict[str, str], *, world: int) -> list[str]:
     return errors
 
 
-__all__ = ["COMMON_ENV", "COMMON_IB_ENV", "PATCH_CONTROLS", "PROFILES", "REFERENCE_IB_ENV", "environment", "problems", "profile",
-           "profile_problems", "profiles_for", "required_patches", "size_bytes"]
+__all__ = ["COMMON_ENV", "COMMON_IB_ENV", "PATCH_CONTROLS", "PROFILES", "REFERENCE_IB_ENV", "environment",
+           "problems", "profile", "profile_problems", "profiles_for", "required_patches", "size_bytes"]

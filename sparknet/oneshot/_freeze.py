@@ -36,12 +36,14 @@ def thaw_kernel_resolution() -> None:
 
 
 def kernel_resolution_frozen() -> bool:
+    """Whether lazy kernel or scratch resolution is refused at the moment."""
     with _lock:
         return _frozen
 
 
 def raise_if_kernel_resolution_frozen(kind: str, *, target: object | None = None,
                                       cache_key: object | None = None) -> None:
+    """Raise KernelResolutionFrozenError, naming ``kind`` and the target, while resolution is frozen."""
     with _lock:
         frozen, reason = _frozen, _reason
     if not frozen:

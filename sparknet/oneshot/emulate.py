@@ -18,6 +18,10 @@ from .runtime import ALGO_CODES, GATHER_CODES, LL_CAP, PACK_BYTES, align_up
 
 
 class EmulatedGroup:
+    """Every rank of a group on one GPU: ``world`` regions and one cooperative launch per
+    collective (rank = blockIdx.y), running the production protocol code; the protocol
+    tests' group."""
+
     def __init__(self, world: int, device: torch.device | int | str = "cuda", *, max_size: int = 8 << 20,
                  max_gather_bytes: int = 4 << 20, timeout_ms: int = 2000):
         self.world = int(world)

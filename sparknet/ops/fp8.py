@@ -22,6 +22,7 @@ from .gemm import _ERRORS, GemmError, _err_word
 
 
 def scale_bytes(rows: int, k: int) -> int:
+    """Bytes of the scale chunks of a ``rows x k`` matrix: 512 per 128 rows and 128 columns."""
     return ((rows + 127) // 128) * (k // 128) * 512
 
 
@@ -60,6 +61,7 @@ def scales_to_dense(sf: torch.Tensor, rows: int, k: int) -> torch.Tensor:
 
 
 def dequantize(q: torch.Tensor, sf: torch.Tensor) -> torch.Tensor:
+    """fp32 values of an e4m3 matrix from its UE8M0 scale chunks (activation or weight layout)."""
     rows, k = q.shape
     s = scales_to_dense(sf, rows, k).repeat_interleave(128, dim=1)
     return q.float() * s

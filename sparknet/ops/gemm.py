@@ -16,6 +16,7 @@ _ERRORS = {1: "an mbarrier wait timed out", 2: "a peer flag wait timed out"}
 
 
 class GemmError(RuntimeError):
+    """A tcgen05 GEMM gave up on a bounded wait (its error word was set)."""
     pass
 
 

@@ -36,6 +36,9 @@ class TPGroup:
 
 def init_tp(*, max_size: int = 8 << 20, max_gather_bytes: int = 16 << 20, timeout_s: int = 120,
             runtime: bool = True, policy=None) -> TPGroup:
+    """Join the tensor-parallel group of this process (LOCAL_RANK's GPU): the default
+    process group, a gloo group for the setup exchange and, with ``runtime=True``, the
+    NVLink runtime."""
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)

@@ -18,6 +18,8 @@ def docker_probe_command(*, image: str, environment: dict[str, str], nproc: int,
                          transport: str = "nvlink", package_source: str | None = None,
                          package_target: str = DEFAULT_PACKAGE_TARGET, memory: str = "64g",
                          timeout_seconds: int = 900, extra_args: tuple[str, ...] = ()) -> list[str]:
+    """The bounded ``docker run`` command that runs the collective probe on one box (memory
+    and time limits, the rendered environment, the GPUs and IPC it needs)."""
     env = dict(environment)
     env.setdefault("NCCL_DEBUG", "INFO")
     env.setdefault("NCCL_DEBUG_SUBSYS", "INIT,GRAPH")

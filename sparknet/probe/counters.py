@@ -61,6 +61,7 @@ def nvlink_counters(nvml: Any = None, *, links: int = 18) -> dict[str, int]:
 
 
 def deltas(before: dict[str, int], after: dict[str, int]) -> dict[str, int]:
+    """The counters that changed between two snapshots, as after minus before."""
     return {k: after[k] - before[k] for k in after if k in before and after[k] != before[k]}
 
 

@@ -36,6 +36,8 @@ def fabricmanager_active(run: Callable[..., Any] = subprocess.run) -> Optional[b
 def local_problems(gmap: dict, node_name: str, transport: str, *, nvml: Any = None,
                    fabricmanager: Optional[Callable[[], Optional[bool]]] = None,
                    which: Callable[[str], Optional[str]] = shutil.which) -> list[str]:
+    """What keeps this host from serving ``node_name`` of the map over ``transport`` (read-
+    only NVML checks; empty when ready)."""
     errors = gpumap.problems(gmap, transport)
     if errors:
         return errors

@@ -52,6 +52,7 @@ def plan(gmap: dict, environments: dict[str, dict[str, str]], *, transport: str,
          probe_args: tuple[str, ...] = (), package_source: str | None = None,
          extra_env: dict[str, str] | None = None, ssh_user: str | None = None,
          target_field: str = "name", local_box: str | None = None) -> list[BoxPlan]:
+    """One probe command per box of the map, with its rendered environment and ssh target."""
     head = gpumap.head_node(gmap)
     user = ssh_user or gmap.get("ssh_user")
     nodes = sorted(gmap["nodes"], key=lambda n: (not n.get("head"), n["name"]))
@@ -71,12 +72,14 @@ def plan(gmap: dict, environments: dict[str, dict[str, str]], *, transport: str,
 
 
 def ssh_command(p: BoxPlan, ssh: tuple[str, ...] = DEFAULT_SSH) -> list[str]:
+    """The command that runs a box's probe: as is on the local box, through ssh otherwise."""
     if p.local:
         return list(p.command)
     return [*ssh, p.target, " ".join(shlex.quote(c) for c in p.command)]
 
 
 def parse_result(text: str) -> dict | None:
+    """The probe's JSON result line from a box's output, or None."""
     for line in reversed(text.splitlines()):
         line = line.strip()
         if line.startswith("{") and '"timings"' in line:
@@ -89,6 +92,7 @@ def parse_result(text: str) -> dict | None:
 
 def run(plans: list[BoxPlan], out: str | Path, *, ssh: tuple[str, ...] = DEFAULT_SSH, timeout: float = 900.0,
         popen: Callable[..., subprocess.Popen] = subprocess.Popen) -> list[BoxOutcome]:
+    """Start every box's probe at once, wait (bounded), and keep each box's log and result."""
     out = Path(out)
     out.mkdir(parents=True, exist_ok=True)
     running = []

@@ -39,6 +39,8 @@ def _cuda_attr(index: int, attr: int) -> Optional[int]:
 
 def nvlink_report(*, nvml: Any = None, cuda_attr: Callable[[int, int], Optional[int]] = _cuda_attr,
                   fabricmanager: Callable[[], Optional[bool]] = fabricmanager_active, dev_root: str = "/dev") -> dict:
+    """What this host offers the NVLink transport: P2P pairs, multicast, fabric handles,
+    IMEX channels and the fabric manager, with a readiness verdict per stage."""
     try:
         nv = nvml if nvml is not None else nvml_mod.load()
     except RuntimeError as exc:
@@ -86,6 +88,7 @@ def nvlink_report(*, nvml: Any = None, cuda_attr: Callable[[int, int], Optional[
 
 
 def render(report: dict) -> str:
+    """The report as text."""
     if "error" in report:
         return f"NVLink report unavailable: {report['error']}\n"
     lines = [f"driver {report['driver']}, {len(report['gpus'])} GPU(s), fabric manager "

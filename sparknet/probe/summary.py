@@ -17,6 +17,7 @@ OPERATIONS = ("all_reduce", "all_gather", "reduce_scatter", "fused_norm")
 
 
 def load_results(directory: str | Path) -> dict[str, dict]:
+    """Probe receipts (``*.json`` with timings) of a directory, by file stem."""
     results = {}
     for path in sorted(Path(directory).glob("*.json")):
         data = json.loads(path.read_text())
@@ -32,10 +33,12 @@ def dtype_name(value: str) -> str:
 
 
 def payload_bytes(row: dict) -> int:
+    """Bytes per rank of a timing row."""
     return int(row["elements_per_rank"]) * ITEM_SIZES[dtype_name(row["dtype"])]
 
 
 def size_label(nbytes: int) -> str:
+    """``n MiB`` / ``n KiB`` / ``n B``."""
     for unit, scale in (("MiB", 1 << 20), ("KiB", 1 << 10)):
         if nbytes % scale == 0:
             return f"{nbytes // scale} {unit}"

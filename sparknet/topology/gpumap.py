@@ -51,6 +51,7 @@ _UUID = re.compile(r"GPU-[0-9a-fA-F]{8}-[0-9a-fA-F]{4}-[0-9a-fA-F]{4}-[0-9a-fA-F
 
 
 def load(path: str | Path) -> dict:
+    """A GPU map from a JSON file."""
     return json.loads(Path(path).read_text())
 
 
@@ -61,6 +62,7 @@ def normalize_pci(bus_id: str) -> str:
 
 
 def node_by_name(gmap: dict, name: str) -> dict:
+    """The node called ``name`` (KeyError otherwise)."""
     for node in gmap.get("nodes", []):
         if node.get("name") == name:
             return node
@@ -68,6 +70,7 @@ def node_by_name(gmap: dict, name: str) -> dict:
 
 
 def head_node(gmap: dict) -> dict:
+    """The map's one head node (ValueError unless exactly one)."""
     heads = [n for n in gmap.get("nodes", []) if n.get("head")]
     if len(heads) != 1:
         raise ValueError("exactly one head node is required")
@@ -75,6 +78,7 @@ def head_node(gmap: dict) -> dict:
 
 
 def gpu_by_rank(node: dict, rank: int) -> dict:
+    """The GPU entry of ``node`` with tensor-parallel rank ``rank``."""
     for gpu in node.get("gpus", []):
         if gpu.get("rank") == rank:
             return gpu
@@ -87,14 +91,17 @@ def ranked_gpus(node: dict) -> list[dict]:
 
 
 def uses_oneshot(transport: str) -> bool:
+    """Whether ``transport`` runs this library's NVLink kernels (not NCCL only)."""
     return transport in ONESHOT_TRANSPORTS
 
 
 def uses_nvls(transport: str) -> bool:
+    """Whether ``transport`` uses the NVLS multicast kernels."""
     return transport == "nvlink-nvls"
 
 
 def world_size(node: dict) -> int:
+    """The number of ranked GPUs of ``node``."""
     return len(ranked_gpus(node))
 
 
@@ -109,6 +116,7 @@ def _interface_problems(label: str, name) -> list[str]:
 
 
 def node_problems(node: dict, transport: str) -> list[str]:
+    """What is wrong with one node of the map for ``transport`` (empty when nothing)."""
     label = f"node {node.get('name', '?')}"
     errors: list[str] = []
     for field, why in _RETIRED_FIELDS.items():

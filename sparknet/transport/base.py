@@ -54,6 +54,8 @@ class TransportCapability:
 
 @runtime_checkable
 class Transport(Protocol):
+    """How a runtime reaches its peers' memory: connect over the exchange group, then every
+    rank's region base and the optional multicast alias."""
     name: str
     world_size: int
     rank: int

@@ -19,11 +19,13 @@ from .base import Geometry, TransportCapability
 
 
 def host_staged_capability() -> TransportCapability:
+    """Whether the host-staged test transport can run here (``/dev/shm``)."""
     return TransportCapability(name="host-staged", available=os.path.isdir("/dev/shm"),
                                reasons=() if os.path.isdir("/dev/shm") else ("/dev/shm missing",))
 
 
 class HostStagedTransport:
+    """A CPU test double of the transport: regions in shared host memory, no GPU."""
     name = "host-staged"
 
     def __init__(self, geometry: Geometry):

@@ -17,6 +17,7 @@ from .base import Geometry, TransportCapability
 
 
 def nvlink_capability(device_index: int = 0) -> TransportCapability:
+    """Whether this host can run the NVLink transport on ``device_index`` (and why not)."""
     reasons, details = [], {}
     try:
         from sparknet import _native
@@ -32,6 +33,8 @@ def nvlink_capability(device_index: int = 0) -> TransportCapability:
 
 
 class NvlinkP2PTransport:
+    """Symmetric regions over NVLink: a CUDA VMM region per rank, descriptors passed to the
+    peers, every peer's region mapped."""
     name = "nvlink-p2p"
 
     def __init__(self, geometry: Geometry):
@@ -96,6 +99,7 @@ class NvlinkP2PTransport:
 
 
 class NvlsTransport(NvlinkP2PTransport):
+    """The NVLink transport plus an NVLS multicast object bound to every rank's buffer."""
     name = "nvlink-nvls"
 
     def _multicast_bytes(self) -> int:
