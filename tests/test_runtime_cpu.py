@@ -192,3 +192,11 @@ def test_pushing_gemm_eligibility():
     assert ok(64, 1024, 8192)                # two ranks: one-shot up to the slot
     rt.world_size = 1
     assert not ok(8, 1024, 8192)             # no peers to push to
+
+
+def test_attention_wrapper_rejects_unknown_variants():
+    from sparknet.ops import decode_attention
+
+    q = torch.zeros(1, 8, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="variant"):
+        decode_attention(q, q, q, torch.ones(1, dtype=torch.int32), 1, variant="paged")
