@@ -10,7 +10,7 @@
 // the accumulator with tcgen05.ld and run the epilogue; the accumulator is double
 // buffered in TMEM so the epilogue of tile i overlaps the MMAs of tile i+1.
 //
-// No TMA load uses .multicast::cluster: the fused kernels run on several GPUs.  Every
+// Every TMA load is a plain per-CTA load (the fused kernels run on several GPUs).  Every
 // mbarrier wait is bounded: a wait that runs out sets the kernel's error word and the
 // roles unwind, free TMEM and return.
 #pragma once
@@ -178,7 +178,7 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
 // 128 rows of A and of B (layout in fp8_quant.cu), staged into TMEM by tcgen05.cp.
 
 // Bulk (non-tensor) copy global -> this CTA's shared memory, completing on `bar`.
-// 16-byte aligned addresses, size a multiple of 16.  No multicast.
+// 16-byte aligned addresses, size a multiple of 16.  Per-CTA destination only.
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))

@@ -5,9 +5,10 @@ keeps on a shared GPU pool:
 
 * nothing traps: no ``trap`` instruction, ``__trap()``, ``__brkpt()`` or device
   ``assert`` (a failed wait ends in a status word and the context stays usable);
-* no bulk or TMA copy with cluster multicast (the collective and fused GEMM kernels
-  run on several GPUs; ``tcgen05.commit`` may still signal a cluster);
-* the protocols' memory-ordering and multicast instructions are where the runtime
+* every bulk copy is a plain per-CTA copy: its qualifiers come from a short
+  allow-list (the collective and fused GEMM kernels run on several GPUs, so each CTA
+  loads its own tiles);
+* the protocols' memory-ordering and NVLS instructions are where the runtime
   expects them.
 """
 
@@ -17,9 +18,14 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent.parent
 SOURCES = sorted(p for p in (ROOT / "csrc").rglob("*") if p.suffix in (".cu", ".cuh", ".h", ".cpp"))
 
-# Kept on separate lines on purpose: no line of this file names such a copy.
-BULK_COPY = "cp.async.bulk"
-MULTICAST = "multicast::"
+BULK_COPY = re.compile(r"cp\.async\.bulk[\w.:]*")
+# The qualifiers a bulk copy here may carry.  Anything else (a new state space, a
+# cluster-wide delivery mode, a gather form) fails the check until reviewed.
+ALLOWED_BULK_QUALIFIERS = {
+    "cp", "async", "bulk", "tensor", "1d", "2d", "3d", "4d", "5d", "tile",
+    "shared::cluster", "shared::cta", "global", "mbarrier::complete_tx::bytes",
+    "bulk_group", "prefetch", "L2", "L2::cache_hint",
+}
 
 
 def code_lines(path):
@@ -42,10 +48,21 @@ def test_nothing_traps():
     assert not hits, hits
 
 
-def test_no_bulk_copy_with_cluster_multicast():
-    hits = [f"{p.relative_to(ROOT)}:{n}: {line.strip()}" for p in SOURCES for n, line in code_lines(p)
-            if BULK_COPY in line and MULTICAST in line]
-    assert not hits, hits
+def _qualifiers(instruction):
+    """Split ``cp.async.bulk.x.y::z`` into its dot-separated parts (``::`` stays inside a part)."""
+    return instruction.split(".")
+
+
+def test_bulk_copies_are_per_cta():
+    found, hits = 0, []
+    for p in SOURCES:
+        for n, line in code_lines(p):
+            for m in BULK_COPY.finditer(line):
+                found += 1
+                extra = set(_qualifiers(m.group(0))) - ALLOWED_BULK_QUALIFIERS
+                if extra:
+                    hits.append(f"{p.relative_to(ROOT)}:{n}: {sorted(extra)}")
+    assert found >= 2 and not hits, hits
 
 
 def test_protocol_instructions_present():
