@@ -65,6 +65,10 @@ def parse_args(argv=None):
     p.add_argument("--attention", choices=("split", "cluster"), default="split",
                    help="decode: span merge through a workspace (split) or a thread-block cluster")
     p.add_argument("--layers", type=int, default=80, help="decode: decoder layers")
+    p.add_argument("--fused-norm-tokens", type=int, nargs="*", default=[1, 8, 32, 128, 256],
+                   help="ours: also time the fused all-reduce + residual + RMSNorm at these token counts "
+                        "(hidden --hidden); none to skip")
+    p.add_argument("--hidden", type=int, default=8192, help="fused norm: hidden size")
     p.add_argument("--json-out", default="")
     return p.parse_args(argv)
 
@@ -136,6 +140,28 @@ def gather_floats(values: list[float], cpu_group) -> list[list[float]]:
     return out
 
 
+def rank_order_sum(x: torch.Tensor, world: int) -> torch.Tensor:
+    """The all-reduce every rank must return: all ranks' inputs (gathered with NCCL)
+    summed in rank order 0..W-1 in fp32 and rounded once to ``x.dtype``."""
+    parts = [torch.empty_like(x) for _ in range(world)]
+    dist.all_gather(parts, x.contiguous())
+    acc = parts[0].float()
+    for p in parts[1:]:
+        acc = acc + p.float()
+    return acc.to(x.dtype)
+
+
+def compare_exact(got: torch.Tensor, want: torch.Tensor, cpu_group, world: int) -> dict:
+    """Bit equality with ``want`` on this rank, and the same digest on every rank."""
+    equal = bool(torch.equal(got.view(torch.int16), want.view(torch.int16)))
+    err = (got.float() - want.float()).abs().max().item()
+    digest = hashlib.sha256(got.view(torch.int16).cpu().numpy().tobytes()).hexdigest()
+    digests = [None] * world
+    dist.all_gather_object(digests, (digest, equal), group=cpu_group)
+    return {"bit_exact": all(e for _, e in digests), "rank_identical": len({d for d, _ in digests}) == 1,
+            "max_abs_err_vs_rank_order_sum": err}
+
+
 def clocks_gpus(world: int) -> list[int]:
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     if vis:
@@ -199,21 +225,21 @@ def run_allreduce(args, rank, world, device, cpu_group):
     gen.manual_seed(1000 + rank)
     inputs = {s: torch.randn(s // 2, generator=gen, device=device, dtype=torch.float32).to(torch.bfloat16)
               for s in sizes}
-    # correctness against NCCL on the same inputs (tolerance: NCCL's order differs), and
-    # identical bits on every rank
+    # correctness: every rank's output must equal, bit for bit, the fp32 sum of all
+    # ranks' bf16 inputs taken in rank order and rounded once (the library's contract),
+    # and be identical on every rank.  NVLS reduces inside the switch in no fixed
+    # order, so a forced --algorithm nvls is held to a tolerance instead.
+    exact_required = args.impl == "ours" and args.algorithm != "nvls"
+    expected = {s: rank_order_sum(inputs[s], world) for s in sizes}
     checks = {}
     for s in sizes:
         got = arm.all_reduce(inputs[s])
-        ref = inputs[s].float().clone()
-        dist.all_reduce(ref)
         torch.cuda.synchronize()
-        err = (got.float() - ref).abs().max().item()
-        digest = hashlib.sha256(got.view(torch.int16).cpu().numpy().tobytes()).hexdigest()
-        digests = [None] * world
-        dist.all_gather_object(digests, digest, group=cpu_group)
-        checks[s] = {"max_abs_err_vs_fp32": err, "rank_identical": len(set(digests)) == 1}
-        if err > 1.0 + 0.25 * world:  # gross errors only: NCCL's bf16 order differs
-            raise RuntimeError(f"all-reduce mismatch at {s} bytes: max error {err}")
+        checks[s] = compare_exact(got, expected[s], cpu_group, world)
+        if exact_required and not checks[s]["bit_exact"]:
+            raise RuntimeError(f"all-reduce at {s} bytes is not the rank-order sum: {checks[s]}")
+        if not checks[s]["rank_identical"] and args.impl == "ours":
+            raise RuntimeError(f"all-reduce at {s} bytes differs across ranks")
 
     stream = torch.cuda.Stream(device=device)
     graphs, outs = {}, {}
@@ -276,12 +302,20 @@ def run_allreduce(args, rank, world, device, cpu_group):
         step_ms.append(sum(max(g[k * n + si] for g in gathered) for si in range(n)))
     if args.impl == "ours":
         arm.rt.check_health()
+    for s in sizes:  # the timed replays' last output is still the rank-order sum
+        after = compare_exact(outs[s], expected[s], cpu_group, world)
+        checks[s]["bit_exact_after_timing"] = after["bit_exact"]
+        if exact_required and not after["bit_exact"]:
+            raise RuntimeError(f"graph-replayed all-reduce at {s} bytes is not the rank-order sum: {after}")
     del graphs, outs  # graphs holding NCCL calls must go before the process group does
     torch.cuda.synchronize()
 
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(arm, args, sizes, rank, world, device, cpu_group)
+    fused = None
+    if args.impl == "ours" and args.fused_norm_tokens:
+        fused = run_fused_norm(arm, args, rank, world, device, cpu_group)
 
     headline = [p50_us[s] for s in sizes if s in HEADLINE_SIZES] or list(p50_us.values())
     value = geomean(headline)
@@ -315,6 +349,8 @@ def run_allreduce(args, rank, world, device, cpu_group):
         "clocks": clocks,
         "e2e": e2e,
     }
+    if fused is not None:
+        result["fused_allreduce_residual_rmsnorm"] = fused
     if args.impl == "ours":
         result["algorithms"] = {str(s): (args.algorithm or arm.rt.algorithm_for(s, torch.bfloat16)) for s in sizes}
         result["native_extension"] = arm.native_path
@@ -379,6 +415,89 @@ def run_e2e(arm, args, sizes, rank, world, device, cpu_group):
         "api": "sparknet.oneshot.AllReduce.all_reduce" if arm.impl == "ours"
         else "sparknet.probe.collectives.PolicyCommunicator.all_reduce (reference)",
     }
+
+
+def run_fused_norm(arm, args, rank, world, device, cpu_group):
+    """The decode epilogue ``residual += all_reduce(x); out = RMSNorm(residual) * gamma``
+    fused in one kernel, per token count: p50 per call (max over ranks) of a graph of 256
+    calls, L2 flushed before each replay; beside it the unfused sequence of this library
+    (one-shot/two-shot all-reduce, then the add + RMSNorm kernel).  Checks: the new
+    residual equals the rank-order all-reduce plus the residual bit for bit, the output
+    is identical on every rank, and it is within one bf16 rounding of an fp32 RMSNorm."""
+    from sparknet import _native
+
+    C = _native.load()
+    L2Flusher = _local("timing").L2Flusher
+    flush = L2Flusher(device)
+    rt, H, eps = arm.rt, args.hidden, 1e-5
+    rows = {}
+    stream = torch.cuda.Stream(device=device)
+    for tokens in args.fused_norm_tokens:
+        gen = torch.Generator(device=device).manual_seed(5000 + 97 * tokens + rank)
+        x = torch.randn(tokens, H, generator=gen, device=device).to(torch.bfloat16)
+        shared = torch.Generator(device=device).manual_seed(77 + tokens)  # residual and gamma: same on all ranks
+        res = torch.randn(tokens, H, generator=shared, device=device).to(torch.bfloat16)
+        gamma = (1.0 + 0.02 * torch.randn(H, generator=shared, device=device)).to(torch.bfloat16)
+        out, res_out = torch.empty_like(x), torch.empty_like(res)
+        ar, out_u, res_u = torch.empty_like(x), torch.empty_like(x), torch.empty_like(res)
+        rt.all_reduce_residual_rmsnorm(x, res, gamma, eps, out=out, residual_out=res_out)
+        torch.cuda.synchronize()
+        want_res = (rank_order_sum(x, world).float() + res.float()).to(torch.bfloat16)
+        r32 = want_res.float()
+        want_out = r32 * torch.rsqrt(r32.pow(2).mean(-1, keepdim=True) + eps) * gamma.float()
+        check = compare_exact(res_out, want_res, cpu_group, world)
+        same_out = compare_exact(out, out, cpu_group, world)["rank_identical"]
+        rel = ((out.float() - want_out).abs() / want_out.abs().clamp_min(1e-3)).max().item()
+        check.update({"out_rank_identical": same_out, "out_max_rel_err_vs_fp32": rel})
+        if not (check["bit_exact"] and same_out and rel <= 2.0 ** -7):
+            raise RuntimeError(f"fused all-reduce + RMSNorm at {tokens} tokens failed its checks: {check}")
+
+        def fused():
+            rt.all_reduce_residual_rmsnorm(x, res, gamma, eps, out=out, residual_out=res_out)
+
+        def unfused():
+            rt.all_reduce(x, out=ar)
+            C.add_rmsnorm(ar, res, res_u, gamma, out_u, eps)
+
+        graphs = {}
+        for name, fn in (("fused", fused), ("unfused", unfused)):
+            stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(stream):
+                fn()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream), rt.capture(stream=stream):
+                for _ in range(CALLS_PER_GRAPH):
+                    fn()
+            graphs[name] = g
+        samples = {name: [] for name in graphs}
+        cur = torch.cuda.current_stream()
+        for step in range(args.warmup + args.steps):
+            for name, g in graphs.items():
+                flush()
+                rt.barrier()
+                st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                st.record(cur)
+                g.replay()
+                en.record(cur)
+                if step >= args.warmup:
+                    samples[name].append((st, en))
+        torch.cuda.synchronize()
+        rt.check_health()
+        if not torch.equal(res_out, want_res):
+            raise RuntimeError(f"graph-replayed fused norm at {tokens} tokens changed its residual output")
+        flat = [st.elapsed_time(en) for name in graphs for (st, en) in samples[name]]
+        gathered = gather_floats(flat, cpu_group)
+        row = {"check": check}
+        for ni, name in enumerate(graphs):
+            per = [max(g[ni * args.steps + k] for g in gathered) for k in range(args.steps)]
+            row[f"{name}_p50_us"] = round(statistics.median(per) * 1000.0 / CALLS_PER_GRAPH, 3)
+        row["algorithm"] = rt._fused_norm_algorithm(tokens, x.numel() * x.element_size())
+        rows[str(tokens)] = row
+        del graphs
+        torch.cuda.synchronize()
+    return {"hidden": H, "dtype": "bf16", "calls_per_graph": CALLS_PER_GRAPH,
+            "unfused": "this library's all_reduce then its add+RMSNorm kernel", "per_tokens": rows}
 
 
 def main():

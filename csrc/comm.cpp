@@ -323,7 +323,7 @@ class Comm {
   FusedPlan plan_fused_norm(const std::vector<at::Tensor>& ins, const std::vector<at::Tensor>& residuals,
                             const at::Tensor& gamma, double eps, const std::vector<at::Tensor>& outs,
                             const std::vector<at::Tensor>& residual_outs, int algo, int cluster, int max_clusters,
-                            bool received) const {
+                            bool received, int threads = 0) const {
     if (received && (emulate_ || (algo != kOneShot && algo != kTwoShot) || world_ < 2))
       throw std::invalid_argument("a received fused norm runs in a real (not emulated) group, one-shot or two-shot");
     check_views(ins, outs);
@@ -342,12 +342,14 @@ class Comm {
     } else if (nbytes > L_.lam_cap) {
       throw std::invalid_argument("tokens exceed fused one-shot capacity");
     }
+    // One 16-byte pack per thread when it fits in a block; otherwise each thread takes
+    // every blockDim-th pack of its CTA's share (the kernel follows the launch it got).
     int cta_packs = int(H / elems / cluster);
-    if (cta_packs > kMaxThreads)
-      throw std::invalid_argument("hidden too large for the cluster size (at most " + std::to_string(kMaxThreads) +
-                                  " packs of 16 bytes per CTA: use a larger cluster)");
+    if (threads < 0 || threads % 32 || threads > kMaxThreads)
+      throw std::invalid_argument("fused norm threads must be 0 (auto) or a multiple of 32 up to " +
+                                  std::to_string(kMaxThreads));
     LaunchGeom g;
-    g.threads = std::max(32, (cta_packs + 31) / 32 * 32);
+    g.threads = threads ? threads : std::min(kMaxThreads, std::max(32, (cta_packs + 31) / 32 * 32));
     int nclusters = int(std::min<int64_t>(T, max_clusters > 0 ? max_clusters : 64));
     if (emulate_) nclusters = std::max(1, std::min(nclusters, (sms_ * 4) / (cluster * world_)));
     g.blocks = nclusters * cluster;
@@ -370,9 +372,9 @@ class Comm {
   void fused_norm(const std::vector<at::Tensor>& ins, const std::vector<at::Tensor>& residuals,
                   const at::Tensor& gamma, double eps, const std::vector<at::Tensor>& outs,
                   const std::vector<at::Tensor>& residual_outs, int algo, int cluster, int max_clusters,
-                  bool received = false) {
+                  bool received = false, int threads = 0) {
     FusedPlan p = plan_fused_norm(ins, residuals, gamma, eps, outs, residual_outs, algo, cluster, max_clusters,
-                                  received);
+                                  received, threads);
     auto stream = at::cuda::getCurrentCUDAStream(device_).stream();
     if (emulate_) {
       EmuViews e = emu_views(ins, outs, &residuals, &residual_outs);
@@ -616,7 +618,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            py::arg("out"), py::arg("err"), py::arg("max_ctas") = 0)
       .def("fused_norm", &Comm::fused_norm, py::arg("ins"), py::arg("residuals"), py::arg("gamma"), py::arg("eps"),
            py::arg("outs"), py::arg("residual_outs"), py::arg("algo"), py::arg("cluster") = 8,
-           py::arg("max_clusters") = 0, py::arg("received") = false)
+           py::arg("max_clusters") = 0, py::arg("received") = false, py::arg("threads") = 0)
       .def("gemm_fused_norm", &Comm::gemm_fused_norm, py::arg("x"), py::arg("w"), py::arg("partial"),
            py::arg("residual"), py::arg("gamma"), py::arg("eps"), py::arg("out"), py::arg("residual_out"),
            py::arg("err"), py::arg("algo") = 0, py::arg("cluster") = 8, py::arg("pdl_gemm") = true)

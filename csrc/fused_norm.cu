@@ -82,7 +82,6 @@ SN_DEV void fused_body(const Job& j, int algo) {
   cg::cluster_group cluster = cg::this_cluster();
   __shared__ float warp_part[32];
   __shared__ float part;
-  __shared__ int ok_s;
 
   Ctrl* ctrl = ctrl_of(j);
   if (int32_t(j.rank) == j.skip_rank) return;
@@ -95,16 +94,20 @@ SN_DEV void fused_body(const Job& j, int algo) {
   constexpr int kElems = 16 / (Codec<D>::kLanes == 2 ? 2 : 4);   // elements per pack
   const uint32_t W = j.world, r = j.rank;
   const uint32_t parity = seq & 1u;
+  // Geometry from the launch as it actually ran: the cluster size and the block size
+  // are read here, not assumed from the host's plan.  A tool that re-issues the launch
+  // without its cluster attribute (a profiler) then still gets a correct result:
+  // every CTA covers row_packs / CL packs, each thread as many strided packs as that
+  // takes; the row's sum of squares is still reduced in a fixed order.
   const uint32_t CL = cluster.num_blocks();
   const uint32_t cta = cluster.block_rank();
   const uint64_t row_packs = j.hidden / kElems;
   const uint64_t cta_packs = row_packs / CL;
+  const uint32_t per_thread = uint32_t((cta_packs + blockDim.x - 1) / blockDim.x);
   const uint64_t T = j.nbytes / (row_packs * kPack);
   const uint32_t nclusters = gridDim.x / CL;
   const uint32_t cid = blockIdx.x / CL;
   const uint64_t half = j.L.lam_cap / 2 / kPack;
-  const uint64_t tpack = uint64_t(cta) * cta_packs + threadIdx.x;    // pack within the row
-  const bool active = threadIdx.x < cta_packs;
 
   const Pack16* x = reinterpret_cast<const Pack16*>(j.in);
   const Pack16* res = reinterpret_cast<const Pack16*>(j.residual);
@@ -112,55 +115,68 @@ SN_DEV void fused_body(const Job& j, int algo) {
   Pack16* out = reinterpret_cast<Pack16*>(j.out);
   Pack16* res_out = reinterpret_cast<Pack16*>(j.residual_out);
   const bool twoshot = (algo == kTwoShot) && W > 1;
-  bool ok = true;
+  bool ok = row_packs % CL == 0;  // always true for a cluster size the host accepts
+  if (!ok) record_failure(m, c, kFailGeometry, r, 0);
+
+  // pack index within the row of this thread's k-th pack, or ~0 when it has none
+  auto row_pack = [&](uint32_t k) -> uint64_t {
+    const uint64_t within = uint64_t(threadIdx.x) + uint64_t(k) * blockDim.x;
+    return within < cta_packs ? uint64_t(cta) * cta_packs + within : ~0ull;
+  };
 
   // 1. push: one-shot sends every row to every peer; two-shot sends row t to its owner.
   //    Skipped when the producer of the input already pushed it (j.received).
-  if (active && W > 1 && !j.received) {
+  if (ok && W > 1 && !j.received) {
     for (uint64_t t = cid; t < T; t += nclusters) {
-      const uint64_t i = t * row_packs + tpack;
-      Pack16 v = pack_canon<D>(m.ld_input(x + i));
-      if (twoshot) {
-        uint32_t q = uint32_t(t % W);
-        if (q != r) {
-          uint64_t slot_pack = (t / W) * row_packs + tpack;
-          m.st_remote(lam_pack(j, q, parity, r, slot_pack), v);
-        }
-      } else {
-        for (uint32_t k = 1; k < W; ++k) {
-          uint32_t q = (r + k) % W;
-          m.st_remote(lam_pack(j, q, parity, r, i), v);
+      for (uint32_t k = 0; k < per_thread; ++k) {
+        const uint64_t tpack = row_pack(k);
+        if (tpack == ~0ull) break;
+        const uint64_t i = t * row_packs + tpack;
+        Pack16 v = pack_canon<D>(m.ld_input(x + i));
+        if (twoshot) {
+          uint32_t q = uint32_t(t % W);
+          if (q != r) m.st_remote(lam_pack(j, q, parity, r, (t / W) * row_packs + tpack), v);
+        } else {
+          for (uint32_t s = 1; s < W; ++s) m.st_remote(lam_pack(j, (r + s) % W, parity, r, i), v);
         }
       }
     }
   }
 
   // 2. two-shot: reduce the rows this rank owns and push the rounded sums back.
-  if (twoshot && active) {
+  if (twoshot && ok) {
     for (uint64_t t = cid; t < T && ok; t += nclusters) {
       if (t % W != r) continue;
-      const uint64_t i = t * row_packs + tpack;
-      const uint64_t slot_pack = (t / W) * row_packs + tpack;
-      Pack16 xs[kMaxRanks];
-      const Pack16 own = pack_canon<D>(m.ld_input(x + i));
-      ok = take_all<DevMem, D>(m, j, c, parity, slot_pack, peers_mask(W, r), xs, 1, 1);
-      if (!ok) break;
-      Pack16 y = pack_canon<D>(sum_rank_order<D>(own, xs, W, r));
-      for (uint32_t k = 1; k < W; ++k) {
-        uint32_t q = (r + k) % W;
-        m.st_remote(lam_pack(j, q, parity, r, half + slot_pack), y);
+      for (uint32_t k = 0; k < per_thread && ok; ++k) {
+        const uint64_t tpack = row_pack(k);
+        if (tpack == ~0ull) break;
+        const uint64_t i = t * row_packs + tpack;
+        const uint64_t slot_pack = (t / W) * row_packs + tpack;
+        Pack16 xs[kMaxRanks];
+        const Pack16 own = pack_canon<D>(m.ld_input(x + i));
+        ok = take_all<DevMem, D>(m, j, c, parity, slot_pack, peers_mask(W, r), xs, 1, 1);
+        if (!ok) break;
+        Pack16 y = pack_canon<D>(sum_rank_order<D>(own, xs, W, r));
+        for (uint32_t s = 1; s < W; ++s) m.st_remote(lam_pack(j, (r + s) % W, parity, r, half + slot_pack), y);
+        // keep the own sum for step 3 in the output buffer (overwritten there)
+        m.st_local(out + i, y);
       }
-      // keep the own sum for step 3 in the output buffer (overwritten there)
-      m.st_local(out + i, y);
     }
   }
 
-  // 3. per row: the all-reduced sum, + residual, RMSNorm over the cluster.
+  // 3. per row: the all-reduced sum, + residual, RMSNorm over the cluster.  Pass A
+  //    writes the new residual and sums its squares; pass B scales it.  The first
+  //    pack stays in registers; any further pack (only when the launch ran with fewer
+  //    CTAs per row than planned) is read back from residual_out, which this thread
+  //    wrote itself.
   for (uint64_t t = cid; t < T; t += nclusters) {
-    const uint64_t i = t * row_packs + tpack;
-    Pack16 sum = pack_fill(0u), newres = pack_fill(0u);
     float sq = 0.0f;
-    if (active && ok) {
+    Pack16 first = pack_fill(0u);
+    for (uint32_t k = 0; k < per_thread && ok; ++k) {
+      const uint64_t tpack = row_pack(k);
+      if (tpack == ~0ull) break;
+      const uint64_t i = t * row_packs + tpack;
+      Pack16 sum = pack_fill(0u);
       if (W == 1) {
         sum = m.ld_input(x + i);
       } else if (twoshot) {
@@ -168,9 +184,7 @@ SN_DEV void fused_body(const Job& j, int algo) {
         if (owner == r) {
           sum = m.ld_peer_data(out + i);
         } else {
-          uint64_t slot_pack = (t / W) * row_packs + tpack;
-          ok = take<D>(m, lam_pack(j, r, parity, owner, half + slot_pack), sum, c,
-                       owner);
+          ok = take<D>(m, lam_pack(j, r, parity, owner, half + (t / W) * row_packs + tpack), sum, c, owner);
         }
       } else {
         Pack16 xs[kMaxRanks];
@@ -178,29 +192,34 @@ SN_DEV void fused_body(const Job& j, int algo) {
         ok = take_all<DevMem, D>(m, j, c, parity, i, peers_mask(W, r), xs, 1, 1);
         if (ok) sum = sum_rank_order<D>(own, xs, W, r);
       }
+      if (!ok) break;
       // residual add (rounded once, as the unfused add would be)
       Acc a;
       acc_zero<D>(a);
       acc_add<D>(a, sum);
       acc_add<D>(a, m.ld_peer_data(res + i));  // coherent: residual_out may alias residual
-      newres = acc_round<D>(a);
+      const Pack16 newres = acc_round<D>(a);
       Acc rr;
       acc_zero<D>(rr);
       acc_add<D>(rr, newres);
       for (int e = 0; e < kElems; ++e) sq += rr.v[e] * rr.v[e];
+      if (k == 0) first = newres;
+      m.st_output(res_out + i, newres);
     }
     // every thread of every CTA of the cluster takes part in the reduction
     float total = row_sumsq(sq, warp_part, &part, cluster);
     float scale = rsqrtf(total / float(j.hidden) + j.eps);
-    if (active && ok) {
+    for (uint32_t k = 0; k < per_thread && ok; ++k) {
+      const uint64_t tpack = row_pack(k);
+      if (tpack == ~0ull) break;
+      const uint64_t i = t * row_packs + tpack;
       Acc rr, g;
       acc_zero<D>(rr);
       acc_zero<D>(g);
-      acc_add<D>(rr, newres);
+      acc_add<D>(rr, k == 0 ? first : m.ld_peer_data(res_out + i));
       acc_add<D>(g, m.ld_input(gamma + tpack));
       Acc o;
       for (int e = 0; e < kElems; ++e) o.v[e] = (rr.v[e] * scale) * g.v[e];
-      m.st_output(res_out + i, newres);
       m.st_output(out + i, acc_round<D>(o));
     }
     cluster.sync();  // partials are rewritten by the next row
@@ -208,7 +227,6 @@ SN_DEV void fused_body(const Job& j, int algo) {
 
   __syncthreads();
   if (threadIdx.x == 0) finish_op(m, ctrl, seq, gridDim.x);
-  (void)ok_s;
 }
 
 template <int D>

@@ -118,10 +118,18 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
 
   cg::cluster_group cluster = cg::this_cluster();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int split = blockIdx.x, tile = blockIdx.y;
-  const int S = int(cluster.num_blocks());  // == splits
-  const int kb0 = split * p.kb_per_split;
-  const int nkb = max(0, min(p.kb_per_split, p.K / kBK - kb0));
+  const int tile = blockIdx.y;
+  const int S = int(cluster.num_blocks());  // == splits, as planned
+  // A launch re-issued without its cluster attribute (a profiler may do that) has
+  // clusters smaller than the split count.  The first cluster then covers the whole
+  // K range, split S ways, and every other CTA exits before it holds any resource, so
+  // each output is still written (or pushed) exactly once.
+  const bool reshaped = S != int(gridDim.x);
+  if (reshaped && blockIdx.x >= unsigned(S)) return;
+  const int split = int(cluster.block_rank());
+  const int kbps = reshaped ? (p.K / kBK + S - 1) / S : p.kb_per_split;
+  const int kb0 = split * kbps;
+  const int nkb = max(0, min(kbps, p.K / kBK - kb0));
   volatile uint32_t* err = p.err;
   const uint32_t ncols = p.mp <= 32 ? 32u : (p.mp <= 64 ? 64u : (p.mp <= 128 ? 128u : 256u));
   const int pitch = p.mp + 1;  // padded row of the parked partial

@@ -388,6 +388,10 @@ static __global__ void __launch_bounds__(kAttnThreads) k_decode_attn_cluster(
   ClusterSmem<G, NT>& sm = *reinterpret_cast<ClusterSmem<G, NT>*>(smem_raw);
   cg::cluster_group cluster = cg::this_cluster();
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // a PDL-launched successor may start early
+  // The merge reads S CTAs' shared memory: a launch that arrives without its S-CTA
+  // cluster (re-issued by a tool without the attribute) must not touch it.  Every CTA
+  // returns before any access; the output rows keep their previous contents.
+  if (cluster.num_blocks() != unsigned(S)) return;
   const int s = blockIdx.x, b = blockIdx.y / Hkv, h = blockIdx.y % Hkv;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int dp = t & 63, hg = t >> 6;

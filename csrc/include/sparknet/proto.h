@@ -52,7 +52,10 @@ enum DType : int { kF16 = 0, kBF16 = 1, kF32 = 2 };
 // kLocal: the one-rank all-reduce, a copy (no protocol)
 enum Algo : int { kOneShot = 0, kTwoShot = 1, kNvls = 2, kLocal = 3 };
 // kFailBounds: a slot access outside its area (builds with SN_BOUNDS_CHECK only)
-enum FailKind : int { kFailNone = 0, kFailTimeout = 1, kFailPoisoned = 2, kFailIterations = 3, kFailBounds = 4 };
+// kFailGeometry: a kernel found a launch shape it cannot serve (the work was skipped)
+enum FailKind : int {
+  kFailNone = 0, kFailTimeout = 1, kFailPoisoned = 2, kFailIterations = 3, kFailBounds = 4, kFailGeometry = 5
+};
 
 SN_HD size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 

@@ -88,12 +88,18 @@ class EmulatedGroup:
                                parts[0].stride(0) * elem, 0, -1, copy_self)
         return parts
 
-    def fused_norm(self, inputs, residuals, gamma, eps=1e-5, algorithm="oneshot", cluster=8):
+    def fused_norm(self, inputs, residuals, gamma, eps=1e-5, algorithm="oneshot", cluster=8, *,
+                   max_clusters: int = 0, threads: int = 0):
+        """Fused all-reduce + residual add + RMSNorm on every emulated rank.
+
+        ``cluster`` CTAs share a row; ``max_clusters`` caps the clusters per rank (0:
+        one per row up to the co-resident limit; fewer makes each cluster loop over
+        rows); ``threads`` forces the block size (0: one 16-byte pack per thread)."""
         outs = [torch.empty_like(x) for x in inputs]
         res_outs = [torch.empty_like(x) for x in residuals]
         with torch.cuda.device(self.device):
             self.comm.fused_norm(list(inputs), list(residuals), gamma, float(eps), outs, res_outs,
-                                 ALGO_CODES[algorithm], cluster, 0)
+                                 ALGO_CODES[algorithm], cluster, max_clusters, False, threads)
         return outs, res_outs
 
     def barrier(self, blocks: int = 1) -> None:

@@ -64,7 +64,8 @@ LL_CAP = 1024 * 1024
 ALGO_CODES = {"oneshot": 0, "twoshot": 1, "nvls": 2, "local": 3}
 GATHER_CODES = {"ll": 0, "push": 1, "nvls": 2}
 FAIL_KINDS = {1: "timed out", 2: "was poisoned", 3: "exceeded its poll limit",
-              4: "accessed a slot out of bounds (bounds-checked build)"}
+              4: "accessed a slot out of bounds (bounds-checked build)",
+              5: "found a launch shape it cannot serve"}
 OP_NAMES = {1: "all-reduce", 2: "all-gather", 3: "reduce-scatter", 4: "exchange", 5: "barrier",
             6: "fused all-reduce+RMSNorm"}
 

@@ -26,6 +26,7 @@ import os
 import statistics
 import sys
 from contextlib import contextmanager, nullcontext
+from dataclasses import dataclass
 from datetime import timedelta
 
 
@@ -38,8 +39,32 @@ def _policy_from_environment():
     return NVLINK_POLICY
 
 
+@dataclass(frozen=True)
+class Route:
+    """Where one probe collective went: ``backend`` is ``nccl`` or the NVLink algorithm
+    (``oneshot``, ``twoshot``, ``nvls``, ``local``) the runtime ran."""
+
+    operation: str
+    backend: str
+    nbytes: int
+
+    @property
+    def nvlink(self) -> bool:
+        return self.backend != "nccl"
+
+
 class PolicyCommunicator:
-    """The explicit policy over torch.distributed (NCCL) and the NVLink runtime."""
+    """The probe's dispatcher: the explicit policy over NCCL and the NVLink runtime.
+
+    Every call is routed by ``route()``: the policy names a backend from the operation,
+    dtype, size and world (rank-invariant), and for an NVLink backend the runtime's own
+    eligibility must agree, otherwise the probe fails instead of quietly using NCCL.
+    Each route is tallied in ``ledger`` (``(operation, backend) -> [calls, bytes]``) so
+    that ``check_runtime_counters`` can hold the runtime's counters to the routing.
+    The reference's probe dispatcher (``sparknet/probe/collectives.py:33-89`` there)
+    has the same public methods over its RoCE runtime; this one adds the forced arms
+    of the crossover sweep and the ledger.
+    """
 
     def __init__(self, runtime, policy, device, world_size):
         import torch
@@ -47,64 +72,142 @@ class PolicyCommunicator:
 
         self._torch, self._dist = torch, dist
         self.runtime, self.policy, self.device, self.world_size = runtime, policy, device, world_size
+        self.ledger: dict[tuple[str, str], list[int]] = {}
+        self.last_route: Route | None = None
 
-    @staticmethod
-    def _dtype_name(t) -> str:
-        return str(t.dtype).replace("torch.", "")
+    # -- routing -------------------------------------------------------------------
+    def route(self, operation: str, tensor, *, dim: int = 0, forced: str | None = None) -> Route:
+        nbytes = tensor.numel() * tensor.element_size()
+        dtype = str(tensor.dtype).rsplit(".", 1)[-1]
+        if forced is not None:
+            backend = forced
+        elif self.runtime is None:
+            backend = "nccl"
+        elif operation == "all_reduce":
+            backend = self.policy.all_reduce_backend(nbytes, dtype, contiguous=tensor.is_contiguous(),
+                                                     world=self.world_size)
+            if backend != "nccl" and not self.runtime.should_allreduce(tensor):
+                raise RuntimeError(f"all-reduce of {nbytes} bytes: the policy chose {backend}, the runtime "
+                                   "refuses the tensor (policy and runtime eligibility disagree)")
+            if backend != "nccl":
+                backend = self.runtime.algorithm_for(nbytes, tensor.dtype)
+        elif operation == "all_gather":
+            backend = self.policy.all_gather_backend(nbytes, dtype, dim=dim, ndim=tensor.dim(),
+                                                     contiguous=tensor.is_contiguous())
+            if backend != "nccl" and not self.runtime.should_all_gather(tensor, dim):
+                raise RuntimeError(f"all-gather of {nbytes} bytes: the policy chose the NVLink kernel, the "
+                                   "runtime refuses the tensor (policy and runtime eligibility disagree)")
+        elif operation == "reduce_scatter":
+            within = self.policy.reduce_scatter_backend(nbytes, self.policy.all_reduce_capacity_bytes) != "nccl"
+            backend = "oneshot" if within and self.runtime.should_reduce_scatter(tensor) else "nccl"
+        else:
+            raise ValueError(f"unknown probe operation {operation!r}")
+        tally = self.ledger.setdefault((operation, backend), [0, 0])
+        tally[0] += 1
+        tally[1] += nbytes
+        self.last_route = Route(operation, backend, nbytes)
+        return self.last_route
 
     def backend_for_all_reduce(self, tensor) -> str:
+        """The backend the policy picks for this tensor (no call is made or tallied)."""
         if self.runtime is None:
             return "nccl"
         nbytes = tensor.numel() * tensor.element_size()
-        return self.policy.all_reduce_backend(nbytes, self._dtype_name(tensor), contiguous=tensor.is_contiguous(),
-                                              world=self.world_size)
+        return self.policy.all_reduce_backend(nbytes, str(tensor.dtype).rsplit(".", 1)[-1],
+                                              contiguous=tensor.is_contiguous(), world=self.world_size)
 
+    # -- collectives -----------------------------------------------------------------
     def all_reduce(self, tensor, *, algorithm: str | None = None):
-        backend = algorithm or self.backend_for_all_reduce(tensor)
-        if backend != "nccl":
-            if algorithm is None and not self.runtime.should_allreduce(tensor):
-                raise RuntimeError("policy and runtime eligibility disagree for all-reduce")
-            return self.runtime.all_reduce(tensor, algorithm=backend)
-        out = tensor.clone()
-        self._dist.all_reduce(out)
-        return out
+        r = self.route("all_reduce", tensor, forced=algorithm)
+        if r.nvlink:
+            return self.runtime.all_reduce(tensor, algorithm=r.backend)
+        result = tensor.clone()
+        self._dist.all_reduce(result)
+        return result
 
     def all_gather(self, tensor, dim=0, *, force_nccl: bool = False):
-        nbytes = tensor.numel() * tensor.element_size()
-        if (not force_nccl and self.runtime is not None
-                and self.policy.all_gather_backend(nbytes, self._dtype_name(tensor), dim=dim, ndim=tensor.dim(),
-                                                   contiguous=tensor.is_contiguous()) == "oneshot"):
-            if not self.runtime.should_all_gather(tensor, dim):
-                raise RuntimeError("policy and runtime eligibility disagree for all-gather")
+        r = self.route("all_gather", tensor, dim=dim, forced="nccl" if force_nccl else None)
+        if r.nvlink:
             return self.runtime.all_gather(tensor, dim=dim)
-        parts = [self._torch.empty_like(tensor) for _ in range(self.world_size)]
-        self._dist.all_gather(parts, tensor.contiguous())
-        return self._torch.cat(parts, dim=dim)
+        pieces = [self._torch.empty_like(tensor) for _ in range(self.world_size)]
+        self._dist.all_gather(pieces, tensor.contiguous())
+        return self._torch.cat(pieces, dim=dim)
 
     def reduce_scatter(self, tensor, dim=0, *, force_nccl: bool = False):
         if dim != 0:
-            raise ValueError("reduce-scatter is tested along dim 0")
-        nbytes = tensor.numel() * tensor.element_size()
-        if (not force_nccl and self.runtime is not None
-                and self.policy.reduce_scatter_backend(nbytes, self.policy.all_reduce_capacity_bytes) == "oneshot"
-                and self.runtime.should_reduce_scatter(tensor)):
+            raise ValueError("the probe reduce-scatters along dim 0 only")
+        r = self.route("reduce_scatter", tensor, forced="nccl" if force_nccl else None)
+        if r.nvlink:
             return self.runtime.reduce_scatter(tensor)
-        out = self._torch.empty((tensor.shape[0] // self.world_size,) + tuple(tensor.shape[1:]), dtype=tensor.dtype,
-                                device=tensor.device)
-        self._dist.reduce_scatter_tensor(out, tensor.contiguous())
-        return out
+        shape = (tensor.shape[0] // self.world_size, *tensor.shape[1:])
+        result = self._torch.empty(shape, dtype=tensor.dtype, device=tensor.device)
+        self._dist.reduce_scatter_tensor(result, tensor.contiguous())
+        return result
+
+
+# runtime call counter that moves for one NVLink route of each operation
+_RUNTIME_COUNTER = {"all_gather": "all_gather", "reduce_scatter": "reduce_scatter"}
+
+
+def runtime_calls_expected(ledger_delta: dict[tuple[str, str], int]) -> dict[str, int]:
+    """The runtime ``stats()['calls']`` increments that the routed calls imply: an
+    all-reduce counts under its algorithm, the other operations under their name;
+    NCCL routes move no runtime counter."""
+    want: dict[str, int] = {}
+    for (operation, backend), calls in ledger_delta.items():
+        if backend == "nccl" or not calls:
+            continue
+        key = backend if operation == "all_reduce" else _RUNTIME_COUNTER[operation]
+        want[key] = want.get(key, 0) + calls
+    return want
+
+
+def check_runtime_counters(before_calls: dict, after_calls: dict, ledger_before: dict, ledger_after: dict,
+                           *, what: str, graph_replays: int = 0, calls_per_graph: int = 0) -> dict[str, int]:
+    """Raise unless the runtime's call counters moved exactly as the routing says.
+
+    Counters move when a call is issued (eagerly or while captured), not on replay, so
+    ``graph_replays`` only matters for the byte estimate the caller derives."""
+    ledger_delta = {k: ledger_after.get(k, [0, 0])[0] - ledger_before.get(k, [0, 0])[0]
+                    for k in set(ledger_after) | set(ledger_before)}
+    want = runtime_calls_expected(ledger_delta)
+    moved = {k: after_calls.get(k, 0) - before_calls.get(k, 0) for k in set(after_calls) | set(before_calls)}
+    moved = {k: v for k, v in moved.items() if v}
+    if moved != want:
+        raise RuntimeError(f"{what}: runtime counters moved {moved}, the policy's routing implies {want}")
+    return want
+
+
+def nvlink_bytes_expected(route: Route, world: int) -> int:
+    """Bytes this rank must send over NVLink for one call on ``route`` (0 for NCCL and
+    for one rank): one-shot pushes the whole message to every peer, two-shot 2(W-1)/W
+    of it, the all-gather its shard to every peer, the reduce-scatter (W-1)/W."""
+    if not route.nvlink or world < 2:
+        return 0
+    n, peers = route.nbytes, world - 1
+    if route.operation == "all_reduce":
+        if route.backend == "oneshot":
+            return n * peers
+        if route.backend in ("twoshot", "nvls"):
+            return 2 * n * peers // world
+        return 0
+    if route.operation == "all_gather":
+        return n * peers
+    return n * peers // world
 
 
 @contextmanager
 def reporting_failure(runtime):
-    """Re-raise whatever follows a failed collective with the runtime's failure report."""
+    """Turn an exception raised after a failed NVLink collective into the runtime's own
+    failure report (which rank was waited for, in which op), chained to the original.
+    Exceptions with no collective failure behind them pass through unchanged."""
     try:
         yield
     except Exception as error:
-        report = runtime.failure() if runtime is not None else None
-        if report is not None:
-            raise RuntimeError(report) from error
-        raise
+        diagnosis = None if runtime is None else runtime.failure()
+        if diagnosis is None:
+            raise
+        raise RuntimeError(diagnosis) from error
 
 
 def _init(args):
@@ -265,7 +368,12 @@ def _correctness(comm, runtime, world, rank, device, dtypes, capture_context):
                           for q in ranks_local]
                 torch.testing.assert_close(rs.float(), _exact_sum(chunks).float(), rtol=1e-2, atol=1.0)
 
+            ledger0 = {k: list(v) for k, v in comm.ledger.items()}
+            calls0 = dict(runtime.stats()["calls"]) if runtime is not None else {}
             verify(collect())
+            if runtime is not None:
+                check_runtime_counters(calls0, dict(runtime.stats()["calls"]), ledger0, comm.ledger,
+                                       what=f"correctness {dtype} {length}")
             stream = torch.cuda.Stream(device=device)
             stream.wait_stream(torch.cuda.current_stream())
             graph = torch.cuda.CUDAGraph()
@@ -308,14 +416,19 @@ def _numerics(comm, args, world, rank, device):
 
 
 def _benchmark(comm, runtime, args, world, rank, device, cpu_group, capture_context, dtypes, nvcounters):
+    """Steady graph-replayed latency per (dtype, size, operation, arm), with two
+    consistency checks per case: the runtime's call counters moved exactly as the
+    routing implies (always), and, with ``--counter-samples``, the NVLink bytes that
+    this job's GPUs sent during the timed replays cover what the NVLink route must send
+    (checked for NVLink routes on several ranks; recorded for NCCL)."""
     import torch
     import torch.distributed as dist
 
     arms = ["policy"]
     if args.sweep and runtime is not None:
         arms = ["oneshot", "twoshot"] + (["nvls"] if runtime.has_multicast else []) + ["nccl"]
+    calls_per_graph, replays_per_sample, samples_per_case = 16, 16, 5
     timings = []
-    use_counters = args.counter_samples
     for dtype in dtypes:
         for length in args.lengths:
             nbytes = length * dtype.itemsize
@@ -326,41 +439,62 @@ def _benchmark(comm, runtime, args, world, rank, device, cpu_group, capture_cont
                     op = _operation(comm, runtime, name, arm, local, scattered, nbytes)
                     if op is None:
                         continue
+                    ledger0 = {k: list(v) for k, v in comm.ledger.items()}
+                    calls0 = dict(runtime.stats()["calls"]) if runtime is not None else {}
                     op()
                     torch.cuda.synchronize()
                     stream = torch.cuda.Stream(device=device)
                     stream.wait_stream(torch.cuda.current_stream())
                     graph = torch.cuda.CUDAGraph()
                     with torch.cuda.graph(graph, stream=stream), capture_context(stream):
-                        outputs = [op() for _ in range(16)]
+                        outputs = [op() for _ in range(calls_per_graph)]
+                    route = comm.last_route
+                    if runtime is not None:
+                        check_runtime_counters(calls0, dict(runtime.stats()["calls"]), ledger0, comm.ledger,
+                                               what=f"{name} [{arm}] {nbytes} B")
                     for _ in range(4):
                         graph.replay()
                     torch.cuda.synchronize()
                     dist.barrier(group=cpu_group)
-                    counters_before = nvcounters.nvlink_counters() if use_counters and rank == 0 else None
+                    own_before = nvcounters.own_gpu_counters(device.index) if args.counter_samples else {}
                     samples = []
-                    for _ in range(5):
+                    for _ in range(samples_per_case):
                         dist.barrier(group=cpu_group)
                         if runtime is not None:
                             runtime.barrier()
                         start = torch.cuda.Event(enable_timing=True)
                         end = torch.cuda.Event(enable_timing=True)
                         start.record()
-                        for _ in range(16):
+                        for _ in range(replays_per_sample):
                             graph.replay()
                         end.record()
                         end.synchronize()
-                        samples.append(start.elapsed_time(end) * 1000 / 256)
+                        samples.append(start.elapsed_time(end) * 1000 / (calls_per_graph * replays_per_sample))
+                    own_after = nvcounters.own_gpu_counters(device.index) if args.counter_samples else {}
+                    tx = None
+                    if "nvlink_tx_kib" in own_before and "nvlink_tx_kib" in own_after:
+                        tx = (own_after["nvlink_tx_kib"] - own_before["nvlink_tx_kib"]) * 1024
                     gathered = [None] * world
-                    dist.all_gather_object(gathered, samples, group=cpu_group)
-                    slowest = [max(g[i] for g in gathered) for i in range(len(samples))]
+                    dist.all_gather_object(gathered, (samples, tx), group=cpu_group)
+                    slowest = [max(g[0][i] for g in gathered) for i in range(len(samples))]
                     row = {"dtype": str(dtype), "elements_per_rank": length, "operation": name, "arm": arm,
-                           "microseconds_per_call": slowest, "median_us": statistics.median(slowest),
-                           "calls_per_graph": 16, "replays_per_sample": 16}
-                    if counters_before is not None:
-                        after = nvcounters.nvlink_counters()
-                        row["nvlink_deltas"] = nvcounters.deltas(counters_before, after)
-                        row["nvlink_error_deltas"] = nvcounters.error_deltas(counters_before, after)
+                           "backend": route.backend, "microseconds_per_call": slowest,
+                           "median_us": statistics.median(slowest), "calls_per_graph": calls_per_graph,
+                           "replays_per_sample": replays_per_sample}
+                    if args.counter_samples:
+                        timed_calls = calls_per_graph * replays_per_sample * samples_per_case
+                        want = nvlink_bytes_expected(route, world) * timed_calls
+                        seen = [g[1] for g in gathered]
+                        row["nvlink_tx_bytes_per_rank"] = seen
+                        row["nvlink_tx_bytes_expected_per_rank"] = want
+                        if all(v is not None for v in seen) and route.nvlink and world > 1:
+                            # NVLink counters count the payload plus protocol overhead;
+                            # sending less than the payload means the route was not taken
+                            short = [r for r, v in enumerate(seen) if v < 0.9 * want]
+                            row["nvlink_counters_agree"] = not short
+                            if short:
+                                raise RuntimeError(f"{name} [{arm}] {nbytes} B: ranks {short} sent {seen} bytes "
+                                                   f"over NVLink, the {route.backend} route needs {want} each")
                     if rank == 0:
                         print(json.dumps({"rank": rank, "timing": row}), flush=True)
                     timings.append(row)
@@ -370,31 +504,25 @@ def _benchmark(comm, runtime, args, world, rank, device, cpu_group, capture_cont
 
 
 def _operation(comm, runtime, name, arm, local, scattered, nbytes):
-    """A zero-argument callable for one (operation, arm), or None if the arm cannot carry it."""
+    """A zero-argument callable for one (operation, arm), or None if the arm cannot carry
+    it.  Every arm goes through the dispatcher, so its ledger sees every call."""
     if name == "all_reduce":
         if arm == "policy":
             return lambda: comm.all_reduce(local)
-        if arm == "nccl":
-            return lambda: comm.all_reduce(local, algorithm="nccl")
-        if runtime is None or nbytes > runtime.max_size:
+        if arm != "nccl":
+            if runtime is None or nbytes > runtime.max_size:
+                return None
+            if arm == "oneshot" and nbytes > runtime._caps[0]:
+                return None
+            if arm == "nvls" and (not runtime.has_multicast or nbytes > runtime._mc[2]):
+                return None
+        return lambda: comm.all_reduce(local, algorithm=arm)
+    if name in ("all_gather", "reduce_scatter"):
+        if arm not in ("policy", "oneshot", "nccl"):
             return None
-        if arm == "oneshot" and nbytes > runtime._caps[0]:
-            return None
-        if arm == "nvls" and (not runtime.has_multicast or nbytes > runtime._mc[2]):
-            return None
-        return lambda: runtime.all_reduce(local, algorithm=arm)
-    if name == "all_gather":
-        if arm in ("policy", "oneshot"):
-            return lambda: comm.all_gather(local, dim=0)
-        if arm == "nccl":
-            return lambda: comm.all_gather(local, dim=0, force_nccl=True)
-        return None
-    if name == "reduce_scatter":
-        if arm in ("policy", "oneshot"):
-            return lambda: comm.reduce_scatter(scattered, dim=0)
-        if arm == "nccl":
-            return lambda: comm.reduce_scatter(scattered, dim=0, force_nccl=True)
-        return None
+        call = comm.all_gather if name == "all_gather" else comm.reduce_scatter
+        tensor = local if name == "all_gather" else scattered
+        return lambda: call(tensor, dim=0, force_nccl=(arm == "nccl"))
     return None
 
 

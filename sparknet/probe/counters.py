@@ -60,6 +60,28 @@ def nvlink_counters(nvml: Any = None, *, links: int = 18) -> dict[str, int]:
     return snap
 
 
+def own_gpu_counters(device_index: int, nvml: Any = None) -> dict[str, int]:
+    """NVLink data counters (KiB sent and received) of the GPU behind the CUDA device
+    ``device_index`` of this process, found by PCI bus id so that other jobs' GPUs on a
+    shared box are never read.  Empty when NVML or the field is unavailable."""
+    try:
+        import torch
+
+        props = torch.cuda.get_device_properties(device_index)
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        nv = nvml if nvml is not None else nvml_mod.load()
+        handle = nv.nvmlDeviceGetHandleByPciBusId_v2(bus)
+    except Exception:  # noqa: BLE001 - counters are evidence, never a reason to fail a probe
+        return {}
+    fv = _field_values(nv, handle, (FI_NVLINK_THROUGHPUT_DATA_TX, FI_NVLINK_THROUGHPUT_DATA_RX))
+    out = {}
+    if FI_NVLINK_THROUGHPUT_DATA_TX in fv:
+        out["nvlink_tx_kib"] = fv[FI_NVLINK_THROUGHPUT_DATA_TX]
+    if FI_NVLINK_THROUGHPUT_DATA_RX in fv:
+        out["nvlink_rx_kib"] = fv[FI_NVLINK_THROUGHPUT_DATA_RX]
+    return out
+
+
 def deltas(before: dict[str, int], after: dict[str, int]) -> dict[str, int]:
     """The counters that changed between two snapshots, as after minus before."""
     return {k: after[k] - before[k] for k in after if k in before and after[k] != before[k]}
@@ -70,4 +92,4 @@ def error_deltas(before: dict[str, int], after: dict[str, int]) -> dict[str, int
     return {k: v for k, v in deltas(before, after).items() if "nvlink_tx" not in k and "nvlink_rx" not in k}
 
 
-__all__ = ["ERROR_COUNTERS", "deltas", "error_deltas", "nvlink_counters"]
+__all__ = ["ERROR_COUNTERS", "deltas", "error_deltas", "nvlink_counters", "own_gpu_counters"]

@@ -162,6 +162,51 @@ def test_fused_allreduce_rmsnorm(groups, device, world, tokens, algorithm):
     torch.testing.assert_close(outs[0].float(), want_out.float(), rtol=1e-2, atol=1e-2)
 
 
+@pytest.mark.parametrize("cluster,threads", [(8, 0), (2, 0), (1, 0), (1, 32), (2, 32)])
+@pytest.mark.parametrize("max_clusters", [1, 2, 0])
+@pytest.mark.parametrize("algorithm", ["oneshot", "twoshot"])
+def test_fused_norm_launch_shapes(groups, device, cluster, threads, max_clusters, algorithm):
+    """The smoke's shape (2 ranks, 2 tokens, hidden 1024, one residual tensor for both
+    ranks) under every launch shape the kernel may meet: clusters of 1, 2 or 8 CTAs per
+    row, 1 or 2 clusters per rank looping over rows, and blocks of 32 threads that hold
+    several packs each (a cluster of 1 with 32 threads is the launch a profiler issues
+    when it drops the cluster attribute).  Repeated, each result checked exactly."""
+    g = groups[2]
+    hidden, tokens = 1024, 2
+    gen = torch.Generator(device=device).manual_seed(11 + cluster + threads + max_clusters)
+    gamma = (1.0 + 0.02 * torch.randn(hidden, generator=gen, device=device)).to(torch.bfloat16)
+    for _ in range(10):
+        xs = [torch.randn(tokens, hidden, generator=gen, device=device).to(torch.bfloat16) for _ in range(2)]
+        residual = torch.randn(tokens, hidden, generator=gen, device=device).to(torch.bfloat16)
+        outs, res_outs = g.fused_norm(xs, [residual] * 2, gamma, 1e-5, algorithm, cluster,
+                                      max_clusters=max_clusters, threads=threads)
+        torch.cuda.synchronize()
+        g.check()
+        want_out, want_res = fused_reference(xs, residual, gamma, 1e-5)
+        for r in range(2):
+            assert torch.equal(res_outs[r], want_res), f"rank {r}: residual differs"
+            assert torch.equal(outs[r].view(torch.int16), outs[0].view(torch.int16)), "ranks must agree"
+        torch.testing.assert_close(outs[0].float(), want_out.float(), rtol=1e-2, atol=1e-2)
+
+
+def test_fused_norm_wide_rows_one_cta(groups, device):
+    """hidden 8192 with one CTA per row: 1024 packs over a 512-thread block, two per thread."""
+    g = groups[4]
+    hidden, tokens = 8192, 8
+    xs = [x.view(tokens, hidden) for x in inputs(4, tokens * hidden, torch.bfloat16, device, seed=3)]
+    gen = torch.Generator(device=device).manual_seed(5)
+    residual = torch.randn(tokens, hidden, generator=gen, device=device).to(torch.bfloat16)
+    gamma = (1.0 + 0.02 * torch.randn(hidden, generator=gen, device=device)).to(torch.bfloat16)
+    outs, res_outs = g.fused_norm(xs, [residual] * 4, gamma, 1e-5, "oneshot", 1)
+    torch.cuda.synchronize()
+    g.check()
+    want_out, want_res = fused_reference(xs, residual, gamma, 1e-5)
+    for r in range(4):
+        assert torch.equal(res_outs[r], want_res)
+        assert torch.equal(outs[r].view(torch.int16), outs[0].view(torch.int16))
+    torch.testing.assert_close(outs[0].float(), want_out.float(), rtol=1e-2, atol=1e-2)
+
+
 def test_graph_replay(groups, device):
     """Collectives captured once replay with a device-resident epoch."""
     g = groups[4]

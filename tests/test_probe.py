@@ -158,3 +158,22 @@ def test_reference_report_names():
 
     assert probe.gpudirect_report is probe.nvlink_report
     assert REQUIRED_API_VERSION == API_VERSION
+
+
+def test_runtime_counters_held_to_routing():
+    from sparknet.probe.collectives import Route, check_runtime_counters, nvlink_bytes_expected
+
+    ledger0 = {("all_reduce", "oneshot"): [2, 64]}
+    ledger1 = {("all_reduce", "oneshot"): [5, 160], ("all_gather", "oneshot"): [1, 32], ("all_reduce", "nccl"): [4, 8]}
+    want = check_runtime_counters({"oneshot": 2}, {"oneshot": 5, "all_gather": 1}, ledger0, ledger1, what="case")
+    assert want == {"oneshot": 3, "all_gather": 1}
+    with pytest.raises(RuntimeError, match="runtime counters moved"):
+        # an NCCL-routed call that moved a runtime counter
+        check_runtime_counters({}, {"twoshot": 1}, {}, {("all_reduce", "nccl"): [1, 16]}, what="case")
+    with pytest.raises(RuntimeError, match="runtime counters moved"):
+        # an NVLink-routed call the runtime never counted
+        check_runtime_counters({}, {}, {}, {("reduce_scatter", "oneshot"): [1, 16]}, what="case")
+    assert nvlink_bytes_expected(Route("all_reduce", "oneshot", 1024), 8) == 7 * 1024
+    assert nvlink_bytes_expected(Route("all_reduce", "twoshot", 1024), 8) == 2 * 1024 * 7 // 8
+    assert nvlink_bytes_expected(Route("all_reduce", "nccl", 1024), 8) == 0
+    assert nvlink_bytes_expected(Route("all_gather", "oneshot", 1024), 4) == 3 * 1024

@@ -200,3 +200,23 @@ def test_attention_wrapper_rejects_unknown_variants():
     q = torch.zeros(1, 8, 128, dtype=torch.bfloat16)
     with pytest.raises(ValueError, match="variant"):
         decode_attention(q, q, q, torch.ones(1, dtype=torch.int32), 1, variant="paged")
+
+
+def test_freeze_gate_refuses_lazy_setup_and_counts():
+    from sparknet.oneshot import _freeze
+
+    _freeze.thaw_kernel_resolution()
+    _freeze.raise_if_kernel_resolution_frozen("gather scratch allocation")  # open: no error
+    before = _freeze.refused_resolutions()
+    _freeze.freeze_kernel_resolution("serving warm-up done")
+    try:
+        assert _freeze.kernel_resolution_frozen()
+        with pytest.raises(_freeze.KernelResolutionFrozenError) as info:
+            _freeze.raise_if_kernel_resolution_frozen("alignment scratch allocation", target=object(), cache_key=(8, 2))
+        text = str(info.value)
+        assert "alignment scratch allocation for object" in text and "(8, 2)" in text
+        assert "serving warm-up done" in text
+        assert _freeze.refused_resolutions() == before + 1
+    finally:
+        _freeze.thaw_kernel_resolution()
+    assert not _freeze.kernel_resolution_frozen()
