@@ -28,11 +28,14 @@ EXAMPLES = Path(__file__).resolve().parent / "topology" / "examples"
 
 
 def _print_env(env: dict[str, str], as_json: bool) -> None:
-    if as_json:
-        print(json.dumps(env, indent=2, sort_keys=True))
-    else:
-        for key in sorted(env):
-            print(f"{key}={env[key]}")
+    """An environment as one JSON object, or as ``export``-ready ``KEY=value`` lines in
+    key order (values quoted for a POSIX shell only where they need it)."""
+    import shlex
+
+    text = json.dumps(env, indent=2, sort_keys=True) if as_json else \
+        "\n".join(f"{k}={shlex.quote(str(v))}" for k, v in sorted(env.items()))
+    if text:
+        print(text)
 
 
 def cmd_topology_validate(args) -> int:
@@ -436,11 +439,13 @@ def parser() -> argparse.ArgumentParser:
 
 
 def split_pass_through(argv: list[str]) -> tuple[list[str], list[str] | None]:
-    """Split ``argv`` at the first bare ``--``: the words after it pass through untouched."""
-    if "--" not in argv:
-        return argv, None
-    index = argv.index("--")
-    return argv[:index], argv[index + 1:]
+    """``(own words, pass-through words)``: everything after the first bare ``--`` is
+    handed to the wrapped program verbatim (``None`` when there is no ``--``), so the
+    probe's own flags never reach this parser."""
+    for position, word in enumerate(argv):
+        if word == "--":
+            return argv[:position], argv[position + 1:]
+    return argv, None
 
 
 def main(argv: list[str] | None = None) -> int:

@@ -29,6 +29,7 @@ import os
 import re
 from collections.abc import Sequence
 from contextlib import contextmanager
+from dataclasses import dataclass
 
 import torch
 import torch.distributed as dist
@@ -57,6 +58,33 @@ def _env(names: Sequence[str], default: str | None = None) -> str | None:
     return default
 
 
+@dataclass(frozen=True)
+class Readiness:
+    """One rank's answer to "can this rank serve the NVLink collectives?": everything
+    that stops it (empty when ready) and the size limits it would register."""
+
+    rank: int
+    blockers: tuple[str, ...]
+    limits: tuple[int, int] | None
+
+
+def agreement(answers: Sequence[Readiness]) -> str | None:
+    """None when every rank is ready with the same limits; otherwise one message that
+    names every blocked rank, or every distinct set of limits and the ranks holding it.
+    Pure function of the gathered answers, so every rank reaches the same verdict."""
+    blocked = [f"rank {a.rank} cannot serve: {'; '.join(a.blockers)}" for a in answers if a.blockers]
+    if blocked:
+        return " | ".join(blocked)
+    holders: dict[tuple[int, int] | None, list[int]] = {}
+    for a in answers:
+        holders.setdefault(a.limits, []).append(a.rank)
+    if len(holders) > 1:
+        spread = ", ".join(f"ranks {ranks}: all-reduce {lim[0]} B / all-gather {lim[1]} B" if lim else
+                           f"ranks {ranks}: none" for lim, ranks in holders.items())
+        return f"size limits disagree across ranks ({spread})"
+    return None
+
+
 class SparknetOneShotAllReduce:
     """Route eligible tensor-parallel collectives to ``sparknet.oneshot`` over NVLink."""
 
@@ -65,75 +93,69 @@ class SparknetOneShotAllReduce:
     def __init__(self, group, device_group, device: torch.device, *, global_ranks: Sequence[int] | None = None,
                  nccl_available: bool = True, in_the_same_node: Sequence[bool] | None = None,
                  runtime_factory=None) -> None:
-        self.disabled = True
-        self.group = group
-        self.device_group = device_group
-        self.device = device
+        self.group, self.device_group, self.device = group, device_group, device
         self.rank = dist.get_rank(group=group)
         self.world_size = dist.get_world_size(group=group)
+        self.global_ranks = tuple(range(self.world_size)) if global_ranks is None else tuple(map(int, global_ranks))
         self._runtime = None
         self._announced: set[str] = set()
-        self.global_ranks = tuple(int(r) for r in (global_ranks if global_ranks is not None
-                                                   else range(self.world_size)))
+        self.disabled = True
         if len(self.global_ranks) != self.world_size:
-            raise ValueError("global ranks must match the process group")
+            raise ValueError(f"{len(self.global_ranks)} global ranks for a group of {self.world_size}")
         if device_group is None:
-            raise RuntimeError("the NVLink adapter requires a CUDA process group")
+            raise RuntimeError("the NVLink adapter needs the CUDA (NCCL) process group beside the CPU group")
         if in_the_same_node is not None and not all(in_the_same_node):
-            logger.info("NVLink collectives skipped: the group spans more than one box")
+            # every rank sees the same list, so every rank leaves the adapter off here
+            logger.info("NVLink collectives off: the tensor-parallel group spans several boxes")
             return
-        reason, limits = self._local_capability()
+        mine = self._assess()
         if not nccl_available:
-            reason = "the policy requires an available NCCL communicator"
-        verdict = self._exchange_vote(reason, limits)
+            mine = Readiness(mine.rank, mine.blockers + ("NCCL must stay available for ineligible inputs",),
+                             mine.limits)
+        answers: list = [None] * self.world_size
+        dist.all_gather_object(answers, mine, group=self.group)
+        verdict = agreement(answers)
         if verdict is not None:
             raise RuntimeError(f"NVLink collective policy unavailable: {verdict}")
-        max_size, max_gather = limits
-        if runtime_factory is None:
+        capacity, gather_shard = mine.limits
+        factory = runtime_factory
+        if factory is None:
             from sparknet import oneshot
 
-            runtime_factory = oneshot.AllReduce.from_exchange_group
+            factory = oneshot.AllReduce.from_exchange_group
         try:
-            self._runtime = runtime_factory(exchange_group=group, device=device, max_size=max_size,
-                                            max_gather_bytes=max_gather)
-            self._runtime.prepare((torch.float16, torch.bfloat16, torch.float32), padded_gather=True)
-        except Exception as exc:  # noqa: BLE001 - the runtime already coordinated ranks
+            runtime = factory(exchange_group=group, device=device, max_size=capacity, max_gather_bytes=gather_shard)
+            runtime.prepare((torch.float16, torch.bfloat16, torch.float32), padded_gather=True)
+        except Exception as exc:  # noqa: BLE001 - the runtime's own set-up is collective
             raise RuntimeError("NVLink collective initialization failed") from exc
-        self.disabled = False
+        self._runtime, self.disabled = runtime, False
         if self.rank == 0:
-            logger.info("Using NVLink collectives: world=%d, all-reduce dispatch <=%d bytes, capacity=%d bytes, "
-                        "all-gather shard <=%d bytes, fused add+RMSNorm on. NCCL handles ineligible inputs; "
-                        "failures are fatal.", self.world_size, self.all_reduce_max_bytes,
-                        self.all_reduce_capacity_bytes, self.all_gather_max_bytes)
+            logger.info("NVLink collectives on (world %d): all-reduce up to %d B of a %d B capacity, all-gather "
+                        "shards up to %d B, fused add + RMSNorm; NCCL carries the rest; a failure is fatal",
+                        self.world_size, self.all_reduce_max_bytes, self.all_reduce_capacity_bytes,
+                        self.all_gather_max_bytes)
 
-    def _local_capability(self):
+    def _assess(self) -> Readiness:
+        """Everything that stops this rank, checked in full (not just the first)."""
+        blockers: list[str] = []
+        limits = None
+        try:
+            capacity = parse_byte_size(_env(ENV_ALLREDUCE_LIMIT, "8MB"))
+            gather_shard = parse_byte_size(_env(ENV_ALLGATHER_LIMIT, "16MB"))
+            limits = (capacity, gather_shard)
+        except ValueError as exc:
+            blockers.append(f"size limit: {exc}")
         try:
             from sparknet import oneshot
         except ImportError as exc:
-            return f"sparknet.oneshot is not importable: {exc}", None
+            blockers.append(f"sparknet.oneshot does not import ({exc})")
+            return Readiness(self.rank, tuple(blockers), limits)
         api = getattr(oneshot, "API_VERSION", None)
         if api != REQUIRED_API_VERSION:
-            return f"sparknet.oneshot API version {api}, adapter needs {REQUIRED_API_VERSION}", None
-        if not oneshot.is_supported(self.device):
-            return "needs a B200 (compute capability 10.0) with the sparknet extension built", None
-        try:
-            limits = (parse_byte_size(_env(ENV_ALLREDUCE_LIMIT, "8MB")),
-                      parse_byte_size(_env(ENV_ALLGATHER_LIMIT, "16MB")))
-        except Exception as exc:  # noqa: BLE001 - reported through the vote
-            return f"invalid size limit: {exc}", None
-        return None, limits
-
-    def _exchange_vote(self, reason, limits):
-        votes = [(None, None)] * self.world_size
-        dist.all_gather_object(votes, (reason, limits), group=self.group)
-        failures = [f"rank {i}: {r}" for i, (r, _) in enumerate(votes) if r]
-        if failures:
-            return "; ".join(failures)
-        reference = votes[0][1]
-        differing = [f"rank {i}: {lim}" for i, (_, lim) in enumerate(votes) if lim != reference]
-        if differing:
-            return f"size limits differ across ranks (rank 0: {reference}; " + "; ".join(differing) + ")"
-        return None
+            blockers.append(f"sparknet.oneshot speaks API {api}, this adapter speaks {REQUIRED_API_VERSION}")
+        elif not oneshot.is_supported(self.device):
+            blockers.append(f"{self.device} is not a B200 (sm_100) with the sparknet extension built")
+        return Readiness(self.rank, tuple(blockers), limits)
 
     def _announce(self, kind: str, message: str, *args) -> None:
         if kind in self._announced:
@@ -233,4 +255,4 @@ class SparknetOneShotAllReduce:
         self.disabled = True
 
 
-__all__ = ["REQUIRED_API_VERSION", "SparknetOneShotAllReduce", "parse_byte_size"]
+__all__ = ["REQUIRED_API_VERSION", "Readiness", "SparknetOneShotAllReduce", "agreement", "parse_byte_size"]

@@ -1178,18 +1178,27 @@ class NvlinkAllReduce:
         return out
 
     # -- capture / diagnostics / lifecycle -----------------------------------------------------
+    def _forget_stream_order(self) -> None:
+        """Drop the remembered launch stream and capture identity (see ``capture``)."""
+        self._last_stream, self._capture_stream, self._capture_id = None, None, 0
+
     @contextmanager
     def capture(self, stream: object = None, *, channel_id: Optional[str] = None):
-        """Context for CUDA graph capture: every collective inside must use one stream."""
-        self._last_stream = None
-        self._capture_stream = None
-        self._capture_id = 0
+        """Scope for CUDA-graph capture of NVLink collectives.
+
+        Captured collectives read their sequence number from the device-resident epoch
+        at replay time, so nothing host-side is baked into the graph.  What the runtime
+        forgets on entry and on exit is its stream ordering: an event recorded outside a
+        capture may not be waited on inside one, and one recorded inside belongs to the
+        graph.  Within the scope every collective uses one stream.  ``stream`` and
+        ``channel_id`` are accepted for the reference's signature; the stream in use is
+        the one the first captured collective runs on."""
+        del stream, channel_id
+        self._forget_stream_order()
         try:
             yield self
         finally:
-            self._capture_stream = None
-            self._capture_id = 0
-            self._last_stream = None
+            self._forget_stream_order()
 
     def _account_reduce(self, algo: str, nbytes: int) -> None:
         if algo == "oneshot":
@@ -1223,24 +1232,27 @@ class NvlinkAllReduce:
         return info
 
     def close(self) -> None:
-        """Release the regions after the device is idle; peers must close collectively."""
+        """Release this rank's regions (collective: every rank closes, none keeps using
+        the group).  The device is drained first, so no kernel of this rank is still
+        reading or writing a peer's region when the mappings go; the trace file stays on
+        disk for collection, only its mapping is dropped."""
         with self._lock:
             if self._closed:
                 return
             self._closed = True
-            with contextlib.suppress(Exception):
+            comm, transport, trace = self._comm, self._transport, self._trace_map
+            self._comm, self._transport, self._trace_map = None, None, None
+            try:
                 torch.cuda.synchronize(self.device)
-            if self._comm is not None and self._trace_map is not None:
+            except Exception:  # noqa: BLE001 - a failed device still releases its mappings
+                logger.debug("device drain before close failed", exc_info=True)
+            if comm is not None and trace is not None:
                 with contextlib.suppress(Exception):
-                    self._comm.set_trace(0, 0)
-                    self._trace_map.flush()
-                # the file stays in /dev/shm for collection; only the mapping goes
-                self._trace_map = None
-            self._comm = None
-            if self._transport is not None:
-                self._transport.stop()
-                self._transport.close()
-                self._transport = None
+                    comm.set_trace(0, 0)  # stop stamping before the mapping goes
+                    trace.flush()
+            if transport is not None:
+                transport.stop()
+                transport.close()
 
     def __del__(self) -> None:  # pragma: no cover - defensive teardown
         # no module globals here: at interpreter exit they may already be gone

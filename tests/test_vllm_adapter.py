@@ -54,9 +54,10 @@ def _worker(rank, world, store, mode, results):
 
     if mode == "mismatch" and rank == 1:
         os.environ["SPARKNET_ALLREDUCE_CAPACITY_BYTES"] = "4MB"
-    mod.SparknetOneShotAllReduce._local_capability = lambda self: (
-        (None, (mod.parse_byte_size(os.environ.get("SPARKNET_ALLREDUCE_CAPACITY_BYTES", "8MB")), 16 << 20))
-        if not (mode == "refuse" and self.rank == 1) else ("no B200 here", None))
+    mod.SparknetOneShotAllReduce._assess = lambda self: (
+        mod.Readiness(self.rank, (), (mod.parse_byte_size(os.environ.get("SPARKNET_ALLREDUCE_CAPACITY_BYTES", "8MB")),
+                                      16 << 20))
+        if not (mode == "refuse" and self.rank == 1) else mod.Readiness(self.rank, ("no B200 here",), None))
     out = {}
     try:
         adapter = mod.SparknetOneShotAllReduce(dist.group.WORLD, object(), torch.device("cpu"),
@@ -96,12 +97,12 @@ def test_adapter_votes_and_routes(tmp_path):
 
 def test_a_refusing_rank_fails_every_rank(tmp_path):
     res = run("refuse", tmp_path)
-    assert all("rank 1: no B200 here" in out.get("error", "") for out in res.values()), res
+    assert all("rank 1 cannot serve: no B200 here" in out.get("error", "") for out in res.values()), res
 
 
 def test_differing_limits_fail_every_rank(tmp_path):
     res = run("mismatch", tmp_path)
-    assert all("size limits differ" in out.get("error", "") for out in res.values()), res
+    assert all("size limits disagree" in out.get("error", "") for out in res.values()), res
 
 
 def test_parse_byte_size():
@@ -110,3 +111,16 @@ def test_parse_byte_size():
     assert parse_byte_size("2MB") == 2 << 20 and parse_byte_size(" 16 kb ") == 16 << 10
     with pytest.raises(ValueError):
         parse_byte_size("0")
+
+
+def test_agreement_lists_every_blocker_and_limit_set():
+    from sparknet.integration.vllm.nvlink_all_reduce import Readiness, agreement
+
+    ok = [Readiness(r, (), (8 << 20, 16 << 20)) for r in range(4)]
+    assert agreement(ok) is None
+    blocked = ok[:2] + [Readiness(2, ("a", "b"), None), Readiness(3, ("c",), None)]
+    text = agreement(blocked)
+    assert "rank 2 cannot serve: a; b" in text and "rank 3 cannot serve: c" in text
+    split = ok[:3] + [Readiness(3, (), (4 << 20, 16 << 20))]
+    text = agreement(split)
+    assert "ranks [0, 1, 2]" in text and "ranks [3]" in text and str(4 << 20) in text
