@@ -32,6 +32,13 @@ def timed(fn, reps=5):
     return st.elapsed_time(en) / reps
 
 
+def gathered_fp32(shard):
+    """Every rank's shard (NCCL all-gather of the bf16 values), stacked in rank order, in fp32."""
+    parts = [torch.empty_like(shard) for _ in range(dist.get_world_size())]
+    dist.all_gather(parts, shard.contiguous())
+    return torch.cat(parts).float()
+
+
 def main():
     local = int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
@@ -54,10 +61,10 @@ def main():
     x = torch.randn(t // world, k, generator=g, device=device).to(torch.bfloat16)
     w = (0.05 * torch.randn(n, k, generator=g, device=device)).to(torch.bfloat16)
     got = rt.ag_gemm(x, w)
-    want = ag_gemm_reference(x, w).float()
+    want = gathered_fp32(x) @ w.float().T  # fp32 product of the gathered operands
     torch.cuda.synchronize()
     err = (got.float() - want).abs().max().item() / max(1e-6, want.abs().max().item())
-    if err > 2e-2:
+    if err > 1e-2:  # bf16 output rounding is 2^-9 relative
         failures.append(f"ag_gemm relative error {err}")
     a = torch.randn(t, k, generator=g, device=device).to(torch.bfloat16)
     got = rt.gemm_rs(a, w[:512])
@@ -106,10 +113,10 @@ def main():
     if chunk_major:
         for copy_ctas in (None, 1, 16):
             got = rt.ag_gemm(x, w, copy_ctas=copy_ctas, copy_order="chunk-major")
-            want = ag_gemm_reference(x, w).float()
+            want = gathered_fp32(x) @ w.float().T
             torch.cuda.synchronize()
             err = (got.float() - want).abs().max().item() / max(1e-6, want.abs().max().item())
-            if err > 2e-2:
+            if err > 1e-2:
                 failures.append(f"ag_gemm chunk-major ({copy_ctas} copy CTAs) relative error {err}")
         got = rt.ag_gemm_fp8(xq, sx, wq, sw, copy_order="chunk-major")
         want = torch.cat(parts) @ fp8.dequantize(wq, sw).T
