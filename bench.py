@@ -315,7 +315,11 @@ def run_allreduce(args, rank, world, device, cpu_group):
         e2e = run_e2e(arm, args, sizes, rank, world, device, cpu_group)
     fused = None
     if args.impl == "ours" and args.fused_norm_tokens:
-        fused = run_fused_norm(arm, args, rank, world, device, cpu_group)
+        try:
+            fused = run_fused_norm(arm, args, rank, world, device, cpu_group)
+        except RuntimeError as exc:  # a side measurement: recorded, the headline stands
+            print(f"fused all-reduce + RMSNorm check failed: {exc}", file=sys.stderr, flush=True)
+            fused = {"failed": str(exc)}
 
     headline = [p50_us[s] for s in sizes if s in HEADLINE_SIZES] or list(p50_us.values())
     value = geomean(headline)
@@ -448,6 +452,7 @@ def run_fused_norm(arm, args, rank, world, device, cpu_group):
         check = compare_exact(res_out, want_res, cpu_group, world)
         same_out = compare_exact(out, out, cpu_group, world)["rank_identical"]
         rel = ((out.float() - want_out).abs() / want_out.abs().clamp_min(1e-3)).max().item()
+        rel = max(gather_floats([rel], cpu_group), key=lambda v: v[0])[0]  # the same verdict on every rank
         check.update({"out_rank_identical": same_out, "out_max_rel_err_vs_fp32": rel})
         if not (check["bit_exact"] and same_out and rel <= 2.0 ** -7):
             raise RuntimeError(f"fused all-reduce + RMSNorm at {tokens} tokens failed its checks: {check}")
@@ -484,7 +489,7 @@ def run_fused_norm(arm, args, rank, world, device, cpu_group):
                     samples[name].append((st, en))
         torch.cuda.synchronize()
         rt.check_health()
-        if not torch.equal(res_out, want_res):
+        if not compare_exact(res_out, want_res, cpu_group, world)["bit_exact"]:
             raise RuntimeError(f"graph-replayed fused norm at {tokens} tokens changed its residual output")
         flat = [st.elapsed_time(en) for name in graphs for (st, en) in samples[name]]
         gathered = gather_floats(flat, cpu_group)

@@ -114,6 +114,8 @@ def main() -> int:
                     help="decode_gemm: skinny_tune(ctas_per_sm) before running (0 = default)")
     ap.add_argument("--pdl", action="store_true", help="decode_gemm: programmatic dependent launch")
     ap.add_argument("--cluster", action="store_true", help="attention: spans merged in a thread-block cluster")
+    ap.add_argument("--impl", type=int, default=0, choices=(0, 1, 2),
+                    help="attention: 0 tensor cores where eligible, 1 CUDA cores, 2 tensor cores")
     ap.add_argument("--stamps", action="store_true",
                     help="decode_gemm: per-CTA %%globaltimer phase stamps of one cold launch (µs percentiles)")
     ap.add_argument("--world", type=int, default=8)
@@ -238,7 +240,7 @@ def main() -> int:
             if args.cluster:
                 C.decode_attention_cluster(q, kk, vv, lengths, out, Lmax, D ** -0.5)
             else:
-                C.decode_attention(q, kk, vv, lengths, out, ws, Lmax, D ** -0.5)
+                C.decode_attention(q, kk, vv, lengths, out, ws, Lmax, D ** -0.5, False, args.impl)
 
         fn = lambda: attend(k, v)  # noqa: E731
         samples = _time(fn, args.warmup, args.iters, device)
@@ -248,7 +250,7 @@ def main() -> int:
         fns = [lambda kk=kk, vv=vv: attend(kk, vv) for kk, vv in kvs]
         row["graph_us"] = _time_graph(fns, 20, device)
         row.update(batch=B, heads=Hq, kv_heads=Hkv, length=L, kv_bytes=kv_bytes, copies=copies,
-                   variant="cluster" if args.cluster else "split")
+                   variant="cluster" if args.cluster else {0: "auto", 1: "simt", 2: "tcgen05"}[args.impl])
     med = statistics.median(samples)
     row.update(median_us=med, min_us=min(samples), iters=len(samples))
     if "bytes_per_rank" in row:

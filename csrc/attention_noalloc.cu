@@ -5,9 +5,13 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <functional>
+#include <mutex>
+#include <stdexcept>
 #include <string>
 
 #include "sparknet/attention_kernels.cuh"
+#include "sparknet/attention_tc.cuh"
 #include "sparknet/noalloc.h"
 
 namespace {
@@ -19,8 +23,15 @@ constexpr int kMaxDevices = 64;
 // its device address comes from cudaGetSymbolAddress, per device.
 static __device__ __align__(256) float g_attention_scratch[kScratchFloats];
 
-float* g_scratch_ptr[kMaxDevices] = {};
-int g_sms[kMaxDevices] = {};
+// Per device: the scratch's device address and the SM count, looked up once.  The
+// once-flags make concurrent first calls from several host threads safe; a lookup that
+// failed throws out of call_once, so the next call on that device tries again.
+struct DeviceSetup {
+  std::once_flag once;
+  float* scratch = nullptr;
+  int sms = 0;
+};
+DeviceSetup g_setup[kMaxDevices];
 thread_local std::string g_error;
 
 int fail(int code, const std::string& what) {
@@ -28,22 +39,29 @@ int fail(int code, const std::string& what) {
   return code;
 }
 
-// Once per device, with that device current: the scratch's device address and the SM
-// count used to split sequences.
+void lookup(int device, DeviceSetup& d) {
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_attention_scratch);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+  int n = 0;
+  e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("cudaDeviceGetAttribute: ") + cudaGetErrorString(e));
+  d.sms = n;
+  d.scratch = static_cast<float*>(p);
+}
+
+// With `device` current: the scratch's device address and the SM count used to split
+// sequences.
 int setup(int device, float** scratch, int* sms) {
   if (device < 0 || device >= kMaxDevices) return fail(1, "device ordinal out of range");
-  if (!g_scratch_ptr[device]) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_attention_scratch);
-    if (e != cudaSuccess) return fail(3, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
-    int n = 0;
-    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
-    if (e != cudaSuccess) return fail(3, std::string("cudaDeviceGetAttribute: ") + cudaGetErrorString(e));
-    g_sms[device] = n;
-    g_scratch_ptr[device] = static_cast<float*>(p);
+  DeviceSetup& d = g_setup[device];
+  try {
+    std::call_once(d.once, lookup, device, std::ref(d));
+  } catch (const std::exception& ex) {
+    return fail(3, ex.what());
   }
-  *scratch = g_scratch_ptr[device];
-  *sms = g_sms[device];
+  *scratch = d.scratch;
+  *sms = d.sms;
   return 0;
 }
 
@@ -51,8 +69,12 @@ int setup(int device, float** scratch, int* sms) {
 
 extern "C" size_t sparknet_decode_attention_scratch_bytes(int B, int Hq, int Hkv, int max_len) {
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || max_len <= 0 || Hq % Hkv) return 0;
-  // the split count depends on the SM count; 148 SMs on B200 (queried per device at run time)
-  return sn::attn::scratch_floats(B, Hq, Hkv, max_len, 148) * sizeof(float);
+  // the split count depends on the SM count: that of the current device, as a call uses
+  int device = 0, sms = 0;
+  if (cudaGetDevice(&device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || sms <= 0)
+    return 0;
+  return sn::attn::scratch_floats(B, Hq, Hkv, max_len, sms) * sizeof(float);
 }
 
 extern "C" const char* sparknet_noalloc_last_error(void) { return g_error.c_str(); }

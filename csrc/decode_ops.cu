@@ -28,6 +28,7 @@
 #include <stdexcept>
 
 #include "sparknet/attention_kernels.cuh"
+#include "sparknet/attention_tc.cuh"
 
 namespace py = pybind11;
 
@@ -236,7 +237,7 @@ void rope_qkv_cache(const at::Tensor& qkv, const at::Tensor& cos_t, const at::Te
 // before the first call (every completed call leaves them zero).
 void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                       const at::Tensor& lengths, at::Tensor& out, at::Tensor& workspace, int max_len, double scale,
-                      bool pdl) {
+                      bool pdl, int impl) {
   check_bf16(q, "q");
   check_bf16(out, "out");
   int B = int(q.size(0)), Hq = int(q.size(1)), Hkv = int(k_cache.size(2)), Lmax = int(k_cache.size(1));
@@ -255,7 +256,7 @@ void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::
       reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr()),
       reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr()), lengths.data_ptr<int>(),
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), workspace.data_ptr<float>(), B, Hq, Hkv, Lmax, max_len,
-      float(scale), sms, stream_of(q), pdl);
+      float(scale), sms, stream_of(q), pdl, impl);
   if (e != cudaSuccess) throw std::runtime_error(std::string("decode_attention launch: ") + cudaGetErrorString(e));
 }
 
@@ -397,8 +398,10 @@ void register_decode(py::module_& m) {
   m.def("rope_qkv_cache", &rope_qkv_cache);
   m.def("decode_attention", &decode_attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("lengths"),
         py::arg("out"), py::arg("workspace"), py::arg("max_len"), py::arg("scale"), py::arg("pdl") = false,
-        "split-KV decode attention; pdl: programmatic dependent launch (keys below lengths[b] - 1 may be "
-        "prefetched while the previous kernel runs, so that kernel must not write them)");
+        py::arg("impl") = 0,
+        "split-KV decode attention; pdl: programmatic dependent launch (the kernel waits for the previous one "
+        "before it reads q, K/V or lengths); impl: 0 tensor cores where eligible, else CUDA cores; 1 CUDA cores; "
+        "2 tensor cores or an error");
   m.def("decode_attention_cluster", &decode_attention_cluster, py::arg("q"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("lengths"), py::arg("out"), py::arg("max_len"), py::arg("scale"),
         py::arg("pdl") = false,

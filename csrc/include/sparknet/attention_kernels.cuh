@@ -35,10 +35,26 @@ static inline int splits(int B, int Hkv, int max_len, int sms) {
 // completes leaves them zero.
 constexpr int kCounterSlots = 4096;
 
+// The tensor-core kernel (attention_tc.cuh) splits a sequence into spans of T tiles of
+// 128 keys, T = 1 or 2, at most kTcMaxSpans spans; 0 tiles = it does not take the problem.
+constexpr int kTcKeys = 128;
+constexpr int kTcMaxSpans = 64;
+static inline int tc_tiles(int max_len) {
+  if (max_len <= kTcMaxSpans * kTcKeys) return 1;
+  if (max_len <= kTcMaxSpans * 2 * kTcKeys) return 2;
+  return 0;
+}
+static inline int tc_splits(int max_len) {
+  const int T = tc_tiles(max_len);
+  return T ? (max_len + T * kTcKeys - 1) / (T * kTcKeys) : 0;
+}
+
 // Floats of scratch the kernels need: the counters, partial outputs [B, Hq, nsplit,
-// 128] and (max, sum) pairs [B, Hq, nsplit, 2].
+// 128] and (max, sum) pairs [B, Hq, nsplit, 2], for the larger split count of the two
+// kernels (either may run: the tensor-core one where it is eligible).
 static inline size_t scratch_floats(int B, int Hq, int Hkv, int max_len, int sms) {
-  return size_t(kCounterSlots) + size_t(B) * Hq * splits(B, Hkv, max_len, sms) * (kHead + 2);
+  const int a = splits(B, Hkv, max_len, sms), b = tc_splits(max_len);
+  return size_t(kCounterSlots) + size_t(B) * Hq * (a > b ? a : b) * (kHead + 2);
 }
 
 // ---------------------------------------------------------------------------
@@ -53,7 +69,7 @@ static inline size_t scratch_floats(int B, int Hq, int Hkv, int max_len, int sms
 // ---------------------------------------------------------------------------
 constexpr int kRowPad = kHead + 8;  // +16 bytes: lane-per-key 16-byte reads spread over banks
 constexpr int kMaxSplits = 64;      // spans per (sequence, KV head)
-constexpr int kMergeBatch = 8;      // partial outputs loaded at once in the merge
+constexpr int kMergeBatch = 32;     // partial outputs loaded at once in the merge
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
   const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
@@ -89,7 +105,9 @@ static __global__ void __launch_bounds__(kAttnThreads) k_decode_attn(const __nv_
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int dp = t & 63, hg = t >> 6;
   const int Hq = G * Hkv;
-  const int len = min(lengths[b], Lmax);
+  // The splits cover nsplit * chunk >= max_len keys (the host sizes chunk from max_len):
+  // a sequence longer than that is attended over its first nsplit * chunk keys only.
+  const int len = min(min(lengths[b], Lmax), nsplit * chunk);
   const int start = s * chunk, end = min(start + chunk, len);
   const int ntiles = end > start ? (end - start + kTile - 1) / kTile : 0;
   const size_t row_stride = size_t(Hkv) * kHead;
@@ -261,11 +279,14 @@ static __global__ void __launch_bounds__(kAttnThreads) k_decode_attn(const __nv_
   // partial outputs in batches of kMergeBatch spans.
   asm volatile("cp.async.wait_all;" ::: "memory");
   float(*wts)[kMaxSplits] = reinterpret_cast<float(*)[kMaxSplits]>(&kt[0][0][0]);  // K tiles are free now
+  float(*sums)[kMaxSplits] = reinterpret_cast<float(*)[kMaxSplits]>(&vt[0][0][0]);  // V tiles too
   static_assert(sizeof(float) * G * kMaxSplits <= sizeof(kt), "merge weights must fit the K tile buffers");
   __shared__ float lsum[G];
-  for (int i = t; i < G * nsplit; i += kAttnThreads) {
+  for (int i = t; i < G * nsplit; i += kAttnThreads) {  // every (max, sum) pair in one parallel pass
     const int g = i / nsplit, sp = i % nsplit;
-    wts[g][sp] = __ldcg(part_ml + ((head0 + g) * nsplit + sp) * 2);  // max (log2 units)
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(part_ml + ((head0 + g) * nsplit + sp) * 2));
+    wts[g][sp] = ml.x;  // max (log2 units)
+    sums[g][sp] = ml.y;
   }
   __syncthreads();
   if (t < G) {
@@ -273,7 +294,7 @@ static __global__ void __launch_bounds__(kAttnThreads) k_decode_attn(const __nv_
     for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, wts[t][sp]);
     float L = 0.0f;
     for (int sp = 0; sp < nsplit; ++sp) {
-      const float ls = __ldcg(part_ml + ((head0 + t) * nsplit + sp) * 2 + 1);
+      const float ls = sums[t][sp];
       const float w = ls > 0.0f ? exp2f(wts[t][sp] - M) : 0.0f;
       wts[t][sp] = w;
       L += ls * w;
@@ -308,7 +329,7 @@ static __global__ void __launch_bounds__(kAttnThreads) k_decode_attn(const __nv_
 // Launch over a scratch laid out as [kCounterSlots ints][part_o][part_ml].  Returns the
 // launch's error (or cudaErrorInvalidValue for an unsupported group size or too many
 // (sequence, KV head) pairs).
-static inline cudaError_t launch_decode_attention(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
+static inline cudaError_t launch_decode_attention_simt(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
                                                   const __nv_bfloat16* v_cache, const int* lengths,
                                                   __nv_bfloat16* out, float* scratch, int B, int Hq, int Hkv,
                                                   int Lmax, int max_len, float scale, int sms, cudaStream_t st,

@@ -28,7 +28,10 @@ extern "C" {
 //   q        [B, Hq, 128]            k_cache, v_cache [B, Lmax, Hkv, 128]
 //   lengths  [B] int32 (keys to attend, including the new token)
 //   out      [B, Hq, 128]            (all device pointers)
-//   max_len  upper bound of lengths (decides the split of each sequence)
+//   max_len  upper bound of lengths (decides the split of each sequence).  A length
+//            above max_len is not an error and is not detected: such a sequence is
+//            attended over its first max_len keys (rounded up to the split size) only,
+//            which gives a wrong output for it.
 //   scale    softmax scale (usually 1/sqrt(128))
 // Returns 0 on success, or a nonzero code with a message from
 // sparknet_noalloc_last_error(): 1 bad argument, 2 problem too large for the built-in
@@ -36,8 +39,10 @@ extern "C" {
 // `stream`; allocates nothing.
 //
 // The first call on a device looks up the device address of the scratch array (a
-// CUDA runtime query, done once per device with that device current); make that
-// first call outside any stream capture.  Every call, on every stream, shares the
+// CUDA runtime query, done once per device with that device current; concurrent first
+// calls from several host threads are safe); make that first call outside any stream
+// capture.  The address is cached for the life of the process: after a
+// cudaDeviceReset of a device, do not call this entry point on that device again.  Every call, on every stream, shares the
 // one scratch array, so calls that may overlap on the GPU (different streams, no
 // ordering between them) race and must not be issued.  The scratch keeps the last
 // call's contents.  It starts with a fixed block of per-(sequence, KV head) counters
@@ -52,7 +57,8 @@ __attribute__((visibility("default"))) int sparknet_decode_attention_noalloc(
 // The message of the last failed call on this host thread ("" after a success).
 __attribute__((visibility("default"))) const char* sparknet_noalloc_last_error(void);
 
-// Bytes of scratch a problem needs (0 if the arguments are invalid); compare with
+// Bytes of scratch a problem needs on the current device (its SM count decides the
+// split), 0 if the arguments are invalid or no device is current; compare with
 // SPARKNET_NOALLOC_SCRATCH_BYTES.
 __attribute__((visibility("default"))) size_t sparknet_decode_attention_scratch_bytes(int B, int Hq, int Hkv,
                                                                                        int max_len);

@@ -192,6 +192,32 @@ def cmd_policy_show(args) -> int:
     return 0
 
 
+def cmd_policy_derive(args) -> int:
+    """Sweep receipts (one ``W=<world>:<receipt.json>`` per world size) -> the measured
+    table the policy's defaults are derived from, plus the limits it implies."""
+    from sparknet.policy import derive_limits, sweep_rows
+
+    rows = []
+    for item in args.receipts:
+        world, _, path = item.partition(":")
+        if not world.startswith("W=") or not path:
+            print(f"error: expected W=<world>:<receipt.json>, got {item!r}", file=sys.stderr)
+            return 2
+        rows += sweep_rows(json.loads(Path(path).read_text()), int(world[2:]))
+    if not rows:
+        print("error: no all-reduce sweep rows in the receipts", file=sys.stderr)
+        return 1
+    limits = derive_limits(rows)
+    table = {"source": args.source, "rows": sorted(rows, key=lambda r: (r["world"], r["nbytes"], r["arm"])),
+             "derived": {"oneshot_max": limits.oneshot_max, "dispatch_max": limits.dispatch_max,
+                         "nvls_min": limits.nvls_min}}
+    text = json.dumps(table, indent=1, sort_keys=False)
+    if args.output:
+        Path(args.output).write_text(text + "\n")
+    print(json.dumps(table["derived"], indent=2))
+    return 0
+
+
 def cmd_probe_doctor(args) -> int:
     from sparknet.probe.doctor import local_problems
 
@@ -382,6 +408,12 @@ def parser() -> argparse.ArgumentParser:
     ps = po.add_parser("show", help="the policy of a profile, or of this environment")
     ps.add_argument("--profile", choices=profiles)
     ps.set_defaults(func=cmd_policy_show)
+    pv = po.add_parser("derive", help="measured policy table from probe sweep receipts")
+    pv.add_argument("receipts", nargs="+", metavar="W=<world>:<receipt.json>")
+    pv.add_argument("--output", default="", help="write the table (sparknet/policy/measured_b200.json)")
+    pv.add_argument("--source", default="sparknet probe collectives --benchmark --sweep --counter-samples",
+                    help="how the receipts were made (recorded in the table)")
+    pv.set_defaults(func=cmd_policy_derive)
 
     pr = sub.add_parser("probe", help="fabric checks and the collective probe").add_subparsers(
         dest="subcommand", required=True)

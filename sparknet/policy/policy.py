@@ -34,6 +34,7 @@ from __future__ import annotations
 
 import json
 from dataclasses import dataclass, field
+from pathlib import Path
 from typing import Mapping
 
 PACK_BYTES = 16
@@ -179,6 +180,91 @@ class CollectivePolicy:
         return policy
 
 
+# -- limits derived from a committed measurement ------------------------------------
+MEASURED_TABLE = Path(__file__).with_name("measured_b200.json")
+
+
+@dataclass(frozen=True)
+class MeasuredLimits:
+    """Per-world-size limits derived from an all-reduce latency sweep.
+
+    - ``oneshot_max``: the largest size up to which one-shot is never slower than
+      two-shot (the one-shot / two-shot crossover);
+    - ``dispatch_max``: the largest size up to which the faster NVLink arm is never
+      slower than NCCL (the all-reduce dispatch ceiling);
+    - ``nvls_min``: the smallest size from which NVLS beats both push arms at every
+      measured size (None when NVLS was not measured or never wins).
+    """
+
+    oneshot_max: Mapping[int, int]
+    dispatch_max: Mapping[int, int]
+    nvls_min: Mapping[int, int | None]
+
+
+def sweep_rows(receipt: Mapping, world: int) -> list[dict]:
+    """All-reduce rows of a probe receipt (``sparknet probe collectives --benchmark
+    --sweep``) as ``{world, nbytes, arm, p50_us}``; the arm is the backend the case
+    ran on (a forced arm outside its range ran elsewhere and is dropped)."""
+    item = {"bfloat16": 2, "float16": 2, "float32": 4}
+    out = []
+    for row in receipt.get("timings", ()):
+        if row.get("operation") != "all_reduce" or row.get("arm") == "policy":
+            continue
+        if row.get("backend", row["arm"]) != row["arm"]:
+            continue
+        dtype = str(row["dtype"]).rsplit(".", 1)[-1]
+        out.append({"world": int(world), "nbytes": int(row["elements_per_rank"]) * item[dtype], "arm": row["arm"],
+                    "p50_us": float(row["median_us"])})
+    return out
+
+
+def _by_world_size(rows) -> dict[int, dict[int, dict[str, float]]]:
+    table: dict[int, dict[int, dict[str, float]]] = {}
+    for row in rows:
+        table.setdefault(int(row["world"]), {}).setdefault(int(row["nbytes"]), {})[row["arm"]] = float(row["p50_us"])
+    return table
+
+
+def derive_limits(rows) -> MeasuredLimits:
+    """``MeasuredLimits`` from sweep rows (``{world, nbytes, arm, p50_us}``).
+
+    Each limit is taken from the smallest size upward and stops at the first size that
+    breaks it, so a limit never skips over a size where its arm lost."""
+    oneshot, dispatch, nvls = {}, {}, {}
+    for world, sizes in _by_world_size(rows).items():
+        one_lim, disp_lim, nvls_from = 0, 0, None
+        one_open = disp_open = True
+        for nbytes in sorted(sizes):
+            arms = sizes[nbytes]
+            push = [arms[a] for a in ("oneshot", "twoshot") if a in arms]
+            if one_open and "oneshot" in arms:
+                if "twoshot" not in arms or arms["oneshot"] <= arms["twoshot"]:
+                    one_lim = nbytes
+                else:
+                    one_open = False
+            if disp_open and push and "nccl" in arms:
+                if min(push) <= arms["nccl"]:
+                    disp_lim = nbytes
+                else:
+                    disp_open = False
+            if "nvls" in arms and push:
+                if arms["nvls"] < min(push):
+                    nvls_from = nvls_from if nvls_from is not None else nbytes
+                else:
+                    nvls_from = None
+        oneshot[world], dispatch[world], nvls[world] = one_lim, disp_lim, nvls_from
+    return MeasuredLimits(oneshot, dispatch, nvls)
+
+
+def load_measured(path: str | Path | None = None) -> MeasuredLimits | None:
+    """The limits derived from the committed sweep (``measured_b200.json`` beside this
+    module), or None if it is absent."""
+    target = Path(path) if path is not None else MEASURED_TABLE
+    if not target.exists():
+        return None
+    return derive_limits(json.loads(target.read_text())["rows"])
+
+
 def crossover_from_timings(rows: list[dict]) -> dict[int, int]:
     """The largest size at which one-shot beat two-shot, per world size.
 
@@ -223,6 +309,7 @@ def policy_for_profile(name: str) -> CollectivePolicy | None:
 
 
 __all__ = [
-    "BACKENDS", "GATHER_ALGORITHMS", "PACK_BYTES", "SUPPORTED_DTYPES", "CollectivePolicy", "NVLINK_POLICY",
-    "crossover_from_timings", "policy_for_profile",
+    "BACKENDS", "GATHER_ALGORITHMS", "MEASURED_TABLE", "PACK_BYTES", "SUPPORTED_DTYPES", "CollectivePolicy",
+    "MeasuredLimits", "NVLINK_POLICY", "crossover_from_timings", "derive_limits", "load_measured",
+    "policy_for_profile", "sweep_rows",
 ]

@@ -37,8 +37,18 @@ def test_rope_qkv_cache(device, native):
         assert torch.equal(vc[b, p[b]], parts[b, Hq + Hkv:])
 
 
-@pytest.mark.parametrize("B,Hq,Hkv,L", [(1, 8, 1, 1025), (4, 8, 1, 300), (2, 64, 8, 129), (64, 8, 1, 1280), (3, 4, 4, 33)])
-def test_decode_attention(device, native, B, Hq, Hkv, L):
+ATTENTION_SHAPES = [(1, 8, 1, 1025), (4, 8, 1, 300), (2, 64, 8, 129), (64, 8, 1, 1280), (3, 4, 4, 33),
+                    (8, 8, 1, 1024), (2, 16, 1, 300), (1, 8, 1, 9000), (2, 8, 1, 128), (1, 1, 1, 200), (4, 16, 4, 257)]
+
+
+@pytest.mark.parametrize("impl", [1, 2])
+@pytest.mark.parametrize("B,Hq,Hkv,L", ATTENTION_SHAPES)
+def test_decode_attention(device, native, B, Hq, Hkv, L, impl):
+    """impl 1: the CUDA-core kernel; impl 2: the tensor-core kernel (tcgen05 QK^T and
+    P V), where it takes the shape.  Both against fp32 attention, twice (PDL on the
+    second call), counters and error word left at zero."""
+    if impl == 2 and B * (L + 7) < 128:
+        pytest.skip("the tensor-core kernel needs at least one 128-key tile of cache")
     Lmax = L + 7
     q = torch.randn(B, Hq, 128, device=device).to(torch.bfloat16)
     kc = torch.randn(B, Lmax, Hkv, 128, device=device).to(torch.bfloat16)
@@ -48,10 +58,10 @@ def test_decode_attention(device, native, B, Hq, Hkv, L):
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     ws = torch.zeros(native.attention_workspace_floats(B, Hq, Hkv, L, sms), dtype=torch.float32, device=device)
     out = torch.empty(B, Hq, 128, dtype=torch.bfloat16, device=device)
-    native.decode_attention(q, kc, vc, lengths, out, ws, L, 1 / math.sqrt(128))
+    native.decode_attention(q, kc, vc, lengths, out, ws, L, 1 / math.sqrt(128), False, impl)
     again = torch.empty_like(out)
     # counters were left at zero; programmatic dependent launch computes the same
-    native.decode_attention(q, kc, vc, lengths, again, ws, L, 1 / math.sqrt(128), True)
+    native.decode_attention(q, kc, vc, lengths, again, ws, L, 1 / math.sqrt(128), True, impl)
     torch.cuda.synchronize()
     assert torch.equal(out, again)
     assert not ws[:4096].view(torch.int32).any()

@@ -67,3 +67,24 @@ def test_multiprocess_fused_prefill_gemms():
 def test_multiprocess_trace_records_peer_arrivals():
     lines = run_workers(_world(), {"SPARKNET_TRACE": "1"})
     assert len(lines) == _world() and all(not l["failures"] and l["trace"]["collectives"] > 10 for l in lines), lines
+
+
+@pytest.mark.skipif(_world() < 2, reason="needs two or more GPUs")
+def test_failstop_qualification_two_gpus():
+    """The fail-stop probe on 2 GPUs, NVLS off: the victim skips one collective on the
+    host (it stays alive, launches nothing); the survivor's bounded wait must end within
+    0.9 x timeout .. 3 x timeout + 2 s with a report naming the victim, then every rank
+    re-arms and a healthy all-reduce is exact, eagerly and from a CUDA graph."""
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", SPARKNET_NVLS="0")
+    cmd = ["timeout", "-k", "30", "400", sys.executable, "-m", "sparknet.probe.failstop", "--world", "2",
+           "--timeout-ms", "1000", "--victim", "1", "--port", str(29300 + os.getpid() % 500)]
+    proc = subprocess.run(cmd, env=env, cwd=ROOT, capture_output=True, text=True, timeout=460)
+    lines = [l for l in proc.stdout.splitlines() if l.startswith("{")]
+    assert lines, proc.stdout[-2000:] + proc.stderr[-3000:]
+    result = json.loads(lines[-1])
+    out_dir = os.environ.get("SPARKNET_TEST_OUT")
+    if out_dir:
+        Path(out_dir, "failstop_w2.json").write_text(json.dumps(result, indent=1))
+    assert proc.returncode == 0 and result["passed"], result
+    survivor = next(r for r in result["results"] if r["rank"] == 0)
+    assert survivor["eager"]["detected"] and "waiting for rank 1" in survivor["eager"]["report"]

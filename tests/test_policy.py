@@ -100,3 +100,41 @@ def test_ag_gemm_copy_ctas_balance():
     assert copy_ctas_for(shard, 1, 2 * T * H * 1280) == 0
     assert copy_ctas_for(1 << 30, 8, 1) == 74              # clamped to half the SMs
     assert copy_ctas_for(1, 8, 1 << 50) == 16
+
+
+def test_derive_limits_stops_at_the_first_loss():
+    from sparknet.policy import derive_limits
+
+    def row(world, kib, arm, us):
+        return {"world": world, "nbytes": kib << 10, "arm": arm, "p50_us": us}
+
+    rows = [
+        row(8, 4, "oneshot", 5), row(8, 4, "twoshot", 7), row(8, 4, "nccl", 20),
+        row(8, 64, "oneshot", 6), row(8, 64, "twoshot", 7), row(8, 64, "nccl", 22),
+        row(8, 512, "oneshot", 11), row(8, 512, "twoshot", 10), row(8, 512, "nccl", 30),
+        row(8, 1024, "oneshot", 9), row(8, 1024, "twoshot", 15), row(8, 1024, "nccl", 35),  # one-shot wins again: ignored
+        row(8, 4096, "twoshot", 40), row(8, 4096, "nccl", 38),                              # NCCL first wins
+        row(8, 8192, "twoshot", 50), row(8, 8192, "nccl", 60),                              # after the first loss: ignored
+        row(8, 512, "nvls", 9), row(8, 1024, "nvls", 8), row(8, 4096, "nvls", 30), row(8, 64, "nvls", 9),
+    ]
+    lim = derive_limits(rows)
+    assert lim.oneshot_max[8] == 64 << 10
+    assert lim.dispatch_max[8] == 1024 << 10
+    assert lim.nvls_min[8] == 512 << 10
+
+
+def test_sweep_rows_keep_cases_that_ran_on_their_arm():
+    from sparknet.policy import sweep_rows
+
+    receipt = {"timings": [
+        {"operation": "all_reduce", "arm": "oneshot", "backend": "oneshot", "dtype": "torch.bfloat16",
+         "elements_per_rank": 2048, "median_us": 5.0},
+        {"operation": "all_reduce", "arm": "policy", "backend": "oneshot", "dtype": "torch.bfloat16",
+         "elements_per_rank": 2048, "median_us": 5.0},
+        {"operation": "all_gather", "arm": "oneshot", "backend": "oneshot", "dtype": "torch.bfloat16",
+         "elements_per_rank": 2048, "median_us": 5.0},
+        {"operation": "all_reduce", "arm": "nccl", "backend": "nccl", "dtype": "torch.float32",
+         "elements_per_rank": 1024, "median_us": 9.0},
+    ]}
+    assert sweep_rows(receipt, 4) == [{"world": 4, "nbytes": 4096, "arm": "oneshot", "p50_us": 5.0},
+                                     {"world": 4, "nbytes": 4096, "arm": "nccl", "p50_us": 9.0}]
