@@ -90,23 +90,6 @@ __host__ __device__ constexpr uint32_t idesc_attn(bool a_mn) {
   return tc::idesc_bf16(kTcHeads) | (a_mn ? (1u << 15) : 0u);
 }
 
-// Bounded wait that ignores other roles' failures: used to let this CTA's own copies land
-// before it exits after an error.
-__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
-  const uint32_t addr = tc::smem_u32(bar);
-  for (uint32_t i = 0; i < tc::kWaitLimit; ++i) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(addr), "r"(parity)
-        : "memory");
-    if (done) return;
-  }
-}
-
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // Byte offset of element (row, col) in a 128-byte-swizzled, K-major block whose rows are
@@ -316,8 +299,8 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
   // the length (never waited for), and every tile after an error.
   if (t == 0) {
     for (int i = *bad ? 0 : ntiles; i < issued; ++i) {
-      mbar_drain(&k_full[i], 0);
-      mbar_drain(&v_full[i], 0);
+      tc::mbar_drain(&k_full[i], 0);
+      tc::mbar_drain(&v_full[i], 0);
     }
     if (*bad) atomicExch(&counters[kErrorSlot], 1);
   }

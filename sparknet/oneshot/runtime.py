@@ -43,7 +43,8 @@ import torch.distributed as dist
 
 from .. import _native
 from ..policy import CollectivePolicy
-from ..policy.policy import DEFAULT_ONESHOT_MAX, ENV_ALGO, ENV_CROSSOVER, ENV_NVLS, PACK_BYTES
+from ..policy.policy import (DEFAULT_ONESHOT_MAX, ENV_ALGO, ENV_CROSSOVER, ENV_NVLS, PACK_BYTES,
+                             default_dispatch_bytes)
 from . import symm, trace
 from ._freeze import raise_if_kernel_resolution_frozen
 
@@ -231,7 +232,7 @@ class NvlinkAllReduce:
         *,
         exchange_group,
         device: torch.device | int | str,
-        max_size: int = DEFAULT_MAX_SIZE,
+        max_size: Optional[int] = None,
         max_gather_bytes: int = DEFAULT_MAX_GATHER_BYTES,
         threads: int = DEFAULT_THREADS,
         blocks: int = DEFAULT_BLOCKS,
@@ -267,6 +268,8 @@ class NvlinkAllReduce:
         self._nvls_bytes = 0      # bytes moved through the multicast alias
         if self.world_size not in SUPPORTED_WORLD_SIZES:
             raise ValueError(f"unsupported world size {self.world_size}; supported: {SUPPORTED_WORLD_SIZES}")
+        if max_size is None:  # room for the measured dispatch ceiling of this world size
+            max_size = max(DEFAULT_MAX_SIZE, default_dispatch_bytes(self.world_size))
         if int(max_size) < PACK_BYTES or int(max_size) % PACK_BYTES:
             raise ValueError("max_size must be a positive multiple of 16 bytes")
         if int(threads) % 32 or not 32 <= int(threads) <= 512:
@@ -278,7 +281,7 @@ class NvlinkAllReduce:
             raise ValueError("; ".join(problems))
         self.max_size = int(max_size)
         self.max_gather_bytes = int(max_gather_bytes)
-        self.dispatch_max_bytes = _env_int(ENV_DISPATCH, min(self.max_size, 2 * 1024 * 1024))
+        self.dispatch_max_bytes = _env_int(ENV_DISPATCH, min(self.max_size, default_dispatch_bytes(self.world_size)))
         if not PACK_BYTES <= self.dispatch_max_bytes <= self.max_size or self.dispatch_max_bytes % PACK_BYTES:
             raise ValueError("the dispatch limit must be 16-byte aligned and within the registered capacity")
         self.timeout_ms = checked_timeout_ms(_env_int(ENV_TIMEOUT_MS, DEFAULT_TIMEOUT_MS))
@@ -364,7 +367,7 @@ class NvlinkAllReduce:
 
     # -- construction ----------------------------------------------------------------
     @classmethod
-    def from_exchange_group(cls, *, exchange_group, device, max_size: int = DEFAULT_MAX_SIZE,
+    def from_exchange_group(cls, *, exchange_group, device, max_size: Optional[int] = None,
                             eager_buffer_bytes: Optional[int] = None,
                             max_gather_bytes: int = DEFAULT_MAX_GATHER_BYTES, threads: int = DEFAULT_THREADS,
                             blocks: int = DEFAULT_BLOCKS, **kwargs: Any) -> "NvlinkAllReduce":
@@ -372,17 +375,19 @@ class NvlinkAllReduce:
         if "kernels" in kwargs:
             raise TypeError("the kernels keyword is not supported: the kernels are compiled ahead of time")
         known = {k: kwargs[k] for k in ("policy", "enable_multicast", "transport", "pdl") if k in kwargs}
-        capacity = max(int(max_size), int(eager_buffer_bytes or 0))
+        capacity = None if max_size is None and not eager_buffer_bytes else \
+            max(int(max_size or 0), int(eager_buffer_bytes or 0))
         return cls(exchange_group=exchange_group, device=device, max_size=capacity,
                    max_gather_bytes=max_gather_bytes, threads=threads, blocks=blocks, **known)
 
     @classmethod
-    def from_process_group(cls, *, process_group, device, max_size: int = DEFAULT_MAX_SIZE,
+    def from_process_group(cls, *, process_group, device, max_size: Optional[int] = None,
                            max_input_bytes: Optional[int] = None, **_ignored: Any) -> "NvlinkAllReduce":
         """Build the runtime with ``process_group`` as both the rank identity and the
         setup exchange (a CPU-capable group, e.g. gloo); further keywords are accepted
         and ignored, as in the reference (``sparknet/oneshot/runtime.py``)."""
-        capacity = max(int(max_size), int(max_input_bytes or 0))
+        capacity = None if max_size is None and not max_input_bytes else \
+            max(int(max_size or 0), int(max_input_bytes or 0))
         return cls(exchange_group=process_group, device=device, max_size=capacity)
 
     # -- policy --------------------------------------------------------------------------

@@ -50,19 +50,23 @@ ENV_CROSSOVER = "SPARKNET_ONESHOT_MAX_BYTES"
 ENV_ALGO = "SPARKNET_ALGO"
 ENV_NVLS = "SPARKNET_NVLS"
 
-# Largest all-reduce (bytes per rank) that one-shot carries, by world size.  Above
-# it two-shot moves less data per link.  Measured on 8x B200 (NVLink 5, NVSwitch) with
-# ``sparknet probe collectives --benchmark --sweep`` (8 GPUs: one-shot 11.9 us vs
-# two-shot 14.5 us at 480 KiB, 17.5 vs 15.1 us at 1 MiB); the values are
-# rank-invariant constants, not runtime measurements.
-DEFAULT_ONESHOT_MAX = {1: 1 << 62, 2: 4 << 20, 4: 512 << 10, 8: 512 << 10}
+# Largest all-reduce (bytes per rank) that one-shot carries, by world size, and the
+# all-reduce dispatch ceiling, by world size.  Both come from the committed sweep
+# (``measured_b200.json`` beside this module, made by ``sparknet probe collectives
+# --benchmark --sweep`` on B200 boxes and ``sparknet policy derive``); they are read
+# once at import, so every rank of a job holds the same values.  Without the file the
+# fallbacks below apply (an earlier W=8 measurement: one-shot 11.9 us vs two-shot
+# 14.5 us at 480 KiB, 17.5 vs 15.1 us at 1 MiB).
+FALLBACK_ONESHOT_MAX = {2: 4 << 20, 4: 512 << 10, 8: 512 << 10}
+FALLBACK_DISPATCH_MAX = 2 << 20
 # Largest all-gather shard that travels in LL8 form (payload + flag per 8 bytes);
 # larger shards use bulk pushes with per-block flags (or NVLS broadcast when enabled).
 # LL doubles the bytes but needs no fence or flag round trip: on 2 GPUs a 256 KiB
 # shard took 19 us as a flagged bulk push, where LL moves it in a few microseconds.
 DEFAULT_LL_MAX = 1 << 20
-# Messages at or above this use NVLS when it is enabled and available.
-DEFAULT_NVLS_MIN = 256 << 10
+# Messages at or above this use NVLS when it is enabled and available (the measured
+# threshold of the smallest world size that has one, else this fallback).
+FALLBACK_NVLS_MIN = 256 << 10
 
 
 @dataclass(frozen=True)
@@ -70,10 +74,10 @@ class CollectivePolicy:
     all_reduce_dispatch_bytes: int
     all_reduce_capacity_bytes: int
     all_gather_shard_bytes: int
-    oneshot_max_bytes: Mapping[int, int] = field(default_factory=lambda: dict(DEFAULT_ONESHOT_MAX))
+    oneshot_max_bytes: Mapping[int, int] = field(default_factory=lambda: dict(DEFAULT_ONESHOT_MAX))  # noqa: F821
     ll_max_bytes: int = DEFAULT_LL_MAX
     allow_nvls: bool = False
-    nvls_min_bytes: int = DEFAULT_NVLS_MIN
+    nvls_min_bytes: int = field(default_factory=lambda: DEFAULT_NVLS_MIN)  # noqa: F821
     force: str | None = None
 
     def problems(self) -> list[str]:
@@ -291,6 +295,24 @@ def crossover_from_timings(rows: list[dict]) -> dict[int, int]:
     return table
 
 
+_MEASURED = load_measured()
+DEFAULT_ONESHOT_MAX = {1: 1 << 62, **FALLBACK_ONESHOT_MAX,
+                       **({w: v for w, v in _MEASURED.oneshot_max.items()} if _MEASURED else {})}
+_DISPATCH_BY_WORLD = dict(_MEASURED.dispatch_max) if _MEASURED else {}
+_nvls = sorted((w, v) for w, v in (_MEASURED.nvls_min.items() if _MEASURED else ()) if v)
+DEFAULT_NVLS_MIN = _nvls[0][1] if _nvls else FALLBACK_NVLS_MIN
+
+
+def default_dispatch_bytes(world: int) -> int:
+    """The all-reduce dispatch ceiling for ``world`` ranks: the measured one (nearest
+    smaller measured world for a world in between), else ``FALLBACK_DISPATCH_MAX``;
+    never below 16 bytes."""
+    if world in _DISPATCH_BY_WORLD:
+        return max(PACK_BYTES, int(_DISPATCH_BY_WORLD[world]))
+    smaller = [w for w in _DISPATCH_BY_WORLD if w <= world]
+    return max(PACK_BYTES, int(_DISPATCH_BY_WORLD[max(smaller)])) if smaller else FALLBACK_DISPATCH_MAX
+
+
 # Profiles for one B200 box: the product (NVLink kernels below 2 MiB dispatch,
 # 8 MiB registered capacity, 16 MiB gather shards).
 NVLINK_POLICY = CollectivePolicy(2 * 1024 * 1024, 8 * 1024 * 1024, 16 * 1024 * 1024)
@@ -309,7 +331,8 @@ def policy_for_profile(name: str) -> CollectivePolicy | None:
 
 
 __all__ = [
-    "BACKENDS", "GATHER_ALGORITHMS", "MEASURED_TABLE", "PACK_BYTES", "SUPPORTED_DTYPES", "CollectivePolicy",
+    "BACKENDS", "DEFAULT_NVLS_MIN", "DEFAULT_ONESHOT_MAX", "GATHER_ALGORITHMS", "MEASURED_TABLE",
+    "default_dispatch_bytes", "PACK_BYTES", "SUPPORTED_DTYPES", "CollectivePolicy",
     "MeasuredLimits", "NVLINK_POLICY", "crossover_from_timings", "derive_limits", "load_measured",
     "policy_for_profile", "sweep_rows",
 ]
