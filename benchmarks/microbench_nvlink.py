@@ -11,6 +11,9 @@ moves ``size`` bytes with ``sparknet._C.nvlink_move``:
 * ``load``       peer -> local (P2P loads, the pull)
 * ``mc_store``   local -> multicast alias (one ``multimem.st`` reaches every GPU)
 * ``mc_reduce``  multicast alias -> local (``multimem.ld_reduce`` sums every GPU's copy)
+* ``bulk``       local -> shared memory -> every target peer by bulk copies (one working
+                 thread per CTA, ``--pieces`` bytes per copy): the push of the fused
+                 all-gather -> GEMM done by the SM's copy engine instead of its threads
 
 Patterns: ``pair`` (rank 0 <-> rank 1 only), ``ring`` (rank r -> r+1, all at once),
 ``all`` (rank r -> every peer in turn, all ranks at once).  Timing: CUDA events around
@@ -35,7 +38,7 @@ import torch.distributed as dist
 ROOT = Path(__file__).resolve().parent.parent
 sys.path.insert(0, str(ROOT))
 
-MODES = {"store": 0, "load": 1, "mc_store": 2, "mc_reduce": 3}
+MODES = {"store": 0, "load": 1, "mc_store": 2, "mc_reduce": 3, "bulk": 4}
 
 
 def main() -> int:
@@ -44,6 +47,8 @@ def main() -> int:
     ap.add_argument("--blocks", type=int, nargs="+", default=[8, 32, 148])
     ap.add_argument("--threads", type=int, default=512)
     ap.add_argument("--ppt", type=int, nargs="+", default=[1, 4])
+    ap.add_argument("--pieces", type=int, nargs="+", default=[16384, 32768],
+                    help="bulk mode: bytes per bulk copy (ppt is ignored)")
     ap.add_argument("--modes", nargs="+", default=["store", "load"], choices=sorted(MODES))
     ap.add_argument("--pattern", default="ring", choices=["pair", "ring", "all"])
     ap.add_argument("--reps", type=int, default=50)
@@ -83,16 +88,21 @@ def main() -> int:
             return [(rank + 1) % world] if world > 1 else [rank]
         return [p for p in range(world) if p != rank] or [rank]
 
+    err = torch.zeros(1, dtype=torch.int32, device=device)
     rows = []
     for mode in args.modes:
         if mode.startswith("mc_") and regions.multicast is None:
             continue
         for size in args.sizes:
             for blocks in args.blocks:
-                for ppt in args.ppt:
+                for ppt in (args.pieces if mode == "bulk" else args.ppt):
                     peers = targets()
 
                     def once():
+                        if mode == "bulk":
+                            C.nvlink_bulk_fanout(src.data_ptr(), [regions.bases[p] for p in peers], size, blocks,
+                                                 ppt, err, local)
+                            return
                         for p in peers:
                             if mode == "store":
                                 s_, d_ = src.data_ptr(), regions.bases[p]
@@ -125,8 +135,11 @@ def main() -> int:
                     active = [per[r] for r in range(world) if (args.pattern != "pair" or r < 2)]
                     worst = max(active)
                     moved = size * max(1, len(peers))
-                    rows.append({"mode": mode, "bytes": size, "blocks": blocks, "threads": args.threads, "ppt": ppt,
-                                 "us": round(worst, 3), "gbs_per_gpu": round(moved / worst / 1e3, 1)})
+                    row = {"mode": mode, "bytes": size, "blocks": blocks, "threads": args.threads, "ppt": ppt,
+                           "us": round(worst, 3), "gbs_per_gpu": round(moved / worst / 1e3, 1)}
+                    if mode == "bulk":
+                        row.update(threads=32, piece=ppt, ppt=None, wait_error=int(err.item()))
+                    rows.append(row)
     receipt = {"benchmark": "microbench_nvlink", "world": world, "pattern": args.pattern, "gemm_corunner": args.gemm,
                "nvls": regions.multicast is not None, "rows": rows,
                "gpu": torch.cuda.get_device_name(device)}

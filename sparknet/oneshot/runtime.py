@@ -73,14 +73,16 @@ OP_NAMES = {1: "all-reduce", 2: "all-gather", 3: "reduce-scatter", 4: "exchange"
 ENV_TIMEOUT_MS = "SPARKNET_TIMEOUT_MS"
 ENV_PDL = "SPARKNET_PDL"
 ENV_AG_COPY_ORDER = "SPARKNET_AG_COPY_ORDER"
-AG_COPY_ORDERS = {"spread": 0, "chunk-major": 1}
+AG_COPY_ORDERS = {"spread": 0, "chunk-major": 1, "bulk": 2}
 
 
 def ag_copy_order(order: Optional[str] = None) -> int:
     """Copy schedule of the fused all-gather -> GEMM: ``spread`` (default: the shard's
-    chunks, or slices of them, spread over the copy CTAs at once) or ``chunk-major``
+    chunks, or slices of them, spread over the copy CTAs at once), ``chunk-major``
     (every copy warp pushes a slice of chunk 0, then of chunk 1, ...: chunks land in the
-    order the GEMM consumes them).  ``order`` overrides ``SPARKNET_AG_COPY_ORDER``."""
+    order the GEMM consumes them) or ``bulk`` (chunk-major, the SM's bulk-copy engine
+    moves the data: one thread per copy CTA issues a bulk load per piece and one bulk
+    store per peer).  ``order`` overrides ``SPARKNET_AG_COPY_ORDER``."""
     name = order if order is not None else (os.environ.get(ENV_AG_COPY_ORDER) or "spread")
     if name not in AG_COPY_ORDERS:
         raise ValueError(f"all-gather copy order must be one of {sorted(AG_COPY_ORDERS)}, got {name!r}")
@@ -203,23 +205,26 @@ class _StatusView:
 # sustains ~9 TFLOP/s per SM in bf16 (1354.8 TFLOP/s over 148 SMs) and ~10.7 in
 # block-scaled fp8.
 PUSH_GBS_PER_CTA = 20.0
+PUSH_GBS_PER_BULK_CTA = 80.0   # the bulk-copy role: one thread per CTA drives the copy engine
+MIN_BULK_COPY_CTAS = 4
 MIN_COPY_CTAS = 16        # fewer measured slower at TP2 and TP8 on every prefill shape
 BF16_GEMM_TFLOPS_PER_SM = 9.0
 FP8_GEMM_TFLOPS_PER_SM = 10.7
 
 
 def copy_ctas_for(shard_bytes: int, world: int, flops: int, *, sms: int = 148,
-                  gemm_tflops_per_sm: float = BF16_GEMM_TFLOPS_PER_SM) -> int:
+                  gemm_tflops_per_sm: float = BF16_GEMM_TFLOPS_PER_SM, push_gbs_per_cta: float = PUSH_GBS_PER_CTA,
+                  min_ctas: int = MIN_COPY_CTAS) -> int:
     """Copy CTAs for the fused all-gather -> GEMM so that pushing the shard to the
     ``world - 1`` peers takes about as long as the GEMM on the remaining SMs:
     c / (sms - c) = (bytes / push rate) / (flops / GEMM rate per SM).  Clamped to
     [16, sms / 2]; rank-invariant (shapes and world only)."""
     if world <= 1:
         return 0
-    t_push = (world - 1) * shard_bytes / (PUSH_GBS_PER_CTA * 1e9)      # seconds with one CTA
+    t_push = (world - 1) * shard_bytes / (push_gbs_per_cta * 1e9)       # seconds with one CTA
     t_gemm = flops / (gemm_tflops_per_sm * 1e12)                          # seconds with one SM
     c = sms * t_push / (t_push + t_gemm)
-    return int(max(MIN_COPY_CTAS, min(sms // 2, round(c))))
+    return int(max(min_ctas, min(sms // 2, round(c))))
 
 
 class NvlinkAllReduce:
@@ -698,8 +703,8 @@ class NvlinkAllReduce:
         """
         order = ag_copy_order(copy_order)
         if copy_ctas is None:
-            copy_ctas = copy_ctas_for(x_shard.numel() * x_shard.element_size(), self.world_size,
-                                      2 * x_shard.shape[0] * self.world_size * x_shard.shape[1] * w.shape[0])
+            copy_ctas = self._copy_ctas(order, x_shard.numel() * x_shard.element_size(),
+                                        2 * x_shard.shape[0] * self.world_size * x_shard.shape[1] * w.shape[0])
         with self._lock:
             self.check_health()
             self._live()
@@ -713,6 +718,13 @@ class NvlinkAllReduce:
                 self._peer_bytes += x_shard.numel() * x_shard.element_size()
                 self._mark_stream(capturing)
         return out
+
+    def _copy_ctas(self, order: int, shard_bytes: int, flops: int) -> int:
+        """Copy CTAs of the fused all-gather -> GEMM for a copy schedule (rank-invariant)."""
+        if order == AG_COPY_ORDERS["bulk"]:
+            return copy_ctas_for(shard_bytes, self.world_size, flops, push_gbs_per_cta=PUSH_GBS_PER_BULK_CTA,
+                                 min_ctas=MIN_BULK_COPY_CTAS)
+        return copy_ctas_for(shard_bytes, self.world_size, flops)
 
     def gemm_rs(self, a: torch.Tensor, w: torch.Tensor, *, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """``reduce_scatter(a @ w.T, dim=0)`` in one kernel (row-parallel prefill GEMM).
@@ -746,9 +758,12 @@ class NvlinkAllReduce:
         """
         order = ag_copy_order(copy_order)
         if copy_ctas is None:
+            bulk = order == AG_COPY_ORDERS["bulk"]
             copy_ctas = copy_ctas_for(xq_shard.numel() + sfa_shard.numel(), self.world_size,
                                       2 * xq_shard.shape[0] * self.world_size * xq_shard.shape[1] * w.shape[0],
-                                      gemm_tflops_per_sm=FP8_GEMM_TFLOPS_PER_SM)
+                                      gemm_tflops_per_sm=FP8_GEMM_TFLOPS_PER_SM,
+                                      push_gbs_per_cta=PUSH_GBS_PER_BULK_CTA if bulk else PUSH_GBS_PER_CTA,
+                                      min_ctas=MIN_BULK_COPY_CTAS if bulk else MIN_COPY_CTAS)
         with self._lock:
             self.check_health()
             self._live()

@@ -24,7 +24,7 @@ BULK_COPY = re.compile(r"cp\.async\.bulk[\w.:]*")
 ALLOWED_BULK_QUALIFIERS = {
     "cp", "async", "bulk", "tensor", "1d", "2d", "3d", "4d", "5d", "tile",
     "shared::cluster", "shared::cta", "global", "mbarrier::complete_tx::bytes",
-    "bulk_group", "prefetch", "L2", "L2::cache_hint",
+    "bulk_group", "prefetch", "L2", "L2::cache_hint", "commit_group", "wait_group", "read",
 }
 
 
