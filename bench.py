@@ -60,8 +60,6 @@ def parse_args(argv=None):
     p.add_argument("--batch", type=int, default=8, help="decode: sequences per step")
     p.add_argument("--fuse-gemm-ar", action="store_true",
                    help="decode: the O / down GEMM epilogues push into the all-reduce (NVLink arm)")
-    p.add_argument("--prefetch", action="store_true",
-                   help="decode: prefetch the next GEMM's weights into L2 during attention and the all-reduces")
     p.add_argument("--attention", choices=("split", "cluster"), default="split",
                    help="decode: span merge through a workspace (split) or a thread-block cluster")
     p.add_argument("--layers", type=int, default=80, help="decode: decoder layers")

@@ -34,14 +34,13 @@ def main() -> int:
     ap.add_argument("--graph", action="store_true", help="time graph replays instead of eager steps")
     ap.add_argument("--gemm", choices=["sparknet", "cublas"], default="sparknet")
     ap.add_argument("--attention", choices=["split", "cluster"], default="split")
-    ap.add_argument("--prefetch", action="store_true", help="L2 prefetch of the next GEMM's weights")
     args = ap.parse_args()
     t = args.tp
     cfg = LlamaConfig(hidden=8192, layers=args.layers, heads=64 // t, kv_heads=max(1, 8 // t), head_dim=128,
                       ffn=28672 // t, vocab=128256 // t)
     device = torch.device("cuda", 0)
     model = TPLlama(cfg, rank=0, world=1, device=device, batch=args.batch, max_len=1280 + 16, gemm=args.gemm,
-                    attention=args.attention, prefetch=args.prefetch)
+                    attention=args.attention)
     model.fill_prompt_cache(1024)
     for _ in range(args.warmup):
         model.step_kernels()

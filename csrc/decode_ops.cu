@@ -335,63 +335,6 @@ void row_argmax(const at::Tensor& logits, int index_offset, at::Tensor& out) {
   else k_row_argmax<4><<<rows, 1024, 0, st>>>(lp, V, index_offset, out.data_ptr<float>());
 }
 
-// ---------------------------------------------------------------------------
-// L2 prefetch of weights ahead of the GEMM that reads them, issued during the phases
-// of a decode step that leave HBM idle (attention, the all-reduces).  Each thread
-// issues cp.async.bulk.prefetch.L2 for one piece of up to 64 KB: no data enters the SM
-// and nothing depends on the prefetch, so it cannot change a result.  The kernel
-// triggers its programmatic successor at once and waits for its own predecessor
-// (griddepcontrol.wait) before it exits, so a successor that waits for it has also
-// waited for the kernel before it: inserting it keeps every data dependency.
-// ---------------------------------------------------------------------------
-constexpr uint64_t kPrefetchPiece = 64 * 1024;
-
-__global__ void __launch_bounds__(256) k_l2_prefetch(const char* p0, uint64_t n0, const char* p1, uint64_t n1) {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  const uint64_t pieces0 = (n0 + kPrefetchPiece - 1) / kPrefetchPiece;
-  const uint64_t pieces = pieces0 + (n1 + kPrefetchPiece - 1) / kPrefetchPiece;
-  for (uint64_t i = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < pieces; i += uint64_t(gridDim.x) * blockDim.x) {
-    const bool first = i < pieces0;
-    const uint64_t off = (first ? i : i - pieces0) * kPrefetchPiece;
-    const uint64_t n = first ? n0 : n1;
-    const char* p = (first ? p0 : p1) + off;
-    const uint32_t bytes = uint32_t(n - off < kPrefetchPiece ? n - off : kPrefetchPiece);
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-  }
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-
-// Prefetch the first `bytes0` of `a` and `bytes1` of `b` (either may be absent or 0;
-// clamped to the tensor) into L2, on the current stream.
-void l2_prefetch(const at::Tensor& a, int64_t bytes0, const c10::optional<at::Tensor>& b, int64_t bytes1, bool pdl) {
-  auto span = [](const at::Tensor& t, int64_t want) -> uint64_t {
-    if (!t.is_cuda() || !t.is_contiguous()) throw std::invalid_argument("l2_prefetch takes contiguous CUDA tensors");
-    if (reinterpret_cast<uintptr_t>(t.data_ptr()) % 16) throw std::invalid_argument("l2_prefetch: 16-byte aligned");
-    const uint64_t have = uint64_t(t.numel()) * t.element_size();
-    const uint64_t n = want < 0 ? have : std::min<uint64_t>(have, uint64_t(want));
-    return n / 16 * 16;  // whole 16-byte units
-  };
-  const uint64_t n0 = span(a, bytes0);
-  const uint64_t n1 = b.has_value() ? span(*b, bytes1) : 0;
-  if (b.has_value() && b->device() != a.device()) throw std::invalid_argument("l2_prefetch: one device");
-  const uint64_t pieces = (n0 + kPrefetchPiece - 1) / kPrefetchPiece + (n1 + kPrefetchPiece - 1) / kPrefetchPiece;
-  c10::cuda::CUDAGuard guard(a.device());
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(unsigned(std::max<uint64_t>(1, std::min<uint64_t>((pieces + 255) / 256, 64))));
-  cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = stream_of(a);
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr.val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
-  const char* p0 = static_cast<const char*>(a.data_ptr());
-  const char* p1 = b.has_value() ? static_cast<const char*>(b->data_ptr()) : p0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, k_l2_prefetch, p0, n0, p1, n1);
-  if (e != cudaSuccess) throw std::runtime_error(std::string("l2_prefetch launch: ") + cudaGetErrorString(e));
-}
-
 }  // namespace
 
 void register_decode(py::module_& m) {
@@ -412,7 +355,4 @@ void register_decode(py::module_& m) {
         py::arg("out"), py::arg("eps"));
   m.def("silu_mul", &silu_mul, py::arg("gate_up"), py::arg("out"), py::arg("block") = 0);
   m.def("row_argmax", &row_argmax);
-  m.def("l2_prefetch", &l2_prefetch, py::arg("a"), py::arg("bytes_a") = -1, py::arg("b") = py::none(),
-        py::arg("bytes_b") = 0, py::arg("pdl") = true,
-        "prefetch the first bytes of a (and b) into L2; -1 = the whole tensor; a hint, no data dependency");
 }

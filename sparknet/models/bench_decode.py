@@ -47,7 +47,7 @@ def run_decode_bench(args, rank, world, device, cpu_group):
     t0 = time.perf_counter()
     model = TPLlama(cfg, rank=rank, world=world, device=device, batch=batch, max_len=max_len, comm=comm,
                     runtime=runtime, group=None, attention=getattr(args, "attention", "split"),
-                    prefetch=getattr(args, "prefetch", False), fuse_gemm_ar=getattr(args, "fuse_gemm_ar", False))
+                    fuse_gemm_ar=getattr(args, "fuse_gemm_ar", False))
     model.fill_prompt_cache(PROMPT)
     torch.cuda.synchronize()
     init_s = time.perf_counter() - t0
@@ -120,7 +120,7 @@ def run_decode_bench(args, rank, world, device, cpu_group):
                    "global_batch": batch, "seq_len": PROMPT, "parallelism": f"tp{world}", "comm": comm,
                    "gemm": model.gemm, "programmatic_dependent_launch": model.pdl,
                    "collective_pdl": bool(runtime.pdl) if runtime is not None else False,
-                   "attention": model.attention, "l2_prefetch": model.prefetch,
+                   "attention": model.attention,
                    "gemm_pushes_all_reduce": model.fuse_gemm_ar,
                    "l2": "weights per step far exceed L2 (126 MB)"},
         "gpu_launches": model.launches_per_step() * args.steps,

@@ -70,8 +70,7 @@ class TPLlama:
 
     def __init__(self, cfg: LlamaConfig, *, rank: int, world: int, device, batch: int, max_len: int,
                  comm: str = "sparknet", runtime=None, group=None, seed: int = 0, gemm: str | None = None,
-                 pdl: bool = True, attention: str = "split", prefetch: bool = False, prefetch_mb: int = 48,
-                 fuse_gemm_ar: bool = False):
+                 pdl: bool = True, attention: str = "split", fuse_gemm_ar: bool = False):
         if cfg.heads % world or cfg.kv_heads % world or cfg.ffn % world or cfg.vocab % world:
             raise ValueError(f"model does not shard evenly over {world} GPUs")
         if comm not in ("sparknet", "nccl"):
@@ -87,12 +86,6 @@ class TPLlama:
             raise ValueError("attention must be 'split' (workspace merge) or 'cluster' (cluster merge)")
         self.gemm = gemm
         self.attention = attention
-        # L2 prefetch of the next GEMM's weights during attention and the all-reduces
-        # (phases that leave HBM idle), at most `prefetch_mb` MB each (L2 is 126 MB): O
-        # before attention, gate/up before the all-reduce after O, the next layer's QKV
-        # (or the LM head) before the all-reduce after down.
-        self.prefetch = bool(prefetch)
-        self.prefetch_bytes = int(prefetch_mb) << 20
         # O and down projections whose GEMM epilogue pushes into the all-reduce
         # (NVLink arm with the tcgen05 decode GEMMs only)
         self.fuse_gemm_ar = bool(fuse_gemm_ar) and comm == "sparknet" and world > 1 and gemm == "sparknet"
@@ -212,8 +205,6 @@ class TPLlama:
                 self._linear(self.x, L["wqkv"], self.qkv)
                 C.rope_qkv_cache(self.qkv, self.cos, self.sin, self.positions, self.q, L["k"], L["v"], self.hq,
                                  self.hkv)
-            if self.prefetch:
-                C.l2_prefetch(L["wo"], self.prefetch_bytes)
             if self.attention == "cluster":
                 C.decode_attention_cluster(self.q, L["k"], L["v"], self.lengths, self.attn, self.max_len, scale,
                                            self.pdl)
@@ -223,22 +214,14 @@ class TPLlama:
             last = i + 1 == len(self.layers)
             nxt = self.norm if last else self.layers[i + 1]["ln1"]
             if self.fuse_gemm_ar:
-                if self.prefetch:
-                    C.l2_prefetch(L["wgu"], self.prefetch_bytes)
                 self._gemm_add_norm(self.attn.view(self.batch, -1), L["wo"], L["ln2"])
                 self._swiglu(self.x, L["wgu"], self.act)
-                if self.prefetch:
-                    C.l2_prefetch(self.lm_head if last else self.layers[i + 1]["wqkv"], self.prefetch_bytes)
                 self._gemm_add_norm(self.act, L["wdown"], nxt)
                 continue
             self._linear(self.attn.view(self.batch, -1), L["wo"], self.partial)
-            if self.prefetch:
-                C.l2_prefetch(L["wgu"], self.prefetch_bytes)
             self._add_norm(self.partial, L["ln2"])
             self._swiglu(self.x, L["wgu"], self.act)
             self._linear(self.act, L["wdown"], self.partial)
-            if self.prefetch:
-                C.l2_prefetch(self.lm_head if last else self.layers[i + 1]["wqkv"], self.prefetch_bytes)
             self._add_norm(self.partial, nxt)
         self._linear(self.x, self.lm_head, self.logits)
         C.row_argmax(self.logits, self.rank * self.v, self.best)
@@ -277,14 +260,12 @@ class TPLlama:
         """This package's kernel launches in one step (torch index/copy ops and cuBLAS
         GEMMs excluded): per layer attention and two norms (fused with the all-reduce on
         the NVLink arm), plus four GEMMs with RoPE and SwiGLU fused (``gemm="sparknet"``)
-        or the RoPE and SwiGLU kernels (cuBLAS arm), plus three L2 prefetches with
-        ``prefetch=True``."""
+        or the RoPE and SwiGLU kernels (cuBLAS arm)."""
         # sparknet: QKV+RoPE, O, gate/up+SwiGLU, down GEMMs; cuBLAS arm: RoPE and SwiGLU kernels
         per_layer = 1 + 2 + (4 if self.gemm == "sparknet" else 2)
         own_gather = 1 if (self.world > 1 and self.comm == "sparknet") else 0
         lm_head = 1 if self.gemm == "sparknet" else 0
-        prefetch = 3 * self.cfg.layers if self.prefetch else 0
-        return 1 + self.cfg.layers * per_layer + lm_head + 1 + own_gather + prefetch
+        return 1 + self.cfg.layers * per_layer + lm_head + 1 + own_gather
 
 
 class _null:

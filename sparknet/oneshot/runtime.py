@@ -60,7 +60,7 @@ DEFAULT_THREADS = 512
 DEFAULT_BLOCKS = 0          # 0: one block per SM at most
 DEFAULT_TIMEOUT_MS = 10_000
 MAX_TIMEOUT_MS = (2**32 - 1) // 1000
-LL_CAP = 1024 * 1024
+LL_CAP = 8 * 1024 * 1024   # LL8 slot: all-gather shards up to this travel as payload + flags
 
 ALGO_CODES = {"oneshot": 0, "twoshot": 1, "nvls": 2, "local": 3}
 GATHER_CODES = {"ll": 0, "push": 1, "nvls": 2}

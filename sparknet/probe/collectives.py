@@ -472,8 +472,8 @@ def _benchmark(comm, runtime, args, world, rank, device, cpu_group, capture_cont
                         samples.append(start.elapsed_time(end) * 1000 / (calls_per_graph * replays_per_sample))
                     own_after = nvcounters.own_gpu_counters(device.index) if args.counter_samples else {}
                     tx = None
-                    if "nvlink_tx_kib" in own_before and "nvlink_tx_kib" in own_after:
-                        tx = (own_after["nvlink_tx_kib"] - own_before["nvlink_tx_kib"]) * 1024
+                    if "nvlink_tx_bytes" in own_before and "nvlink_tx_bytes" in own_after:
+                        tx = own_after["nvlink_tx_bytes"] - own_before["nvlink_tx_bytes"]
                     gathered = [None] * world
                     dist.all_gather_object(gathered, (samples, tx), group=cpu_group)
                     slowest = [max(g[0][i] for g in gathered) for i in range(len(samples))]
@@ -487,6 +487,7 @@ def _benchmark(comm, runtime, args, world, rank, device, cpu_group, capture_cont
                         seen = [g[1] for g in gathered]
                         row["nvlink_tx_bytes_per_rank"] = seen
                         row["nvlink_tx_bytes_expected_per_rank"] = want
+                        row["nvlink_counter_source"] = own_after.get("source") or own_after.get("why")
                         if all(v is not None for v in seen) and route.nvlink and world > 1:
                             # NVLink counters count the payload plus protocol overhead;
                             # sending less than the payload means the route was not taken

@@ -60,26 +60,63 @@ def nvlink_counters(nvml: Any = None, *, links: int = 18) -> dict[str, int]:
     return snap
 
 
-def own_gpu_counters(device_index: int, nvml: Any = None) -> dict[str, int]:
-    """NVLink data counters (KiB sent and received) of the GPU behind the CUDA device
-    ``device_index`` of this process, found by PCI bus id so that other jobs' GPUs on a
-    shared box are never read.  Empty when NVML or the field is unavailable."""
-    try:
-        import torch
+# Blackwell's byte counters (per link: scope = link index), used where the
+# throughput fields above are not offered.
+FI_NVLINK_COUNT_XMIT_BYTES = 202
+FI_NVLINK_COUNT_RCV_BYTES = 204
 
-        props = torch.cuda.get_device_properties(device_index)
-        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+
+def _handle_of_device(nv, device_index: int):
+    """The NVML handle of this process's CUDA device ``device_index``, matched by PCI bus
+    id (so another job's GPU on a shared box is never read)."""
+    import torch
+
+    props = torch.cuda.get_device_properties(device_index)
+    want = (int(props.pci_domain_id), int(props.pci_bus_id), int(props.pci_device_id))
+    for h in nvml_mod.handles(nv):
+        info = nv.nvmlDeviceGetPciInfo(h)
+        if (int(info.domain), int(info.bus), int(info.device)) == want:
+            return h
+    raise LookupError(f"no NVML device at PCI {want}")
+
+
+def _scoped_sum(nv, handle, field: int, links: int):
+    getter = getattr(nv, "nvmlDeviceGetFieldValues", None)
+    if getter is None:
+        return None
+    try:
+        values = getter(handle, [(field, link) for link in range(links)])
+    except Exception:  # noqa: BLE001
+        return None
+    total, seen = 0, 0
+    for v in values:
+        if getattr(v, "nvmlReturn", 1) == 0:
+            raw = getattr(v, "value", None)
+            total += int(getattr(raw, "ullVal", raw if isinstance(raw, int) else 0))
+            seen += 1
+    return total if seen else None
+
+
+def own_gpu_counters(device_index: int, nvml: Any = None, *, links: int = 18) -> dict:
+    """NVLink bytes sent and received so far by the GPU behind the CUDA device
+    ``device_index`` of this process: ``nvlink_tx_bytes`` / ``nvlink_rx_bytes`` and the
+    NVML source used.  Tries the aggregate data-throughput fields (KiB), then the
+    per-link byte counters summed over links.  Empty (with ``why``) when NVML offers
+    neither: counters are evidence, never a reason to fail a probe."""
+    try:
         nv = nvml if nvml is not None else nvml_mod.load()
-        handle = nv.nvmlDeviceGetHandleByPciBusId_v2(bus)
-    except Exception:  # noqa: BLE001 - counters are evidence, never a reason to fail a probe
-        return {}
+        handle = _handle_of_device(nv, device_index)
+    except Exception as exc:  # noqa: BLE001
+        return {"why": f"{type(exc).__name__}: {exc}"}
     fv = _field_values(nv, handle, (FI_NVLINK_THROUGHPUT_DATA_TX, FI_NVLINK_THROUGHPUT_DATA_RX))
-    out = {}
-    if FI_NVLINK_THROUGHPUT_DATA_TX in fv:
-        out["nvlink_tx_kib"] = fv[FI_NVLINK_THROUGHPUT_DATA_TX]
-    if FI_NVLINK_THROUGHPUT_DATA_RX in fv:
-        out["nvlink_rx_kib"] = fv[FI_NVLINK_THROUGHPUT_DATA_RX]
-    return out
+    if FI_NVLINK_THROUGHPUT_DATA_TX in fv and FI_NVLINK_THROUGHPUT_DATA_RX in fv:
+        return {"nvlink_tx_bytes": fv[FI_NVLINK_THROUGHPUT_DATA_TX] * 1024,
+                "nvlink_rx_bytes": fv[FI_NVLINK_THROUGHPUT_DATA_RX] * 1024, "source": "throughput_data_kib"}
+    tx = _scoped_sum(nv, handle, FI_NVLINK_COUNT_XMIT_BYTES, links)
+    rx = _scoped_sum(nv, handle, FI_NVLINK_COUNT_RCV_BYTES, links)
+    if tx is not None and rx is not None:
+        return {"nvlink_tx_bytes": tx, "nvlink_rx_bytes": rx, "source": "count_bytes_per_link"}
+    return {"why": "NVML offers neither NVLink throughput fields nor per-link byte counters here"}
 
 
 def deltas(before: dict[str, int], after: dict[str, int]) -> dict[str, int]:
