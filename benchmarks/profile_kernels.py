@@ -117,7 +117,8 @@ def main() -> int:
     ap.add_argument("--impl", type=int, default=0, choices=(0, 1, 2),
                     help="attention: 0 tensor cores where eligible, 1 CUDA cores, 2 tensor cores")
     ap.add_argument("--stamps", action="store_true",
-                    help="decode_gemm: per-CTA %%globaltimer phase stamps of one cold launch (µs percentiles)")
+                    help="decode_gemm, attention --impl 2: per-CTA %%globaltimer phase stamps of one cold launch "
+                         "(µs percentiles)")
     ap.add_argument("--world", type=int, default=8)
     ap.add_argument("--bytes", type=int, default=2 << 20, help="bytes per rank (collectives)")
     ap.add_argument("--algorithm", default="", help="oneshot/twoshot (all-reduce, fused norm), ll/push (gather)")
@@ -242,6 +243,34 @@ def main() -> int:
             else:
                 C.decode_attention(q, kk, vv, lengths, out, ws, Lmax, D ** -0.5, False, args.impl)
 
+        if args.stamps and args.impl == 2 and not args.cluster:
+            # one cold launch with per-CTA phase stamps (tensor-core kernel)
+            nsplit = -(-Lmax // (128 if Lmax <= 64 * 128 else 256))
+            st = torch.zeros(B * Hkv * nsplit * 10, dtype=torch.int64, device=device)
+            flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+            flush.fill_(1)
+            torch.cuda.synchronize(device)
+            C.decode_attention(q, k, v, lengths, out, ws, Lmax, D ** -0.5, False, 2, st)
+            torch.cuda.synchronize(device)
+            t = st.view(-1, 10).double().cpu() / 1000.0
+            t0 = t[:, 0].min()
+            names = ["entry", "setup", "issue_q_len", "first_k", "scores", "softmax", "output", "partial_count",
+                     "merge"]
+            phases = {}
+            prev = None
+            for i, n in enumerate(names):
+                col = t[:, i]
+                ok = col > 0
+                if i == 0:
+                    d = col - t0
+                else:
+                    d = (col - prev)[ok & (prev > 0)]
+                if d.numel():
+                    phases[n] = {"p50": round(float(d.median()), 2), "max": round(float(d.max()), 2),
+                                 "ctas": int(d.numel())}
+                prev = torch.where(ok, col, prev) if prev is not None else col
+            phases["span"] = round(float(t.max() - t0), 2)
+            row["phases_us"] = phases
         fn = lambda: attend(k, v)  # noqa: E731
         samples = _time(fn, args.warmup, args.iters, device)
         kv_bytes = 2 * B * Hkv * L * D * 2

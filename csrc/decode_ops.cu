@@ -237,7 +237,7 @@ void rope_qkv_cache(const at::Tensor& qkv, const at::Tensor& cos_t, const at::Te
 // before the first call (every completed call leaves them zero).
 void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
                       const at::Tensor& lengths, at::Tensor& out, at::Tensor& workspace, int max_len, double scale,
-                      bool pdl, int impl) {
+                      bool pdl, int impl, const c10::optional<at::Tensor>& stamps) {
   check_bf16(q, "q");
   check_bf16(out, "out");
   int B = int(q.size(0)), Hq = int(q.size(1)), Hkv = int(k_cache.size(2)), Lmax = int(k_cache.size(1));
@@ -252,11 +252,16 @@ void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::
   size_t need = sn::attn::scratch_floats(B, Hq, Hkv, max_len, sms);
   if (workspace.scalar_type() != at::kFloat || !workspace.is_contiguous() || size_t(workspace.numel()) < need)
     throw std::invalid_argument("workspace too small for the attention partials");
+  if (stamps.has_value() &&
+      (impl != 2 || stamps->scalar_type() != at::kLong || !stamps->is_contiguous() ||
+       size_t(stamps->numel()) < size_t(B) * Hkv * std::max(1, sn::attn::tc_splits(max_len)) * sn::attn::kTcStamps))
+    throw std::invalid_argument("stamps: impl 2 and a contiguous int64 tensor of (grid CTAs x 10) entries");
   cudaError_t e = sn::attn::launch_decode_attention(
       reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr()),
       reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr()), lengths.data_ptr<int>(),
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), workspace.data_ptr<float>(), B, Hq, Hkv, Lmax, max_len,
-      float(scale), sms, stream_of(q), pdl, impl);
+      float(scale), sms, stream_of(q), pdl, impl,
+      stamps.has_value() ? reinterpret_cast<uint64_t*>(stamps->data_ptr<int64_t>()) : nullptr);
   if (e != cudaSuccess) throw std::runtime_error(std::string("decode_attention launch: ") + cudaGetErrorString(e));
 }
 
@@ -341,10 +346,10 @@ void register_decode(py::module_& m) {
   m.def("rope_qkv_cache", &rope_qkv_cache);
   m.def("decode_attention", &decode_attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"), py::arg("lengths"),
         py::arg("out"), py::arg("workspace"), py::arg("max_len"), py::arg("scale"), py::arg("pdl") = false,
-        py::arg("impl") = 0,
+        py::arg("impl") = 0, py::arg("stamps") = py::none(),
         "split-KV decode attention; pdl: programmatic dependent launch (the kernel waits for the previous one "
-        "before it reads q, K/V or lengths); impl: 0 tensor cores where eligible, else CUDA cores; 1 CUDA cores; "
-        "2 tensor cores or an error");
+        "before it reads q, K/V or lengths); impl: 0 or 1 CUDA cores, 2 tensor cores (or an error where not "
+        "eligible); stamps (impl 2): int64 tensor of grid x 10 phase timestamps");
   m.def("decode_attention_cluster", &decode_attention_cluster, py::arg("q"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("lengths"), py::arg("out"), py::arg("max_len"), py::arg("scale"),
         py::arg("pdl") = false,

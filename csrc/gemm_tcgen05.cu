@@ -81,7 +81,7 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kEpiWarps = 4;
 constexpr int kGroupM = 16;     // row blocks per rasterisation band
 constexpr int kCopyPpt = 4;     // all-gather copy CTAs: packs in flight per thread
-constexpr int kBulkPiece = 32 * 1024;  // all-gather bulk copy role: bytes per bulk copy (two stages)
+constexpr int kBulkPiece = 64 * 1024;  // all-gather bulk copy role: bytes per bulk copy (two stages)
 
 struct GemmParams {
   int M, N, K;

@@ -46,6 +46,7 @@ constexpr int kTileBytes = 2 * kHalfBytes;    // 32 KB
 constexpr int kQHalfBytes = kTcHeads * 128;   // 16 rows x 128 B
 constexpr int kPAtomBytes = kTcHeads * 128;   // 16 heads x 64 keys of P (bf16)
 constexpr int kErrorSlot = kCounterSlots - 1; // workspace int: nonzero after a wait ran out
+constexpr int kTcStamps = 10;                 // phase stamps per CTA (profiling)
 
 template <int T>
 struct TcLayout {  // byte offsets from the 1024-aligned base of dynamic shared memory
@@ -104,8 +105,17 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
     k_decode_attn_tc(const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v,
                      const __nv_bfloat16* __restrict__ q, const int* __restrict__ lengths,
                      __nv_bfloat16* __restrict__ out, int* counters, float* part_o, float* part_ml, int Hkv, int Lmax,
-                     float scale_log2) {
+                     float scale_log2, uint64_t* stamps) {
   static_assert(G >= 1 && G <= kTcHeads, "one KV head's query heads must fit the MMA's N");
+  // optional phase timing: thread 0 of each CTA records %globaltimer at kTcStamps points
+  auto stamp = [&](int i) {
+    if (stamps && threadIdx.x == 0) {
+      uint64_t now;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+      stamps[(size_t(blockIdx.y) * gridDim.x + blockIdx.x) * kTcStamps + i] = now;
+    }
+  };
+  stamp(0);  // entry
   using L = TcLayout<T>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -139,6 +149,7 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  stamp(1);  // barriers and TMEM ready
   const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   // q, the newest key / value row and the lengths are written by earlier kernels
@@ -176,6 +187,7 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
   const int ntiles = end > start ? (end - start + kTcKeys - 1) / kTcKeys : 0;  // <= issued
   fence_async_smem();
   __syncthreads();
+  stamp(2);  // loads issued, Q staged, length known
 
   float m_span[kTcHeads], l_span[kTcHeads];  // per head: span max (log2 units), sum
 #pragma unroll
@@ -193,6 +205,7 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
       tc::tc_fence_after();
       for (int i = 0; i < ntiles; ++i) {
         if (!tc::mbar_wait(&k_full[i], 0, bad)) break;
+        if (i == 0) stamp(3);  // first K tile landed
         tc::tc_fence_after();
         const uint8_t* kt = base + L::k + i * kTileBytes;
 #pragma unroll
@@ -206,6 +219,7 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
     }
     __syncwarp();
     bool ok = tc::mbar_wait(s_done, 0, bad);
+    stamp(4);  // scores in TMEM
     tc::tc_fence_after();
     // softmax: thread t owns key t of every tile
     float sc[T][kTcHeads];
@@ -250,6 +264,7 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
       for (int off = 16; off > 0; off >>= 1) l_span[g] += __shfl_xor_sync(0xffffffffu, l_span[g], off);
       if (lane == 0) red[4 * kTcHeads + warp * kTcHeads + g] = l_span[g];
     }
+    stamp(5);  // softmax done, P staged
     // V rows past the span may hold anything (another sequence, unwritten cache): zero
     // them, so that 0 * V stays 0 in the second product
     for (int i = 0; i < ntiles; ++i) {
@@ -292,6 +307,7 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
     if (!*bad && tc::mbar_wait(o_done, 0, bad)) {
       tc::tc_fence_after();
       tc::tmem_ld16(lane_base + kTcOutCol, o);  // thread t: dimension t, one column per head
+      stamp(6);  // output accumulator read
     }
   }
 
@@ -329,6 +345,7 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   if (t == 0) *last = atomicAdd(&counters[blockIdx.x], 1) == nsplit - 1;
   __syncthreads();
+  stamp(7);  // partial stored, counted
   if (!*last) return;
   __threadfence();
 
@@ -384,6 +401,7 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
     const float Ltot = stat[2 * g], inv = Ltot > 0.0f ? 1.0f / Ltot : 0.0f;
     out[(head0 + g) * kHead + t] = __float2bfloat16_rn(acc[g] * inv);
   }
+  stamp(8);  // merged
   if (t == 0) counters[blockIdx.x] = 0;
 }
 
@@ -436,7 +454,7 @@ template <int G, int T>
 static inline cudaError_t launch_tc_gt(const CUtensorMap& mk, const CUtensorMap& mv, const __nv_bfloat16* q,
                                        const int* lengths, __nv_bfloat16* out, int* counters, float* part_o,
                                        float* part_ml, int B, int Hkv, int Lmax, int nsplit, float scale_log2,
-                                       cudaStream_t st, bool pdl) {
+                                       cudaStream_t st, bool pdl, uint64_t* stamps) {
   auto kernel = k_decode_attn_tc<G, T>;
   static int attr_set[64] = {0};  // function attributes belong to each device's context
   int dev = 0;
@@ -456,14 +474,16 @@ static inline cudaError_t launch_tc_gt(const CUtensorMap& mk, const CUtensorMap&
   attr.val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = &attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, mk, mv, q, lengths, out, counters, part_o, part_ml, Hkv, Lmax, scale_log2);
+  return cudaLaunchKernelEx(&cfg, kernel, mk, mv, q, lengths, out, counters, part_o, part_ml, Hkv, Lmax, scale_log2,
+                            stamps);
 }
 
 // Launch over the shared workspace layout [kCounterSlots ints][part_o][part_ml].
 static inline cudaError_t launch_decode_attention_tc(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
                                                      const __nv_bfloat16* v_cache, const int* lengths,
                                                      __nv_bfloat16* out, float* scratch, int B, int Hq, int Hkv,
-                                                     int Lmax, int max_len, float scale, cudaStream_t st, bool pdl) {
+                                                     int Lmax, int max_len, float scale, cudaStream_t st, bool pdl,
+                                                     uint64_t* stamps = nullptr) {
   CUtensorMap mk, mv;
   if (!make_cache_map(&mk, k_cache, B, Lmax, Hkv) || !make_cache_map(&mv, v_cache, B, Lmax, Hkv))
     return cudaErrorInvalidValue;
@@ -475,7 +495,7 @@ static inline cudaError_t launch_decode_attention_tc(const __nv_bfloat16* q, con
 #define SN_TC(GG, TT)                                                                                            \
   if (G == GG && T == TT)                                                                                        \
     return launch_tc_gt<GG, TT>(mk, mv, q, lengths, out, counters, part_o, part_ml, B, Hkv, Lmax, nsplit, sl2, st, \
-                                pdl);
+                                pdl, stamps);
   SN_TC(1, 1) SN_TC(2, 1) SN_TC(4, 1) SN_TC(8, 1) SN_TC(16, 1)
   SN_TC(1, 2) SN_TC(2, 2) SN_TC(4, 2) SN_TC(8, 2) SN_TC(16, 2)
 #undef SN_TC
@@ -483,17 +503,21 @@ static inline cudaError_t launch_decode_attention_tc(const __nv_bfloat16* q, con
 }
 
 // The decode attention entry used by the torch op and the allocation-free C entry
-// point: the tensor-core kernel where it is eligible (impl 0 or 2), else the CUDA-core
-// kernel (impl 0 or 1).  impl 2 on an ineligible problem is cudaErrorNotSupported.
+// point.  impl 0 (default) and 1: the CUDA-core kernel; impl 2: the tensor-core kernel,
+// cudaErrorNotSupported where it is not eligible.  (The tensor-core kernel is correct
+// but measured slower than the CUDA-core one on the decode shapes -- 27 vs 11 us at
+// batch 8 x 1024 keys -- so it is not the default.)  `stamps` (impl 2 only): per-CTA
+// phase timestamps, kTcStamps each, or null.
 static inline cudaError_t launch_decode_attention(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
                                                   const __nv_bfloat16* v_cache, const int* lengths,
                                                   __nv_bfloat16* out, float* scratch, int B, int Hq, int Hkv,
                                                   int Lmax, int max_len, float scale, int sms, cudaStream_t st,
-                                                  bool pdl = false, int impl = 0) {
-  if (impl != 1 && tc_eligible(q, k_cache, v_cache, B, Hq, Hkv, Lmax, max_len))
+                                                  bool pdl = false, int impl = 0, uint64_t* stamps = nullptr) {
+  if (impl == 2) {
+    if (!tc_eligible(q, k_cache, v_cache, B, Hq, Hkv, Lmax, max_len)) return cudaErrorNotSupported;
     return launch_decode_attention_tc(q, k_cache, v_cache, lengths, out, scratch, B, Hq, Hkv, Lmax, max_len, scale,
-                                      st, pdl);
-  if (impl == 2) return cudaErrorNotSupported;
+                                      st, pdl, stamps);
+  }
   return launch_decode_attention_simt(q, k_cache, v_cache, lengths, out, scratch, B, Hq, Hkv, Lmax, max_len, scale,
                                       sms, st, pdl);
 }

@@ -205,8 +205,11 @@ class _StatusView:
 # sustains ~9 TFLOP/s per SM in bf16 (1354.8 TFLOP/s over 148 SMs) and ~10.7 in
 # block-scaled fp8.
 PUSH_GBS_PER_CTA = 20.0
-PUSH_GBS_PER_BULK_CTA = 80.0   # the bulk-copy role: one thread per CTA drives the copy engine
-MIN_BULK_COPY_CTAS = 4
+# the bulk-copy role (one thread per CTA drives the SM's copy engine): measured with the
+# microbenchmark's bulk mode on 2 B200s, 64 KB pieces: 39-41 GB/s for one CTA, 543 GB/s
+# for 16 (P2P stores from 512 threads: 29-30 GB/s and 422 GB/s)
+PUSH_GBS_PER_BULK_CTA = 34.0
+MIN_BULK_COPY_CTAS = 8
 MIN_COPY_CTAS = 16        # fewer measured slower at TP2 and TP8 on every prefill shape
 BF16_GEMM_TFLOPS_PER_SM = 9.0
 FP8_GEMM_TFLOPS_PER_SM = 10.7
