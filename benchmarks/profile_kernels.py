@@ -246,16 +246,16 @@ def main() -> int:
         if args.stamps and args.impl == 2 and not args.cluster:
             # one cold launch with per-CTA phase stamps (tensor-core kernel)
             nsplit = -(-Lmax // (128 if Lmax <= 64 * 128 else 256))
-            st = torch.zeros(B * Hkv * nsplit * 10, dtype=torch.int64, device=device)
+            st = torch.zeros(B * Hkv * nsplit * 12, dtype=torch.int64, device=device)
             flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
             flush.fill_(1)
             torch.cuda.synchronize(device)
             C.decode_attention(q, k, v, lengths, out, ws, Lmax, D ** -0.5, False, 2, st)
             torch.cuda.synchronize(device)
-            t = st.view(-1, 10).double().cpu() / 1000.0
+            t = st.view(-1, 12).double().cpu() / 1000.0
             t0 = t[:, 0].min()
             names = ["entry", "setup", "issue_q_len", "first_k", "scores", "softmax", "output", "partial_count",
-                     "merge"]
+                     "merge_ml", "merge_weights", "merge_sum", "merge_out"]
             phases = {}
             prev = None
             for i, n in enumerate(names):

@@ -255,7 +255,7 @@ void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::
   if (stamps.has_value() &&
       (impl != 2 || stamps->scalar_type() != at::kLong || !stamps->is_contiguous() ||
        size_t(stamps->numel()) < size_t(B) * Hkv * std::max(1, sn::attn::tc_splits(max_len)) * sn::attn::kTcStamps))
-    throw std::invalid_argument("stamps: impl 2 and a contiguous int64 tensor of (grid CTAs x 10) entries");
+    throw std::invalid_argument("stamps: impl 2 and a contiguous int64 tensor of (grid CTAs x 12) entries");
   cudaError_t e = sn::attn::launch_decode_attention(
       reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr()),
       reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr()), lengths.data_ptr<int>(),
@@ -349,7 +349,7 @@ void register_decode(py::module_& m) {
         py::arg("impl") = 0, py::arg("stamps") = py::none(),
         "split-KV decode attention; pdl: programmatic dependent launch (the kernel waits for the previous one "
         "before it reads q, K/V or lengths); impl: 0 or 1 CUDA cores, 2 tensor cores (or an error where not "
-        "eligible); stamps (impl 2): int64 tensor of grid x 10 phase timestamps");
+        "eligible); stamps (impl 2): int64 tensor of grid x 12 phase timestamps");
   m.def("decode_attention_cluster", &decode_attention_cluster, py::arg("q"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("lengths"), py::arg("out"), py::arg("max_len"), py::arg("scale"),
         py::arg("pdl") = false,

@@ -46,7 +46,7 @@ constexpr int kTileBytes = 2 * kHalfBytes;    // 32 KB
 constexpr int kQHalfBytes = kTcHeads * 128;   // 16 rows x 128 B
 constexpr int kPAtomBytes = kTcHeads * 128;   // 16 heads x 64 keys of P (bf16)
 constexpr int kErrorSlot = kCounterSlots - 1; // workspace int: nonzero after a wait ran out
-constexpr int kTcStamps = 10;                 // phase stamps per CTA (profiling)
+constexpr int kTcStamps = 12;                 // phase stamps per CTA (profiling)
 
 template <int T>
 struct TcLayout {  // byte offsets from the 1024-aligned base of dynamic shared memory
@@ -360,6 +360,7 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
     ml[2 * i + 1] = v.y;
   }
   __syncthreads();
+  stamp(8);  // merge: (max, sum) pairs loaded
   if (t < G) {
     float M = -INFINITY;
     for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, ml[2 * (t * nsplit + sp)]);
@@ -373,6 +374,7 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
     stat[2 * t] = Ltot;
   }
   __syncthreads();
+  stamp(9);  // merge: weights formed
   // the partial outputs of every (head, span) pair, kBatch loads in flight before any
   // is used: one L2 round trip per kBatch pairs, not one per head
   constexpr int kBatch = 64;
@@ -396,12 +398,13 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
       }
     }
   }
+  stamp(10);  // merge: partial outputs summed
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     const float Ltot = stat[2 * g], inv = Ltot > 0.0f ? 1.0f / Ltot : 0.0f;
     out[(head0 + g) * kHead + t] = __float2bfloat16_rn(acc[g] * inv);
   }
-  stamp(8);  // merged
+  stamp(11);  // merged
   if (t == 0) counters[blockIdx.x] = 0;
 }
 
