@@ -217,10 +217,11 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
 
   // Every DSMEM load of an output element is issued before the fixed-order sum.
   if (p.mode == 0) {
-    // this CTA's rows: r = split, split + S, ...; thread -> (row, column) pairs
+    // this CTA's rows: r = split, split + S, ...; thread -> (row, token) pairs with the row
+    // fastest, so a warp's stores of one token row are contiguous in Y
     const int my_rows = (kWRows - split + S - 1) / S;
     for (int e = threadIdx.x; e < my_rows * p.M; e += blockDim.x) {
-      const int r = split + (e / p.M) * S, m = e % p.M;
+      const int r = split + (e % my_rows) * S, m = e / my_rows;  // neighbouring threads: neighbouring rows
       const int n = tile * kWRows + r;
       float v[kMaxSplits];
 #pragma unroll
@@ -234,7 +235,7 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
     // one head per tile: rows r and r + 64 form a RoPE pair
     const int my_rows = (64 - split + S - 1) / S;
     for (int e = threadIdx.x; e < my_rows * p.M; e += blockDim.x) {
-      const int r = split + (e / p.M) * S, m = e % p.M;
+      const int r = split + (e % my_rows) * S, m = e / my_rows;  // neighbouring threads: neighbouring rows
       float va[kMaxSplits], vb[kMaxSplits];
 #pragma unroll
       for (int s = 0; s < kMaxSplits; ++s) {
@@ -322,7 +323,7 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
     // SwiGLU: rows 0..63 gate, 64..127 up of the same 64 features
     const int my_rows = (64 - split + S - 1) / S;
     for (int e = threadIdx.x; e < my_rows * p.M; e += blockDim.x) {
-      const int r = split + (e / p.M) * S, m = e % p.M;
+      const int r = split + (e % my_rows) * S, m = e / my_rows;  // neighbouring threads: neighbouring rows
       float vg[kMaxSplits], vu[kMaxSplits];
 #pragma unroll
       for (int s = 0; s < kMaxSplits; ++s) {
