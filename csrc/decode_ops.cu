@@ -348,8 +348,9 @@ void register_decode(py::module_& m) {
         py::arg("out"), py::arg("workspace"), py::arg("max_len"), py::arg("scale"), py::arg("pdl") = false,
         py::arg("impl") = 0, py::arg("stamps") = py::none(),
         "split-KV decode attention; pdl: programmatic dependent launch (the kernel waits for the previous one "
-        "before it reads q, K/V or lengths); impl: 0 or 1 CUDA cores, 2 tensor cores (or an error where not "
-        "eligible); stamps (impl 2): int64 tensor of grid x 12 phase timestamps");
+        "before it reads q, K/V or lengths); impl: 0 tensor cores for 32 or more (sequence, KV head) pairs where "
+        "eligible, else CUDA cores; 1 CUDA cores; 2 tensor cores (or an error where not eligible); stamps (impl 2): "
+        "int64 tensor of grid x 12 phase timestamps");
   m.def("decode_attention_cluster", &decode_attention_cluster, py::arg("q"), py::arg("k_cache"),
         py::arg("v_cache"), py::arg("lengths"), py::arg("out"), py::arg("max_len"), py::arg("scale"),
         py::arg("pdl") = false,

@@ -217,11 +217,10 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
 
   // Every DSMEM load of an output element is issued before the fixed-order sum.
   if (p.mode == 0) {
-    // this CTA's rows: r = split, split + S, ...; thread -> (row, token) pairs with the row
-    // fastest, so a warp's stores of one token row are contiguous in Y
+    // this CTA's rows: r = split, split + S, ...; thread -> (row, column) pairs
     const int my_rows = (kWRows - split + S - 1) / S;
     for (int e = threadIdx.x; e < my_rows * p.M; e += blockDim.x) {
-      const int r = split + (e % my_rows) * S, m = e / my_rows;  // neighbouring threads: neighbouring rows
+      const int r = split + (e / p.M) * S, m = e % p.M;
       const int n = tile * kWRows + r;
       float v[kMaxSplits];
 #pragma unroll
@@ -235,7 +234,7 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
     // one head per tile: rows r and r + 64 form a RoPE pair
     const int my_rows = (64 - split + S - 1) / S;
     for (int e = threadIdx.x; e < my_rows * p.M; e += blockDim.x) {
-      const int r = split + (e % my_rows) * S, m = e / my_rows;  // neighbouring threads: neighbouring rows
+      const int r = split + (e / p.M) * S, m = e % p.M;
       float va[kMaxSplits], vb[kMaxSplits];
 #pragma unroll
       for (int s = 0; s < kMaxSplits; ++s) {
@@ -323,7 +322,10 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
     // SwiGLU: rows 0..63 gate, 64..127 up of the same 64 features
     const int my_rows = (64 - split + S - 1) / S;
     for (int e = threadIdx.x; e < my_rows * p.M; e += blockDim.x) {
-      const int r = split + (e % my_rows) * S, m = e / my_rows;  // neighbouring threads: neighbouring rows
+      // without split-K a warp's 32 rows of one token are contiguous in Y and conflict-free
+      // in the parked partial; with split-K neighbouring tokens of one row are
+      const bool row_fast = S == 1;
+      const int r = split + (row_fast ? e % my_rows : e / p.M) * S, m = row_fast ? e / my_rows : e % p.M;
       float vg[kMaxSplits], vu[kMaxSplits];
 #pragma unroll
       for (int s = 0; s < kMaxSplits; ++s) {

@@ -512,21 +512,26 @@ static inline cudaError_t launch_decode_attention_tc(const __nv_bfloat16* q, con
 }
 
 // The decode attention entry used by the torch op and the allocation-free C entry
-// point.  impl 0 (default) and 1: the CUDA-core kernel; impl 2: the tensor-core kernel,
-// cudaErrorNotSupported where it is not eligible.  (The tensor-core kernel is correct
-// but measured slower than the CUDA-core one on the decode shapes -- 27 vs 11 us at
-// batch 8 x 1024 keys -- so it is not the default.)  `stamps` (impl 2 only): per-CTA
-// phase timestamps, kTcStamps each, or null.
+// point.  impl 0 (default): the tensor-core kernel where it is eligible and there are at
+// least kTcMinPairs (sequence, KV head) pairs, else the CUDA-core kernel; impl 1: the
+// CUDA-core kernel; impl 2: the tensor-core kernel, cudaErrorNotSupported where it is not
+// eligible.  Measured on one B200, 1024 keys, 8 query heads per KV head (graph-timed µs,
+// tensor cores / CUDA cores): batch 1: 12.7 / 10.3, batch 8: 13.4 / 11.4, batch 64:
+// 19.7 / 28.8 -- the tensor-core kernel's fixed cost (span merge) outweighs its faster
+// math on few pairs.  `stamps` (tensor-core kernel only): per-CTA phase timestamps,
+// kTcStamps each, or null.
+constexpr int kTcMinPairs = 32;
+
 static inline cudaError_t launch_decode_attention(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
                                                   const __nv_bfloat16* v_cache, const int* lengths,
                                                   __nv_bfloat16* out, float* scratch, int B, int Hq, int Hkv,
                                                   int Lmax, int max_len, float scale, int sms, cudaStream_t st,
                                                   bool pdl = false, int impl = 0, uint64_t* stamps = nullptr) {
-  if (impl == 2) {
-    if (!tc_eligible(q, k_cache, v_cache, B, Hq, Hkv, Lmax, max_len)) return cudaErrorNotSupported;
+  const bool tc = impl == 2 || (impl == 0 && B * Hkv >= kTcMinPairs);
+  if (tc && tc_eligible(q, k_cache, v_cache, B, Hq, Hkv, Lmax, max_len))
     return launch_decode_attention_tc(q, k_cache, v_cache, lengths, out, scratch, B, Hq, Hkv, Lmax, max_len, scale,
                                       st, pdl, stamps);
-  }
+  if (impl == 2) return cudaErrorNotSupported;
   return launch_decode_attention_simt(q, k_cache, v_cache, lengths, out, scratch, B, Hq, Hkv, Lmax, max_len, scale,
                                       sms, st, pdl);
 }
