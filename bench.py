@@ -60,8 +60,8 @@ def parse_args(argv=None):
     p.add_argument("--batch", type=int, default=8, help="decode: sequences per step")
     p.add_argument("--fuse-gemm-ar", action="store_true",
                    help="decode: the O / down GEMM epilogues push into the all-reduce (NVLink arm)")
-    p.add_argument("--attention", choices=("split", "cluster"), default="split",
-                   help="decode: span merge through a workspace (split) or a thread-block cluster")
+    p.add_argument("--attention", choices=("auto", "simt", "tcgen05"), default="auto",
+                   help="decode: attention kernel (auto: tensor cores from 32 sequence-head pairs)")
     p.add_argument("--layers", type=int, default=80, help="decode: decoder layers")
     p.add_argument("--fused-norm-tokens", type=int, nargs="*", default=[1, 8, 32, 128, 256],
                    help="ours: also time the fused all-reduce + residual + RMSNorm at these token counts "

@@ -33,7 +33,7 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--graph", action="store_true", help="time graph replays instead of eager steps")
     ap.add_argument("--gemm", choices=["sparknet", "cublas"], default="sparknet")
-    ap.add_argument("--attention", choices=["split", "cluster"], default="split")
+    ap.add_argument("--attention", choices=["auto", "simt", "tcgen05"], default="auto")
     args = ap.parse_args()
     t = args.tp
     cfg = LlamaConfig(hidden=8192, layers=args.layers, heads=64 // t, kv_heads=max(1, 8 // t), head_dim=128,

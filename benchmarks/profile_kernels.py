@@ -113,7 +113,6 @@ def main() -> int:
     ap.add_argument("--tune", type=int, default=0, metavar="CTAS_PER_SM",
                     help="decode_gemm: skinny_tune(ctas_per_sm) before running (0 = default)")
     ap.add_argument("--pdl", action="store_true", help="decode_gemm: programmatic dependent launch")
-    ap.add_argument("--cluster", action="store_true", help="attention: spans merged in a thread-block cluster")
     ap.add_argument("--impl", type=int, default=0, choices=(0, 1, 2),
                     help="attention: 0 tensor cores where eligible, 1 CUDA cores, 2 tensor cores")
     ap.add_argument("--stamps", action="store_true",
@@ -238,12 +237,9 @@ def main() -> int:
         sms = torch.cuda.get_device_properties(device).multi_processor_count
         ws = torch.zeros(C.attention_workspace_floats(B, Hq, Hkv, Lmax, sms), dtype=torch.float32, device=device)
         def attend(kk, vv):
-            if args.cluster:
-                C.decode_attention_cluster(q, kk, vv, lengths, out, Lmax, D ** -0.5)
-            else:
-                C.decode_attention(q, kk, vv, lengths, out, ws, Lmax, D ** -0.5, False, args.impl)
+            C.decode_attention(q, kk, vv, lengths, out, ws, Lmax, D ** -0.5, False, args.impl)
 
-        if args.stamps and args.impl == 2 and not args.cluster:
+        if args.stamps and args.impl == 2:
             # one cold launch with per-CTA phase stamps (tensor-core kernel)
             nsplit = -(-Lmax // (128 if Lmax <= 64 * 128 else 256))
             st = torch.zeros(B * Hkv * nsplit * 12, dtype=torch.int64, device=device)
@@ -279,7 +275,7 @@ def main() -> int:
         fns = [lambda kk=kk, vv=vv: attend(kk, vv) for kk, vv in kvs]
         row["graph_us"] = _time_graph(fns, 20, device)
         row.update(batch=B, heads=Hq, kv_heads=Hkv, length=L, kv_bytes=kv_bytes, copies=copies,
-                   variant="cluster" if args.cluster else {0: "auto", 1: "simt", 2: "tcgen05"}[args.impl])
+                   variant={0: "auto", 1: "simt", 2: "tcgen05"}[args.impl])
     med = statistics.median(samples)
     row.update(median_us=med, min_us=min(samples), iters=len(samples))
     if "bytes_per_rank" in row:

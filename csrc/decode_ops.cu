@@ -265,30 +265,6 @@ void decode_attention(const at::Tensor& q, const at::Tensor& k_cache, const at::
   if (e != cudaSuccess) throw std::runtime_error(std::string("decode_attention launch: ") + cudaGetErrorString(e));
 }
 
-// The cluster variant (attention_kernels.cuh k_decode_attn_cluster): the spans of one
-// (sequence, KV head) form a thread-block cluster and merge through distributed shared
-// memory, so it needs no workspace.
-void decode_attention_cluster(const at::Tensor& q, const at::Tensor& k_cache, const at::Tensor& v_cache,
-                              const at::Tensor& lengths, at::Tensor& out, int max_len, double scale, bool pdl) {
-  check_bf16(q, "q");
-  check_bf16(out, "out");
-  int B = int(q.size(0)), Hq = int(q.size(1)), Hkv = int(k_cache.size(2)), Lmax = int(k_cache.size(1));
-  if (q.size(2) != kHead) throw std::invalid_argument("head_dim must be 128");
-  if (Hq % Hkv) throw std::invalid_argument("query heads must be a multiple of KV heads");
-  int G = Hq / Hkv;
-  if (G != 1 && G != 2 && G != 4 && G != 8 && G != 16) throw std::invalid_argument("unsupported GQA group size");
-  if (max_len > Lmax || max_len <= 0) throw std::invalid_argument("max_len must be in 1..cache length");
-  c10::cuda::CUDAGuard guard(q.device());
-  int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
-  cudaError_t e = sn::attn::launch_decode_attention_cluster(
-      reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr()),
-      reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr()), lengths.data_ptr<int>(),
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), B, Hq, Hkv, Lmax, max_len, float(scale), sms, stream_of(q),
-      pdl);
-  if (e != cudaSuccess)
-    throw std::runtime_error(std::string("decode_attention_cluster launch: ") + cudaGetErrorString(e));
-}
-
 size_t attention_workspace_floats(int B, int Hq, int Hkv, int max_len, int sms) {
   return sn::attn::scratch_floats(B, Hq, Hkv, max_len, sms);
 }
@@ -351,11 +327,6 @@ void register_decode(py::module_& m) {
         "before it reads q, K/V or lengths); impl: 0 tensor cores for 32 or more (sequence, KV head) pairs where "
         "eligible, else CUDA cores; 1 CUDA cores; 2 tensor cores (or an error where not eligible); stamps (impl 2): "
         "int64 tensor of grid x 12 phase timestamps");
-  m.def("decode_attention_cluster", &decode_attention_cluster, py::arg("q"), py::arg("k_cache"),
-        py::arg("v_cache"), py::arg("lengths"), py::arg("out"), py::arg("max_len"), py::arg("scale"),
-        py::arg("pdl") = false,
-        "split-KV decode attention whose spans merge in a thread-block cluster (no workspace); pdl as for "
-        "decode_attention");
   m.def("attention_workspace_floats", &attention_workspace_floats);
   m.def("add_rmsnorm", &add_rmsnorm, py::arg("x"), py::arg("residual"), py::arg("residual_out"), py::arg("gamma"),
         py::arg("out"), py::arg("eps"));

@@ -3,7 +3,6 @@
 // (attention_noalloc.cu).  One query token per sequence; head_dim 128.
 #pragma once
 
-#include <cooperative_groups.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -366,338 +365,6 @@ static inline cudaError_t launch_decode_attention_simt(const __nv_bfloat16* q, c
     default:
       return cudaErrorInvalidValue;
   }
-}
-
-// ---------------------------------------------------------------------------
-// Cluster split-KV decode attention.  grid (S, B * Hkv), cluster (S, 1, 1), block 256,
-// S = 8 or 16.  The S spans of one (sequence, KV head) are the S CTAs of one
-// thread-block cluster.  Each CTA keeps NT tiles of K and V in flight (a ring of NT
-// buffers in dynamic shared memory, so a span of up to NT * 32 keys costs one memory
-// latency), parks its unnormalised output and (max, sum) in its own shared memory, and
-// after a cluster barrier the cluster merges the S spans through distributed shared
-// memory in span order.  Compared with k_decode_attn there is no workspace, no
-// counter, no global round trip between the spans and the merge.  Scores are in log2
-// units; the score and P V phases are those of k_decode_attn.
-// ---------------------------------------------------------------------------
-constexpr int kClusterNT = 4;  // tiles in flight per CTA
-
-template <int G, int NT>
-struct ClusterSmem {  // every array 16-byte aligned (vector accesses), whatever G is
-  alignas(16) float qs[G][kHead];
-  alignas(16) __nv_bfloat16 kt[NT][kTile][kRowPad];
-  alignas(16) __nv_bfloat16 vt[NT][kTile][kRowPad];
-  alignas(16) float ps[G][kTile];
-  alignas(16) float corr[G];
-  alignas(16) float po[G][kHead];  // this span's unnormalised output, read by the cluster's merge
-  alignas(16) float pml[G][2];     // this span's (max, sum)
-};
-
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-template <int G, int S, int NT>
-static __global__ void __launch_bounds__(kAttnThreads) k_decode_attn_cluster(
-    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k_cache,
-    const __nv_bfloat16* __restrict__ v_cache, const int* __restrict__ lengths, __nv_bfloat16* __restrict__ out,
-    int Hkv, int Lmax, int chunk, float scale_log2) {
-  namespace cg = cooperative_groups;
-  constexpr int kHW = (G + 7) / 8;  // heads per warp in the score phase
-  constexpr int kHT = (G + 3) / 4;  // heads per thread in the P V phase
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  ClusterSmem<G, NT>& sm = *reinterpret_cast<ClusterSmem<G, NT>*>(smem_raw);
-  cg::cluster_group cluster = cg::this_cluster();
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // a PDL-launched successor may start early
-  // The merge reads S CTAs' shared memory: a launch that arrives without its S-CTA
-  // cluster (re-issued by a tool without the attribute) must not touch it.  Every CTA
-  // returns before any access; the output rows keep their previous contents.
-  if (cluster.num_blocks() != unsigned(S)) return;
-  const int s = blockIdx.x, b = blockIdx.y / Hkv, h = blockIdx.y % Hkv;
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const int dp = t & 63, hg = t >> 6;
-  const int Hq = G * Hkv;
-  const int len = min(lengths[b], Lmax);
-  const int start = s * chunk, end = min(start + chunk, len);
-  const int ntiles = end > start ? (end - start + kTile - 1) / kTile : 0;
-  const size_t row_stride = size_t(Hkv) * kHead;
-  const __nv_bfloat16* kbase = k_cache + (size_t(b) * Lmax * Hkv + h) * kHead;
-  const __nv_bfloat16* vbase = v_cache + (size_t(b) * Lmax * Hkv + h) * kHead;
-
-  // one tile = 32 keys x 256 bytes of K and of V, 4 copies of 16 bytes per thread each;
-  // one commit group per tile (possibly empty), so NT groups are always outstanding
-  auto issue = [&](int tile_idx) {
-    if (tile_idx < ntiles) {
-      const int k0 = start + tile_idx * kTile, buf = tile_idx % NT;
-#pragma unroll
-      for (int r = 0; r < (kTile * kHead / 8) / kAttnThreads; ++r) {
-        const int i = r * kAttnThreads + t, key = i / (kHead / 8), c = i % (kHead / 8);
-        const bool valid = k0 + key < end;
-        const size_t off = size_t(valid ? k0 + key : start) * row_stride + c * 8;
-        cp_async16(&sm.kt[buf][key][c * 8], kbase + off, valid);
-        cp_async16(&sm.vt[buf][key][c * 8], vbase + off, valid);
-      }
-    }
-    cp_async_commit();
-  };
-  // Programmatic dependent launch: the leading tiles wholly below the newest key (the
-  // one the preceding kernel writes) are requested before griddepcontrol.wait.
-  int pre = 0;
-  while (pre < NT && pre < ntiles && start + (pre + 1) * kTile <= len - 1) issue(pre++);
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  for (int i = pre; i < NT; ++i) issue(i);
-  for (int i = t; i < G * kHead; i += kAttnThreads) {
-    const int g = i / kHead, d = i % kHead;
-    sm.qs[g][d] = bf(q[(size_t(b) * Hq + h * G + g) * kHead + d]) * scale_log2;
-  }
-  float m[kHW], l[kHW];
-#pragma unroll
-  for (int j = 0; j < kHW; ++j) {
-    m[j] = -INFINITY;
-    l[j] = 0.0f;
-  }
-  float2 acc[kHT];
-#pragma unroll
-  for (int i = 0; i < kHT; ++i) acc[i] = make_float2(0.0f, 0.0f);
-
-  for (int it = 0; it < ntiles; ++it) {
-    const int buf = it % NT;
-    const int nk = min(kTile, end - (start + it * kTile));
-    cp_async_wait<NT - 1>();  // tile `it` has landed (groups complete in order)
-    __syncthreads();
-    if (warp < G) {
-      float dot[kHW];
-#pragma unroll
-      for (int j = 0; j < kHW; ++j) dot[j] = 0.0f;
-#pragma unroll
-      for (int c = 0; c < kHead / 8; ++c) {
-        const uint4 kv = *reinterpret_cast<const uint4*>(&sm.kt[buf][lane][c * 8]);
-        const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kv);
-        float kf[8];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __bfloat1622float2(k2[e]);
-          kf[2 * e] = f.x;
-          kf[2 * e + 1] = f.y;
-        }
-#pragma unroll
-        for (int j = 0; j < kHW; ++j) {
-          const int g = warp + 8 * j;
-          if (g < G) {
-            const float4 qa = *reinterpret_cast<const float4*>(&sm.qs[g][c * 8]);
-            const float4 qb = *reinterpret_cast<const float4*>(&sm.qs[g][c * 8 + 4]);
-            dot[j] += qa.x * kf[0] + qa.y * kf[1] + qa.z * kf[2] + qa.w * kf[3] + qb.x * kf[4] + qb.y * kf[5] +
-                      qb.z * kf[6] + qb.w * kf[7];
-          }
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < kHW; ++j) {
-        const int g = warp + 8 * j;
-        if (g < G) {
-          const float sc = lane < nk ? dot[j] : -INFINITY;
-          float tmax = sc;
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, o));
-          const float mnew = fmaxf(m[j], tmax);
-          const float pr = lane < nk ? exp2f(sc - mnew) : 0.0f;
-          float psum = pr;
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
-          const float cf = exp2f(m[j] - mnew);
-          l[j] = l[j] * cf + psum;
-          m[j] = mnew;
-          sm.ps[g][lane] = pr;
-          if (lane == 0) sm.corr[g] = cf;
-        }
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int i = 0; i < kHT; ++i) {
-      const int g = hg + 4 * i;
-      if (g < G) {
-        const float cf = sm.corr[g];
-        acc[i].x *= cf;
-        acc[i].y *= cf;
-      }
-    }
-    for (int key = 0; key < nk; ++key) {
-      const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sm.vt[buf][key][2 * dp]));
-#pragma unroll
-      for (int i = 0; i < kHT; ++i) {
-        const int g = hg + 4 * i;
-        if (g < G) {
-          const float pr = sm.ps[g][key];
-          acc[i].x = fmaf(pr, v.x, acc[i].x);
-          acc[i].y = fmaf(pr, v.y, acc[i].y);
-        }
-      }
-    }
-    __syncthreads();  // buffer `buf`, ps and corr are free again
-    issue(it + NT);
-  }
-  asm volatile("cp.async.wait_all;" ::: "memory");
-
-  // park this span's partial, then merge the cluster's spans in span order
-  if (warp < G && lane == 0) {
-#pragma unroll
-    for (int j = 0; j < kHW; ++j) {
-      const int g = warp + 8 * j;
-      if (g < G) {
-        sm.pml[g][0] = m[j];
-        sm.pml[g][1] = l[j];
-      }
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < kHT; ++i) {
-    const int g = hg + 4 * i;
-    if (g < G) *reinterpret_cast<float2*>(&sm.po[g][2 * dp]) = acc[i];
-  }
-  cluster.sync();  // every span's partial is parked and visible to the cluster
-  const size_t head0 = size_t(b) * Hq + h * G;
-  for (int idx = s * kAttnThreads + t; idx < G * (kHead / 2); idx += S * kAttnThreads) {
-    const int g = idx / (kHead / 2), d2 = idx % (kHead / 2);
-    float mx[S], ls[S];
-    float2 ov[S];
-#pragma unroll
-    for (int r = 0; r < S; ++r) {  // every remote load issued before any is used
-      const ClusterSmem<G, NT>* peer = cluster.map_shared_rank(&sm, r);
-      mx[r] = peer->pml[g][0];
-      ls[r] = peer->pml[g][1];
-      ov[r] = *reinterpret_cast<const float2*>(&peer->po[g][2 * d2]);
-    }
-    float M = -INFINITY;
-#pragma unroll
-    for (int r = 0; r < S; ++r) M = fmaxf(M, mx[r]);
-    float L = 0.0f;
-    float2 o = make_float2(0.0f, 0.0f);
-#pragma unroll
-    for (int r = 0; r < S; ++r) {
-      const float w = ls[r] > 0.0f ? exp2f(mx[r] - M) : 0.0f;
-      L += ls[r] * w;
-      o.x += ov[r].x * w;
-      o.y += ov[r].y * w;
-    }
-    const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-    *reinterpret_cast<__nv_bfloat162*>(out + (head0 + g) * kHead + 2 * d2) = __floats2bfloat162_rn(o.x * inv, o.y * inv);
-  }
-  cluster.sync();  // partials stay readable until every CTA of the cluster is done
-}
-
-// Cluster size for B * Hkv clusters: 16 spans while that keeps the grid within two
-// waves of the SMs, else 8.
-static inline int cluster_spans(int B, int Hkv, int sms) { return B * Hkv * 16 <= 2 * sms ? 16 : 8; }
-
-// Whether clusters of 16 CTAs of this kernel can be scheduled at all on the current
-// device (the answer depends on the GPU's partitioning): asked once per device.
-template <int G>
-static inline bool cluster16_fits() {
-  static int answer[64] = {0};  // 0 unknown, 1 fits, 2 does not
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return false;
-  if (dev >= 0 && dev < 64 && answer[dev]) return answer[dev] == 1;
-  auto kernel = k_decode_attn_cluster<G, 16, kClusterNT>;
-  const int smem = int(sizeof(ClusterSmem<G, kClusterNT>));
-  bool fits = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess &&
-              cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
-  if (fits) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(16, 1, 1);
-    cfg.blockDim = dim3(kAttnThreads, 1, 1);
-    cfg.dynamicSmemBytes = size_t(smem);
-    cudaLaunchAttribute attr;
-    attr.id = cudaLaunchAttributeClusterDimension;
-    attr.val.clusterDim.x = 16;
-    attr.val.clusterDim.y = 1;
-    attr.val.clusterDim.z = 1;
-    cfg.attrs = &attr;
-    cfg.numAttrs = 1;
-    int clusters = 0;
-    fits = cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) == cudaSuccess && clusters > 0;
-  }
-  (void)cudaGetLastError();  // clear the error a refused query may leave behind
-  if (dev >= 0 && dev < 64) answer[dev] = fits ? 1 : 2;
-  return fits;
-}
-
-template <int G, int S>
-static inline cudaError_t launch_cluster_g(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
-                                           const __nv_bfloat16* v_cache, const int* lengths, __nv_bfloat16* out,
-                                           int B, int Hkv, int Lmax, int chunk, float scale_log2, cudaStream_t st,
-                                           bool pdl) {
-  auto kernel = k_decode_attn_cluster<G, S, kClusterNT>;
-  const int smem = int(sizeof(ClusterSmem<G, kClusterNT>));
-  // function attributes belong to each device's context: set once per device (the
-  // first call, which is an eager one before any graph capture)
-  static int attr_done[64] = {0};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64 || !attr_done[dev]) {
-    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e == cudaSuccess && S > 8) e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) attr_done[dev] = 1;
-  }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(S, B * Hkv, 1);
-  cfg.blockDim = dim3(kAttnThreads, 1, 1);
-  cfg.dynamicSmemBytes = size_t(smem);
-  cfg.stream = st;
-  cudaLaunchAttribute attrs[2];
-  attrs[0].id = cudaLaunchAttributeClusterDimension;
-  attrs[0].val.clusterDim.x = S;
-  attrs[0].val.clusterDim.y = 1;
-  attrs[0].val.clusterDim.z = 1;
-  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attrs[1].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
-  cfg.attrs = attrs;
-  cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, kernel, q, k_cache, v_cache, lengths, out, Hkv, Lmax, chunk, scale_log2);
-}
-
-// The cluster variant: no workspace.  Returns the launch's error (cudaErrorInvalidValue
-// for an unsupported group size).
-static inline cudaError_t launch_decode_attention_cluster(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
-                                                          const __nv_bfloat16* v_cache, const int* lengths,
-                                                          __nv_bfloat16* out, int B, int Hq, int Hkv, int Lmax,
-                                                          int max_len, float scale, int sms, cudaStream_t st,
-                                                          bool pdl = false) {
-  if (Hkv <= 0 || Hq % Hkv || B <= 0 || max_len <= 0 || B * Hkv > 65535) return cudaErrorInvalidValue;
-  const int G = Hq / Hkv;
-  int S = cluster_spans(B, Hkv, sms);
-  if (S == 16) {
-    bool fits = false;
-    switch (G) {
-      case 1: fits = cluster16_fits<1>(); break;
-      case 2: fits = cluster16_fits<2>(); break;
-      case 4: fits = cluster16_fits<4>(); break;
-      case 8: fits = cluster16_fits<8>(); break;
-      case 16: fits = cluster16_fits<16>(); break;
-      default: return cudaErrorInvalidValue;
-    }
-    if (!fits) S = 8;  // portable cluster size
-  }
-  const int chunk = ((max_len + S - 1) / S + kTile - 1) / kTile * kTile;
-  const float scale_log2 = scale * kLog2e;
-#define SN_ATC(GG)                                                                                              \
-  case GG:                                                                                                      \
-    return S == 16 ? launch_cluster_g<GG, 16>(q, k_cache, v_cache, lengths, out, B, Hkv, Lmax, chunk, scale_log2, \
-                                              st, pdl)                                                          \
-                   : launch_cluster_g<GG, 8>(q, k_cache, v_cache, lengths, out, B, Hkv, Lmax, chunk, scale_log2,  \
-                                             st, pdl);
-  switch (G) {
-    SN_ATC(1)
-    SN_ATC(2)
-    SN_ATC(4)
-    SN_ATC(8)
-    SN_ATC(16)
-    default:
-      return cudaErrorInvalidValue;
-  }
-#undef SN_ATC
 }
 
 }  // namespace attn

@@ -46,7 +46,7 @@ def run_decode_bench(args, rank, world, device, cpu_group):
         runtime.prepare((torch.bfloat16,))
     t0 = time.perf_counter()
     model = TPLlama(cfg, rank=rank, world=world, device=device, batch=batch, max_len=max_len, comm=comm,
-                    runtime=runtime, group=None, attention=getattr(args, "attention", "split"),
+                    runtime=runtime, group=None, attention=getattr(args, "attention", "auto"),
                     fuse_gemm_ar=getattr(args, "fuse_gemm_ar", False))
     model.fill_prompt_cache(PROMPT)
     torch.cuda.synchronize()

@@ -30,6 +30,7 @@ import torch
 import torch.distributed as dist
 
 from .. import _native
+from ..ops.attention import VARIANTS as ATTENTION_VARIANTS
 from ..ops.decode_gemm import INTERLEAVE_ROWS, DecodeGemm
 
 
@@ -70,7 +71,7 @@ class TPLlama:
 
     def __init__(self, cfg: LlamaConfig, *, rank: int, world: int, device, batch: int, max_len: int,
                  comm: str = "sparknet", runtime=None, group=None, seed: int = 0, gemm: str | None = None,
-                 pdl: bool = True, attention: str = "split", fuse_gemm_ar: bool = False):
+                 pdl: bool = True, attention: str = "auto", fuse_gemm_ar: bool = False):
         if cfg.heads % world or cfg.kv_heads % world or cfg.ffn % world or cfg.vocab % world:
             raise ValueError(f"model does not shard evenly over {world} GPUs")
         if comm not in ("sparknet", "nccl"):
@@ -82,8 +83,8 @@ class TPLlama:
             raise ValueError("gemm must be 'sparknet' or 'cublas'")
         if (cfg.ffn // world) % INTERLEAVE_ROWS:
             raise ValueError("the FFN shard must be a multiple of 64 features")
-        if attention not in ("split", "cluster"):
-            raise ValueError("attention must be 'split' (workspace merge) or 'cluster' (cluster merge)")
+        if attention not in ATTENTION_VARIANTS:
+            raise ValueError(f"attention must be one of {sorted(ATTENTION_VARIANTS)}")
         self.gemm = gemm
         self.attention = attention
         # O and down projections whose GEMM epilogue pushes into the all-reduce
@@ -205,12 +206,8 @@ class TPLlama:
                 self._linear(self.x, L["wqkv"], self.qkv)
                 C.rope_qkv_cache(self.qkv, self.cos, self.sin, self.positions, self.q, L["k"], L["v"], self.hq,
                                  self.hkv)
-            if self.attention == "cluster":
-                C.decode_attention_cluster(self.q, L["k"], L["v"], self.lengths, self.attn, self.max_len, scale,
-                                           self.pdl)
-            else:
-                C.decode_attention(self.q, L["k"], L["v"], self.lengths, self.attn, self.workspace, self.max_len,
-                                   scale, self.pdl)
+            C.decode_attention(self.q, L["k"], L["v"], self.lengths, self.attn, self.workspace, self.max_len,
+                               scale, self.pdl, ATTENTION_VARIANTS[self.attention])
             last = i + 1 == len(self.layers)
             nxt = self.norm if last else self.layers[i + 1]["ln1"]
             if self.fuse_gemm_ar:

@@ -75,42 +75,6 @@ def test_decode_attention(device, native, B, Hq, Hkv, L, impl):
         torch.testing.assert_close(out[b].float(), ref, rtol=2e-2, atol=2e-2)
 
 
-EXPERIMENTAL = pytest.mark.skipif(os.environ.get("SPARKNET_TEST_EXPERIMENTAL") != "1",
-                                  reason="kernel not yet run on a GPU: SPARKNET_TEST_EXPERIMENTAL=1 runs it")
-
-
-@EXPERIMENTAL
-@pytest.mark.parametrize("B,Hq,Hkv,L", [(1, 8, 1, 1025), (4, 8, 1, 300), (2, 64, 8, 129), (64, 8, 1, 1280),
-                                        (3, 4, 4, 33), (8, 8, 1, 1296), (2, 16, 1, 40), (1, 1, 1, 7)])
-def test_decode_attention_cluster(device, native, B, Hq, Hkv, L):
-    """The cluster variant against the fp32 reference, and against the split-KV kernel."""
-    Lmax = L + 7
-    q = torch.randn(B, Hq, 128, device=device).to(torch.bfloat16)
-    kc = torch.randn(B, Lmax, Hkv, 128, device=device).to(torch.bfloat16)
-    vc = torch.randn(B, Lmax, Hkv, 128, device=device).to(torch.bfloat16)
-    lengths = torch.randint(1, L + 1, (B,), dtype=torch.int32, device=device)
-    lengths[0] = L
-    out = torch.empty(B, Hq, 128, dtype=torch.bfloat16, device=device)
-    native.decode_attention_cluster(q, kc, vc, lengths, out, L, 1 / math.sqrt(128))
-    again = torch.empty_like(out)
-    native.decode_attention_cluster(q, kc, vc, lengths, again, L, 1 / math.sqrt(128), True)
-    sms = torch.cuda.get_device_properties(device).multi_processor_count
-    ws = torch.zeros(native.attention_workspace_floats(B, Hq, Hkv, L, sms), dtype=torch.float32, device=device)
-    split = torch.empty_like(out)
-    native.decode_attention(q, kc, vc, lengths, split, ws, L, 1 / math.sqrt(128))
-    torch.cuda.synchronize()
-    assert torch.equal(out, again)  # deterministic: spans merge in span order
-    torch.testing.assert_close(out.float(), split.float(), rtol=1e-2, atol=1e-2)
-    G = Hq // Hkv
-    for b in range(B):
-        n = int(lengths[b])
-        k = kc[b, :n].float().repeat_interleave(G, dim=1)
-        v = vc[b, :n].float().repeat_interleave(G, dim=1)
-        s = torch.einsum("hd,nhd->hn", q[b].float(), k) / math.sqrt(128)
-        ref = torch.einsum("hn,nhd->hd", s.softmax(-1), v)
-        torch.testing.assert_close(out[b].float(), ref, rtol=2e-2, atol=2e-2)
-
-
 def test_add_rmsnorm_silu_argmax(device, native):
     x = torch.randn(5, 8192, device=device).to(torch.bfloat16)
     r = torch.randn(5, 8192, device=device).to(torch.bfloat16)
@@ -242,16 +206,16 @@ def test_decode_qkv_rope_epilogue(device, native, B, Hq, Hkv):
         assert not kc[b, others].any() and not vc[b, others].any(), "wrote outside the token's position"
 
 
-@EXPERIMENTAL
-def test_cluster_attention_keeps_the_step(device, native):
-    """The cluster-merged attention gives the split-KV step's logits (within bf16)."""
+def test_attention_kernels_keep_the_step(device, native):
+    """A decode step with the tensor-core attention gives the CUDA-core step's logits
+    (within bf16): the two kernels are interchangeable inside the model."""
     from sparknet.models.llama import LlamaConfig, TPLlama
 
     cfg = LlamaConfig.tiny(layers=3)
     logits = []
-    for attention in ("split", "cluster"):
-        m = TPLlama(cfg, rank=0, world=1, device=device, batch=4, max_len=64, attention=attention)
-        m.fill_prompt_cache(20)
+    for attention in ("simt", "tcgen05"):
+        m = TPLlama(cfg, rank=0, world=1, device=device, batch=4, max_len=256, attention=attention)
+        m.fill_prompt_cache(150)
         m.tokens.copy_(torch.tensor([3, 9, 1, 4], device=device))
         m.step_kernels()
         m.step_kernels()
@@ -272,8 +236,9 @@ def test_parallel_layer_decode_uses_the_decode_gemm(device, native):
     torch.testing.assert_close(y.float(), x.float() @ w.float().T, rtol=2e-2, atol=2e-2)
 
 
-def test_ops_decode_attention_wrapper(device, native):
-    """sparknet.ops.decode_attention (split-KV, its own workspace), against fp32, twice."""
+@pytest.mark.parametrize("variant", ["auto", "simt", "tcgen05"])
+def test_ops_decode_attention_wrapper(device, native, variant):
+    """sparknet.ops.decode_attention (its own workspace), every variant, against fp32, twice."""
     from sparknet.ops import decode_attention
 
     B, Hq, Hkv, L = 3, 16, 2, 200
@@ -282,7 +247,7 @@ def test_ops_decode_attention_wrapper(device, native):
         kc = torch.randn(B, L + 8, Hkv, 128, device=device).to(torch.bfloat16)
         vc = torch.randn(B, L + 8, Hkv, 128, device=device).to(torch.bfloat16)
         lengths = torch.tensor([L, 17, 150], dtype=torch.int32, device=device)
-        out = decode_attention(q, kc, vc, lengths, L)
+        out = decode_attention(q, kc, vc, lengths, L, variant=variant)
         torch.cuda.synchronize()
         G = Hq // Hkv
         for b in range(B):
