@@ -29,11 +29,15 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cooperative_groups.h>
+
 #include "sparknet/attention_kernels.cuh"
 #include "sparknet/tc_gemm.cuh"
 
 namespace sn {
 namespace attn {
+
+namespace cg = cooperative_groups;
 
 // kTcKeys (keys per tile = MMA M of the score product), kTcMaxSpans, tc_tiles() and
 // tc_splits() are in attention_kernels.cuh, beside the workspace size they decide.
@@ -47,6 +51,7 @@ constexpr int kQHalfBytes = kTcHeads * 128;   // 16 rows x 128 B
 constexpr int kPAtomBytes = kTcHeads * 128;   // 16 heads x 64 keys of P (bf16)
 constexpr int kErrorSlot = kCounterSlots - 1; // workspace int: nonzero after a wait ran out
 constexpr int kTcStamps = 12;                 // phase stamps per CTA (profiling)
+constexpr int kClusterMaxSpans = 8;           // spans merged in a (portable) cluster
 
 template <int T>
 struct TcLayout {  // byte offsets from the 1024-aligned base of dynamic shared memory
@@ -129,7 +134,11 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
   volatile uint32_t* bad = reinterpret_cast<volatile uint32_t*>(base + L::misc + 4);
   int* last = reinterpret_cast<int*>(base + L::misc + 8);
 
-  const int b = blockIdx.x / Hkv, h = blockIdx.x % Hkv, s = blockIdx.y, nsplit = gridDim.y;
+  // grid (spans, sequences x KV heads); the spans of one (sequence, KV head) are one
+  // cluster when the launch asked for it (the merge then runs in distributed shared memory)
+  const int bh = blockIdx.y, b = bh / Hkv, h = bh % Hkv, s = blockIdx.x, nsplit = gridDim.x;
+  cg::cluster_group cluster = cg::this_cluster();
+  const bool cluster_merge = nsplit > 1 && cluster.num_blocks() == unsigned(nsplit);
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int Hq = G * Hkv;
   const size_t head0 = size_t(b) * Hq + size_t(h) * G;
@@ -332,6 +341,51 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
     }
     return;
   }
+  if (cluster_merge) {
+    // Each span parks its unnormalised output [G][128] and (max, sum) per head in its own
+    // shared memory (the K tiles are free); after a cluster barrier span r finalises heads
+    // r, r + nsplit, ...: thread t reads dimension t of every span's partial through
+    // distributed shared memory (every load issued before the sum) and merges in span order.
+    float* park = reinterpret_cast<float*>(base + L::k);  // [G][128] outputs, then [G][2] (max, sum)
+#pragma unroll
+    for (int g = 0; g < G; ++g) park[g * kTcThreads + t] = o[g];
+    if (t < G) {
+      park[G * kTcThreads + 2 * t] = m_span[t];
+      park[G * kTcThreads + 2 * t + 1] = l_span[t];
+    }
+    cluster.sync();
+    stamp(7);  // partials parked in the cluster
+#pragma unroll 1
+    for (int g = s; g < G; g += nsplit) {
+      float mx[kClusterMaxSpans], ls[kClusterMaxSpans], ov[kClusterMaxSpans];
+#pragma unroll
+      for (int r = 0; r < kClusterMaxSpans; ++r) {
+        if (r < nsplit) {
+          const float* pr = cluster.map_shared_rank(park, r);
+          mx[r] = pr[G * kTcThreads + 2 * g];
+          ls[r] = pr[G * kTcThreads + 2 * g + 1];
+          ov[r] = pr[g * kTcThreads + t];
+        }
+      }
+      float M = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < kClusterMaxSpans; ++r)
+        if (r < nsplit) M = fmaxf(M, mx[r]);
+      float Lt = 0.0f, acc = 0.0f;
+#pragma unroll
+      for (int r = 0; r < kClusterMaxSpans; ++r) {
+        if (r < nsplit) {
+          const float w = ls[r] > 0.0f ? exp2f(mx[r] - M) : 0.0f;
+          Lt += ls[r] * w;
+          acc += ov[r] * w;
+        }
+      }
+      out[(head0 + g) * kHead + t] = __float2bfloat16_rn(Lt > 0.0f ? acc / Lt : 0.0f);
+    }
+    stamp(11);  // merged
+    cluster.sync();  // every span's partial stays readable until the cluster is done
+    return;
+  }
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     const size_t row = (head0 + g) * nsplit + s;
@@ -343,7 +397,7 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
   }
   __threadfence();
   __syncthreads();
-  if (t == 0) *last = atomicAdd(&counters[blockIdx.x], 1) == nsplit - 1;
+  if (t == 0) *last = atomicAdd(&counters[bh], 1) == nsplit - 1;
   __syncthreads();
   stamp(7);  // partial stored, counted
   if (!*last) return;
@@ -411,7 +465,7 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
     out[(head0 + g) * kHead + t] = __float2bfloat16_rn(acc[g] * inv);
   }
   stamp(11);  // merged
-  if (t == 0) counters[blockIdx.x] = 0;
+  if (t == 0) counters[bh] = 0;
 }
 
 // --- host side ----------------------------------------------------------------------
@@ -462,8 +516,8 @@ static inline bool tc_eligible(const void* q, const void* k_cache, const void* v
 template <int G, int T>
 static inline cudaError_t launch_tc_gt(const CUtensorMap& mk, const CUtensorMap& mv, const __nv_bfloat16* q,
                                        const int* lengths, __nv_bfloat16* out, int* counters, float* part_o,
-                                       float* part_ml, int B, int Hkv, int Lmax, int nsplit, float scale_log2,
-                                       cudaStream_t st, bool pdl, uint64_t* stamps) {
+                                       float* part_ml, int B, int Hkv, int Lmax, int nsplit, int cluster,
+                                       float scale_log2, cudaStream_t st, bool pdl, uint64_t* stamps) {
   auto kernel = k_decode_attn_tc<G, T>;
   static int attr_set[64] = {0};  // function attributes belong to each device's context
   int dev = 0;
@@ -474,20 +528,35 @@ static inline cudaError_t launch_tc_gt(const CUtensorMap& mk, const CUtensorMap&
     if (dev >= 0 && dev < 64) attr_set[dev] = 1;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(B * Hkv, nsplit, 1);
+  cfg.gridDim = dim3(nsplit, B * Hkv, 1);
   cfg.blockDim = dim3(kTcThreads, 1, 1);
   cfg.dynamicSmemBytes = TcLayout<T>::bytes;
   cfg.stream = st;
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr.val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
+  cudaLaunchAttribute attrs[2];
+  attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  attrs[1].id = cudaLaunchAttributeClusterDimension;
+  attrs[1].val.clusterDim.x = cluster;
+  attrs[1].val.clusterDim.y = 1;
+  attrs[1].val.clusterDim.z = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = cluster > 1 ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kernel, mk, mv, q, lengths, out, counters, part_o, part_ml, Hkv, Lmax, scale_log2,
                             stamps);
 }
 
-// Launch over the shared workspace layout [kCounterSlots ints][part_o][part_ml].
+// Spans for the cluster merge: up to kClusterMaxSpans spans of T = 1 or 2 tiles cover
+// sequences up to 2048 keys; 0 = use the workspace merge (tc_tiles / tc_splits).
+static inline void cluster_plan(int max_len, int& T, int& nsplit) {
+  T = max_len <= kClusterMaxSpans * kTcKeys ? 1 : 2;
+  nsplit = (max_len + T * kTcKeys - 1) / (T * kTcKeys);
+  if (nsplit > kClusterMaxSpans) T = nsplit = 0;
+}
+
+// Launch over the shared workspace layout [kCounterSlots ints][part_o][part_ml].  Up to
+// 2048 keys the spans of a (sequence, KV head) form one cluster and merge in distributed
+// shared memory (the workspace is then used only if a tool re-issues the launch without
+// its cluster attribute); longer sequences use the workspace merge.
 static inline cudaError_t launch_decode_attention_tc(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
                                                      const __nv_bfloat16* v_cache, const int* lengths,
                                                      __nv_bfloat16* out, float* scratch, int B, int Hq, int Hkv,
@@ -496,15 +565,23 @@ static inline cudaError_t launch_decode_attention_tc(const __nv_bfloat16* q, con
   CUtensorMap mk, mv;
   if (!make_cache_map(&mk, k_cache, B, Lmax, Hkv) || !make_cache_map(&mv, v_cache, B, Lmax, Hkv))
     return cudaErrorInvalidValue;
-  const int G = Hq / Hkv, T = tc_tiles(max_len), nsplit = tc_splits(max_len);
+  int T = 0, nsplit = 0;
+  cluster_plan(max_len, T, nsplit);
+  const int cluster = nsplit > 1 ? nsplit : 1;
+  if (!T) {
+    T = tc_tiles(max_len);
+    nsplit = tc_splits(max_len);
+  }
+  const int G = Hq / Hkv;
   int* counters = reinterpret_cast<int*>(scratch);
   float* part_o = scratch + kCounterSlots;
   float* part_ml = part_o + size_t(B) * Hq * nsplit * kHead;
   const float sl2 = scale * kLog2e;
-#define SN_TC(GG, TT)                                                                                            \
-  if (G == GG && T == TT)                                                                                        \
-    return launch_tc_gt<GG, TT>(mk, mv, q, lengths, out, counters, part_o, part_ml, B, Hkv, Lmax, nsplit, sl2, st, \
-                                pdl, stamps);
+  const int cl = (cluster > 1 && nsplit == cluster) ? cluster : 1;
+#define SN_TC(GG, TT)                                                                                       \
+  if (G == GG && T == TT)                                                                                   \
+    return launch_tc_gt<GG, TT>(mk, mv, q, lengths, out, counters, part_o, part_ml, B, Hkv, Lmax, nsplit, cl, \
+                                sl2, st, pdl, stamps);
   SN_TC(1, 1) SN_TC(2, 1) SN_TC(4, 1) SN_TC(8, 1) SN_TC(16, 1)
   SN_TC(1, 2) SN_TC(2, 2) SN_TC(4, 2) SN_TC(8, 2) SN_TC(16, 2)
 #undef SN_TC
