@@ -56,10 +56,10 @@ def parse_args(argv=None):
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--algorithm", default=None, help="force oneshot|twoshot|nvls (ours)")
     p.add_argument("--pdl", action="store_true",
-                   help="ours: launch the collectives with programmatic dependent launch")
+                   help="ours: launch the collectives with programmatic dependent launch (the default)")
+    p.add_argument("--no-pdl", action="store_true",
+                   help="ours: launch the collectives without programmatic dependent launch")
     p.add_argument("--batch", type=int, default=8, help="decode: sequences per step")
-    p.add_argument("--fuse-gemm-ar", action="store_true",
-                   help="decode: the O / down GEMM epilogues push into the all-reduce (NVLink arm)")
     p.add_argument("--attention", choices=("auto", "simt", "tcgen05"), default="auto",
                    help="decode: attention kernel (auto: tensor cores from 32 sequence-head pairs)")
     p.add_argument("--layers", type=int, default=80, help="decode: decoder layers")
@@ -173,7 +173,7 @@ class Arm:
     """One implementation: how to all-reduce, align ranks and capture."""
 
     def __init__(self, impl: str, rank: int, world: int, device, cpu_group, algorithm: str | None,
-                 pdl: bool = False):
+                 pdl: bool | None = None):
         self.impl, self.rank, self.world, self.device = impl, rank, world, device
         self.algorithm = algorithm
         self.launches_per_call = 1
@@ -182,8 +182,8 @@ class Arm:
             from sparknet.oneshot import AllReduce
 
             self.rt = AllReduce.from_exchange_group(exchange_group=cpu_group, device=device)
-            if pdl:
-                self.rt.set_pdl(True)
+            if pdl is not None:
+                self.rt.set_pdl(pdl)
             self.rt.prepare((torch.bfloat16,))
             self.native_path = _native.loaded_path()
             self.align_buf = torch.zeros(8, dtype=torch.bfloat16, device=device)
@@ -216,7 +216,8 @@ def run_allreduce(args, rank, world, device, cpu_group):
     ClockSampler = _local("clocks").ClockSampler
     L2Flusher, geomean = _local("timing").L2Flusher, _local("timing").geomean
 
-    arm = Arm(args.impl, rank, world, device, cpu_group, args.algorithm, pdl=args.pdl)
+    arm = Arm(args.impl, rank, world, device, cpu_group, args.algorithm,
+              pdl=False if args.no_pdl else (True if args.pdl else None))
     flush = L2Flusher(device)
     sizes = [int(s) for s in args.sizes]
     gen = torch.Generator(device=device)
@@ -442,7 +443,8 @@ def run_fused_norm(arm, args, rank, world, device, cpu_group):
         gamma = (1.0 + 0.02 * torch.randn(H, generator=shared, device=device)).to(torch.bfloat16)
         out, res_out = torch.empty_like(x), torch.empty_like(res)
         ar, out_u, res_u = torch.empty_like(x), torch.empty_like(x), torch.empty_like(res)
-        rt.all_reduce_residual_rmsnorm(x, res, gamma, eps, out=out, residual_out=res_out)
+        rt.all_reduce_residual_rmsnorm(x, res, gamma, eps, out=out, residual_out=res_out,
+                                       algorithm=rt._fused_norm_algorithm(tokens, x.numel() * x.element_size()))
         torch.cuda.synchronize()
         want_res = (rank_order_sum(x, world).float() + res.float()).to(torch.bfloat16)
         r32 = want_res.float()
@@ -455,8 +457,10 @@ def run_fused_norm(arm, args, rank, world, device, cpu_group):
         if not (check["bit_exact"] and same_out and rel <= 2.0 ** -7):
             raise RuntimeError(f"fused all-reduce + RMSNorm at {tokens} tokens failed its checks: {check}")
 
-        def fused():
-            rt.all_reduce_residual_rmsnorm(x, res, gamma, eps, out=out, residual_out=res_out)
+        algo = rt._fused_norm_algorithm(tokens, x.numel() * x.element_size())
+
+        def fused():  # the single kernel, at every token count (the API switches to the pair above a threshold)
+            rt.all_reduce_residual_rmsnorm(x, res, gamma, eps, out=out, residual_out=res_out, algorithm=algo)
 
         def unfused():
             rt.all_reduce(x, out=ar)
@@ -495,7 +499,8 @@ def run_fused_norm(arm, args, rank, world, device, cpu_group):
         for ni, name in enumerate(graphs):
             per = [max(g[ni * args.steps + k] for g in gathered) for k in range(args.steps)]
             row[f"{name}_p50_us"] = round(statistics.median(per) * 1000.0 / CALLS_PER_GRAPH, 3)
-        row["algorithm"] = rt._fused_norm_algorithm(tokens, x.numel() * x.element_size())
+        row["algorithm"] = algo
+        row["api_runs"] = "fused kernel" if tokens <= rt.fused_norm_max_tokens() else "all-reduce + add/RMSNorm kernel"
         rows[str(tokens)] = row
         del graphs
         torch.cuda.synchronize()

@@ -323,9 +323,7 @@ class Comm {
   FusedPlan plan_fused_norm(const std::vector<at::Tensor>& ins, const std::vector<at::Tensor>& residuals,
                             const at::Tensor& gamma, double eps, const std::vector<at::Tensor>& outs,
                             const std::vector<at::Tensor>& residual_outs, int algo, int cluster, int max_clusters,
-                            bool received, int threads = 0) const {
-    if (received && (emulate_ || (algo != kOneShot && algo != kTwoShot) || world_ < 2))
-      throw std::invalid_argument("a received fused norm runs in a real (not emulated) group, one-shot or two-shot");
+                            int threads = 0) const {
     check_views(ins, outs);
     check_views(residuals, residual_outs);
     require_aligned(gamma, "gamma");
@@ -365,16 +363,15 @@ class Comm {
     j.gamma = ptr_of(gamma);
     j.eps = float(eps);
     j.hidden = uint32_t(H);
-    j.received = received ? 1u : 0u;
     return FusedPlan{j, g, dtype_code(x)};
   }
 
   void fused_norm(const std::vector<at::Tensor>& ins, const std::vector<at::Tensor>& residuals,
                   const at::Tensor& gamma, double eps, const std::vector<at::Tensor>& outs,
                   const std::vector<at::Tensor>& residual_outs, int algo, int cluster, int max_clusters,
-                  bool received = false, int threads = 0) {
+                  int threads = 0) {
     FusedPlan p = plan_fused_norm(ins, residuals, gamma, eps, outs, residual_outs, algo, cluster, max_clusters,
-                                  received, threads);
+                                  threads);
     auto stream = at::cuda::getCurrentCUDAStream(device_).stream();
     if (emulate_) {
       EmuViews e = emu_views(ins, outs, &residuals, &residual_outs);
@@ -384,26 +381,7 @@ class Comm {
     }
   }
 
-  // Decode: partial = x @ w.T on the decode GEMM, whose epilogue pushes every finished
-  // group of the partial into the peers' slots (one-shot: to every peer; two-shot: each
-  // row to its owner), then the fused all-reduce + residual + RMSNorm, which only
-  // receives.  Two launches on the current stream.
-  void gemm_fused_norm(const at::Tensor& x, const at::Tensor& w, at::Tensor& partial, const at::Tensor& residual,
-                       const at::Tensor& gamma, double eps, at::Tensor& out, at::Tensor& residual_out,
-                       at::Tensor& err, int algo, int cluster, bool pdl_gemm) {
-    if (emulate_ || world_ < 2) throw std::invalid_argument("the pushing decode GEMM needs a real group of 2..8 ranks");
-    if (algo != kOneShot && algo != kTwoShot) throw std::invalid_argument("one-shot or two-shot");
-    if (x.scalar_type() != at::kBFloat16 || partial.scalar_type() != at::kBFloat16)
-      throw std::invalid_argument("bf16 activations and partial");
-    if (residual.sizes() != partial.sizes() || out.sizes() != partial.sizes() ||
-        residual_out.sizes() != partial.sizes() || partial.dim() != 2 || gamma.numel() != partial.size(1))
-      throw std::invalid_argument("residual, out and residual_out like partial [tokens, N]; gamma [N]");
-    // Every check before the first launch: the GEMM writes into the peers' slots, so
-    // nothing may stop the collective that consumes them once it has run.
-    FusedPlan plan = plan_fused_norm({partial}, {residual}, gamma, eps, {out}, {residual_out}, algo, cluster, 0, true);
-    tc::skinny_gemm_push(view_, L_, rank_, world_, x, w, partial, err, 0, pdl_gemm, algo == kTwoShot);
-    launch_fused_norm(plan.j, nullptr, plan.dtype, algo, plan.g, at::cuda::getCurrentCUDAStream(device_).stream());
-  }
+
 
   // -- fused prefill GEMMs (tcgen05) ----------------------------------------------
   RegionDesc region() const {
@@ -618,10 +596,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            py::arg("out"), py::arg("err"), py::arg("max_ctas") = 0)
       .def("fused_norm", &Comm::fused_norm, py::arg("ins"), py::arg("residuals"), py::arg("gamma"), py::arg("eps"),
            py::arg("outs"), py::arg("residual_outs"), py::arg("algo"), py::arg("cluster") = 8,
-           py::arg("max_clusters") = 0, py::arg("received") = false, py::arg("threads") = 0)
-      .def("gemm_fused_norm", &Comm::gemm_fused_norm, py::arg("x"), py::arg("w"), py::arg("partial"),
-           py::arg("residual"), py::arg("gamma"), py::arg("eps"), py::arg("out"), py::arg("residual_out"),
-           py::arg("err"), py::arg("algo") = 0, py::arg("cluster") = 8, py::arg("pdl_gemm") = true)
+           py::arg("max_clusters") = 0, py::arg("threads") = 0)
       .def("status", &Comm::status, py::arg("which") = 0)
       .def("failed_seq", &Comm::failed_seq, py::arg("which") = 0)
       .def("set_timeout_us", &Comm::set_timeout_us)

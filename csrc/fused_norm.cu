@@ -125,8 +125,7 @@ SN_DEV void fused_body(const Job& j, int algo) {
   };
 
   // 1. push: one-shot sends every row to every peer; two-shot sends row t to its owner.
-  //    Skipped when the producer of the input already pushed it (j.received).
-  if (ok && W > 1 && !j.received) {
+  if (ok && W > 1) {
     for (uint64_t t = cid; t < T; t += nclusters) {
       for (uint32_t k = 0; k < per_thread; ++k) {
         const uint64_t tpack = row_pack(k);

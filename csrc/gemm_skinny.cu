@@ -17,10 +17,7 @@
 // tiles are [64 gate rows; 64 up rows] of the same 64 features, and writes
 // Y[m, f] = silu(gate) * up for the N/2 features (no intermediate tensor); mode 2 is the
 // QKV projection with RoPE (rotate-half, fp32) and the KV-cache write, one 128-row
-// tile per head (no qkv tensor, no separate RoPE kernel); mode 3 writes Y like mode 0
-// and pushes every finished 8-feature group into the peers' all-reduce slots, one-shot
-// or two-shot layout (the push half of the fused all-reduce + residual + RMSNorm that
-// follows).
+// tile per head (no qkv tensor, no separate RoPE kernel).
 //
 // Every mbarrier wait is bounded (sets the error word and unwinds).
 // Reference: none (the reference has no model GEMMs).
@@ -75,10 +72,6 @@ struct SkinnyParams {
   const int* positions;
   int hq, hkv, lmax;
   uint64_t* stamps;   // optional: kStamps %globaltimer values per CTA (phase timing), or null
-  // mode 3: the collective's view (regions of every rank, layout, rank, world); read
-  // in place from the kernel parameters, like the collective kernels' Job
-  Job pj;
-  int push_twoshot;   // mode 3: push each row to its owner (two-shot) instead of to every peer
 };
 
 constexpr int kStamps = 8;
@@ -263,61 +256,6 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
       dst[r] = __float2bfloat16_rn(x1);
       dst[r + 64] = __float2bfloat16_rn(x2);
     }
-  } else if (p.mode == 3) {
-    // Y in 8-feature groups (CTA `split` takes groups split, split + S, ...), each group
-    // summed over the splits in split order exactly as mode 0 sums an element, and
-    // pushed, sentinel-safe, into Lamport slot [parity][rank]: of every peer at the
-    // one-shot layout's pack index (token * N / 8 + feature / 8), or (two-shot) of the
-    // row's owner (token % world) at (token / world) * N / 8 + feature / 8.  The parity
-    // is that of the collective that follows this kernel: the epoch read here plus one.
-    // The read comes after griddepcontrol.wait (the main loop waited), so the previous
-    // collective has completed on this rank.  A poisoned rank pushes nothing (the
-    // collective exits at entry).
-    const Job& j = p.pj;
-    DevMem dm;
-    const Ctrl* ctrl = reinterpret_cast<const Ctrl*>(j.v.base[j.rank] + j.L.ctrl_off);
-    uint32_t epoch, poison;
-    dm.ld_volatile_pair(&ctrl->epoch, epoch, poison);
-    const uint32_t parity = next_seq(epoch) & 1u;
-    const int my_groups = (kWRows / 8 - split + S - 1) / S;
-    const uint64_t row_packs = uint64_t(p.N) / 8;
-    for (int e = threadIdx.x; e < my_groups * p.M; e += blockDim.x) {
-      const int g = split + (e / p.M) * S, m = e % p.M;
-      const int n0 = tile * kWRows + g * 8;
-      float acc8[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int r = g * 8 + k;
-        float v[kMaxSplits];
-#pragma unroll
-        for (int s = 0; s < kMaxSplits; ++s) v[s] = s < S ? cluster.map_shared_rank(part, s)[r * pitch + m] : 0.0f;
-        float acc = 0.0f;
-#pragma unroll
-        for (int s = 0; s < kMaxSplits; ++s) acc += v[s];
-        acc8[k] = acc;
-      }
-      if (n0 < p.N) {  // N is a multiple of 8: the whole group is in range
-        Pack16 pk;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const __nv_bfloat162 h2 = __floats2bfloat162_rn(acc8[2 * k], acc8[2 * k + 1]);
-          pk.w[k] = *reinterpret_cast<const uint32_t*>(&h2);
-        }
-        dm.st_output(reinterpret_cast<Pack16*>(p.Y + size_t(m) * p.ldy + n0), pk);
-        if (!poison) {
-          const Pack16 c = pack_canon<kBF16>(pk);
-          const uint64_t idx = uint64_t(m) * row_packs + uint64_t(n0) / 8;
-          if (p.push_twoshot) {
-            const uint32_t owner = uint32_t(m) % j.world;
-            if (owner != j.rank)
-              dm.st_remote(lam_pack(j, owner, parity, j.rank, uint64_t(m / int(j.world)) * row_packs + uint64_t(n0) / 8),
-                           c);
-          } else {
-            for (uint32_t k = 1; k < j.world; ++k) dm.st_remote(lam_pack(j, (j.rank + k) % j.world, parity, j.rank, idx), c);
-          }
-        }
-      }
-    }
   } else {
     // SwiGLU: rows 0..63 gate, 64..127 up of the same 64 features
     const int my_rows = (64 - split + S - 1) / S;
@@ -501,56 +439,6 @@ void skinny_qkv_rope(const at::Tensor& X, const at::Tensor& W, const at::Tensor&
   p.hq = hq;
   p.hkv = hkv;
   p.lmax = int(k_cache.size(1));
-  launch_skinny(W, X, p, pl, dev, pdl);
-}
-
-// Decode GEMM whose epilogue also performs the push of the all-reduce that follows
-// (mode 3): Y = X W^T, and every 16-byte group of Y goes to slot [parity][rank] of every
-// peer's region (one-shot) or of its row's owner (`twoshot`).  The caller launches the
-// receiving fused all-reduce + residual + RMSNorm right after it on the same stream,
-// having checked its arguments first.
-void skinny_gemm_push(const View& view, const Layout& L, int rank, int world, const at::Tensor& X,
-                      const at::Tensor& W, at::Tensor& Y, at::Tensor& err, int max_splits, bool pdl, bool twoshot) {
-  check_mat(X, "X");
-  check_mat(W, "W");
-  check_mat(Y, "Y");
-  const int M = int(X.size(0)), K = int(X.size(1)), N = int(W.size(0));
-  if (W.size(1) != K) throw std::invalid_argument("X and W must share K");
-  if (M < 1 || M > kMaxTokens) throw std::invalid_argument("the pushing decode GEMM takes 1..256 token rows");
-  if (K % kBK) throw std::invalid_argument("K must be a multiple of 64");
-  if (N % 8) throw std::invalid_argument("the pushing decode GEMM needs N a multiple of 8 (16-byte groups)");
-  if (Y.size(0) != M || Y.size(1) != N || !Y.is_contiguous() || reinterpret_cast<uintptr_t>(Y.data_ptr()) % 16)
-    throw std::invalid_argument("Y must be a contiguous, 16-byte aligned [M, N] tensor");
-  if (world < 2 || world > kMaxRanks || rank < 0 || rank >= world)
-    throw std::invalid_argument("the pushing decode GEMM needs 2..8 ranks");
-  if (!twoshot && uint64_t(M) * N * 2 > L.lam_cap) throw std::invalid_argument("M x N exceeds the one-shot slot");
-  if (twoshot && uint64_t((M + world - 1) / world) * N * 2 > L.lam_cap / 2)
-    throw std::invalid_argument("the rows per owner exceed the two-shot slot");
-  const int dev = X.device().index();
-  c10::cuda::CUDAGuard guard(X.device());
-  int sms = 0;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  Plan pl = plan(M, N, K, sms, max_splits);
-  SkinnyParams p;
-  memset(&p, 0, sizeof(p));
-  p.M = M;
-  p.N = N;
-  p.K = K;
-  p.mp = pl.mp;
-  p.stages = pl.stages;
-  p.kb_per_split = pl.kb_per_split;
-  p.splits = pl.splits;
-  p.tiles = pl.tiles;
-  p.mode = 3;
-  p.Y = reinterpret_cast<__nv_bfloat16*>(Y.data_ptr());
-  p.ldy = int(Y.stride(0));
-  p.err = reinterpret_cast<uint32_t*>(err.data_ptr());
-  p.pj.v = view;
-  p.pj.L = L;
-  p.pj.rank = uint32_t(rank);
-  p.pj.world = uint32_t(world);
-  p.pj.skip_rank = -1;
-  p.push_twoshot = twoshot ? 1 : 0;
   launch_skinny(W, X, p, pl, dev, pdl);
 }
 

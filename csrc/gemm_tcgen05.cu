@@ -81,7 +81,6 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kEpiWarps = 4;
 constexpr int kGroupM = 16;     // row blocks per rasterisation band
 constexpr int kCopyPpt = 4;     // all-gather copy CTAs: packs in flight per thread
-constexpr int kBulkPiece = 64 * 1024;  // all-gather bulk copy role: bytes per bulk copy (two stages)
 
 struct GemmParams {
   int M, N, K;
@@ -95,8 +94,7 @@ struct GemmParams {
   // ag copy role
   const char* shard;
   int copy_ctas;
-  int copy_order;    // 0: chunks (or their slices) spread over the copy CTAs; 1: chunk-major per warp;
-                     // 2: chunk-major bulk copies (one thread per copy CTA drives the bulk-copy engine)
+  int copy_order;    // 0: chunks (or their slices) spread over the copy CTAs; 1: chunk-major per warp
   // fp8: UE8M0 scale chunks (512 bytes per 128 rows and 128 K), laid out [row block][K block]
   const uint8_t* sfa;       // A's (ag: this rank's shard's)
   const uint8_t* sfb;
@@ -189,65 +187,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   // orders its stores before its count with a system-scope fence, and the CTA that
   // completes the count (a counter in this rank's control words, reset by that CTA)
   // fences again and raises the flags.
-  if (int(blockIdx.x) < copy_ctas && p.copy_order == 2) {
-    // Bulk copies: one thread per copy CTA drives the SM's bulk-copy engine, so the push
-    // costs no thread bandwidth.  Chunk by chunk (the order the GEMM consumes them), each
-    // chunk -- and, fp8, its scale block -- is cut into kBulkPiece-byte pieces; copy CTA b
-    // takes pieces b, b + copy_ctas, ...: one bulk load from this rank's shard into a
-    // shared-memory stage, then one bulk store of the stage into every peer's slot.  Two
-    // stages: the load of a piece overlaps the stores of the previous one.  At the end of
-    // a chunk each CTA waits for its stores to complete, orders them (async-proxy fence,
-    // then a system-scope fence) before its count, and the CTA that completes the count
-    // raises the chunk's flag at every peer.
-    if (threadIdx.x != 0) return;
-    const int chunks = p.shard_rows / kBM;
-    const uint64_t chunk_bytes = uint64_t(kBM) * p.K * kEsz;
-    const uint64_t sf_bytes = F8 ? uint64_t(p.K / kBKe) * 512 : 0;
-    const uint64_t data_pieces = (chunk_bytes + kBulkPiece - 1) / kBulkPiece;
-    const uint64_t pieces = data_pieces + (sf_bytes + kBulkPiece - 1) / kBulkPiece;
-    Ctrl* ctrl = ctrl_of(p);
-    mbar_init(&full[0], 1);
-    mbar_init(&full[1], 1);
-    fence_barrier_init();
-    uint32_t it = 0;
-    bool ok = true;
-    for (int c = 0; c < chunks && ok; ++c) {
-      for (uint64_t j = blockIdx.x; j < pieces; j += copy_ctas, ++it) {
-        const bool scales = j >= data_pieces;
-        const uint64_t off = (scales ? j - data_pieces : j) * kBulkPiece;
-        const uint64_t left = (scales ? sf_bytes : chunk_bytes) - off;
-        const uint32_t n = uint32_t(left < uint64_t(kBulkPiece) ? left : uint64_t(kBulkPiece));
-        const char* src = scales ? reinterpret_cast<const char*>(p.sfa) + c * sf_bytes + off
-                                 : p.shard + c * chunk_bytes + off;
-        const uint64_t dst = scales ? p.sfa_slot_off + c * sf_bytes + off : c * chunk_bytes + off;
-        uint64_t* bar = &full[it & 1];
-        uint8_t* stage = smem + (it & 1) * kBulkPiece;
-        asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");  // the stage's previous stores read it
-        mbar_expect_tx(bar, n);
-        bulk_load(stage, src, n, bar);
-        if (!mbar_wait(bar, (it >> 1) & 1u, err)) {
-          ok = false;
-          break;
-        }
-        for (int k = 1; k < W; ++k)
-          bulk_store(slot(p, (rank + k) % W, parity, rank) + dst, stage, n);
-        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-      }
-      asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // this CTA's stores of the chunk completed
-      if (!ok) break;
-      asm volatile("fence.proxy.async.global;" ::: "memory");
-      m.fence_sys();
-      const uint32_t prev = atomicAdd(&ctrl->chunk_count[c], 1u);
-      if (prev == uint32_t(copy_ctas) - 1u) {
-        m.fence_sys();
-        ctrl->chunk_count[c] = 0;  // every copy CTA counted: re-armed for the next collective
-        for (int k = 1; k < W; ++k) m.st_release_u32(gflag(p, (rank + k) % W, rank, c), seq);
-      }
-    }
-    if (err_local) atomicExch(p.err, err_local);
-    finish_op(m, ctrl_of(p), seq, gridDim.x);
-    return;
-  }
   if (int(blockIdx.x) < copy_ctas && p.copy_order == 1) {
     // Chunk-major, per warp: every copy warp pushes an equal slice of chunk 0, then of
     // chunk 1, ..., so chunks complete in the order the GEMM consumes them (chunk c of
@@ -727,7 +666,7 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, at::Tensor& e
 
 void ag_gemm(const RegionDesc& reg, const at::Tensor& x_shard, const at::Tensor& B, at::Tensor& C, at::Tensor& err,
              int copy_ctas, int max_ctas, int copy_order) {
-  if (copy_order < 0 || copy_order > 2) throw std::invalid_argument("copy_order: 0 spread, 1 chunk-major, 2 bulk");
+  if (copy_order != 0 && copy_order != 1) throw std::invalid_argument("copy_order: 0 spread, 1 chunk-major");
   check_mat(x_shard, "x_shard");
   check_mat(B, "B");
   check_mat(C, "C");
@@ -836,7 +775,7 @@ void gemm_fp8(const at::Tensor& A, const at::Tensor& sfa, const at::Tensor& B, c
 void ag_gemm_fp8(const RegionDesc& reg, const at::Tensor& xq_shard, const at::Tensor& sfa_shard, const at::Tensor& B,
                  const at::Tensor& sfb, at::Tensor& C, at::Tensor& err, int copy_ctas, int max_ctas,
                  int copy_order) {
-  if (copy_order < 0 || copy_order > 2) throw std::invalid_argument("copy_order: 0 spread, 1 chunk-major, 2 bulk");
+  if (copy_order != 0 && copy_order != 1) throw std::invalid_argument("copy_order: 0 spread, 1 chunk-major");
   check_fp8_mat(xq_shard, "xq_shard");
   check_fp8_mat(B, "B");
   check_mat(C, "C");

@@ -26,11 +26,6 @@ void gemm_rs_fp8(const RegionDesc& reg, const at::Tensor& A, const at::Tensor& s
                  const at::Tensor& sfb, at::Tensor& C_shard, at::Tensor& err, int max_ctas);
 void gemm_rs(const RegionDesc& reg, const at::Tensor& A, const at::Tensor& B, at::Tensor& C_shard, at::Tensor& err,
              int max_ctas);
-// Decode GEMM Y = X W^T whose epilogue pushes Y into the peers' all-reduce slots (every
-// row to every peer, or with `twoshot` each row to its owner; gemm_skinny.cu); the
-// receiving fused norm follows on the same stream.
-void skinny_gemm_push(const View& view, const Layout& L, int rank, int world, const at::Tensor& X,
-                      const at::Tensor& W, at::Tensor& Y, at::Tensor& err, int max_splits, bool pdl, bool twoshot);
 }  // namespace tc
 
 }  // namespace sn

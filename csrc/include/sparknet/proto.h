@@ -37,7 +37,7 @@ namespace sn {
 // ---------------------------------------------------------------------------
 // Limits and ABI
 // ---------------------------------------------------------------------------
-constexpr int kAbiVersion = 7;       // bumped when Layout/Ctrl/Status/Job change
+constexpr int kAbiVersion = 8;       // bumped when Layout/Ctrl/Status/Job change
 constexpr int kMaxRanks = 8;         // one NVSwitch box
 constexpr int kMaxBlocks = 256;      // per launch (grid.x)
 constexpr int kChunkCounters = 1024; // fused all-gather->GEMM: 128-row chunks per shard
@@ -434,10 +434,6 @@ struct Job {
   // then lets the next such launch be scheduled (launch_dependents): the successor
   // can only start once every block of this grid is resident.
   uint32_t pdl;
-  // fused norm: 1 when every rank's input was already pushed into the Lamport slots the
-  // kernel reads (one-shot: every peer's; two-shot: the row owners'), by the decode
-  // GEMM's epilogue; the kernel then skips its own push.
-  uint32_t received;
   // Trace ring (device pointer of the pinned trace file's records), or null.
   uint64_t* trace;
 };

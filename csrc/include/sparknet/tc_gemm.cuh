@@ -202,15 +202,6 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint
                : "memory");
 }
 
-// Bulk (non-tensor) copy of `bytes` from this CTA's shared memory to global memory (this
-// GPU's or a peer's mapping), in the current bulk async-group.  16-byte aligned
-// addresses, size a multiple of 16.
-__device__ __forceinline__ void bulk_store(void* gdst, const void* smem_src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;"
-               ::"l"(reinterpret_cast<uint64_t>(gdst)), "r"(smem_u32(smem_src)), "r"(bytes)
-               : "memory");
-}
-
 // Descriptor of a 512-byte scale chunk for tcgen05.cp: K-major, no swizzle, 32 rows of
 // 16 bytes, 8-row core matrices 128 bytes apart.
 __device__ __forceinline__ uint64_t smem_desc_sf(const void* chunk) {

@@ -41,13 +41,12 @@ def run_decode_bench(args, rank, world, device, cpu_group):
 
         runtime = AllReduce.from_exchange_group(exchange_group=cpu_group, device=device,
                                                 max_size=max(8 << 20, batch * cfg.hidden * 2 * 2))
-        if getattr(args, "pdl", False):
-            runtime.set_pdl(True)  # the fused all-reduce + norm launches during the GEMM before it
+        if getattr(args, "no_pdl", False):
+            runtime.set_pdl(False)  # on by default: the fused all-reduce + norm launches during the GEMM before it
         runtime.prepare((torch.bfloat16,))
     t0 = time.perf_counter()
     model = TPLlama(cfg, rank=rank, world=world, device=device, batch=batch, max_len=max_len, comm=comm,
-                    runtime=runtime, group=None, attention=getattr(args, "attention", "auto"),
-                    fuse_gemm_ar=getattr(args, "fuse_gemm_ar", False))
+                    runtime=runtime, group=None, attention=getattr(args, "attention", "auto"))
     model.fill_prompt_cache(PROMPT)
     torch.cuda.synchronize()
     init_s = time.perf_counter() - t0
@@ -121,7 +120,7 @@ def run_decode_bench(args, rank, world, device, cpu_group):
                    "gemm": model.gemm, "programmatic_dependent_launch": model.pdl,
                    "collective_pdl": bool(runtime.pdl) if runtime is not None else False,
                    "attention": model.attention,
-                   "gemm_pushes_all_reduce": model.fuse_gemm_ar,
+
                    "l2": "weights per step far exceed L2 (126 MB)"},
         "gpu_launches": model.launches_per_step() * args.steps,
         "clocks": clocks,

@@ -71,7 +71,7 @@ class TPLlama:
 
     def __init__(self, cfg: LlamaConfig, *, rank: int, world: int, device, batch: int, max_len: int,
                  comm: str = "sparknet", runtime=None, group=None, seed: int = 0, gemm: str | None = None,
-                 pdl: bool = True, attention: str = "auto", fuse_gemm_ar: bool = False):
+                 pdl: bool = True, attention: str = "auto"):
         if cfg.heads % world or cfg.kv_heads % world or cfg.ffn % world or cfg.vocab % world:
             raise ValueError(f"model does not shard evenly over {world} GPUs")
         if comm not in ("sparknet", "nccl"):
@@ -87,9 +87,6 @@ class TPLlama:
             raise ValueError(f"attention must be one of {sorted(ATTENTION_VARIANTS)}")
         self.gemm = gemm
         self.attention = attention
-        # O and down projections whose GEMM epilogue pushes into the all-reduce
-        # (NVLink arm with the tcgen05 decode GEMMs only)
-        self.fuse_gemm_ar = bool(fuse_gemm_ar) and comm == "sparknet" and world > 1 and gemm == "sparknet"
         self.cfg, self.rank, self.world, self.device = cfg, rank, world, torch.device(device)
         self.batch, self.max_len, self.comm, self.runtime, self.group = batch, max_len, comm, runtime, group
         self.C = _native.load()
@@ -165,12 +162,6 @@ class TPLlama:
             dist.all_reduce(partial, group=self.group)
             self.C.add_rmsnorm(partial, self.res, self.res, gamma, self.x, eps)
 
-    def _gemm_add_norm(self, x, w, gamma):
-        """partial = x @ w.T, residual += all_reduce(partial), x = rms_norm(residual) * gamma,
-        with the GEMM's epilogue doing the all-reduce's push."""
-        self.runtime.gemm_all_reduce_residual_rmsnorm(x, w, self.res, gamma, self.cfg.eps, partial=self.partial,
-                                                      out=self.x, residual_out=self.res, pdl=self.pdl)
-
     def _gather_best(self):
         if self.world == 1:
             return self.best
@@ -210,11 +201,6 @@ class TPLlama:
                                scale, self.pdl, ATTENTION_VARIANTS[self.attention])
             last = i + 1 == len(self.layers)
             nxt = self.norm if last else self.layers[i + 1]["ln1"]
-            if self.fuse_gemm_ar:
-                self._gemm_add_norm(self.attn.view(self.batch, -1), L["wo"], L["ln2"])
-                self._swiglu(self.x, L["wgu"], self.act)
-                self._gemm_add_norm(self.act, L["wdown"], nxt)
-                continue
             self._linear(self.attn.view(self.batch, -1), L["wo"], self.partial)
             self._add_norm(self.partial, L["ln2"])
             self._swiglu(self.x, L["wgu"], self.act)

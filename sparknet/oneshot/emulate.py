@@ -99,7 +99,7 @@ class EmulatedGroup:
         res_outs = [torch.empty_like(x) for x in residuals]
         with torch.cuda.device(self.device):
             self.comm.fused_norm(list(inputs), list(residuals), gamma, float(eps), outs, res_outs,
-                                 ALGO_CODES[algorithm], cluster, max_clusters, False, threads)
+                                 ALGO_CODES[algorithm], cluster, max_clusters, threads)
         return outs, res_outs
 
     def barrier(self, blocks: int = 1) -> None:

@@ -60,7 +60,7 @@ DEFAULT_THREADS = 512
 DEFAULT_BLOCKS = 0          # 0: one block per SM at most
 DEFAULT_TIMEOUT_MS = 10_000
 MAX_TIMEOUT_MS = (2**32 - 1) // 1000
-LL_CAP = 8 * 1024 * 1024   # LL8 slot: all-gather shards up to this travel as payload + flags
+LL_CAP = 4 * 1024 * 1024   # LL8 slot: all-gather shards up to this travel as payload + flags
 
 ALGO_CODES = {"oneshot": 0, "twoshot": 1, "nvls": 2, "local": 3}
 GATHER_CODES = {"ll": 0, "push": 1, "nvls": 2}
@@ -73,16 +73,14 @@ OP_NAMES = {1: "all-reduce", 2: "all-gather", 3: "reduce-scatter", 4: "exchange"
 ENV_TIMEOUT_MS = "SPARKNET_TIMEOUT_MS"
 ENV_PDL = "SPARKNET_PDL"
 ENV_AG_COPY_ORDER = "SPARKNET_AG_COPY_ORDER"
-AG_COPY_ORDERS = {"spread": 0, "chunk-major": 1, "bulk": 2}
+AG_COPY_ORDERS = {"spread": 0, "chunk-major": 1}
 
 
 def ag_copy_order(order: Optional[str] = None) -> int:
     """Copy schedule of the fused all-gather -> GEMM: ``spread`` (default: the shard's
-    chunks, or slices of them, spread over the copy CTAs at once), ``chunk-major``
+    chunks, or slices of them, spread over the copy CTAs at once) or ``chunk-major``
     (every copy warp pushes a slice of chunk 0, then of chunk 1, ...: chunks land in the
-    order the GEMM consumes them) or ``bulk`` (chunk-major, the SM's bulk-copy engine
-    moves the data: one thread per copy CTA issues a bulk load per piece and one bulk
-    store per peer).  ``order`` overrides ``SPARKNET_AG_COPY_ORDER``."""
+    order the GEMM consumes them).  ``order`` overrides ``SPARKNET_AG_COPY_ORDER``."""
     name = order if order is not None else (os.environ.get(ENV_AG_COPY_ORDER) or "spread")
     if name not in AG_COPY_ORDERS:
         raise ValueError(f"all-gather copy order must be one of {sorted(AG_COPY_ORDERS)}, got {name!r}")
@@ -205,11 +203,7 @@ class _StatusView:
 # sustains ~9 TFLOP/s per SM in bf16 (1354.8 TFLOP/s over 148 SMs) and ~10.7 in
 # block-scaled fp8.
 PUSH_GBS_PER_CTA = 20.0
-# the bulk-copy role (one thread per CTA drives the SM's copy engine): measured with the
-# microbenchmark's bulk mode on 2 B200s, 64 KB pieces: 39-41 GB/s for one CTA, 543 GB/s
-# for 16 (P2P stores from 512 threads: 29-30 GB/s and 422 GB/s)
-PUSH_GBS_PER_BULK_CTA = 34.0
-MIN_BULK_COPY_CTAS = 8
+FUSED_NORM_MAX_TOKENS = {1: 0, 2: 32, 8: 128}   # by world size; see NvlinkAllReduce.fused_norm_max_tokens
 MIN_COPY_CTAS = 16        # fewer measured slower at TP2 and TP8 on every prefill shape
 BF16_GEMM_TFLOPS_PER_SM = 9.0
 FP8_GEMM_TFLOPS_PER_SM = 10.7
@@ -368,7 +362,7 @@ class NvlinkAllReduce:
             self._comm.set_trace(address, trace.file_bytes())
             logger.info("collective trace %s", self.trace_path)
         self.has_multicast = bool(self._comm.has_multicast)
-        self.set_pdl(os.environ.get(ENV_PDL, "0") == "1" if pdl is None else bool(pdl))
+        self.set_pdl(os.environ.get(ENV_PDL, "1") != "0" if pdl is None else bool(pdl))
         if self.rank == 0:
             logger.info("NVLink collectives ready: world=%d region=%d MiB multicast=%s max_size=%d",
                         self.world_size, region_bytes >> 20, self.has_multicast, self.max_size)
@@ -580,6 +574,8 @@ class NvlinkAllReduce:
         """Fused ``residual += all_reduce(inp); out = rms_norm(residual) * gamma``.
 
         ``inp`` and ``residual`` are ``[tokens, hidden]``; returns ``(out, residual_out)``.
+        One kernel up to :meth:`fused_norm_max_tokens` rows (bf16), the all-reduce then the
+        add + RMSNorm kernel above it (or with ``algorithm`` forced, always one kernel).
         Rounds exactly where the unfused sequence would (after the all-reduce and after
         the add), so the new residual equals ``all_reduce(inp) + residual`` bit for bit,
         and every rank computes identical outputs.  ``residual_out`` may alias
@@ -597,6 +593,15 @@ class NvlinkAllReduce:
                     raise ValueError("fused norm tensors must be contiguous, 16-byte aligned, on the runtime device")
             tokens, hidden = inp.shape
             nbytes = inp.numel() * inp.element_size()
+            if (algorithm is None and inp.dtype == torch.bfloat16 and tokens > self.fused_norm_max_tokens()
+                    and self._accepts_allreduce(inp, self.max_size)):
+                # more rows than the fused kernel wins at: the all-reduce, then the add +
+                # RMSNorm kernel (the same residual bits; the output within one rounding)
+                out = self.all_reduce(inp, out=out, stream=stream)
+                residual_out = torch.empty_like(residual) if residual_out is None else residual_out
+                with torch.cuda.device(self.device), self._stream_ctx(stream):
+                    _native.load().add_rmsnorm(out, residual, residual_out, gamma, out, float(eps))
+                return out, residual_out
             if algorithm is None:
                 algorithm = self._fused_norm_algorithm(tokens, nbytes)
             with torch.cuda.device(self.device), self._stream_ctx(stream):
@@ -613,80 +618,21 @@ class NvlinkAllReduce:
             self.check_health()
         return out, residual_out
 
+    def fused_norm_max_tokens(self) -> int:
+        """Most rows the single-kernel all-reduce + residual + RMSNorm carries; more go to
+        the all-reduce then the add + RMSNorm kernel.  Measured with ``bench.py`` (256-call
+        graphs, hidden 8192): on 8 B200s the fused kernel won up to 128 tokens (16.9 vs
+        17.6 us) and lost at 256 (28.5 vs 22.8 us); on 2 it won up to 32 and lost at 128
+        (14.5 vs 12.3 us); on one GPU the copy + add-norm pair was always faster."""
+        table = FUSED_NORM_MAX_TOKENS
+        smaller = [w for w in table if w <= self.world_size]
+        return table[max(smaller)] if smaller else 0
+
     def _fused_norm_algorithm(self, tokens: int, nbytes: int) -> str:
         """One-shot or two-shot for the fused norm (rank-invariant: sizes and world)."""
         if self.world_size <= 2 or nbytes <= self.policy.oneshot_limit(self.world_size) or tokens < self.world_size:
             return "oneshot"
         return "twoshot"
-
-    def gemm_push_eligible(self, x: torch.Tensor, w: torch.Tensor, cluster: int = 8) -> bool:
-        """Whether ``gemm_all_reduce_residual_rmsnorm`` runs its fused form for these
-        shapes: several ranks, bf16, 1..256 tokens, K a multiple of 64, N a multiple of
-        8 x cluster, and the message within the slot of the algorithm the fused norm
-        picks (one-shot: the whole message; two-shot: each owner's rows in half a slot).
-        Depends on shapes, dtype and world size only (rank-invariant)."""
-        if x.dim() != 2 or w.dim() != 2 or x.shape[1] != w.shape[1]:
-            return False
-        tokens, k, n = x.shape[0], x.shape[1], w.shape[0]
-        nbytes = tokens * n * 2
-        if not (self.world_size > 1 and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
-                and 1 <= tokens <= 256 and k % 64 == 0 and n % (8 * cluster) == 0):
-            return False
-        if self._fused_norm_algorithm(tokens, nbytes) == "oneshot":
-            return nbytes <= self._caps[0]
-        return -(-tokens // self.world_size) * n * 2 <= self._caps[0] // 2
-
-    def gemm_all_reduce_residual_rmsnorm(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor,
-                                         gamma: torch.Tensor, eps: float = 1e-5, *,
-                                         partial: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-                                         residual_out: Optional[torch.Tensor] = None, cluster: int = 8,
-                                         pdl: bool = True) -> tuple[torch.Tensor, torch.Tensor]:
-        """Decode row-parallel projection and its collective: ``partial = x @ w.T``,
-        ``residual += all_reduce(partial)``, ``out = rms_norm(residual) * gamma``.
-
-        The decode GEMM's epilogue pushes each finished 16-byte group of ``partial``
-        into the peers' slots of the algorithm the fused norm picks (one-shot: every
-        peer; two-shot: the row's owner), so the fused all-reduce kernel that follows
-        only receives: the push overlaps the GEMM's other tiles and leaves the
-        collective's critical path.  The results equal the unfused
-        ``linear`` + ``all_reduce_residual_rmsnorm`` bit for bit.  Shapes it cannot
-        carry (:meth:`gemm_push_eligible`) run that unfused pair instead; the choice
-        depends on shapes and world size only, so every rank makes it alike.  ``pdl``
-        launches the GEMM with programmatic dependent launch.
-        """
-        tokens = x.shape[0] if x.dim() == 2 else 0
-        n = w.shape[0] if w.dim() == 2 else 0
-        nbytes = tokens * n * 2
-        if partial is None:
-            partial = torch.empty((tokens, n), dtype=torch.bfloat16, device=x.device)
-        if not self.gemm_push_eligible(x, w, cluster):
-            from sparknet.ops.decode_gemm import linear
-
-            linear(x, w, partial)
-            return self.all_reduce_residual_rmsnorm(partial, residual, gamma, eps, out=out,
-                                                    residual_out=residual_out, cluster=cluster)
-        with self._lock:
-            self.check_health()
-            self._live()
-            for t in (x, w, residual, gamma, partial):
-                if not t.is_cuda or t.device != self.device or not t.is_contiguous() or t.data_ptr() % PACK_BYTES:
-                    raise ValueError("tensors must be contiguous, 16-byte aligned, on the runtime device")
-            if residual.shape != (tokens, n) or gamma.shape != (n,) or partial.shape != (tokens, n):
-                raise ValueError("residual and partial [tokens, N], gamma [N]")
-            with torch.cuda.device(self.device):
-                capturing = torch.cuda.is_current_stream_capturing()
-                out = torch.empty_like(residual) if out is None else out
-                residual_out = torch.empty_like(residual) if residual_out is None else residual_out
-                self._order_stream(capturing)
-                algorithm = self._fused_norm_algorithm(tokens, nbytes)
-                self._comm.gemm_fused_norm(x, w, partial, residual, gamma, float(eps), out, residual_out,
-                                           self._gemm_err(), ALGO_CODES[algorithm], cluster, bool(pdl))
-                self._calls["fused_norm"] += 1
-                self._account_reduce(algorithm, nbytes)
-                self._mark_stream(capturing)
-        if not capturing:
-            self.check_health()
-        return out, residual_out
 
     # -- fused prefill GEMMs (tcgen05) -------------------------------------------------------
     def _gemm_err(self) -> torch.Tensor:
@@ -706,8 +652,8 @@ class NvlinkAllReduce:
         """
         order = ag_copy_order(copy_order)
         if copy_ctas is None:
-            copy_ctas = self._copy_ctas(order, x_shard.numel() * x_shard.element_size(),
-                                        2 * x_shard.shape[0] * self.world_size * x_shard.shape[1] * w.shape[0])
+            copy_ctas = copy_ctas_for(x_shard.numel() * x_shard.element_size(), self.world_size,
+                                      2 * x_shard.shape[0] * self.world_size * x_shard.shape[1] * w.shape[0])
         with self._lock:
             self.check_health()
             self._live()
@@ -721,13 +667,6 @@ class NvlinkAllReduce:
                 self._peer_bytes += x_shard.numel() * x_shard.element_size()
                 self._mark_stream(capturing)
         return out
-
-    def _copy_ctas(self, order: int, shard_bytes: int, flops: int) -> int:
-        """Copy CTAs of the fused all-gather -> GEMM for a copy schedule (rank-invariant)."""
-        if order == AG_COPY_ORDERS["bulk"]:
-            return copy_ctas_for(shard_bytes, self.world_size, flops, push_gbs_per_cta=PUSH_GBS_PER_BULK_CTA,
-                                 min_ctas=MIN_BULK_COPY_CTAS)
-        return copy_ctas_for(shard_bytes, self.world_size, flops)
 
     def gemm_rs(self, a: torch.Tensor, w: torch.Tensor, *, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """``reduce_scatter(a @ w.T, dim=0)`` in one kernel (row-parallel prefill GEMM).
@@ -761,12 +700,9 @@ class NvlinkAllReduce:
         """
         order = ag_copy_order(copy_order)
         if copy_ctas is None:
-            bulk = order == AG_COPY_ORDERS["bulk"]
             copy_ctas = copy_ctas_for(xq_shard.numel() + sfa_shard.numel(), self.world_size,
                                       2 * xq_shard.shape[0] * self.world_size * xq_shard.shape[1] * w.shape[0],
-                                      gemm_tflops_per_sm=FP8_GEMM_TFLOPS_PER_SM,
-                                      push_gbs_per_cta=PUSH_GBS_PER_BULK_CTA if bulk else PUSH_GBS_PER_CTA,
-                                      min_ctas=MIN_BULK_COPY_CTAS if bulk else MIN_COPY_CTAS)
+                                      gemm_tflops_per_sm=FP8_GEMM_TFLOPS_PER_SM)
         with self._lock:
             self.check_health()
             self._live()
@@ -821,7 +757,9 @@ class NvlinkAllReduce:
         runs; it waits (``griddepcontrol.wait``) until that kernel has finished before it
         reads its sequence number, and lets its own successor be scheduled once all of
         its blocks are running, so a chain of collectives (a graph) overlaps every
-        launch with the previous call.  Off by default (``SPARKNET_PDL=1`` turns it on).
+        launch with the previous call.  On by default (``SPARKNET_PDL=0`` turns it off):
+        measured on B200 boxes (256-call graphs, geomean of 10 KiB-2 MiB), 6.35 -> 5.78 us
+        at 2 ranks and 9.65 -> 8.98 us at 8 ranks.
         The one-rank copy always uses it.  Affects the calls issued after it, and graphs
         captured after it.
         """

@@ -61,10 +61,12 @@ FALLBACK_ONESHOT_MAX = {2: 4 << 20, 4: 512 << 10, 8: 512 << 10}
 FALLBACK_DISPATCH_MAX = 2 << 20
 # Largest all-gather shard that travels in LL8 form (payload + flag per 8 bytes);
 # larger shards use bulk pushes with per-block flags (or NVLS broadcast when enabled).
-# LL doubles the bytes but needs no fence or flag round trip.  Measured on 2 B200s
-# (probe sweep): LL 8.6 us at a 1 MiB shard against NCCL's 22.9 us, while the flagged
-# bulk push took 35.1 us at 2 MiB (NCCL 32.4 us), so LL carries shards up to 8 MiB.
-DEFAULT_LL_MAX = 8 << 20
+# LL doubles the bytes but needs no fence or flag round trip.  Measured (probe sweeps):
+# on 2 B200s LL took 8.6 us at a 1 MiB shard against NCCL's 22.9 us while the flagged
+# bulk push took 35.1 us at 2 MiB (NCCL 32.4 us); on 8 B200s LL beat NCCL up to a 4 MiB
+# shard (105.4 vs 113.0 us) and lost at 8 MiB (211.0 vs 195.8 us).  LL carries shards
+# up to 4 MiB.
+DEFAULT_LL_MAX = 4 << 20
 # Messages at or above this use NVLS when it is enabled and available (the measured
 # threshold of the smallest world size that has one, else this fallback).
 FALLBACK_NVLS_MIN = 256 << 10

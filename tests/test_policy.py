@@ -58,8 +58,8 @@ def test_all_gather_backend_and_algorithm():
     assert p.all_gather_backend((16 << 20) + 16, "bfloat16", dim=0, ndim=1) == "nccl"
     assert p.all_gather_algorithm(1024, row_bytes=1024, nvls_available=False) == "ll"
     assert p.all_gather_algorithm(1 << 20, row_bytes=4096, nvls_available=True) == "ll"
-    assert p.all_gather_algorithm(8 << 20, row_bytes=4096, nvls_available=True) == "ll"
-    assert p.all_gather_algorithm((8 << 20) + 16, row_bytes=4096, nvls_available=True) == "push"
+    assert p.all_gather_algorithm(4 << 20, row_bytes=4096, nvls_available=True) == "ll"
+    assert p.all_gather_algorithm((4 << 20) + 16, row_bytes=4096, nvls_available=True) == "push"
     assert make(allow_nvls=True).all_gather_algorithm(16 << 20, row_bytes=4096, nvls_available=True) == "nvls"
     assert p.all_gather_algorithm(1020, row_bytes=12, nvls_available=False) == "push"
 

@@ -167,33 +167,6 @@ def test_reference_exports_are_importable():
     assert oneshot.discover_nvlink_gpus() == ()  # no CUDA device on this host
 
 
-def test_pushing_gemm_eligibility():
-    """When the decode projection runs with its GEMM pushing into the all-reduce: the
-    shapes a real group's fused norm carries; everything else takes the unfused pair."""
-    from sparknet.oneshot.runtime import NvlinkAllReduce
-    from sparknet.policy import NVLINK_POLICY
-
-    rt = NvlinkAllReduce.__new__(NvlinkAllReduce)
-    rt.policy, rt._caps, rt.world_size = NVLINK_POLICY, (8 << 20, 1 << 20, 16 << 20), 8
-    bf = torch.bfloat16
-
-    def ok(tokens, k, n, dtype=bf):
-        return rt.gemm_push_eligible(torch.empty(tokens, k, dtype=dtype), torch.empty(n, k, dtype=dtype))
-
-    assert ok(8, 1024, 8192) and ok(8, 3584, 8192) and ok(1, 64, 512)
-    assert not ok(8, 1000, 8192)             # K not a multiple of 64
-    assert not ok(8, 1024, 8200)             # N not a multiple of 8 x cluster
-    assert not ok(300, 1024, 8192)           # beyond the decode GEMM's 256 rows
-    assert ok(64, 1024, 8192)                # 1 MiB at W = 8: two-shot, 8 rows per owner
-    assert rt._fused_norm_algorithm(64, 64 * 8192 * 2) == "twoshot"
-    assert rt._fused_norm_algorithm(8, 8 * 8192 * 2) == "oneshot"
-    assert not ok(8, 1024, 8192, torch.float16)
-    rt.world_size = 2
-    assert ok(64, 1024, 8192)                # two ranks: one-shot up to the slot
-    rt.world_size = 1
-    assert not ok(8, 1024, 8192)             # no peers to push to
-
-
 def test_attention_wrapper_rejects_unknown_variants():
     from sparknet.ops import decode_attention
 

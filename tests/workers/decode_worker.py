@@ -15,69 +15,6 @@ import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 
-def gemm_pushes_all_reduce(rt, cfg, rank, world, device, results):
-    """The decode GEMM whose epilogue pushes into the all-reduce gives the unfused
-    sequence's bits: eagerly on both slot parities, from a replayed graph, and as the
-    O / down projections of the decode step."""
-    from sparknet.models.llama import TPLlama
-    from sparknet.ops.decode_gemm import linear
-
-    g = torch.Generator(device=device).manual_seed(11 + rank)
-    # 8 tokens: one-shot; 64 tokens x 8192: two-shot at 4 or more ranks (one-shot at 2)
-    for tokens, n in ((8, 2048), (64, 8192)):
-        xs = torch.randn(tokens, 1024, generator=g, device=device).to(torch.bfloat16)
-        ws = (0.05 * torch.randn(n, 1024, generator=g, device=device)).to(torch.bfloat16)
-        gs = (1 + 0.1 * torch.randn(n, device=device)).to(torch.bfloat16)
-        rs = torch.randn(tokens, n, generator=torch.Generator(device=device).manual_seed(5), device=device)
-        rs = rs.to(torch.bfloat16)
-        if not rt.gemm_push_eligible(xs, ws):
-            results["failures"].append(f"{tokens} x {n} not eligible for the pushing GEMM")
-            continue
-        for call in range(2):  # both slot parities
-            partial = linear(xs, ws)
-            want_out, want_res = rt.all_reduce_residual_rmsnorm(partial, rs.clone(), gs, 1e-5)
-            got_out, got_res = rt.gemm_all_reduce_residual_rmsnorm(xs, ws, rs.clone(), gs, 1e-5)
-            torch.cuda.synchronize()
-            if not (torch.equal(got_out, want_out) and torch.equal(got_res, want_res)):
-                results["failures"].append(f"pushing GEMM differs from the unfused sequence ({tokens} x {n}, "
-                                           f"call {call})")
-    x = torch.randn(8, 1024, generator=g, device=device).to(torch.bfloat16)
-    w = (0.05 * torch.randn(2048, 1024, generator=g, device=device)).to(torch.bfloat16)
-    gamma = (1 + 0.1 * torch.randn(2048, device=device)).to(torch.bfloat16)
-    res0 = torch.randn(8, 2048, generator=torch.Generator(device=device).manual_seed(5), device=device)
-    res0 = res0.to(torch.bfloat16)
-    res, out, part = res0.clone(), torch.empty_like(res0), torch.empty_like(res0)
-    stream = torch.cuda.Stream(device=device)
-    stream.wait_stream(torch.cuda.current_stream())
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream), rt.capture(stream=stream):
-        rt.gemm_all_reduce_residual_rmsnorm(x, w, res, gamma, 1e-5, partial=part, out=out, residual_out=res)
-    want = res0.clone()
-    for rep in range(3):
-        graph.replay()
-        want_out, want = rt.all_reduce_residual_rmsnorm(linear(x, w), want, gamma, 1e-5)
-        torch.cuda.synchronize()
-        if not (torch.equal(out, want_out) and torch.equal(res, want)):
-            results["failures"].append(f"pushing GEMM graph replay {rep} differs")
-    del graph
-    logits = {}
-    for fused in (False, True):
-        m = TPLlama(cfg, rank=rank, world=world, device=device, batch=4, max_len=64, comm="sparknet", runtime=rt,
-                    seed=3, fuse_gemm_ar=fused)
-        m.fill_prompt_cache(10)
-        m.tokens.copy_(torch.tensor([1, 2, 3, 4], device=device))
-        m.capture()
-        for _ in range(3):
-            m.replay()
-        torch.cuda.synchronize()
-        logits[fused] = (m.logits.clone(), m.tokens.clone())
-        m.release()
-        del m
-    if not (torch.equal(logits[True][0], logits[False][0]) and torch.equal(logits[True][1], logits[False][1])):
-        results["failures"].append("decode step with pushing GEMMs differs from the unfused step")
-    results["gemm_pushes_all_reduce_checked"] = True
-
-
 def main():
     local = int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
@@ -121,8 +58,6 @@ def main():
     if not torch.allclose(x_s, x_n, rtol=5e-2, atol=5e-2):
         results["failures"].append(f"hidden states differ between arms: {(x_s - x_n).abs().max().item()}")
     results["tokens_equal_between_arms"] = bool(torch.equal(t_s, t_n))
-    if os.environ.get("SPARKNET_TEST_EXPERIMENTAL") == "1":
-        gemm_pushes_all_reduce(rt, cfg, rank, world, device, results)
     results["rt_health"] = rt.failure()
     torch.cuda.synchronize()
     dist.barrier(group=cpu)

@@ -108,22 +108,6 @@ def main():
         failures.append(f"gemm_rs_fp8 relative error {err}")
     if rt.gemm_error() or rt.failure():
         failures.append(f"error word (fp8) {rt.gemm_error()} / {rt.failure()}")
-    # the bulk-copy push of the all-gather -> GEMM, against the same fp32 oracles
-    for copy_ctas in (None, 1, 7):
-        got = rt.ag_gemm(x, w, copy_ctas=copy_ctas, copy_order="bulk")
-        want = gathered_fp32(x) @ w.float().T
-        torch.cuda.synchronize()
-        err = (got.float() - want).abs().max().item() / max(1e-6, want.abs().max().item())
-        if err > 1e-2:
-            failures.append(f"ag_gemm bulk ({copy_ctas} copy CTAs) relative error {err}")
-    got = rt.ag_gemm_fp8(xq, sx, wq, sw, copy_order="bulk")
-    want = torch.cat(parts) @ fp8.dequantize(wq, sw).T
-    torch.cuda.synchronize()
-    err = (got.float() - want).abs().max().item() / max(1e-6, want.abs().max().item())
-    if err > 1e-2:
-        failures.append(f"ag_gemm_fp8 bulk relative error {err}")
-    if rt.gemm_error() or rt.failure():
-        failures.append(f"error word (bulk) {rt.gemm_error()} / {rt.failure()}")
     # the chunk-major copy schedule of the all-gather -> GEMM (opt-in: SPARKNET_PREFILL_CHUNK_MAJOR=1)
     chunk_major = os.environ.get("SPARKNET_PREFILL_CHUNK_MAJOR") == "1"
     if chunk_major:
@@ -158,10 +142,6 @@ def main():
                            "nvlink_bytes_in": (world - 1) * (T // world) * H * 2}
             cases[name + "_copy16"] = {"fused_ms": fused16, "nccl_cublas_ms": base, "flops": 2 * T * H * n,
                                        "nvlink_bytes_in": (world - 1) * (T // world) * H * 2}
-            fused_bulk = timed(lambda: rt.ag_gemm(x, w, out=out, copy_order="bulk"))
-            cases[name + "_bulk"] = {"fused_ms": fused_bulk, "nccl_cublas_ms": base, "flops": 2 * T * H * n,
-                                     "nvlink_bytes_in": (world - 1) * (T // world) * H * 2,
-                                     "copy_ctas": rt._copy_ctas(2, (T // world) * H * 2, 2 * T * H * n)}
             if chunk_major:
                 fused_cm = timed(lambda: rt.ag_gemm(x, w, out=out, copy_order="chunk-major"))
                 cases[name + "_chunk_major"] = {"fused_ms": fused_cm, "nccl_cublas_ms": base,
