@@ -61,7 +61,7 @@ def parse_args(argv=None):
                    help="ours: launch the collectives without programmatic dependent launch")
     p.add_argument("--batch", type=int, default=8, help="decode: sequences per step")
     p.add_argument("--attention", choices=("auto", "simt", "tcgen05"), default="auto",
-                   help="decode: attention kernel (auto: tensor cores from 32 sequence-head pairs)")
+                   help="decode: attention kernel (auto: tensor cores where their cluster merge fits one wave or from 32 sequence-head pairs)")
     p.add_argument("--layers", type=int, default=80, help="decode: decoder layers")
     p.add_argument("--fused-norm-tokens", type=int, nargs="*", default=[1, 8, 32, 128, 256],
                    help="ours: also time the fused all-reduce + residual + RMSNorm at these token counts "

@@ -553,20 +553,32 @@ static inline void cluster_plan(int max_len, int& T, int& nsplit) {
   if (nsplit > kClusterMaxSpans) T = nsplit = 0;
 }
 
-// Launch over the shared workspace layout [kCounterSlots ints][part_o][part_ml].  Up to
-// 2048 keys the spans of a (sequence, KV head) form one cluster and merge in distributed
-// shared memory (the workspace is then used only if a tool re-issues the launch without
-// its cluster attribute); longer sequences use the workspace merge.
+// Whether the cluster merge applies: a cluster plan exists and the whole grid fits in one
+// wave of one CTA per SM.  Clusters of up to 8 CTAs must be co-scheduled on one GPC, and
+// with several waves that constraint costs more than the merge saves (measured on one
+// B200, 1024 keys, 8 query heads per KV head, graph-timed: batch 64 = 512 CTAs took
+// 25.7 us with clusters against 19.7 us with the workspace merge).
+static inline bool cluster_merge_fits(int B, int Hkv, int max_len, int sms) {
+  int T = 0, nsplit = 0;
+  cluster_plan(max_len, T, nsplit);
+  return T != 0 && int64_t(B) * Hkv * nsplit <= sms;
+}
+
+// Launch over the shared workspace layout [kCounterSlots ints][part_o][part_ml].  With
+// `cluster_merge` (only where cluster_merge_fits) the spans of a (sequence, KV head) form
+// one cluster and merge in distributed shared memory (the workspace is then used only if
+// a tool re-issues the launch without its cluster attribute); otherwise the spans merge
+// through the workspace.
 static inline cudaError_t launch_decode_attention_tc(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
                                                      const __nv_bfloat16* v_cache, const int* lengths,
                                                      __nv_bfloat16* out, float* scratch, int B, int Hq, int Hkv,
                                                      int Lmax, int max_len, float scale, cudaStream_t st, bool pdl,
-                                                     uint64_t* stamps = nullptr) {
+                                                     bool cluster_merge, uint64_t* stamps = nullptr) {
   CUtensorMap mk, mv;
   if (!make_cache_map(&mk, k_cache, B, Lmax, Hkv) || !make_cache_map(&mv, v_cache, B, Lmax, Hkv))
     return cudaErrorInvalidValue;
   int T = 0, nsplit = 0;
-  cluster_plan(max_len, T, nsplit);
+  if (cluster_merge) cluster_plan(max_len, T, nsplit);
   const int cluster = nsplit > 1 ? nsplit : 1;
   if (!T) {
     T = tc_tiles(max_len);
@@ -589,14 +601,15 @@ static inline cudaError_t launch_decode_attention_tc(const __nv_bfloat16* q, con
 }
 
 // The decode attention entry used by the torch op and the allocation-free C entry
-// point.  impl 0 (default): the tensor-core kernel where it is eligible and there are at
-// least kTcMinPairs (sequence, KV head) pairs, else the CUDA-core kernel; impl 1: the
-// CUDA-core kernel; impl 2: the tensor-core kernel, cudaErrorNotSupported where it is not
-// eligible.  Measured on one B200, 1024 keys, 8 query heads per KV head (graph-timed µs,
-// tensor cores / CUDA cores): batch 1: 12.7 / 10.3, batch 8: 13.4 / 11.4, batch 64:
-// 19.7 / 28.8 -- the tensor-core kernel's fixed cost (span merge) outweighs its faster
-// math on few pairs.  `stamps` (tensor-core kernel only): per-CTA phase timestamps,
-// kTcStamps each, or null.
+// point.  impl 0 (default): the tensor-core kernel where it is eligible and either its
+// cluster merge fits (cluster_merge_fits) or there are at least kTcMinPairs (sequence, KV
+// head) pairs, else the CUDA-core kernel; impl 1: the CUDA-core kernel; impl 2: the
+// tensor-core kernel, cudaErrorNotSupported where it is not eligible.  Measured on one
+// B200, 8 query heads per KV head (graph-timed us, tensor cores / CUDA cores): 1024 keys,
+// batch 1: 8.1 / 10.2 and batch 8: 8.5 / 11.4 (cluster merge); batch 64: 19.7 / 28.7
+// (workspace merge); 4096 keys, batch 8: 28.4 / 22.6 (workspace merge: 32 spans per pair
+// on 8 pairs leave the merge on the critical path).  `stamps` (tensor-core kernel only):
+// per-CTA phase timestamps, kTcStamps each, or null.
 constexpr int kTcMinPairs = 32;
 
 static inline cudaError_t launch_decode_attention(const __nv_bfloat16* q, const __nv_bfloat16* k_cache,
@@ -604,10 +617,11 @@ static inline cudaError_t launch_decode_attention(const __nv_bfloat16* q, const 
                                                   __nv_bfloat16* out, float* scratch, int B, int Hq, int Hkv,
                                                   int Lmax, int max_len, float scale, int sms, cudaStream_t st,
                                                   bool pdl = false, int impl = 0, uint64_t* stamps = nullptr) {
-  const bool tc = impl == 2 || (impl == 0 && B * Hkv >= kTcMinPairs);
+  const bool fits = cluster_merge_fits(B, Hkv, max_len, sms);
+  const bool tc = impl == 2 || (impl == 0 && (fits || B * Hkv >= kTcMinPairs));
   if (tc && tc_eligible(q, k_cache, v_cache, B, Hq, Hkv, Lmax, max_len))
     return launch_decode_attention_tc(q, k_cache, v_cache, lengths, out, scratch, B, Hq, Hkv, Lmax, max_len, scale,
-                                      st, pdl, stamps);
+                                      st, pdl, fits, stamps);
   if (impl == 2) return cudaErrorNotSupported;
   return launch_decode_attention_simt(q, k_cache, v_cache, lengths, out, scratch, B, Hq, Hkv, Lmax, max_len, scale,
                                       sms, st, pdl);

@@ -24,12 +24,6 @@ NVCC_FLAGS = ARCH_FLAGS + [
     "-U__CUDA_NO_BFLOAT16_CONVERSIONS__",
 ]
 CXX_FLAGS = ["-O3", "-std=c++17", "-Wall", "-Wno-unused-function"]
-# SPARKNET_BOUNDS_CHECK=1: a debug build whose protocol slot accesses are checked
-# (a violation is recorded as failure kind 4 and poisons the rank instead of
-# touching a neighbouring slot).  Off in normal builds: the checks cost registers.
-if os.environ.get("SPARKNET_BOUNDS_CHECK") == "1":
-    NVCC_FLAGS.append("-DSN_BOUNDS_CHECK")
-    CXX_FLAGS.append("-DSN_BOUNDS_CHECK")
 
 
 def sources():

@@ -10,8 +10,10 @@ finds in a workspace).  Two kernels share the workspace layout:
 * ``variant="tcgen05"``: tensor cores, 128-key K/V tiles by TMA, ``Q K^T`` and
   ``P V`` by ``tcgen05.mma`` with scores and output in TMEM
   (``csrc/include/sparknet/attention_tc.cuh``);
-* ``variant="auto"`` (default): the tensor-core kernel from 32 (sequence, KV head)
-  pairs up, where it was measured faster, else the CUDA-core kernel.
+* ``variant="auto"`` (default): the tensor-core kernel where its spans can merge in one
+  thread-block cluster (sequences up to 2048 keys, the whole grid in one wave of one
+  CTA per SM) or from 32 (sequence, KV head) pairs up, where it was measured faster;
+  else the CUDA-core kernel.
 
 The workspace is held per device here (its counters must start at zero; every completed
 call leaves them so), or passed in.  ``q`` is ``[B, Hq, 128]``, the caches
