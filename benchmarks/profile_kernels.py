@@ -126,7 +126,8 @@ def main() -> int:
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=7168)
     ap.add_argument("--k", type=int, default=8192)
-    ap.add_argument("--block-n", type=int, default=256)
+    ap.add_argument("--block-n", type=lambda v: v if v == "pair" else int(v), default="pair",
+                    help="gemm: 256, 128 or pair (a CTA pair per 256 x 256 tile)")
     ap.add_argument("--batch", type=int, default=8)
     ap.add_argument("--heads", type=int, default=8)
     ap.add_argument("--kv-heads", type=int, default=1)

@@ -400,14 +400,13 @@ class Comm {
   }
 
   void ag_gemm(const at::Tensor& x_shard, const at::Tensor& w, at::Tensor& out, at::Tensor& err, int copy_ctas,
-               int max_ctas, int copy_order) {
-    tc::ag_gemm(region(), x_shard, w, out, err, copy_ctas, max_ctas, copy_order);
+               int max_ctas) {
+    tc::ag_gemm(region(), x_shard, w, out, err, copy_ctas, max_ctas);
   }
 
   void ag_gemm_fp8(const at::Tensor& xq_shard, const at::Tensor& sfa_shard, const at::Tensor& w,
-                   const at::Tensor& sfw, at::Tensor& out, at::Tensor& err, int copy_ctas, int max_ctas,
-                   int copy_order) {
-    tc::ag_gemm_fp8(region(), xq_shard, sfa_shard, w, sfw, out, err, copy_ctas, max_ctas, copy_order);
+                   const at::Tensor& sfw, at::Tensor& out, at::Tensor& err, int copy_ctas, int max_ctas) {
+    tc::ag_gemm_fp8(region(), xq_shard, sfa_shard, w, sfw, out, err, copy_ctas, max_ctas);
   }
   void gemm_rs_fp8(const at::Tensor& a, const at::Tensor& sfa, const at::Tensor& w, const at::Tensor& sfw,
                    at::Tensor& out, at::Tensor& err, int max_ctas) {
@@ -527,6 +526,7 @@ uint64_t layout_total(int world, uint64_t lam_cap, uint64_t ll_cap, uint64_t pus
 
 void register_trace(py::module_& m);
 void register_gemm(py::module_& m);
+void register_gemm_pair(py::module_& m);
 void register_decode(py::module_& m);
 void register_skinny(py::module_& m);
 void register_fp8(py::module_& m);
@@ -586,12 +586,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
            py::arg("valid_out_bytes"), py::arg("copy_self"), py::arg("threads") = 0, py::arg("max_blocks") = 0)
       .def("barrier", &Comm::barrier, py::arg("blocks") = 1)
       .def("ag_gemm", &Comm::ag_gemm, py::arg("x_shard"), py::arg("w"), py::arg("out"), py::arg("err"),
-           py::arg("copy_ctas") = 16, py::arg("max_ctas") = 0, py::arg("copy_order") = 0)
+           py::arg("copy_ctas") = 16, py::arg("max_ctas") = 0)
       .def("gemm_rs", &Comm::gemm_rs, py::arg("a"), py::arg("w"), py::arg("out"), py::arg("err"),
            py::arg("max_ctas") = 0)
       .def("ag_gemm_fp8", &Comm::ag_gemm_fp8, py::arg("xq_shard"), py::arg("sfa_shard"), py::arg("w"),
-           py::arg("sfw"), py::arg("out"), py::arg("err"), py::arg("copy_ctas") = 8, py::arg("max_ctas") = 0,
-           py::arg("copy_order") = 0)
+           py::arg("sfw"), py::arg("out"), py::arg("err"), py::arg("copy_ctas") = 8, py::arg("max_ctas") = 0)
       .def("gemm_rs_fp8", &Comm::gemm_rs_fp8, py::arg("a"), py::arg("sfa"), py::arg("w"), py::arg("sfw"),
            py::arg("out"), py::arg("err"), py::arg("max_ctas") = 0)
       .def("fused_norm", &Comm::fused_norm, py::arg("ins"), py::arg("residuals"), py::arg("gamma"), py::arg("eps"),
@@ -615,6 +614,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
 
   register_trace(m);
   register_gemm(m);
+  register_gemm_pair(m);
   register_decode(m);
   register_skinny(m);
   register_fp8(m);

@@ -94,7 +94,6 @@ struct GemmParams {
   // ag copy role
   const char* shard;
   int copy_ctas;
-  int copy_order;    // 0: chunks (or their slices) spread over the copy CTAs; 1: chunk-major per warp
   // fp8: UE8M0 scale chunks (512 bytes per 128 rows and 128 K), laid out [row block][K block]
   const uint8_t* sfa;       // A's (ag: this rank's shard's)
   const uint8_t* sfb;
@@ -187,68 +186,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   // orders its stores before its count with a system-scope fence, and the CTA that
   // completes the count (a counter in this rank's control words, reset by that CTA)
   // fences again and raises the flags.
-  if (int(blockIdx.x) < copy_ctas && p.copy_order == 1) {
-    // Chunk-major, per warp: every copy warp pushes an equal slice of chunk 0, then of
-    // chunk 1, ..., so chunks complete in the order the GEMM consumes them (chunk c of
-    // every shard before chunk c+1) instead of all at the end.  Each warp publishes its
-    // slice by itself (its lanes' stores, ordered by __syncwarp, before a system-scope
-    // fence and its count), so one warp's drain does not hold up the others; the warp
-    // that completes a chunk's count (a counter in this rank's control words, reset by
-    // that warp) fences again and raises the chunk's flag at every peer.
-    const int chunks = p.shard_rows / kBM;
-    const int nw = copy_ctas * kWarps, gw = int(blockIdx.x) * kWarps + warp;
-    const uint64_t chunk_packs = uint64_t(kBM) * p.K * kEsz / kPack;
-    const uint64_t sf_packs = F8 ? uint64_t(p.K / kBKe) * 512 / kPack : 0;
-    Ctrl* ctrl = ctrl_of(p);
-    for (int c = 0; c < chunks; ++c) {
-      const uint64_t lo = chunk_packs * gw / nw, hi = chunk_packs * (gw + 1) / nw;
-      const Pack16* src = reinterpret_cast<const Pack16*>(p.shard) + uint64_t(c) * chunk_packs;
-      for (uint64_t i0 = lo + lane; i0 < hi; i0 += uint64_t(kCopyPpt) * 32) {
-        Pack16 v[kCopyPpt];
-#pragma unroll
-        for (int k2 = 0; k2 < kCopyPpt; ++k2) {
-          const uint64_t i = i0 + uint64_t(k2) * 32;
-          if (i < hi) v[k2] = m.ld_input(src + i);
-        }
-#pragma unroll
-        for (int k2 = 0; k2 < kCopyPpt; ++k2) {
-          const uint64_t i = i0 + uint64_t(k2) * 32;
-          if (i < hi)
-            for (int k = 1; k < W; ++k) {
-              const int q = (rank + k) % W;
-              m.st_remote(reinterpret_cast<Pack16*>(slot(p, q, parity, rank)) + uint64_t(c) * chunk_packs + i,
-                          v[k2]);
-            }
-        }
-      }
-      if (F8) {
-        const uint64_t slo = sf_packs * gw / nw, shi = sf_packs * (gw + 1) / nw;
-        const Pack16* ssrc = reinterpret_cast<const Pack16*>(p.sfa) + uint64_t(c) * sf_packs;
-        for (uint64_t i = slo + lane; i < shi; i += 32) {
-          Pack16 v = m.ld_input(ssrc + i);
-          for (int k = 1; k < W; ++k) {
-            const int q = (rank + k) % W;
-            m.st_remote(reinterpret_cast<Pack16*>(slot(p, q, parity, rank) + p.sfa_slot_off) +
-                            uint64_t(c) * sf_packs + i, v);
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) {
-        m.fence_sys();
-        const uint32_t prev = atomicAdd(&ctrl->chunk_count[c], 1u);
-        if (prev == uint32_t(nw) - 1u) {
-          m.fence_sys();
-          ctrl->chunk_count[c] = 0;  // every warp counted: re-armed for the next collective
-          for (int k = 1; k < W; ++k) m.st_release_u32(gflag(p, (rank + k) % W, rank, c), seq);
-        }
-      }
-      __syncwarp();
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) finish_op(m, ctrl_of(p), seq, gridDim.x);
-    return;
-  }
   if (int(blockIdx.x) < copy_ctas) {
     const int chunks = p.shard_rows / kBM;
     const int slices = max(1, copy_ctas / max(1, chunks));
@@ -665,8 +602,7 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, at::Tensor& e
 }
 
 void ag_gemm(const RegionDesc& reg, const at::Tensor& x_shard, const at::Tensor& B, at::Tensor& C, at::Tensor& err,
-             int copy_ctas, int max_ctas, int copy_order) {
-  if (copy_order != 0 && copy_order != 1) throw std::invalid_argument("copy_order: 0 spread, 1 chunk-major");
+             int copy_ctas, int max_ctas) {
   check_mat(x_shard, "x_shard");
   check_mat(B, "B");
   check_mat(C, "C");
@@ -688,7 +624,6 @@ void ag_gemm(const RegionDesc& reg, const at::Tensor& x_shard, const at::Tensor&
   p.slot_rows = int(reg.push_cap / row_bytes);
   p.shard = static_cast<const char*>(x_shard.data_ptr());
   p.copy_ctas = W > 1 ? std::max(1, copy_ctas) : 0;
-  p.copy_order = copy_order;
   CUtensorMap ma = make_map(x_shard.data_ptr(), shard_rows, K, K, kBM);
   // every push slot of this rank's region, both parities, as one [2*W*slot_rows, K] matrix
   CUtensorMap ma2 = make_map(reg.base[reg.rank] + reg.push_off, uint64_t(2) * W * p.slot_rows, K, K, kBM);
@@ -773,9 +708,7 @@ void gemm_fp8(const at::Tensor& A, const at::Tensor& sfa, const at::Tensor& B, c
 }
 
 void ag_gemm_fp8(const RegionDesc& reg, const at::Tensor& xq_shard, const at::Tensor& sfa_shard, const at::Tensor& B,
-                 const at::Tensor& sfb, at::Tensor& C, at::Tensor& err, int copy_ctas, int max_ctas,
-                 int copy_order) {
-  if (copy_order != 0 && copy_order != 1) throw std::invalid_argument("copy_order: 0 spread, 1 chunk-major");
+                 const at::Tensor& sfb, at::Tensor& C, at::Tensor& err, int copy_ctas, int max_ctas) {
   check_fp8_mat(xq_shard, "xq_shard");
   check_fp8_mat(B, "B");
   check_mat(C, "C");
@@ -800,7 +733,6 @@ void ag_gemm_fp8(const RegionDesc& reg, const at::Tensor& xq_shard, const at::Te
   p.slot_rows = int(reg.push_cap / uint64_t(K));
   p.shard = static_cast<const char*>(xq_shard.data_ptr());
   p.copy_ctas = W > 1 ? std::max(1, copy_ctas) : 0;
-  p.copy_order = copy_order;
   p.sfa = static_cast<const uint8_t*>(sfa_shard.data_ptr());
   p.sfb = static_cast<const uint8_t*>(sfb.data_ptr());
   p.sfa_slot_off = data_bytes;

@@ -16,12 +16,11 @@ struct RegionDesc {
 };
 
 namespace tc {
-// copy_order: 0 spreads the shard's chunks (or their slices) over the copy CTAs; 1
-// pushes the chunks one after another, every copy warp taking a slice of each.
+// The copy CTAs spread the shard's chunks (or slices of them) among themselves.
 void ag_gemm(const RegionDesc& reg, const at::Tensor& x_shard, const at::Tensor& B, at::Tensor& C, at::Tensor& err,
-             int copy_ctas, int max_ctas, int copy_order);
+             int copy_ctas, int max_ctas);
 void ag_gemm_fp8(const RegionDesc& reg, const at::Tensor& xq_shard, const at::Tensor& sfa_shard, const at::Tensor& B,
-                 const at::Tensor& sfb, at::Tensor& C, at::Tensor& err, int copy_ctas, int max_ctas, int copy_order);
+                 const at::Tensor& sfb, at::Tensor& C, at::Tensor& err, int copy_ctas, int max_ctas);
 void gemm_rs_fp8(const RegionDesc& reg, const at::Tensor& A, const at::Tensor& sfa, const at::Tensor& B,
                  const at::Tensor& sfb, at::Tensor& C_shard, at::Tensor& err, int max_ctas);
 void gemm_rs(const RegionDesc& reg, const at::Tensor& A, const at::Tensor& B, at::Tensor& C_shard, at::Tensor& err,

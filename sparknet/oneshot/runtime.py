@@ -72,19 +72,6 @@ OP_NAMES = {1: "all-reduce", 2: "all-gather", 3: "reduce-scatter", 4: "exchange"
 
 ENV_TIMEOUT_MS = "SPARKNET_TIMEOUT_MS"
 ENV_PDL = "SPARKNET_PDL"
-ENV_AG_COPY_ORDER = "SPARKNET_AG_COPY_ORDER"
-AG_COPY_ORDERS = {"spread": 0, "chunk-major": 1}
-
-
-def ag_copy_order(order: Optional[str] = None) -> int:
-    """Copy schedule of the fused all-gather -> GEMM: ``spread`` (default: the shard's
-    chunks, or slices of them, spread over the copy CTAs at once) or ``chunk-major``
-    (every copy warp pushes a slice of chunk 0, then of chunk 1, ...: chunks land in the
-    order the GEMM consumes them).  ``order`` overrides ``SPARKNET_AG_COPY_ORDER``."""
-    name = order if order is not None else (os.environ.get(ENV_AG_COPY_ORDER) or "spread")
-    if name not in AG_COPY_ORDERS:
-        raise ValueError(f"all-gather copy order must be one of {sorted(AG_COPY_ORDERS)}, got {name!r}")
-    return AG_COPY_ORDERS[name]
 ENV_DISPATCH = "SPARKNET_ALLREDUCE_DISPATCH_MAX_BYTES"
 # Settings of the reference's RoCE transport have no meaning on NVLink; refused with
 # the reason instead of silently ignored.
@@ -215,7 +202,7 @@ def copy_ctas_for(shard_bytes: int, world: int, flops: int, *, sms: int = 148,
     """Copy CTAs for the fused all-gather -> GEMM so that pushing the shard to the
     ``world - 1`` peers takes about as long as the GEMM on the remaining SMs:
     c / (sms - c) = (bytes / push rate) / (flops / GEMM rate per SM).  Clamped to
-    [16, sms / 2]; rank-invariant (shapes and world only)."""
+    [min_ctas, sms / 2]; rank-invariant (shapes and world only)."""
     if world <= 1:
         return 0
     t_push = (world - 1) * shard_bytes / (push_gbs_per_cta * 1e9)       # seconds with one CTA
@@ -641,16 +628,15 @@ class NvlinkAllReduce:
         return self._gemm_err_word
 
     def ag_gemm(self, x_shard: torch.Tensor, w: torch.Tensor, *, out: Optional[torch.Tensor] = None,
-                copy_ctas: Optional[int] = None, copy_order: Optional[str] = None) -> torch.Tensor:
+                copy_ctas: Optional[int] = None) -> torch.Tensor:
         """``all_gather(x_shard, dim=0) @ w.T`` in one kernel (sequence-parallel prefill).
 
         ``x_shard`` is this rank's ``[T/W, K]`` rows, ``w`` this rank's ``[N, K]``
         column shard (K-major).  Copy CTAs push the shard to every peer chunk by chunk
         while tcgen05 tiles consume own rows first and peers' rows as they land.  The
         number of copy CTAs defaults to :func:`copy_ctas_for` (push time balanced against
-        GEMM time); ``copy_order`` picks their schedule (:func:`ag_copy_order`).
+        GEMM time).
         """
-        order = ag_copy_order(copy_order)
         if copy_ctas is None:
             copy_ctas = copy_ctas_for(x_shard.numel() * x_shard.element_size(), self.world_size,
                                       2 * x_shard.shape[0] * self.world_size * x_shard.shape[1] * w.shape[0])
@@ -663,7 +649,7 @@ class NvlinkAllReduce:
                     out = torch.empty((x_shard.shape[0] * self.world_size, w.shape[0]), dtype=x_shard.dtype,
                                       device=self.device)
                 self._order_stream(capturing)
-                self._comm.ag_gemm(x_shard, w, out, self._gemm_err(), int(copy_ctas), 0, order)
+                self._comm.ag_gemm(x_shard, w, out, self._gemm_err(), int(copy_ctas), 0)
                 self._peer_bytes += x_shard.numel() * x_shard.element_size()
                 self._mark_stream(capturing)
         return out
@@ -689,16 +675,14 @@ class NvlinkAllReduce:
         return out
 
     def ag_gemm_fp8(self, xq_shard: torch.Tensor, sfa_shard: torch.Tensor, w: torch.Tensor, sfw: torch.Tensor, *,
-                    out: Optional[torch.Tensor] = None, copy_ctas: Optional[int] = None,
-                    copy_order: Optional[str] = None) -> torch.Tensor:
+                    out: Optional[torch.Tensor] = None, copy_ctas: Optional[int] = None) -> torch.Tensor:
         """Block-scaled fp8 ``all_gather(x_shard) @ w.T`` in one kernel, bf16 out.
 
         ``xq_shard``/``sfa_shard`` and ``w``/``sfw`` come from
         ``sparknet.ops.fp8.quantize_act`` / ``quantize_weight`` (e4m3 with UE8M0 scales
         per 1 x 128 and 128 x 128).  The shard's rows and scales cross NVLink in fp8,
-        half the bytes of the bf16 gather.  ``copy_order`` as for :meth:`ag_gemm`.
+        half the bytes of the bf16 gather.
         """
-        order = ag_copy_order(copy_order)
         if copy_ctas is None:
             copy_ctas = copy_ctas_for(xq_shard.numel() + sfa_shard.numel(), self.world_size,
                                       2 * xq_shard.shape[0] * self.world_size * xq_shard.shape[1] * w.shape[0],
@@ -712,8 +696,7 @@ class NvlinkAllReduce:
                     out = torch.empty((xq_shard.shape[0] * self.world_size, w.shape[0]), dtype=torch.bfloat16,
                                       device=self.device)
                 self._order_stream(capturing)
-                self._comm.ag_gemm_fp8(xq_shard, sfa_shard, w, sfw, out, self._gemm_err(), int(copy_ctas), 0,
-                                       order)
+                self._comm.ag_gemm_fp8(xq_shard, sfa_shard, w, sfw, out, self._gemm_err(), int(copy_ctas), 0)
                 self._peer_bytes += xq_shard.numel() + sfa_shard.numel()
                 self._mark_stream(capturing)
         return out

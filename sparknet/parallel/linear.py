@@ -68,17 +68,15 @@ class _ParallelLinear:
 class ColumnParallelLinear(_ParallelLinear):
     """Output features sharded over ranks: weight ``[out/W, in]``."""
 
-    def __init__(self, weight_shard: torch.Tensor, runtime, *, fp8: bool = False, copy_order: Optional[str] = None):
+    def __init__(self, weight_shard: torch.Tensor, runtime, *, fp8: bool = False):
         super().__init__(weight_shard, runtime, fp8=fp8, what="[out/W, in]")
-        self.copy_order = copy_order
 
     def forward(self, x_shard: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Sequence-parallel: all-gather the token shards and multiply, fused."""
         if self.fp8:
             xq, sx = self._quantize(x_shard)
-            return self.runtime.ag_gemm_fp8(xq, sx, self.weight_q, self.weight_scales, out=out,
-                                            copy_order=self.copy_order)
-        return self.runtime.ag_gemm(x_shard, self.weight, out=out, copy_order=self.copy_order)
+            return self.runtime.ag_gemm_fp8(xq, sx, self.weight_q, self.weight_scales, out=out)
+        return self.runtime.ag_gemm(x_shard, self.weight, out=out)
 
     def decode(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Replicated activations: a local GEMM, no collective."""

@@ -9,7 +9,7 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 128), (1000, 1280, 1024), (384, 4096, 8192),
                                    (4096, 1280, 8192), (130, 96, 192)])
-@pytest.mark.parametrize("block_n", [256, 128])
+@pytest.mark.parametrize("block_n", [256, 128, "pair"])
 def test_gemm_matches_fp32(device, native, M, N, K, block_n):
     from sparknet.ops.gemm import gemm
 
@@ -32,11 +32,13 @@ def test_gemm_throughput(device, native):
     b = torch.randn(N, K, device=device).to(torch.bfloat16)
     c = torch.empty(M, N, dtype=torch.bfloat16, device=device)
     for _ in range(3):
-        gemm(a, b, c)
+        gemm(a, b, c, block_n=256)
+        gemm(a, b, c, block_n="pair")
         torch.mm(a, b.T)
     torch.cuda.synchronize()
     res = {}
-    for name, fn in (("tcgen05", lambda: gemm(a, b, c)), ("cublas", lambda: torch.mm(a, b.T))):
+    for name, fn in (("tcgen05", lambda: gemm(a, b, c, block_n=256)), ("tcgen05_pair", lambda: gemm(a, b, c, block_n="pair")),
+                     ("cublas", lambda: torch.mm(a, b.T))):
         st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         st.record()
         for _ in range(10):
@@ -45,8 +47,9 @@ def test_gemm_throughput(device, native):
         en.synchronize()
         res[name] = 2 * M * N * K * 10 / (st.elapsed_time(en) / 1000) / 1e12
     print(f"\nGEMM {M}x{N}x{K} TFLOP/s: {res}")
-    gemm(a, b, c, check=True)
-    assert res["tcgen05"] > 100
+    gemm(a, b, c, block_n=256, check=True)
+    gemm(a, b, c, block_n="pair", check=True)
+    assert res["tcgen05"] > 100 and res["tcgen05_pair"] > 100
 
 
 def test_fp8_gemm_throughput(device, native):

@@ -22,11 +22,11 @@ class Recorder:
 def test_bf16_forward_routes_to_the_fused_kernels():
     rt = Recorder()
     w = torch.zeros(256, 512, dtype=torch.bfloat16)
-    col = L.ColumnParallelLinear(w, rt, copy_order="chunk-major")
+    col = L.ColumnParallelLinear(w, rt)
     x = torch.zeros(128, 512, dtype=torch.bfloat16)
     assert col.forward(x) == "ag_gemm"
     name, args, kwargs = rt.calls[-1]
-    assert args[1] is col.weight and kwargs == {"out": None, "copy_order": "chunk-major"}
+    assert args[1] is col.weight and kwargs == {"out": None}
     row = L.RowParallelLinear(w, rt)
     assert row.forward(x) == "gemm_rs" and rt.calls[-1][2] == {"out": None}
 

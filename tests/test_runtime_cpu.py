@@ -127,18 +127,6 @@ def test_stream_switch_orders_after_the_previous_stream(monkeypatch):
     assert log[2:] == [("record", "b"), ("wait", "a", rt._stream_event)]
 
 
-def test_ag_copy_order_setting(monkeypatch):
-    from sparknet.oneshot.runtime import ag_copy_order
-
-    monkeypatch.delenv("SPARKNET_AG_COPY_ORDER", raising=False)
-    assert ag_copy_order() == 0 and ag_copy_order("chunk-major") == 1
-    monkeypatch.setenv("SPARKNET_AG_COPY_ORDER", "chunk-major")
-    assert ag_copy_order() == 1 and ag_copy_order("spread") == 0
-    monkeypatch.setenv("SPARKNET_AG_COPY_ORDER", "diagonal")
-    with pytest.raises(ValueError, match="copy order"):
-        ag_copy_order()
-
-
 def test_entry_point_imports_the_built_extension_in_a_fresh_interpreter():
     """What the build check runs after compiling: a new interpreter that has not
     imported torch yet must still import the extension."""

@@ -25,6 +25,9 @@ ALLOWED_BULK_QUALIFIERS = {
     "cp", "async", "bulk", "tensor", "1d", "2d", "3d", "4d", "5d", "tile",
     "shared::cluster", "shared::cta", "global", "mbarrier::complete_tx::bytes",
     "bulk_group", "prefetch", "L2", "L2::cache_hint", "commit_group", "wait_group", "read",
+    # a CTA-pair GEMM's tile load: into the issuing CTA's own shared memory, completing
+    # on an mbarrier that may sit in the other CTA of the pair
+    "cta_group::2",
 }
 
 

@@ -108,24 +108,6 @@ def main():
         failures.append(f"gemm_rs_fp8 relative error {err}")
     if rt.gemm_error() or rt.failure():
         failures.append(f"error word (fp8) {rt.gemm_error()} / {rt.failure()}")
-    # the chunk-major copy schedule of the all-gather -> GEMM (opt-in: SPARKNET_PREFILL_CHUNK_MAJOR=1)
-    chunk_major = os.environ.get("SPARKNET_PREFILL_CHUNK_MAJOR") == "1"
-    if chunk_major:
-        for copy_ctas in (None, 1, 16):
-            got = rt.ag_gemm(x, w, copy_ctas=copy_ctas, copy_order="chunk-major")
-            want = gathered_fp32(x) @ w.float().T
-            torch.cuda.synchronize()
-            err = (got.float() - want).abs().max().item() / max(1e-6, want.abs().max().item())
-            if err > 1e-2:
-                failures.append(f"ag_gemm chunk-major ({copy_ctas} copy CTAs) relative error {err}")
-        got = rt.ag_gemm_fp8(xq, sx, wq, sw, copy_order="chunk-major")
-        want = torch.cat(parts) @ fp8.dequantize(wq, sw).T
-        torch.cuda.synchronize()
-        err = (got.float() - want).abs().max().item() / max(1e-6, want.abs().max().item())
-        if err > 1e-2:
-            failures.append(f"ag_gemm_fp8 chunk-major relative error {err}")
-        if rt.gemm_error() or rt.failure():
-            failures.append(f"error word (chunk-major) {rt.gemm_error()} / {rt.failure()}")
     results["correct"] = not failures
     # -- timing at the prefill shapes
     if os.environ.get("SPARKNET_PREFILL_BENCH", "1") == "1" and not failures:
@@ -142,11 +124,6 @@ def main():
                            "nvlink_bytes_in": (world - 1) * (T // world) * H * 2}
             cases[name + "_copy16"] = {"fused_ms": fused16, "nccl_cublas_ms": base, "flops": 2 * T * H * n,
                                        "nvlink_bytes_in": (world - 1) * (T // world) * H * 2}
-            if chunk_major:
-                fused_cm = timed(lambda: rt.ag_gemm(x, w, out=out, copy_order="chunk-major"))
-                cases[name + "_chunk_major"] = {"fused_ms": fused_cm, "nccl_cublas_ms": base,
-                                                "flops": 2 * T * H * n,
-                                                "nvlink_bytes_in": (world - 1) * (T // world) * H * 2}
         for name, kk in (("gemm_rs_o", H // world), ("gemm_rs_down", F // world)):
             a = torch.randn(T, kk, generator=g, device=device).to(torch.bfloat16)
             w = (0.02 * torch.randn(H, kk, generator=g, device=device)).to(torch.bfloat16)
@@ -165,12 +142,6 @@ def main():
             fused = timed(lambda: rt.ag_gemm_fp8(xq, sx, wq, sw, out=out))
             cases[name] = {"fused_ms": fused, "nccl_cublas_ms": cases[name[:-4]]["nccl_cublas_ms"],
                            "flops": 2 * T * H * n, "nvlink_bytes_in": (world - 1) * (T // world) * H}
-            if chunk_major:
-                fused_cm = timed(lambda: rt.ag_gemm_fp8(xq, sx, wq, sw, out=out, copy_order="chunk-major"))
-                cases[name + "_chunk_major"] = {"fused_ms": fused_cm,
-                                                "nccl_cublas_ms": cases[name[:-4]]["nccl_cublas_ms"],
-                                                "flops": 2 * T * H * n,
-                                                "nvlink_bytes_in": (world - 1) * (T // world) * H}
         for name, kk in (("gemm_rs_o_fp8", H // world), ("gemm_rs_down_fp8", F // world)):
             aq, sa = fp8.quantize_act(torch.randn(T, kk, generator=g, device=device).to(torch.bfloat16))
             wq, sw = fp8.quantize_weight((0.02 * torch.randn(H, kk, generator=g, device=device)).to(torch.bfloat16))
