@@ -1,12 +1,12 @@
 // tcgen05 GEMM over CTA pairs (cta_group::2) for sm_100a:  C[M, N] = A[M, K] B[N, K]^T.
 //
-// A pair of CTAs (a cluster of 2, fixed at compile time) owns a 256 x 256 output tile.
-// Each CTA stages 128 rows of A and 128 rows of B per K step (32 KB), so a stage costs
-// each SM half the B bytes of a one-CTA 128 x 256 tile, and the pair's tensor cores
-// read one 256 x 256 x 16 MMA from both CTAs' shared memory.  One elected thread of the
-// even CTA issues every MMA; each CTA's TMEM holds its own 128 rows of the fp32
-// accumulator (two 256-column buffers, so the epilogue of one tile overlaps the MMAs of
-// the next).
+// A pair of CTAs (a cluster of 2, fixed at compile time) owns a 256 x BN output tile
+// (BN = 256 is the one built).  Each CTA stages 128 rows of A and BN / 2 rows of B per
+// K step (32 KB), so a stage costs each SM half the B bytes of a one-CTA
+// 128 x 256 tile, and the pair's tensor cores read one 256 x BN x 16 MMA from both CTAs'
+// shared memory.  One elected thread of the even CTA issues every MMA; each CTA's TMEM
+// holds its own 128 rows of the fp32 accumulator (two BN-column buffers, so the
+// epilogue of one tile overlaps the MMAs of the next).
 //
 // Roles per CTA (192 threads): warp 0 issues the CTA's own TMA loads (one thread),
 // warp 1 allocates TMEM for the pair and, in the even CTA, issues the MMAs; warps 2..5
@@ -46,20 +46,30 @@ namespace pair {
 
 constexpr int kThreads = 192;
 constexpr int kEpiWarps = 4;
-constexpr int kTileM = 256, kTileN = 256;   // per pair
-constexpr int kHalf = 128;                  // rows of A and of B per CTA
+constexpr int kTileM = 256;                 // rows per pair tile
+constexpr int kHalf = 128;                  // rows of A per CTA
 constexpr int kStages = 6;
-constexpr int kStageBytes = 2 * kHalf * 128;                 // A half + B half, 128-byte rows
-constexpr int kStageRowBytes = 144;                          // epilogue staging row (padded)
-constexpr int kEpiBytes = kEpiWarps * 32 * kStageRowBytes;
-constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024 + 256;
-constexpr uint32_t kTmemCols = 512;                          // two 256-column accumulators
-constexpr int kGroupM = 8;                                   // pair row blocks per raster band
-static_assert(kSmemBytes <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
+constexpr uint32_t kTmemCols = 512;         // two accumulators of up to 256 columns
+constexpr int kGroupM = 8;                  // pair row blocks per raster band
 
-// Instruction descriptor: bf16 x bf16 -> f32, K-major A and B, M = 256 (the pair), N = 256.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kTileN >> 3) << 17) |
-                            (uint32_t(kTileM >> 4) << 24);
+// Shared-memory plan and instruction descriptor for a pair tile 256 x BN (BN / 2 rows of
+// B per CTA).  The epilogue drains the accumulator in chunks of CW columns.
+template <int BN>
+struct Plan {
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "pair tile N must be a multiple of 32 in 64..256");
+  static constexpr int kBRows = BN / 2;
+  static constexpr int kABytes = kHalf * 128;
+  static constexpr int kStageBytes = kABytes + kBRows * 128;      // 128-byte rows (64 bf16 of K)
+  static constexpr int kCW = BN % 64 == 0 ? 64 : 32;
+  static constexpr int kStageRowBytes = kCW * 2 + 16;             // padded staging row
+  static constexpr int kEpiBytes = kEpiWarps * 32 * kStageRowBytes;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 1024 + 256;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory plan exceeds the per-CTA limit");
+  static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-byte aligned for the 128-byte swizzle");
+  // bf16 x bf16 -> f32, K-major A and B, M = 256 (the pair), N = BN
+  static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) |
+                                     (uint32_t(kTileM >> 4) << 24);
+};
 
 __device__ __forceinline__ uint32_t rank_in_pair() {
   uint32_t r;
@@ -106,12 +116,13 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
-__device__ __forceinline__ void mma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+__device__ __forceinline__ void mma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate)
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -133,8 +144,12 @@ struct Params {
   uint32_t* err;
 };
 
+template <int BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     k_gemm_pair(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Params p) {
+  using P = Plan<BN>;
+  constexpr int kStageBytes = P::kStageBytes, kEpiBytes = P::kEpiBytes, kStageRowBytes = P::kStageRowBytes;
+  constexpr int kTileN = BN, kCW = P::kCW;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* epi = smem + kStages * kStageBytes;
@@ -210,11 +225,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           uint8_t* sa = smem + stage * kStageBytes;
-          uint8_t* sb = sa + kHalf * 128;
+          uint8_t* sb = sa + P::kABytes;
           if (leader) mbar_expect_tx(&full[stage], 2 * kStageBytes);
           const uint32_t fb = full0 + uint32_t(stage * sizeof(uint64_t));
           tma_load_pair(sa, &map_a, kb * kBK, m0 + int(cta) * kHalf, fb);
-          tma_load_pair(sb, &map_b, kb * kBK, n0 + int(cta) * kHalf, fb);
+          tma_load_pair(sb, &map_b, kb * kBK, n0 + int(cta) * P::kBRows, fb);
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
@@ -246,9 +261,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           uint8_t* sa = smem + stage * kStageBytes;
-          const uint64_t adesc = smem_desc_sw128(sa), bdesc = smem_desc_sw128(sa + kHalf * 128);
+          const uint64_t adesc = smem_desc_sw128(sa), bdesc = smem_desc_sw128(sa + P::kABytes);
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) mma_pair(d, adesc + uint64_t(2 * k), bdesc + uint64_t(2 * k), (kb | k) ? 1u : 0u);
+          for (int k = 0; k < kBK / 16; ++k)
+            mma_pair(d, adesc + uint64_t(2 * k), bdesc + uint64_t(2 * k), P::kIdesc, (kb | k) ? 1u : 0u);
           const uint32_t off = uint32_t(stage * sizeof(uint64_t));
           commit_pair(empty_at[0] + off);
           commit_pair(empty_at[1] + off);
@@ -283,14 +299,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int row0 = m0 + int(cta) * kHalf + quad * 32;
       const uint32_t taddr = tmem_base + (uint32_t(quad * 32) << 16) + uint32_t(acc * kTileN);
+      // kCW columns at a time: TMEM -> registers (this thread's row) -> staging rows ->
+      // stores with kCW / 8 lanes per row segment (256 / kCW rows per instruction)
+      constexpr int kLanesPerRow = kCW / 8, kRowsPerStore = 32 / kLanesPerRow;
 #pragma unroll 1
-      for (int c = 0; c < kTileN / 64; ++c) {
-        float v[64];
-        tmem_ld32(taddr + uint32_t(c * 64), v);
-        tmem_ld32(taddr + uint32_t(c * 64 + 32), v + 32);
+      for (int c = 0; c < kTileN / kCW; ++c) {
+        float v[kCW];
+#pragma unroll
+        for (int h = 0; h < kCW / 32; ++h) tmem_ld32(taddr + uint32_t(c * kCW + 32 * h), v + 32 * h);
         uint4* my_row = reinterpret_cast<uint4*>(wst + lane * kStageRowBytes);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < kCW / 8; ++q) {
           uint4 pk;
           pk.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
           pk.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
@@ -299,12 +318,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           my_row[q] = pk;
         }
         __syncwarp();
-        const int gn = n0 + c * 64 + (lane & 7) * 8;
+        const int seg = lane % kLanesPerRow;
+        const int gn = n0 + c * kCW + seg * 8;
 #pragma unroll
-        for (int rr = 0; rr < 8; ++rr) {
-          const int r = rr * 4 + (lane >> 3);
+        for (int rr = 0; rr < kLanesPerRow; ++rr) {
+          const int r = rr * kRowsPerStore + lane / kLanesPerRow;
           const int grow = row0 + r;
-          const uint4 pk = *reinterpret_cast<const uint4*>(wst + r * kStageRowBytes + (lane & 7) * 16);
+          const uint4 pk = *reinterpret_cast<const uint4*>(wst + r * kStageRowBytes + seg * 16);
           if (grow < p.M && gn < p.N) *reinterpret_cast<uint4*>(p.C + size_t(grow) * p.ldc + gn) = pk;
         }
         __syncwarp();
@@ -350,23 +370,31 @@ void gemm_pair(const at::Tensor& A, const at::Tensor& B, at::Tensor& C, at::Tens
   c10::cuda::CUDAGuard guard(A.device());
   pair::Params p{M, N, K, reinterpret_cast<__nv_bfloat16*>(C.data_ptr()), int(C.stride(0)),
                  reinterpret_cast<uint32_t*>(err.data_ptr())};
-  CUtensorMap ma = make_map(A.data_ptr(), M, K, A.stride(0), pair::kHalf);
-  CUtensorMap mb = make_map(B.data_ptr(), N, K, B.stride(0), pair::kHalf);
   int sms = 0;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, A.device().index());
-  const int tiles = ((M + pair::kTileM - 1) / pair::kTileM) * ((N + pair::kTileN - 1) / pair::kTileN);
-  int pairs = std::min(tiles, sms / 2);
-  if (max_pairs > 0) pairs = std::min(pairs, max_pairs);
-  static bool attr_done[64] = {};
   const int dev = A.device().index();
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int pair_slots = sms / 2;
+  if (max_pairs > 0) pair_slots = std::min(pair_slots, max_pairs);
+  // Pair tile N is 256.  Narrower tiles (224, 192) fill the persistent grid's last round
+  // better (8192 x 7168: 13.8 rounds of 74 pairs instead of 12.1) but measured slower at
+  // every shape tried (8192 x 7168 x 8192: 1368 / 1238 against 1433 TFLOP/s): each MMA
+  // still reads all of A's tile, so A costs more shared-memory bandwidth per FLOP.
+  const int tiles_m = (M + pair::kTileM - 1) / pair::kTileM;
+  const int bn = 256;
+  const int tiles = tiles_m * ((N + bn - 1) / bn);
+  const int pairs = std::min(tiles, pair_slots);
+  auto s = at::cuda::getCurrentCUDAStream(dev).stream();
+  CUtensorMap ma = make_map(A.data_ptr(), M, K, A.stride(0), pair::kHalf);
+  CUtensorMap mb = make_map(B.data_ptr(), N, K, B.stride(0), uint32_t(bn / 2));
+  using P = pair::Plan<256>;
+  static bool attr_done[64] = {};
   if (dev < 0 || dev >= 64 || !attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(pair::k_gemm_pair, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         pair::kSmemBytes);
+    cudaError_t e = cudaFuncSetAttribute(pair::k_gemm_pair<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         P::kSmemBytes);
     if (e != cudaSuccess) throw std::runtime_error(std::string("gemm_pair smem attribute: ") + cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) attr_done[dev] = true;
   }
-  auto s = at::cuda::getCurrentCUDAStream(dev).stream();
-  pair::k_gemm_pair<<<2 * pairs, pair::kThreads, pair::kSmemBytes, s>>>(ma, mb, p);
+  pair::k_gemm_pair<256><<<2 * pairs, pair::kThreads, P::kSmemBytes, s>>>(ma, mb, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("gemm_pair launch: ") + cudaGetErrorString(e));
 }

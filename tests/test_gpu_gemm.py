@@ -8,7 +8,7 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 128), (1000, 1280, 1024), (384, 4096, 8192),
-                                   (4096, 1280, 8192), (130, 96, 192)])
+                                   (4096, 1280, 8192), (130, 96, 192), (1000, 1344, 1024), (4096, 7168, 512)])
 @pytest.mark.parametrize("block_n", [256, 128, "pair"])
 def test_gemm_matches_fp32(device, native, M, N, K, block_n):
     from sparknet.ops.gemm import gemm
