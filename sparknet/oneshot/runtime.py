@@ -825,14 +825,26 @@ class NvlinkAllReduce:
             return False
         return dim == 0 or (inp.shape[-1] * inp.element_size()) % PACK_BYTES == 0
 
+    def _gather_algorithm_fits(self, algo: str, shard_bytes: int) -> bool:
+        if algo == "ll":
+            return shard_bytes <= self._caps[1]
+        if algo == "nvls":
+            return self.has_multicast and shard_bytes * self.world_size <= self._mc[2]
+        return algo == "push"
+
     def _launch_gather(self, src: torch.Tensor, dst: torch.Tensor, shard_bytes: int, row_bytes: int,
-                       dst_row_stride: int, dst_src_stride: int) -> None:
-        algo = self.policy.all_gather_algorithm(shard_bytes, row_bytes=row_bytes or shard_bytes,
-                                                nvls_available=self.has_multicast)
-        if algo == "ll" and shard_bytes > self._caps[1]:
-            algo = "push"
-        if algo == "nvls" and shard_bytes * self.world_size > self._mc[2]:
-            algo = "push"
+                       dst_row_stride: int, dst_src_stride: int, forced: Optional[str] = None) -> None:
+        if forced is not None:
+            if not self._gather_algorithm_fits(forced, shard_bytes):
+                raise ValueError(f"all-gather algorithm {forced!r} cannot carry a {shard_bytes}-byte shard here")
+            algo = forced
+        else:
+            algo = self.policy.all_gather_algorithm(shard_bytes, row_bytes=row_bytes or shard_bytes,
+                                                    nvls_available=self.has_multicast)
+            if algo == "ll" and shard_bytes > self._caps[1]:
+                algo = "push"
+            if algo == "nvls" and shard_bytes * self.world_size > self._mc[2]:
+                algo = "push"
         self._comm.all_gather([src], [dst], shard_bytes, row_bytes, dst_row_stride, dst_src_stride,
                               GATHER_CODES[algo], self._threads, self._blocks)
         self._calls["all_gather"] += 1
@@ -842,8 +854,12 @@ class NvlinkAllReduce:
             self._peer_bytes += shard_bytes * (2 if algo == "ll" else 1)  # LL8 carries a flag per word
 
     def all_gather(self, inp: torch.Tensor, *, dim: int = -1, out: Optional[torch.Tensor] = None,
-                   stream: object = None, sliced: bool = False) -> torch.Tensor:
-        """Concatenate every rank's ``inp`` along ``dim`` (0 or the last dim)."""
+                   stream: object = None, sliced: bool = False, algorithm: Optional[str] = None) -> torch.Tensor:
+        """Concatenate every rank's ``inp`` along ``dim`` (0 or the last dim).  ``algorithm``
+        (``ll``, ``push`` or ``nvls``) overrides the policy's choice, as the probe's
+        crossover sweep does; a choice that cannot carry the shard raises."""
+        if algorithm is not None and algorithm not in GATHER_CODES:
+            raise ValueError(f"all-gather algorithm must be one of {sorted(GATHER_CODES)}, got {algorithm!r}")
         with self._lock:
             self.check_health()
             if not self.should_all_gather(inp, dim, sliced=sliced):
@@ -858,6 +874,9 @@ class NvlinkAllReduce:
             with torch.cuda.device(self.device), self._stream_ctx(stream):
                 capturing = torch.cuda.is_current_stream_capturing()
                 if nbytes > self.max_gather_bytes:
+                    if algorithm not in (None, "push"):
+                        raise ValueError(f"a {nbytes}-byte shard is gathered in slices by the push kernel; "
+                                         f"{algorithm!r} cannot carry it")
                     out = torch.empty(shape, dtype=inp.dtype, device=inp.device) if out is None else out
                     self._order_stream(capturing)
                     self._sliced_gather(inp, out, dim)
@@ -872,7 +891,7 @@ class NvlinkAllReduce:
                         row = inp.shape[-1] * inp.element_size()
                         row_stride, src_stride = row * self.world_size, row
                     self._order_stream(capturing)
-                    self._launch_gather(inp, out, nbytes, row, row_stride, src_stride)
+                    self._launch_gather(inp, out, nbytes, row, row_stride, src_stride, forced=algorithm)
                     self._mark_stream(capturing)
                     result = out
                 else:
@@ -880,7 +899,7 @@ class NvlinkAllReduce:
                     staged, gathered = self._gather_scratch(padded)
                     staged[:nbytes].copy_(inp.reshape(-1).view(torch.uint8))
                     self._order_stream(capturing)
-                    self._launch_gather(staged, gathered, padded, 0, 0, padded)
+                    self._launch_gather(staged, gathered, padded, 0, 0, padded, forced=algorithm)
                     self._mark_stream(capturing)
                     stacked = (gathered.view(self.world_size, padded)[:, :nbytes].reshape(-1).view(inp.dtype)
                                .reshape(self.world_size, *inp.shape))

@@ -125,10 +125,12 @@ class PolicyCommunicator:
         self._dist.all_reduce(result)
         return result
 
-    def all_gather(self, tensor, dim=0, *, force_nccl: bool = False):
-        r = self.route("all_gather", tensor, dim=dim, forced="nccl" if force_nccl else None)
+    def all_gather(self, tensor, dim=0, *, force_nccl: bool = False, algorithm: str | None = None):
+        """``algorithm`` (``ll``, ``push`` or ``nvls``) forces the NVLink kernel's protocol
+        (the crossover sweep's arms); ``force_nccl`` forces NCCL."""
+        r = self.route("all_gather", tensor, dim=dim, forced="nccl" if force_nccl else algorithm)
         if r.nvlink:
-            return self.runtime.all_gather(tensor, dim=dim)
+            return self.runtime.all_gather(tensor, dim=dim, algorithm=algorithm)
         pieces = [self._torch.empty_like(tensor) for _ in range(self.world_size)]
         self._dist.all_gather(pieces, tensor.contiguous())
         return self._torch.cat(pieces, dim=dim)
@@ -192,7 +194,7 @@ def nvlink_bytes_expected(route: Route, world: int) -> int:
             return 2 * n * peers // world
         return 0
     if route.operation == "all_gather":
-        return n * peers
+        return n if route.backend == "nvls" else n * peers  # NVLS: one copy, the switch fans it out
     return n * peers // world
 
 
@@ -518,6 +520,10 @@ def _operation(comm, runtime, name, arm, local, scattered, nbytes):
             if arm == "nvls" and (not runtime.has_multicast or nbytes > runtime._mc[2]):
                 return None
         return lambda: comm.all_reduce(local, algorithm=arm)
+    if name == "all_gather" and arm == "nvls":
+        if runtime is None or not runtime.has_multicast or nbytes * runtime.world_size > runtime._mc[2]:
+            return None
+        return lambda: comm.all_gather(local, dim=0, algorithm="nvls")
     if name in ("all_gather", "reduce_scatter"):
         if arm not in ("policy", "oneshot", "nccl"):
             return None

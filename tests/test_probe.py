@@ -177,3 +177,5 @@ def test_runtime_counters_held_to_routing():
     assert nvlink_bytes_expected(Route("all_reduce", "twoshot", 1024), 8) == 2 * 1024 * 7 // 8
     assert nvlink_bytes_expected(Route("all_reduce", "nccl", 1024), 8) == 0
     assert nvlink_bytes_expected(Route("all_gather", "oneshot", 1024), 4) == 3 * 1024
+    assert nvlink_bytes_expected(Route("all_gather", "nvls", 1024), 4) == 1024  # one copy, fanned out by the switch
+    assert nvlink_bytes_expected(Route("all_gather", "ll", 1024), 4) == 3 * 1024
