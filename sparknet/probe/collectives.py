@@ -426,9 +426,17 @@ def _benchmark(comm, runtime, args, world, rank, device, cpu_group, capture_cont
     import torch
     import torch.distributed as dist
 
-    arms = ["policy"]
-    if args.sweep and runtime is not None:
-        arms = ["oneshot", "twoshot"] + (["nvls"] if runtime.has_multicast else []) + ["nccl"]
+    def arms_for(operation: str) -> list[str]:
+        """The sweep's arms per operation (every algorithm the runtime has for it), else
+        the policy's own choice."""
+        if not args.sweep or runtime is None:
+            return ["policy"]
+        nvls = ["nvls"] if runtime.has_multicast else []
+        if operation == "all_reduce":
+            return ["oneshot", "twoshot"] + nvls + ["nccl"]
+        if operation == "all_gather":
+            return ["ll", "push"] + nvls + ["nccl"]
+        return ["oneshot", "nccl"]
     calls_per_graph, replays_per_sample, samples_per_case = 16, 16, 5
     timings = []
     for dtype in dtypes:
@@ -437,7 +445,7 @@ def _benchmark(comm, runtime, args, world, rank, device, cpu_group, capture_cont
             local = torch.full((length,), rank + 1, device=device, dtype=dtype)
             scattered = torch.cat([local + 8 * p for p in range(world)])
             for name in args.operations:
-                for arm in arms:
+                for arm in arms_for(name):
                     op = _operation(comm, runtime, name, arm, local, scattered, nbytes)
                     if op is None:
                         continue
@@ -520,10 +528,12 @@ def _operation(comm, runtime, name, arm, local, scattered, nbytes):
             if arm == "nvls" and (not runtime.has_multicast or nbytes > runtime._mc[2]):
                 return None
         return lambda: comm.all_reduce(local, algorithm=arm)
-    if name == "all_gather" and arm == "nvls":
-        if runtime is None or not runtime.has_multicast or nbytes * runtime.world_size > runtime._mc[2]:
+    if name == "all_gather" and arm in ("ll", "push", "nvls"):
+        # the NVLink all-gather with its protocol forced: LL8 (flag in every 8-byte word),
+        # the bulk push (flag per shard) or NVLS multicast stores
+        if runtime is None or nbytes > runtime.max_gather_bytes or not runtime._gather_algorithm_fits(arm, nbytes):
             return None
-        return lambda: comm.all_gather(local, dim=0, algorithm="nvls")
+        return lambda: comm.all_gather(local, dim=0, algorithm=arm)
     if name in ("all_gather", "reduce_scatter"):
         if arm not in ("policy", "oneshot", "nccl"):
             return None
