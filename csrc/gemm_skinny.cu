@@ -31,6 +31,7 @@
 #include <algorithm>
 #include <stdexcept>
 #include <string>
+#include <type_traits>
 
 #include "sparknet/dev_mem.cuh"
 #include "sparknet/gemm_fused.h"
@@ -88,8 +89,8 @@ __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
 // grid (splits, tiles), cluster (splits, 1, 1): the K splits of one weight tile are one
 // thread-block cluster.  After the main loop each CTA parks its fp32 partial tile in
-// its own shared memory; after a cluster barrier, CTA r sums rows r, r + S, ... of the
-// tile over the S partials through distributed shared memory, in split order, and
+// its own shared memory; after a cluster barrier, CTA r sums its contiguous block of the
+// tile's rows over the S partials through distributed shared memory, in split order, and
 // writes them; a second cluster barrier keeps every partial alive until all reads are
 // done.  No global scratch, no atomics.
 //
@@ -107,7 +108,7 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
   uint64_t* empty = full + p.stages;
   uint64_t* done = empty + p.stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-  float* part = reinterpret_cast<float*>(base);  // [128][mp + 1] fp32, over the stage buffers once they are idle
+  float* part = reinterpret_cast<float*>(base);  // [mp][128] fp32 (token-major), over the idle stage buffers
 
   cg::cluster_group cluster = cg::this_cluster();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -125,7 +126,6 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
   const int nkb = max(0, min(kbps, p.K / kBK - kb0));
   volatile uint32_t* err = p.err;
   const uint32_t ncols = p.mp <= 32 ? 32u : (p.mp <= 64 ? 64u : (p.mp <= 128 ? 128u : 256u));
-  const int pitch = p.mp + 1;  // padded row of the parked partial
 
   if (threadIdx.x == 0) {
     stamp(p, 0);  // entry
@@ -202,82 +202,109 @@ __global__ void __launch_bounds__(kSkThreads) k_skinny(const __grid_constant__ C
       for (int j = 0; j < 16; ++j) v[j] = 0.0f;
     }
 #pragma unroll
-    for (int j = 0; j < 16; ++j) part[row * pitch + c * 16 + j] = v[j];
+    for (int j = 0; j < 16; ++j) part[(c * 16 + j) * kWRows + row] = v[j];  // a warp: 32 consecutive words
   }
   tc_fence_before();
   cluster.sync();  // every split's partial is parked
   if (threadIdx.x == 64) stamp(p, 6);
 
-  // Every DSMEM load of an output element is issued before the fixed-order sum.
-  if (p.mode == 0) {
-    // this CTA's rows: r = split, split + S, ...; thread -> (row, column) pairs
-    const int my_rows = (kWRows - split + S - 1) / S;
-    for (int e = threadIdx.x; e < my_rows * p.M; e += blockDim.x) {
-      const int r = split + (e / p.M) * S, m = e % p.M;
+  // CTA `split` writes a contiguous block of the tile's rows (mode 0) or row pairs
+  // (modes 1 and 2: gate/up halves, RoPE pairs).  The partials are parked token-major
+  // and neighbouring lanes take neighbouring rows, so a warp reads consecutive words of
+  // each partial (distributed shared memory is served in sectors, like global memory;
+  // the row-major layout read with rows across lanes took 2x longer) and stores
+  // neighbouring outputs of one token.  Loads are issued before the sums and stores
+  // they feed (the stores could alias them as far as the compiler knows); each sum runs
+  // over the splits in split order.
+  constexpr int kWarps = kSkThreads / 32;
+  auto partial = [&](int s, int r, int m) -> float {
+    return cluster.map_shared_rank(part, s)[m * kWRows + r];
+  };
+  // Rounding and writing one output (row r of the tile, or pair r, r + 64) for token m.
+  auto emit = [&](int r, int m, float x1, float x2) {
+    if (p.mode == 0) {
       const int n = tile * kWRows + r;
-      float v[kMaxSplits];
-#pragma unroll
-      for (int s = 0; s < kMaxSplits; ++s) v[s] = s < S ? cluster.map_shared_rank(part, s)[r * pitch + m] : 0.0f;
-      float acc = 0.0f;
-#pragma unroll
-      for (int s = 0; s < kMaxSplits; ++s) acc += v[s];
-      if (n < p.N) p.Y[size_t(m) * p.ldy + n] = __float2bfloat16_rn(acc);
+      if (n < p.N) p.Y[size_t(m) * p.ldy + n] = __float2bfloat16_rn(x1);
+      return;
     }
-  } else if (p.mode == 2) {
-    // one head per tile: rows r and r + 64 form a RoPE pair
-    const int my_rows = (64 - split + S - 1) / S;
-    for (int e = threadIdx.x; e < my_rows * p.M; e += blockDim.x) {
-      const int r = split + (e / p.M) * S, m = e % p.M;
-      float va[kMaxSplits], vb[kMaxSplits];
-#pragma unroll
-      for (int s = 0; s < kMaxSplits; ++s) {
-        const float* ps = cluster.map_shared_rank(part, s < S ? s : 0);
-        va[s] = s < S ? ps[r * pitch + m] : 0.0f;
-        vb[s] = s < S ? ps[(r + 64) * pitch + m] : 0.0f;
-      }
-      float x1 = 0.0f, x2 = 0.0f;
-#pragma unroll
-      for (int s = 0; s < kMaxSplits; ++s) {
-        x1 += va[s];
-        x2 += vb[s];
-      }
-      const int pos = p.positions[m];
-      __nv_bfloat16* dst;
-      if (tile < p.hq + p.hkv) {  // q or k: rotate
-        const float c = p.cos_t[size_t(pos) * 64 + r], sn = p.sin_t[size_t(pos) * 64 + r];
-        const float y1 = x1 * c - x2 * sn, y2 = x2 * c + x1 * sn;
-        x1 = y1;
-        x2 = y2;
-      }
-      if (tile < p.hq) dst = p.q_out + (size_t(m) * p.hq + tile) * kWRows;
-      else if (tile < p.hq + p.hkv)
-        dst = p.k_cache + ((size_t(m) * p.lmax + pos) * p.hkv + (tile - p.hq)) * kWRows;
-      else dst = p.v_cache + ((size_t(m) * p.lmax + pos) * p.hkv + (tile - p.hq - p.hkv)) * kWRows;
-      dst[r] = __float2bfloat16_rn(x1);
-      dst[r + 64] = __float2bfloat16_rn(x2);
+    if (p.mode == 1) {  // rows 0..63 gate, 64..127 up of the same 64 features
+      p.Y[size_t(m) * p.ldy + tile * 64 + r] = __float2bfloat16_rn(silu(x1) * x2);
+      return;
     }
+    const int pos = p.positions[m];
+    __nv_bfloat16* dst;
+    if (tile < p.hq + p.hkv) {  // q or k: rotate
+      const float cs = p.cos_t[size_t(pos) * 64 + r], sn = p.sin_t[size_t(pos) * 64 + r];
+      const float y1 = x1 * cs - x2 * sn, y2 = x2 * cs + x1 * sn;
+      x1 = y1;
+      x2 = y2;
+    }
+    if (tile < p.hq) dst = p.q_out + (size_t(m) * p.hq + tile) * kWRows;
+    else if (tile < p.hq + p.hkv)
+      dst = p.k_cache + ((size_t(m) * p.lmax + pos) * p.hkv + (tile - p.hq)) * kWRows;
+    else dst = p.v_cache + ((size_t(m) * p.lmax + pos) * p.hkv + (tile - p.hq - p.hkv)) * kWRows;
+    dst[r] = __float2bfloat16_rn(x1);
+    dst[r + 64] = __float2bfloat16_rn(x2);
+  };
+  const bool pairs = p.mode != 0;
+  const int span = pairs ? 64 : kWRows;  // rows (mode 0) or row pairs (modes 1, 2) of a tile
+  const int rb = (span + S - 1) / S, r0 = min(span, split * rb), r1 = min(span, r0 + rb);
+  if (S > 1) {
+    // Split K: a small block of rows per CTA, so all threads share its (row, token)
+    // elements, row-fastest, a batch at a time (4 single rows or 2 row pairs).
+    // Measured at 64 tokens against one warp per token: 39 against 54 us for
+    // 5120 x 8192, 23.7 against 30.9 us for 8192 x 4096.
+    const int nr = r1 - r0, total = max(0, nr) * p.M;
+    auto run = [&](auto batch_tag, auto pair_tag) {
+      constexpr int kBatch = decltype(batch_tag)::value;
+      constexpr bool kPairs = decltype(pair_tag)::value;
+      for (int e0 = threadIdx.x; e0 < total; e0 += kBatch * blockDim.x) {
+        float va[kBatch][kMaxSplits], vb[kBatch][kPairs ? kMaxSplits : 1];
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+          const int e = e0 + b * int(blockDim.x);
+          const bool in = e < total;
+          const int r = r0 + (in ? e % nr : 0), m = in ? e / nr : 0;
+#pragma unroll
+          for (int q = 0; q < kMaxSplits; ++q) {
+            va[b][q] = (in && q < S) ? partial(q, r, m) : 0.0f;
+            if constexpr (kPairs) vb[b][q] = (in && q < S) ? partial(q, r + 64, m) : 0.0f;
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+          const int e = e0 + b * int(blockDim.x);
+          if (e >= total) break;
+          float x1 = 0.0f, x2 = 0.0f;
+#pragma unroll
+          for (int q = 0; q < kMaxSplits; ++q) {
+            x1 += va[b][q];
+            if constexpr (kPairs) x2 += vb[b][q];
+          }
+          emit(r0 + e % nr, e / nr, x1, x2);
+        }
+      }
+    };
+    if (pairs) run(std::integral_constant<int, 2>{}, std::true_type{});
+    else run(std::integral_constant<int, 4>{}, std::false_type{});
   } else {
-    // SwiGLU: rows 0..63 gate, 64..127 up of the same 64 features
-    const int my_rows = (64 - split + S - 1) / S;
-    for (int e = threadIdx.x; e < my_rows * p.M; e += blockDim.x) {
-      // without split-K a warp's 32 rows of one token are contiguous in Y and conflict-free
-      // in the parked partial; with split-K neighbouring tokens of one row are
-      const bool row_fast = S == 1;
-      const int r = split + (row_fast ? e % my_rows : e / p.M) * S, m = row_fast ? e / my_rows : e % p.M;
-      float vg[kMaxSplits], vu[kMaxSplits];
+    // One split: the whole tile is this CTA's own partial.  Warp w takes tokens w, w + 4,
+    // ...; its lanes take the rows (no division per element) and read the partial from
+    // their own shared memory.  Measured at 64 tokens, 28672 x 8192: 98.8 us against
+    // 109.4 us with the element loop above.  The sum starts from 0.0f as in the split
+    // path, so both round the same value.
+    constexpr int kChunks = kWRows / 32;
+    for (int m = warp; m < p.M; m += kWarps) {
+      float v[kChunks];
 #pragma unroll
-      for (int s = 0; s < kMaxSplits; ++s) {
-        const float* ps = cluster.map_shared_rank(part, s < S ? s : 0);
-        vg[s] = s < S ? ps[r * pitch + m] : 0.0f;
-        vu[s] = s < S ? ps[(r + 64) * pitch + m] : 0.0f;
-      }
-      float g = 0.0f, u = 0.0f;
+      for (int c = 0; c < kChunks; ++c) v[c] = 0.0f + part[m * kWRows + c * 32 + lane];
+      if (!pairs) {
 #pragma unroll
-      for (int s = 0; s < kMaxSplits; ++s) {
-        g += vg[s];
-        u += vu[s];
+        for (int c = 0; c < kChunks; ++c) emit(c * 32 + lane, m, v[c], 0.0f);
+      } else {
+#pragma unroll
+        for (int c = 0; c < kChunks / 2; ++c) emit(c * 32 + lane, m, v[c], v[c + kChunks / 2]);
       }
-      p.Y[size_t(m) * p.ldy + tile * 64 + r] = __float2bfloat16_rn(silu(g) * u);
     }
   }
   cluster.sync();  // partials stay readable until every CTA of the cluster is done
@@ -317,7 +344,7 @@ void check_mat(const at::Tensor& t, const char* name) {
 }
 
 void launch_skinny(const at::Tensor& W, const at::Tensor& X, const SkinnyParams& p, const Plan& pl, int dev, bool pdl) {
-  if (size_t(kWRows) * (pl.mp + 1) * 4 > size_t(pl.stages) * (kWStage + pl.mp * kBK * 2))
+  if (size_t(kWRows) * pl.mp * 4 > size_t(pl.stages) * (kWStage + pl.mp * kBK * 2))
     throw std::logic_error("decode GEMM: the parked partial does not fit the stage buffers");
   CUtensorMap mw = make_map(W.data_ptr(), p.N, p.K, W.stride(0), kWRows);
   CUtensorMap mx = make_map(X.data_ptr(), p.M, p.K, X.stride(0), pl.mp);
