@@ -205,12 +205,13 @@ def cmd_policy_derive(args) -> int:
             return 2
         rows += sweep_rows(json.loads(Path(path).read_text()), int(world[2:]))
     if not rows:
-        print("error: no all-reduce sweep rows in the receipts", file=sys.stderr)
+        print("error: no all-reduce or all-gather sweep rows in the receipts", file=sys.stderr)
         return 1
     limits = derive_limits(rows)
-    table = {"source": args.source, "rows": sorted(rows, key=lambda r: (r["world"], r["nbytes"], r["arm"])),
+    order = lambda r: (r.get("operation", "all_reduce"), r["world"], r["nbytes"], r["arm"])  # noqa: E731
+    table = {"source": args.source, "rows": sorted(rows, key=order),
              "derived": {"oneshot_max": limits.oneshot_max, "dispatch_max": limits.dispatch_max,
-                         "nvls_min": limits.nvls_min}}
+                         "nvls_min": limits.nvls_min, "ll_max": limits.ll_max}}
     text = json.dumps(table, indent=1, sort_keys=False)
     if args.output:
         Path(args.output).write_text(text + "\n")

@@ -61,12 +61,12 @@ FALLBACK_ONESHOT_MAX = {2: 4 << 20, 4: 512 << 10, 8: 512 << 10}
 FALLBACK_DISPATCH_MAX = 2 << 20
 # Largest all-gather shard that travels in LL8 form (payload + flag per 8 bytes);
 # larger shards use bulk pushes with per-block flags (or NVLS broadcast when enabled).
-# LL doubles the bytes but needs no fence or flag round trip.  Measured (probe sweeps):
-# on 2 B200s LL took 8.6 us at a 1 MiB shard against NCCL's 22.9 us while the flagged
-# bulk push took 35.1 us at 2 MiB (NCCL 32.4 us); on 8 B200s LL beat NCCL up to a 4 MiB
-# shard (105.4 vs 113.0 us) and lost at 8 MiB (211.0 vs 195.8 us).  LL carries shards
-# up to 4 MiB.
-DEFAULT_LL_MAX = 4 << 20
+# LL doubles the bytes but needs no fence or flag round trip.  The default is derived
+# from the committed table (``ll_max`` of the worlds whose sweep timed the all-gather
+# protocols separately; on 2 B200s LL beat the push, NVLS and NCCL up to its 4 MiB slot,
+# 20.7 against 23.1 / 41.1 / 39.5 us at 4 MiB); this fallback applies without it.  On 8
+# B200s LL beat NCCL up to 4 MiB (105.4 vs 113.0 us) and lost at 8 MiB (211.0 vs 195.8).
+FALLBACK_LL_MAX = 4 << 20
 # Messages at or above this use NVLS when it is enabled and available (the measured
 # threshold of the smallest world size that has one, else this fallback).
 FALLBACK_NVLS_MIN = 256 << 10
@@ -78,7 +78,7 @@ class CollectivePolicy:
     all_reduce_capacity_bytes: int
     all_gather_shard_bytes: int
     oneshot_max_bytes: Mapping[int, int] = field(default_factory=lambda: dict(DEFAULT_ONESHOT_MAX))  # noqa: F821
-    ll_max_bytes: int = DEFAULT_LL_MAX
+    ll_max_bytes: int = field(default_factory=lambda: DEFAULT_LL_MAX)
     allow_nvls: bool = False
     nvls_min_bytes: int = field(default_factory=lambda: DEFAULT_NVLS_MIN)  # noqa: F821
     force: str | None = None
@@ -193,41 +193,58 @@ MEASURED_TABLE = Path(__file__).with_name("measured_b200.json")
 
 @dataclass(frozen=True)
 class MeasuredLimits:
-    """Per-world-size limits derived from an all-reduce latency sweep.
+    """Per-world-size limits derived from latency sweeps.
 
     - ``oneshot_max``: the largest size up to which one-shot is never slower than
       two-shot (the one-shot / two-shot crossover);
     - ``dispatch_max``: the largest size up to which the faster NVLink arm is never
       slower than NCCL (the all-reduce dispatch ceiling);
     - ``nvls_min``: the smallest size from which NVLS beats both push arms at every
-      measured size (None when NVLS was not measured or never wins).
+      measured size (None when NVLS was not measured or never wins);
+    - ``ll_max``: the largest all-gather shard up to which the LL8 protocol is never
+      slower than any other all-gather arm (only worlds whose sweep timed the
+      protocols separately).
     """
 
     oneshot_max: Mapping[int, int]
     dispatch_max: Mapping[int, int]
     nvls_min: Mapping[int, int | None]
+    ll_max: Mapping[int, int] = field(default_factory=dict)
+
+
+SWEPT_OPERATIONS = ("all_reduce", "all_gather")
 
 
 def sweep_rows(receipt: Mapping, world: int) -> list[dict]:
-    """All-reduce rows of a probe receipt (``sparknet probe collectives --benchmark
-    --sweep``) as ``{world, nbytes, arm, p50_us}``; the arm is the backend the case
-    ran on (a forced arm outside its range ran elsewhere and is dropped)."""
+    """All-reduce and all-gather rows of a probe receipt (``sparknet probe collectives
+    --benchmark --sweep``) as ``{world, nbytes, arm, p50_us}`` (plus ``operation`` for
+    the all-gather); the arm is the backend the case ran on (a forced arm outside its
+    range ran elsewhere and is dropped).  All-gather rows count only when the sweep
+    timed its protocols (``ll``, ``push``, ``nvls``) as separate arms."""
     item = {"bfloat16": 2, "float16": 2, "float32": 4}
     out = []
     for row in receipt.get("timings", ()):
-        if row.get("operation") != "all_reduce" or row.get("arm") == "policy":
+        operation = row.get("operation")
+        if operation not in SWEPT_OPERATIONS or row.get("arm") == "policy":
             continue
         if row.get("backend", row["arm"]) != row["arm"]:
             continue
+        if operation == "all_gather" and row["arm"] not in ("ll", "push", "nvls", "nccl"):
+            continue
         dtype = str(row["dtype"]).rsplit(".", 1)[-1]
-        out.append({"world": int(world), "nbytes": int(row["elements_per_rank"]) * item[dtype], "arm": row["arm"],
-                    "p50_us": float(row["median_us"])})
+        entry = {"world": int(world), "nbytes": int(row["elements_per_rank"]) * item[dtype], "arm": row["arm"],
+                 "p50_us": float(row["median_us"])}
+        if operation != "all_reduce":
+            entry["operation"] = operation
+        out.append(entry)
     return out
 
 
-def _by_world_size(rows) -> dict[int, dict[int, dict[str, float]]]:
+def _by_world_size(rows, operation: str = "all_reduce") -> dict[int, dict[int, dict[str, float]]]:
     table: dict[int, dict[int, dict[str, float]]] = {}
     for row in rows:
+        if row.get("operation", "all_reduce") != operation:
+            continue
         table.setdefault(int(row["world"]), {}).setdefault(int(row["nbytes"]), {})[row["arm"]] = float(row["p50_us"])
     return table
 
@@ -260,7 +277,22 @@ def derive_limits(rows) -> MeasuredLimits:
                 else:
                     nvls_from = None
         oneshot[world], dispatch[world], nvls[world] = one_lim, disp_lim, nvls_from
-    return MeasuredLimits(oneshot, dispatch, nvls)
+    ll = {}
+    for world, sizes in _by_world_size(rows, "all_gather").items():
+        # only sizes at which the protocols themselves were timed (a receipt of another
+        # sweep may add NCCL-only rows at other sizes)
+        timed = [n for n in sorted(sizes) if any(a in sizes[n] for a in ("ll", "push", "nvls"))]
+        if not timed:
+            continue
+        ll_lim = 0
+        for nbytes in timed:
+            arms = sizes[nbytes]
+            others = [v for a, v in arms.items() if a != "ll"]
+            if "ll" not in arms or (others and arms["ll"] > min(others)):
+                break  # beyond the LL slot, or LL lost: the limit stops here
+            ll_lim = nbytes
+        ll[world] = ll_lim
+    return MeasuredLimits(oneshot, dispatch, nvls, ll)
 
 
 def load_measured(path: str | Path | None = None) -> MeasuredLimits | None:
@@ -304,6 +336,8 @@ DEFAULT_ONESHOT_MAX = {1: 1 << 62, **FALLBACK_ONESHOT_MAX,
 _DISPATCH_BY_WORLD = dict(_MEASURED.dispatch_max) if _MEASURED else {}
 _nvls = sorted((w, v) for w, v in (_MEASURED.nvls_min.items() if _MEASURED else ()) if v)
 DEFAULT_NVLS_MIN = _nvls[0][1] if _nvls else FALLBACK_NVLS_MIN
+_ll = [v for v in (_MEASURED.ll_max.values() if _MEASURED else ()) if v]
+DEFAULT_LL_MAX = min(_ll) if _ll else FALLBACK_LL_MAX  # the smallest measured limit holds for every world
 
 
 def default_dispatch_bytes(world: int) -> int:

@@ -139,3 +139,48 @@ def test_sweep_rows_keep_cases_that_ran_on_their_arm():
     ]}
     assert sweep_rows(receipt, 4) == [{"world": 4, "nbytes": 4096, "arm": "oneshot", "p50_us": 5.0},
                                      {"world": 4, "nbytes": 4096, "arm": "nccl", "p50_us": 9.0}]
+
+
+def test_sweep_rows_take_the_all_gather_protocol_arms():
+    from sparknet.policy import sweep_rows
+
+    def ag(arm, elements, us, backend=None):
+        return {"operation": "all_gather", "arm": arm, "backend": backend or arm, "dtype": "torch.bfloat16",
+                "elements_per_rank": elements, "median_us": us}
+
+    receipt = {"timings": [ag("ll", 2048, 4.5), ag("push", 2048, 9.7), ag("nccl", 2048, 12.7),
+                           ag("oneshot", 2048, 5.0),              # the policy's pick, not a protocol arm
+                           ag("nvls", 4096, 20.0, backend="push")]}  # ran elsewhere: dropped
+    rows = sweep_rows(receipt, 2)
+    assert [(r["arm"], r["nbytes"], r["operation"]) for r in rows] == [
+        ("ll", 4096, "all_gather"), ("push", 4096, "all_gather"), ("nccl", 4096, "all_gather")]
+
+
+def test_derive_ll_limit_from_the_protocol_sweep():
+    from sparknet.policy import derive_limits
+
+    def row(world, kib, arm, us, op="all_gather"):
+        return {"world": world, "nbytes": kib << 10, "arm": arm, "p50_us": us, "operation": op}
+
+    rows = [
+        row(2, 4, "ll", 4.5), row(2, 4, "push", 9.7), row(2, 4, "nvls", 17.0), row(2, 4, "nccl", 12.7),
+        row(2, 8, "nccl", 13.0),                                     # an NCCL-only size from another sweep
+        row(2, 1024, "ll", 8.3), row(2, 1024, "push", 17.3), row(2, 1024, "nccl", 21.8),
+        row(2, 4096, "ll", 20.7), row(2, 4096, "push", 23.1), row(2, 4096, "nccl", 39.5),
+        row(2, 8192, "push", 30.7), row(2, 8192, "nccl", 51.2),     # beyond the LL slot
+        row(8, 4, "nccl", 29.0),                                     # no protocol rows at W = 8
+        row(4, 4, "ll", 6.0), row(4, 4, "push", 9.0),
+        row(4, 64, "ll", 12.0), row(4, 64, "push", 10.0),            # LL loses: the limit stops at 4 KiB
+        row(4, 128, "ll", 11.0), row(4, 128, "push", 14.0),
+    ]
+    lim = derive_limits(rows)
+    assert lim.ll_max == {2: 4096 << 10, 4: 4 << 10}
+    assert lim.oneshot_max == {} and lim.dispatch_max == {}         # all-gather rows leave the all-reduce limits alone
+
+
+def test_committed_table_sets_the_ll_default():
+    from sparknet.policy import load_measured, policy
+
+    lim = load_measured()
+    assert lim is not None and lim.ll_max
+    assert policy.DEFAULT_LL_MAX == min(v for v in lim.ll_max.values() if v)
