@@ -153,7 +153,8 @@ def test_tiny_model_step_matches_torch(device, native, gemm):
 
 @pytest.mark.parametrize("M,N,K,swiglu,max_splits", [
     (1, 1280, 8192, False, 0), (8, 8192, 1024, False, 0), (8, 7168, 8192, True, 0), (33, 1000, 512, False, 0),
-    (64, 2048, 3584, False, 0), (16, 512, 1024, False, 1), (200, 384, 256, True, 0), (8, 16032, 8192, False, 0)])
+    (64, 2048, 3584, False, 0), (16, 512, 1024, False, 1), (200, 384, 256, True, 0), (8, 16032, 8192, False, 0),
+    (64, 1000, 512, False, 1), (64, 1024, 512, True, 1), (37, 896, 2048, True, 3)])
 def test_decode_gemm(device, native, M, N, K, swiglu, max_splits):
     from sparknet.ops.decode_gemm import DecodeGemm, split_gate_up
 
