@@ -161,29 +161,34 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
   stamp(1);  // barriers and TMEM ready
   const uint32_t lane_base = tmem + (uint32_t(warp * 32) << 16);
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  // q, the newest key / value row and the lengths are written by earlier kernels
-  asm volatile("griddepcontrol.wait;" ::: "memory");
 
-  // Every tile that starts inside this sequence's cache is requested at once, before the
-  // length is known (a tile past the length is masked, then drained before exit), so the
-  // K/V round trip overlaps the loads of q and of the length.
+  // Every tile that starts inside this sequence's cache is requested at once, before q
+  // is staged (a tile past the length is masked, then drained before exit), so the K/V
+  // round trip overlaps the loads of q.  Programmatic dependent launch: the preceding
+  // kernel may still be writing q and the newest key / value row (lengths[b] - 1); the
+  // lengths and the older rows come from kernels before it.  Tiles wholly below the
+  // newest key are therefore requested before griddepcontrol.wait, the rest after it.
   const int chunk = T * kTcKeys;
   const int start = s * chunk;
   const int issued = start < Lmax ? min(T, (Lmax - start + kTcKeys - 1) / kTcKeys) : 0;
+  auto issue_tile = [&](int i) {
+    const int row = b * Lmax + start + i * kTcKeys;
+    tc::mbar_expect_tx(&k_full[i], kTileBytes);
+    tma_load_3d(base + L::k + i * kTileBytes, &map_k, 0, h, row, &k_full[i]);
+    tma_load_3d(base + L::k + i * kTileBytes + kHalfBytes, &map_k, 64, h, row, &k_full[i]);
+    tc::mbar_expect_tx(&v_full[i], kTileBytes);
+    tma_load_3d(base + L::v + i * kTileBytes, &map_v, 0, h, row, &v_full[i]);
+    tma_load_3d(base + L::v + i * kTileBytes + kHalfBytes, &map_v, 64, h, row, &v_full[i]);
+  };
+  int early = 0;
   if (t == 0) {
-    for (int i = 0; i < issued; ++i) {
-      const int row = b * Lmax + start + i * kTcKeys;
-      tc::mbar_expect_tx(&k_full[i], kTileBytes);
-      tma_load_3d(base + L::k + i * kTileBytes, &map_k, 0, h, row, &k_full[i]);
-      tma_load_3d(base + L::k + i * kTileBytes + kHalfBytes, &map_k, 64, h, row, &k_full[i]);
-    }
-    for (int i = 0; i < issued; ++i) {
-      const int row = b * Lmax + start + i * kTcKeys;
-      tc::mbar_expect_tx(&v_full[i], kTileBytes);
-      tma_load_3d(base + L::v + i * kTileBytes, &map_v, 0, h, row, &v_full[i]);
-      tma_load_3d(base + L::v + i * kTileBytes + kHalfBytes, &map_v, 64, h, row, &v_full[i]);
-    }
+    const int newest = min(lengths[b], Lmax) - 1;
+    while (early < issued && start + (early + 1) * kTcKeys <= newest) ++early;
+    for (int i = 0; i < early; ++i) issue_tile(i);
   }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (t == 0)
+    for (int i = early; i < issued; ++i) issue_tile(i);
   // Q: 16 rows (G real heads, the rest zero) x 128 dims into the swizzled B-operand image
   for (int i = t; i < kTcHeads * 16; i += kTcThreads) {
     const int r = i >> 4, c = i & 15;  // row, 16-byte chunk of the 256-byte row

@@ -19,7 +19,11 @@ The workspace is held per device here (its counters must start at zero; every co
 call leaves them so), or passed in.  ``q`` is ``[B, Hq, 128]``, the caches
 ``[B, Lmax, Hkv, 128]``, ``lengths`` ``[B]`` int32 (keys to attend, the new token
 included, at most ``max_len``).  ``pdl=True`` launches with programmatic dependent
-launch (the kernel waits for its predecessor before it reads q, K/V or lengths).
+launch: the kernel may start while its predecessor runs.  It reads ``lengths`` and the
+K/V rows below the newest key (``lengths[b] - 1``) before it waits for the predecessor,
+q and the newest key / value row after; so the immediately preceding kernel may write q
+and the newest cache row (as the decode step's QKV GEMM does), not ``lengths`` or older
+rows.
 """
 
 from __future__ import annotations
