@@ -38,7 +38,8 @@ def test_rope_qkv_cache(device, native):
 
 
 ATTENTION_SHAPES = [(1, 8, 1, 1025), (4, 8, 1, 300), (2, 64, 8, 129), (64, 8, 1, 1280), (3, 4, 4, 33),
-                    (8, 8, 1, 1024), (2, 16, 1, 300), (1, 8, 1, 9000), (2, 8, 1, 128), (1, 1, 1, 200), (4, 16, 4, 257)]
+                    (8, 8, 1, 1024), (2, 16, 1, 300), (1, 8, 1, 9000), (2, 8, 1, 128), (1, 1, 1, 200), (4, 16, 4, 257),
+                    (32, 16, 2, 700), (8, 64, 8, 1024)]
 
 
 @pytest.mark.parametrize("impl", [1, 2])
