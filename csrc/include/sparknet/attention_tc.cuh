@@ -61,8 +61,8 @@ struct TcLayout {  // byte offsets from the 1024-aligned base of dynamic shared 
   static constexpr int p = q + 2 * kQHalfBytes;                // P[t][atom]
   static constexpr int red = p + T * 2 * kPAtomBytes;          // [2][4][16] floats: per-warp max, sum
   static constexpr int stat = red + 2 * 4 * kTcHeads * 4;      // [16][2] floats: span max, sum
-  static constexpr int bars = stat + kTcHeads * 2 * 4;         // mbarriers: k_full[T], v_full[T], s_done, o_done
-  static constexpr int misc = bars + (2 * T + 2) * 8;          // tmem slot, error flag, last flag
+  static constexpr int bars = stat + kTcHeads * 2 * 4;         // mbarriers: k_full[T], v_full[T], s_done, o_done, m_full
+  static constexpr int misc = bars + (2 * T + 3) * 8;          // tmem slot, error flag, last flag
   static constexpr int end = misc + 16;
   static constexpr int bytes = end + 1024;                     // + alignment slack
 };
@@ -130,6 +130,7 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* v_full = k_full + T;
   uint64_t* s_done = v_full + T;
   uint64_t* o_done = s_done + 1;
+  uint64_t* m_full = o_done + 1;  // workspace merge: the partial outputs' bulk copy
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + L::misc);
   volatile uint32_t* bad = reinterpret_cast<volatile uint32_t*>(base + L::misc + 4);
   int* last = reinterpret_cast<int*>(base + L::misc + 8);
@@ -150,6 +151,7 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
     }
     tc::mbar_init(s_done, 1);
     tc::mbar_init(o_done, 1);
+    tc::mbar_init(m_full, 1);
     *bad = 0u;
     tc::fence_barrier_init();
   }
@@ -410,8 +412,24 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
 
   // Merge the spans of each head in span order.  Every (max, sum) pair is loaded in one
   // parallel pass, the weights are formed per head, then each thread (one dimension)
-  // loads its partial outputs in batches with every load of a batch issued first.
+  // sums its partial outputs.  The partial outputs of this KV head's G heads are one
+  // contiguous block; when it fits the free K/V tiles, one bulk copy brings it into
+  // shared memory while the (max, sum) pairs load and the weights form (measured at 64
+  // sequence-head pairs x 9 spans: the L2 loop below took 5 us, three dependent round
+  // trips of 32 loads).
   float* ml = reinterpret_cast<float*>(base + L::k);  // [G][nsplit][2]; K tiles are free now
+  float* accs = ml + 2 * G * nsplit;                    // [G][kTcThreads] running sums
+  const int pairs = G * nsplit;
+  const uint32_t po_bytes = uint32_t(pairs) * kHead * 4;
+  const uint32_t ps_off = (uint32_t(2 * G * nsplit + G * kTcThreads) * 4 + 15u) & ~15u;
+  const float* po_all = part_o + head0 * nsplit * kHead;  // pair i = g * nsplit + sp at [i * kHead]
+  const bool staged = ps_off + po_bytes <= uint32_t(L::q - L::k);
+  float* ps = reinterpret_cast<float*>(base + L::k + ps_off);
+  if (staged && t == 0) {
+    asm volatile("fence.proxy.async.global;" ::: "memory");  // the other spans' stores before the copy reads
+    tc::mbar_expect_tx(m_full, po_bytes);
+    tc::bulk_load(ps, po_all, po_bytes, m_full);
+  }
   for (int i = t; i < G * nsplit; i += kTcThreads) {
     const size_t row = (head0 + i / nsplit) * nsplit + i % nsplit;
     const float2 v = __ldcg(reinterpret_cast<const float2*>(part_ml + row * 2));
@@ -434,29 +452,45 @@ static __global__ void __launch_bounds__(kTcThreads, 1)
   }
   __syncthreads();
   stamp(9);  // merge: weights formed
-  // The partial outputs of every (head, span) pair, kBatch loads in flight before any is
-  // used (one L2 round trip per kBatch pairs).  The loop is kept compact on purpose: the
-  // merge runs once per (sequence, KV head), so its code is always cold in the
-  // instruction cache, and a fully unrolled form spent ~29 us fetching instructions.
-  // Each head's sum goes to a shared-memory column of this thread, spans in order.
+  // Each head's sum goes to a shared-memory column of this thread, spans in order.  The
+  // loop is kept compact on purpose: the merge runs once per (sequence, KV head), so its
+  // code is always cold in the instruction cache, and a fully unrolled form spent ~29 us
+  // fetching instructions.  From L2, kBatch loads are in flight before any is used.
   constexpr int kBatch = 32;
-  float* accs = ml + 2 * G * nsplit;  // [G][kTcThreads] running sums
 #pragma unroll 1
   for (int g = 0; g < G; ++g) accs[g * kTcThreads + t] = 0.0f;
-  const float* po = part_o + head0 * nsplit * kHead + t;  // pair i = g * nsplit + sp at po[i * kHead]
-  const int pairs = G * nsplit;
+  if (staged) {
+    // a failed wait leaves the partials unread: the error word reports the launch
+    if (tc::mbar_wait(m_full, 0, bad)) {
+      // per head a register sum over the spans in order (from 0, as the L2 path sums)
 #pragma unroll 1
-  for (int i0 = 0; i0 < pairs; i0 += kBatch) {
-    float v[kBatch];
+      for (int g = 0; g < G; ++g) {
+        const float* pg = ps + size_t(g) * nsplit * kHead + t;
+        const float* wg = ml + 2 * g * nsplit;
+        float a = 0.0f;
+#pragma unroll 4
+        for (int sp = 0; sp < nsplit; ++sp) a += pg[sp * kHead] * wg[2 * sp];
+        accs[g * kTcThreads + t] = a;
+      }
+    } else {
+      if (t == 0) atomicExch(&counters[kErrorSlot], 1);
+      tc::mbar_drain(m_full, 0);  // the copy lands before this CTA's shared memory goes away
+    }
+  } else {
+    const float* po = po_all + t;
+#pragma unroll 1
+    for (int i0 = 0; i0 < pairs; i0 += kBatch) {
+      float v[kBatch];
 #pragma unroll
-    for (int j = 0; j < kBatch; ++j) v[j] = i0 + j < pairs ? __ldcg(po + size_t(i0 + j) * kHead) : 0.0f;
-    int g = i0 / nsplit, sp = i0 - g * nsplit;
+      for (int j = 0; j < kBatch; ++j) v[j] = i0 + j < pairs ? __ldcg(po + size_t(i0 + j) * kHead) : 0.0f;
+      int g = i0 / nsplit, sp = i0 - g * nsplit;
 #pragma unroll
-    for (int j = 0; j < kBatch; ++j) {
-      if (i0 + j < pairs) accs[g * kTcThreads + t] += v[j] * ml[2 * (i0 + j)];
-      if (++sp == nsplit) {
-        sp = 0;
-        ++g;
+      for (int j = 0; j < kBatch; ++j) {
+        if (i0 + j < pairs) accs[g * kTcThreads + t] += v[j] * ml[2 * (i0 + j)];
+        if (++sp == nsplit) {
+          sp = 0;
+          ++g;
+        }
       }
     }
   }
