@@ -181,3 +181,32 @@ def test_freeze_gate_refuses_lazy_setup_and_counts():
     finally:
         _freeze.thaw_kernel_resolution()
     assert not _freeze.kernel_resolution_frozen()
+
+
+def _bare_runtime(**attrs):
+    """An NvlinkAllReduce shell with only the attributes a host-side rule reads."""
+    from sparknet.oneshot.runtime import NvlinkAllReduce
+
+    rt = object.__new__(NvlinkAllReduce)
+    for name, value in attrs.items():
+        setattr(rt, name, value)
+    return rt
+
+
+def test_forced_gather_protocol_must_fit():
+    rt = _bare_runtime(world_size=8, _caps=(2 << 20, 4 << 20), _mc=(0, 0, 16 << 20), has_multicast=True)
+    assert rt._gather_algorithm_fits("ll", 4 << 20) and not rt._gather_algorithm_fits("ll", (4 << 20) + 16)
+    assert rt._gather_algorithm_fits("nvls", 2 << 20)                    # 8 x 2 MiB fills the 16 MiB window
+    assert not rt._gather_algorithm_fits("nvls", (2 << 20) + 16)
+    assert rt._gather_algorithm_fits("push", 1 << 30)
+    assert not _bare_runtime(world_size=8, _caps=(0, 0), _mc=(0, 0, 16 << 20),
+                             has_multicast=False)._gather_algorithm_fits("nvls", 4096)
+
+
+def test_fused_norm_token_limit_by_world():
+    from sparknet.oneshot.runtime import FUSED_NORM_MAX_TOKENS
+
+    limits = {w: _bare_runtime(world_size=w).fused_norm_max_tokens() for w in (1, 2, 4, 8)}
+    assert limits == {1: FUSED_NORM_MAX_TOKENS[1], 2: FUSED_NORM_MAX_TOKENS[2], 4: FUSED_NORM_MAX_TOKENS[2],
+                      8: FUSED_NORM_MAX_TOKENS[8]}
+    assert limits[1] == 0 and limits[2] < limits[8]
