@@ -50,6 +50,19 @@ _LIMITS = {
     "TIMEOUT_MS": "10000",
 }
 _NO_LIMITS = {key: None for key in _LIMITS}
+
+
+def _measured_limits(world: int) -> dict[str, str]:
+    """The limits of a profile pinned to one world size: the all-reduce dispatch ceiling
+    measured for it (``sparknet/policy/measured_b200.json``), with the registered capacity
+    raised to hold it; the general limits where nothing was measured."""
+    from sparknet.policy.policy import default_dispatch_bytes
+
+    limits = dict(_LIMITS)
+    dispatch = default_dispatch_bytes(world)
+    limits["ALLREDUCE_DISPATCH_MAX_BYTES"] = str(dispatch)
+    limits["ALLREDUCE_CAPACITY_BYTES"] = str(max(int(_LIMITS["ALLREDUCE_CAPACITY_BYTES"]), dispatch))
+    return limits
 _WORLDS = (1, 2, 4, 8)
 
 PROFILES: dict[str, dict[str, Any]] = {
@@ -64,10 +77,11 @@ PROFILES: dict[str, dict[str, Any]] = {
     "nvlink-8": {
         "transport": "nvlink",
         "node_counts": (8,),
-        "status": "product on a full box: as nvlink, pinned to tensor-parallel size 8 (every GPU of an HGX B200)",
+        "status": "product on a full box: as nvlink, pinned to tensor-parallel size 8 (every GPU of an HGX B200), "
+                  "with the all-reduce dispatch ceiling measured at 8 GPUs (the NVLink kernels beat NCCL up to it)",
         "nccl": {"NCCL_NVLS_ENABLE": None, "NCCL_P2P_LEVEL": None, "NCCL_ALGO": None, "NCCL_PROTO": None},
-        "limits": dict(_LIMITS),
-        "evidence": "bench.py --gpus 8 and the decode benchmark on 8x B200",
+        "limits": _measured_limits(8),
+        "evidence": "bench.py --gpus 8, the decode benchmark and the 8-GPU probe sweep on 8x B200",
     },
     "nvlink-nvls": {
         "transport": "nvlink-nvls",
