@@ -75,3 +75,14 @@ def test_recipes_are_current():
     out = subprocess.run([sys.executable, str(root / "recipes" / "generate.py"), "--check"], capture_output=True,
                          text=True)
     assert out.returncode == 0, out.stdout + out.stderr
+
+
+def test_full_box_profile_carries_the_measured_dispatch_ceiling():
+    from sparknet.policy import default_dispatch_bytes, policy_for_profile
+
+    pol = policy_for_profile("nvlink-8")
+    assert pol.all_reduce_dispatch_bytes == default_dispatch_bytes(8)
+    assert pol.all_reduce_capacity_bytes >= pol.all_reduce_dispatch_bytes
+    assert not nccl.problems(nccl.environment("nvlink-8"), world=8)
+    general = policy_for_profile("nvlink")
+    assert general.all_reduce_dispatch_bytes == 2 << 20   # valid at every world size, W = 4 unmeasured
