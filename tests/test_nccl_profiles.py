@@ -78,7 +78,8 @@ def test_recipes_are_current():
 
 
 def test_full_box_profile_carries_the_measured_dispatch_ceiling():
-    from sparknet.policy import default_dispatch_bytes, policy_for_profile
+    from sparknet.policy import policy_for_profile
+    from sparknet.policy.policy import default_dispatch_bytes
 
     pol = policy_for_profile("nvlink-8")
     assert pol.all_reduce_dispatch_bytes == default_dispatch_bytes(8)
